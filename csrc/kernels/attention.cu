@@ -1,0 +1,489 @@
+// Paged flash attention over the block-table KV cache (prefill chunks, decode, split-KV combine).
+//
+// Replaces the reference's attention paths: ggml-cuda flash_attn_ext_f16 (fattn-mma-f16.cuh:1707,
+// contiguous llama KV, used for prefill) and flash_attn_ext_vec (fattn-vec.cuh:21, decode), plus
+// vm_c's unreachable paged kernels (src/cuda/attention_kernels.cu:37,140,271). Here the KV cache
+// is vm_c's paged layout: per layer [num_blocks, 2 (K,V), Hkv, block_size=16, D] bf16, addressed
+// through per-request block tables.
+//
+// GQA packing: all G = Hq/Hkv query heads that share a KV head are processed by one CTA as rows of
+// one tile (packed row = token * G + head), so every K/V byte is loaded once per group. Tiles are
+// 16 packed rows per warp and use mma.sync m16n8k16 (bf16 -> fp32): a decode tile has only
+// G (4..8) real rows, below the 64/128-row minimum of a tcgen05 MMA, and decode attention is bound
+// by HBM bandwidth, not by tensor throughput.
+//
+//  * attn_decode_kernel  : 16 packed rows per CTA (q_len * G <= 16), 4 warps walk disjoint KV pages
+//                          (per-warp cp.async double buffering) and merge through shared memory.
+//                          grid.z splits the KV range across CTAs; partials (+LSE) are merged by
+//                          attn_combine_kernel.
+//  * attn_prefill_kernel : 64 packed rows per CTA (4 warps x 16), 64-key tiles shared by the warps,
+//                          causal mask against each row's absolute position.
+#include "attention.h"
+#include "common.cuh"
+
+namespace vmc {
+namespace {
+
+constexpr int kBS = 16;  // tokens per KV block
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct Frag {
+  static constexpr int KD = D / 16;  // k-steps over the head dim
+  static constexpr int ND = D / 8;   // n-tiles over the head dim
+  static constexpr int RB = D * 2 + 16;  // padded smem row stride (bytes) -> conflict-free ldmatrix
+};
+
+struct AttnParams {
+  const __nv_bfloat16* q;   // [T, Hq, D]
+  const __nv_bfloat16* kv;  // [num_blocks, 2, Hkv, 16, D]
+  const int32_t* q_start;   // [R + 1]
+  const int32_t* ctx_len;   // [R]
+  const int32_t* block_tables;  // [R, max_blocks]
+  int max_blocks;
+  int Hq, Hkv, G;
+  float scale_log2;         // softmax scale * log2(e)
+  __nv_bfloat16* out;       // [T, Hq, D]
+  int splits;
+  float* part_o;            // [splits, T, Hq, D] (split-KV only)
+  float* part_lse;          // [splits, T, Hq]
+  int req_offset;           // first request index handled by this launch
+};
+
+// Copy one 16 x D page (K or V) into a padded smem tile (rows 16*slot .. 16*slot+15).
+template <int D>
+__device__ __forceinline__ void load_page_warp(uint8_t* smem_tile, int row0, const __nv_bfloat16* src, int lane) {
+  constexpr int CH = D / 8;           // 16-byte chunks per row
+  constexpr int TOTAL = kBS * CH;     // chunks per page
+#pragma unroll
+  for (int i = lane; i < TOTAL; i += 32) {
+    const int r = i / CH, c = i % CH;
+    cp_async16(smem_u32(smem_tile + (row0 + r) * Frag<D>::RB + c * 16), src + r * D + c * 8);
+  }
+}
+
+// Load Q fragments for the 16 packed rows starting at `prow0` of request r.
+template <int D>
+__device__ __forceinline__ void load_q_frags(const AttnParams& p, int qs, int qlen, int kvh, int prow0, int lane,
+                                             uint32_t (&qa)[Frag<D>::KD][4]) {
+  const int rows = qlen * p.G;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int pr = prow0 + (lane >> 2) + 8 * half;
+    const bool valid = pr < rows;
+    const int t = valid ? pr / p.G : 0, g = valid ? pr % p.G : 0;
+    const __nv_bfloat16* qrow = p.q + (static_cast<int64_t>(qs + t) * p.Hq + kvh * p.G + g) * D;
+#pragma unroll
+    for (int kd = 0; kd < Frag<D>::KD; ++kd) {
+      const int d0 = 16 * kd + 2 * (lane & 3);
+      qa[kd][half] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
+      qa[kd][2 + half] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+    }
+  }
+}
+
+// One 16-key step of attention for a warp's 16 rows. K/V rows key0..key0+15 of the smem tiles.
+// kpos0: absolute position of the first key; qpos_lo/hi: absolute positions of this thread's two
+// rows (or -1 for invalid rows); klimit: number of valid keys (context length).
+template <int D>
+__device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV, int key0, int kpos0,
+                                            const uint32_t (&qa)[Frag<D>::KD][4], int qpos_lo, int qpos_hi,
+                                            float scale_log2, float (&o)[Frag<D>::ND][4], float (&m)[2],
+                                            float (&l)[2], int lane) {
+  constexpr int RB = Frag<D>::RB;
+  float s[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
+  // S = Q K^T over 16 keys (two n-tiles of 8).
+#pragma unroll
+  for (int kd = 0; kd < Frag<D>::KD; ++kd) {
+    uint32_t b[4];
+    const int i = lane;
+    const int key = key0 + (i & 7) + 8 * (i >> 4);
+    const int dim = 16 * kd + 8 * ((i >> 3) & 1);
+    ldmatrix_x4(b, smem_u32(sK + key * RB + dim * 2));
+    mma_bf16_16816(s[0], qa[kd], b[0], b[1]);
+    mma_bf16_16816(s[1], qa[kd], b[2], b[3]);
+  }
+  // Mask + online softmax. Thread holds rows (lane/4) [e=0,1] and (lane/4 + 8) [e=2,3].
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int kp = kpos0 + 8 * j + 2 * (lane & 3) + (e & 1);
+      const int qp = (e < 2) ? qpos_lo : qpos_hi;
+      float v = s[j][e] * scale_log2;
+      if (kp > qp) v = -INFINITY;
+      s[j][e] = v;
+      mx[e >> 1] = fmaxf(mx[e >> 1], v);
+    }
+  }
+  float corr[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    const float mnew = fmaxf(m[h], mx[h]);
+    corr[h] = (mnew == -INFINITY) ? 1.f : exp2f(m[h] - mnew);
+    m[h] = mnew;
+  }
+  float rs[2] = {0.f, 0.f};
+  uint32_t pa[4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float pv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float mm = m[e >> 1];
+      pv[e] = (mm == -INFINITY) ? 0.f : exp2f(s[j][e] - mm);
+      rs[e >> 1] += pv[e];
+    }
+    // A fragment of P (16 rows x 16 keys): a0/a1 from n-tile 0, a2/a3 from n-tile 1.
+    pa[2 * j] = pack_bf16x2(pv[0], pv[1]);
+    pa[2 * j + 1] = pack_bf16x2(pv[2], pv[3]);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+    rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+    l[h] = l[h] * corr[h] + rs[h];
+  }
+#pragma unroll
+  for (int nd = 0; nd < Frag<D>::ND; ++nd) {
+    o[nd][0] *= corr[0];
+    o[nd][1] *= corr[0];
+    o[nd][2] *= corr[1];
+    o[nd][3] *= corr[1];
+  }
+  // O += P V (16 keys = one k-step).
+#pragma unroll
+  for (int nd = 0; nd < Frag<D>::ND; nd += 2) {
+    uint32_t b[4];
+    const int i = lane;
+    const int key = key0 + (i & 7) + 8 * ((i >> 3) & 1);
+    const int dim = 8 * nd + 8 * (i >> 4);
+    ldmatrix_x4_trans(b, smem_u32(sV + key * RB + dim * 2));
+    mma_bf16_16816(o[nd], pa, b[0], b[1]);
+    mma_bf16_16816(o[nd + 1], pa, b[2], b[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Decode: one CTA = (request, kv head, split); 16 packed rows; 4 warps split the pages.
+
+template <int D>
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int total_tokens) {
+  constexpr int RB = Frag<D>::RB;
+  constexpr int ND = Frag<D>::ND;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y;
+  const int r = blockIdx.x + p.req_offset;
+  const int split = blockIdx.z;
+  const int qs = p.q_start[r], qlen = p.q_start[r + 1] - qs;
+  const int ctx = p.ctx_len[r];
+  if (qlen <= 0) return;
+  const int nblocks = (ctx + kBS - 1) / kBS;
+  const int per_split = (nblocks + p.splits - 1) / p.splits;
+  const int b0 = split * per_split, b1 = min(nblocks, b0 + per_split);
+  const int32_t* bt = p.block_tables + static_cast<int64_t>(r) * p.max_blocks;
+
+  uint32_t qa[Frag<D>::KD][4];
+  load_q_frags<D>(p, qs, qlen, kvh, 0, lane, qa);
+  const int rows = qlen * p.G;
+  const int pr_lo = lane >> 2, pr_hi = pr_lo + 8;
+  const int qpos_lo = pr_lo < rows ? ctx - qlen + pr_lo / p.G : -1;
+  const int qpos_hi = pr_hi < rows ? ctx - qlen + pr_hi / p.G : -1;
+
+  float o[ND][4];
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+
+  // Per-warp double buffer: stage s holds K rows [0,16) and V rows [0,16) of one page.
+  uint8_t* wsm = smem + warp * (2 * 2 * kBS * RB);
+  auto sK = [&](int s) { return wsm + s * (2 * kBS * RB); };
+  auto sV = [&](int s) { return wsm + s * (2 * kBS * RB) + kBS * RB; };
+  const int64_t page_elems = static_cast<int64_t>(kBS) * D;
+  auto issue = [&](int b, int s) {
+    const int blk = bt[b];
+    const __nv_bfloat16* kp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + kvh) * page_elems;
+    const __nv_bfloat16* vp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + p.Hkv + kvh) * page_elems;
+    load_page_warp<D>(sK(s), 0, kp, lane);
+    load_page_warp<D>(sV(s), 0, vp, lane);
+  };
+  int b = b0 + warp;
+  int stage = 0;
+  if (b < b1) issue(b, 0);
+  cp_async_commit();
+  for (; b < b1; b += 4) {
+    const int nb = b + 4;
+    if (nb < b1) issue(nb, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    attn_step16<D>(sK(stage), sV(stage), 0, b * kBS, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane);
+    __syncwarp();
+    stage ^= 1;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // Merge the 4 warps: each writes (m, l, o) for its 16 rows to smem; warp 0 combines.
+  float* mo = reinterpret_cast<float*>(smem);           // [4][16][D]
+  float* ml = mo + 4 * 16 * D;                          // [4][16][2]
+  const int rlo = lane >> 2, rhi = rlo + 8;
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) {
+    const int d = 8 * nd + 2 * (lane & 3);
+    mo[(warp * 16 + rlo) * D + d] = o[nd][0];
+    mo[(warp * 16 + rlo) * D + d + 1] = o[nd][1];
+    mo[(warp * 16 + rhi) * D + d] = o[nd][2];
+    mo[(warp * 16 + rhi) * D + d + 1] = o[nd][3];
+  }
+  if ((lane & 3) == 0) {
+    ml[(warp * 16 + rlo) * 2 + 0] = m[0];
+    ml[(warp * 16 + rlo) * 2 + 1] = l[0];
+    ml[(warp * 16 + rhi) * 2 + 0] = m[1];
+    ml[(warp * 16 + rhi) * 2 + 1] = l[1];
+  }
+  __syncthreads();
+  // 128 threads: thread -> (row = tid / 8, 8 dim-chunks of D/8 each)
+  const int row = threadIdx.x >> 3;
+  if (row < rows) {
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, ml[(w * 16 + row) * 2]);
+    float L = 0.f, wsc[4];
+    for (int w = 0; w < 4; ++w) {
+      const float mw = ml[(w * 16 + row) * 2];
+      wsc[w] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      L += wsc[w] * ml[(w * 16 + row) * 2 + 1];
+    }
+    const int t = row / p.G, g = row % p.G;
+    const int64_t orow = static_cast<int64_t>(qs + t) * p.Hq + kvh * p.G + g;
+    constexpr int PER = D / 8;
+    const int d0 = (threadIdx.x & 7) * PER;
+    if (p.splits == 1) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      for (int d = d0; d < d0 + PER; d += 2) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int w = 0; w < 4; ++w) {
+          a0 += wsc[w] * mo[(w * 16 + row) * D + d];
+          a1 += wsc[w] * mo[(w * 16 + row) * D + d + 1];
+        }
+        *reinterpret_cast<uint32_t*>(p.out + orow * D + d) = pack_bf16x2(a0 * inv, a1 * inv);
+      }
+    } else {
+      // Partial: normalised O and log2-sum-exp of this split.
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      float* po = p.part_o + (static_cast<int64_t>(split) * total_tokens * p.Hq + orow) * D;
+      for (int d = d0; d < d0 + PER; ++d) {
+        float a = 0.f;
+        for (int w = 0; w < 4; ++w) a += wsc[w] * mo[(w * 16 + row) * D + d];
+        po[d] = a * inv;
+      }
+      if ((threadIdx.x & 7) == 0)
+        p.part_lse[static_cast<int64_t>(split) * total_tokens * p.Hq + orow] = (L > 0.f) ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// Merge split-KV partials: one warp per (token, head).
+template <int D>
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
+                                    int64_t rows, __nv_bfloat16* __restrict__ out) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, part_lse[s * rows + row]);
+  float wsum = 0.f;
+  float acc[D / 32];
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) acc[i] = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float lse = part_lse[s * rows + row];
+    const float w = (lse == -INFINITY) ? 0.f : exp2f(lse - M);
+    wsum += w;
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) acc[i] += w * part_o[(s * rows + row) * D + lane + 32 * i];
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) out[row * D + lane + 32 * i] = __float2bfloat16(acc[i] * inv);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Prefill / extend: one CTA = (64 packed rows, kv head, request). 64-key tiles shared by warps.
+
+template <int D>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
+  constexpr int RB = Frag<D>::RB;
+  constexpr int ND = Frag<D>::ND;
+  constexpr int TK = 64;  // keys per tile (4 pages)
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.z + p.req_offset;
+  const int kvh = blockIdx.y;
+  const int qs = p.q_start[r], qlen = p.q_start[r + 1] - qs;
+  const int rows = qlen * p.G;
+  const int prow_cta = blockIdx.x * 64;
+  if (prow_cta >= rows) return;
+  const int ctx = p.ctx_len[r];
+  const int32_t* bt = p.block_tables + static_cast<int64_t>(r) * p.max_blocks;
+  const int prow0 = prow_cta + 16 * warp;
+
+  uint32_t qa[Frag<D>::KD][4];
+  load_q_frags<D>(p, qs, qlen, kvh, prow0, lane, qa);
+  const int pr_lo = prow0 + (lane >> 2), pr_hi = pr_lo + 8;
+  const int qpos_lo = pr_lo < rows ? ctx - qlen + pr_lo / p.G : -1;
+  const int qpos_hi = pr_hi < rows ? ctx - qlen + pr_hi / p.G : -1;
+  // Keys needed by this CTA: up to the largest query position among its rows.
+  const int last_row = min(rows, prow_cta + 64) - 1;
+  const int kmax = ctx - qlen + last_row / p.G + 1;  // exclusive
+  const int ntiles = (kmax + TK - 1) / TK;
+  // Rows of this warp that exist at all (skip compute for fully invalid warps).
+  const bool warp_active = prow0 < rows;
+  const int warp_qmax = warp_active ? (ctx - qlen + (min(rows, prow0 + 16) - 1) / p.G) : -1;
+
+  float o[ND][4];
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+
+  auto sK = [&](int s) { return smem + s * (2 * TK * RB); };
+  auto sV = [&](int s) { return smem + s * (2 * TK * RB) + TK * RB; };
+  const int64_t page_elems = static_cast<int64_t>(kBS) * D;
+  constexpr int CH = D / 8;
+  auto issue = [&](int tile, int s) {
+    // 4 pages x (K, V) x 16 rows x CH chunks, spread over 128 threads.
+    constexpr int TOTAL = 4 * 2 * kBS * CH;
+    for (int i = threadIdx.x; i < TOTAL; i += 128) {
+      const int c = i % CH;
+      const int rr = (i / CH) % kBS;
+      const int kvsel = (i / (CH * kBS)) % 2;
+      const int pg = i / (CH * kBS * 2);
+      const int b = tile * 4 + pg;
+      const bool valid = b * kBS < kmax;
+      const int blk = valid ? bt[b] : 0;
+      const __nv_bfloat16* src =
+          p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + kvsel * p.Hkv + kvh) * page_elems + rr * D + c * 8;
+      uint8_t* dst = (kvsel ? sV(s) : sK(s)) + (pg * kBS + rr) * RB + c * 16;
+      cp_async16_zfill(smem_u32(dst), src, valid);
+    }
+  };
+  issue(0, 0);
+  cp_async_commit();
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int s = tile & 1;
+    if (tile + 1 < ntiles) issue(tile + 1, s ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (warp_active) {
+#pragma unroll
+      for (int sub = 0; sub < TK / 16; ++sub) {
+        const int kpos0 = tile * TK + sub * 16;
+        if (kpos0 <= warp_qmax && kpos0 < kmax)
+          attn_step16<D>(sK(s), sV(s), sub * 16, kpos0, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  if (!warp_active) return;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int pr = (half ? pr_hi : pr_lo);
+    if (pr >= rows) continue;
+    const int t = pr / p.G, g = pr % p.G;
+    const int64_t row = static_cast<int64_t>(qs + t) * p.Hq + kvh * p.G + g;
+    const float inv = l[half] > 0.f ? 1.f / l[half] : 0.f;
+    __nv_bfloat16* dst = p.out + row * D;
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+      const int d = 8 * nd + 2 * (lane & 3);
+      *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16x2(o[nd][2 * half] * inv, o[nd][2 * half + 1] * inv);
+    }
+  }
+}
+
+template <int D>
+void launch_decode(const AttnParams& p, int num_reqs, int total_tokens, cudaStream_t st) {
+  constexpr int RB = Frag<D>::RB;
+  const int smem_pipe = 4 * 2 * 2 * kBS * RB;
+  const int smem_merge = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
+  const int smem = smem_pipe > smem_merge ? smem_pipe : smem_merge;
+  static bool cfg = false;
+  if (!cfg) {
+    VMC_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cfg = true;
+  }
+  dim3 grid(num_reqs, p.Hkv, p.splits);
+  attn_decode_kernel<D><<<grid, 128, smem, st>>>(p, total_tokens);
+  VMC_CUDA_CHECK(cudaGetLastError());
+  if (p.splits > 1) {
+    const int64_t rows = static_cast<int64_t>(total_tokens) * p.Hq;
+    attn_combine_kernel<D><<<static_cast<int>((rows + 3) / 4), 128, 0, st>>>(p.part_o, p.part_lse, p.splits, rows, p.out);
+    VMC_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+template <int D>
+void launch_prefill(const AttnParams& p, int num_reqs, int max_qlen, cudaStream_t st) {
+  constexpr int RB = Frag<D>::RB;
+  const int smem = 2 * 2 * 64 * RB;
+  static bool cfg = false;
+  if (!cfg) {
+    VMC_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cfg = true;
+  }
+  dim3 grid((max_qlen * p.G + 63) / 64, p.Hkv, num_reqs);
+  attn_prefill_kernel<D><<<grid, 128, smem, st>>>(p);
+  VMC_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace
+
+void paged_attention(const AttnLaunch& a, cudaStream_t st) {
+  VMC_CHECK(a.Hq % a.Hkv == 0, "attention: Hq must be a multiple of Hkv");
+  AttnParams p;
+  p.q = static_cast<const __nv_bfloat16*>(a.q);
+  p.kv = static_cast<const __nv_bfloat16*>(a.kv);
+  p.q_start = a.q_start;
+  p.ctx_len = a.ctx_len;
+  p.block_tables = a.block_tables;
+  p.max_blocks = a.max_blocks;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.G = a.Hq / a.Hkv;
+  p.scale_log2 = a.scale * kLog2e;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.splits = a.decode ? (a.splits < 1 ? 1 : a.splits) : 1;
+  p.part_o = a.part_o;
+  p.part_lse = a.part_lse;
+  p.req_offset = a.req_offset;
+  if (a.num_reqs <= 0) return;
+  if (a.decode) {
+    VMC_CHECK(a.max_qlen * p.G <= 16, "attention: decode path needs q_len * group <= 16");
+    VMC_CHECK(p.splits == 1 || (a.part_o && a.part_lse), "attention: split-KV needs partial buffers");
+    switch (a.D) {
+      case 32: launch_decode<32>(p, a.num_reqs, a.total_tokens, st); break;
+      case 64: launch_decode<64>(p, a.num_reqs, a.total_tokens, st); break;
+      case 128: launch_decode<128>(p, a.num_reqs, a.total_tokens, st); break;
+      default: throw std::runtime_error("attention: unsupported head dim");
+    }
+  } else {
+    switch (a.D) {
+      case 32: launch_prefill<32>(p, a.num_reqs, a.max_qlen, st); break;
+      case 64: launch_prefill<64>(p, a.num_reqs, a.max_qlen, st); break;
+      case 128: launch_prefill<128>(p, a.num_reqs, a.max_qlen, st); break;
+      default: throw std::runtime_error("attention: unsupported head dim");
+    }
+  }
+}
+
+}  // namespace vmc

@@ -1,0 +1,30 @@
+// Host interface of the paged attention kernels (attention.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vmc {
+
+struct AttnLaunch {
+  const void* q;             // bf16 [T, Hq, D]
+  const void* kv;            // bf16 [num_blocks, 2, Hkv, 16, D] (one layer)
+  const int32_t* q_start;    // [R + 1] token offsets of the requests (device)
+  const int32_t* ctx_len;    // [R] context length after this step (device)
+  const int32_t* block_tables;  // [R, max_blocks] (device)
+  int max_blocks;
+  int num_reqs;              // requests handled by this launch
+  int req_offset;            // index of the first of them in q_start / ctx_len / block_tables
+  int max_qlen;              // upper bound of q_len over these requests
+  int total_tokens;          // rows of the split-KV partial buffers
+  int Hq, Hkv, D;
+  float scale;
+  bool decode;               // true: q_len * (Hq/Hkv) <= 16 decode kernel; false: prefill kernel
+  int splits;                // split-KV CTAs per (request, kv head) for decode
+  float* part_o;             // [splits, total_tokens, Hq, D] fp32 (splits > 1)
+  float* part_lse;           // [splits, total_tokens, Hq] fp32
+  void* out;                 // bf16 [T, Hq, D]
+};
+
+void paged_attention(const AttnLaunch& a, cudaStream_t st);
+
+}  // namespace vmc

@@ -1,0 +1,170 @@
+// Python bindings of the sm_100a kernels. Every op takes preallocated torch tensors and launches on
+// the current CUDA stream (so the calls can be captured into CUDA graphs); none allocates.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "attention.h"
+#include "gemm_tcgen05.h"
+#include "layers.h"
+#include "sampling.h"
+#include "weights.h"
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+template <typename T>
+T* ptr(const torch::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T>
+T* opt_ptr(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void gemm(int wf, torch::Tensor w, int64_t N, int64_t K, torch::Tensor x, int64_t M, torch::Tensor out,
+          int64_t out_mode, int64_t splits, int64_t bn, torch::Tensor err) {
+  check_cuda(w, "w");
+  check_cuda(x, "x");
+  check_cuda(out, "out");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16, "gemm: x must be bf16");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "gemm: x must be 2-D with unit inner stride");
+  TORCH_CHECK(x.size(0) >= M && x.size(1) >= K, "gemm: x too small");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= M, "gemm: bad output");
+  const bool f32_out = out_mode == vmc::kGemmOutF32 || out_mode == vmc::kGemmOutF32Add;
+  TORCH_CHECK(out.scalar_type() == (f32_out ? torch::kFloat32 : torch::kBFloat16), "gemm: output dtype mismatch");
+  TORCH_CHECK(w.numel() >= vmc::tiled_weight_bytes(wf, N, K), "gemm: weight buffer too small");
+  vmc::gemm_tcgen05(wf, w.data_ptr(), static_cast<int>(N), static_cast<int>(K), x.data_ptr(), static_cast<int>(M),
+                    static_cast<int>(x.stride(0)), out.data_ptr(), static_cast<int>(out.stride(0)),
+                    static_cast<int>(out_mode), static_cast<int>(splits), static_cast<int>(bn),
+                    ptr<uint32_t>(err), cur_stream());
+}
+
+void repack_weight(int wf, int src_type, torch::Tensor src, int64_t N, int64_t K, torch::Tensor dst) {
+  check_cuda(src, "src");
+  check_cuda(dst, "dst");
+  TORCH_CHECK(dst.numel() * dst.element_size() >= vmc::tiled_weight_bytes(wf, N, K), "repack: dst too small");
+  vmc::repack_weight(wf, src_type, src.data_ptr(), static_cast<int>(N), static_cast<int>(K), dst.data_ptr(),
+                     cur_stream());
+}
+
+void untile_bf16(torch::Tensor tiles, int64_t N, int64_t K, torch::Tensor out) {
+  vmc::untile_bf16(tiles.data_ptr(), static_cast<int>(N), static_cast<int>(K), out.data_ptr(), cur_stream());
+}
+
+void quantize_blocks(int gtype, torch::Tensor x, torch::Tensor out) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "quantize: x must be contiguous fp32");
+  vmc::quantize_blocks(gtype, ptr<float>(x), x.numel(), out.data_ptr(), cur_stream());
+}
+
+void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, torch::Tensor ctx_len,
+                     torch::Tensor block_tables, int64_t num_reqs, int64_t req_offset, int64_t max_qlen,
+                     int64_t total_tokens, int64_t Hq, int64_t Hkv, int64_t D, double scale, bool decode,
+                     int64_t splits, c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse,
+                     torch::Tensor out) {
+  vmc::AttnLaunch a;
+  a.q = q.data_ptr();
+  a.kv = kv.data_ptr();
+  a.q_start = ptr<int32_t>(q_start);
+  a.ctx_len = ptr<int32_t>(ctx_len);
+  a.block_tables = ptr<int32_t>(block_tables);
+  a.max_blocks = static_cast<int>(block_tables.size(-1));
+  a.num_reqs = static_cast<int>(num_reqs);
+  a.req_offset = static_cast<int>(req_offset);
+  a.max_qlen = static_cast<int>(max_qlen);
+  a.total_tokens = static_cast<int>(total_tokens);
+  a.Hq = static_cast<int>(Hq);
+  a.Hkv = static_cast<int>(Hkv);
+  a.D = static_cast<int>(D);
+  a.scale = static_cast<float>(scale);
+  a.decode = decode;
+  a.splits = static_cast<int>(splits);
+  a.part_o = opt_ptr<float>(part_o);
+  a.part_lse = opt_ptr<float>(part_lse);
+  a.out = out.data_ptr();
+  vmc::paged_attention(a, cur_stream());
+}
+
+void embed(torch::Tensor ids, int64_t T, torch::Tensor table, int gtype, int64_t row_bytes, int64_t H,
+           c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> out_bf16) {
+  vmc::embed(ptr<int32_t>(ids), static_cast<int>(T), table.data_ptr(), gtype, row_bytes, static_cast<int>(H),
+             opt_ptr<float>(resid), opt_ptr<void>(out_bf16), cur_stream());
+}
+
+void add_rmsnorm(torch::Tensor resid, c10::optional<torch::Tensor> delta, int64_t ndelta, int64_t delta_stride,
+                 torch::Tensor w, int64_t T, int64_t H, double eps, c10::optional<torch::Tensor> out) {
+  TORCH_CHECK(resid.scalar_type() == torch::kFloat32, "add_rmsnorm: residual must be fp32");
+  const bool f32 = delta.has_value() && delta->defined() && delta->scalar_type() == torch::kFloat32;
+  vmc::add_rmsnorm(ptr<float>(resid), opt_ptr<void>(delta), f32, static_cast<int>(ndelta), delta_stride, ptr<float>(w),
+                   static_cast<int>(T), static_cast<int>(H), static_cast<float>(eps), opt_ptr<void>(out), cur_stream());
+}
+
+void rope_store(torch::Tensor qkv, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor pos,
+                torch::Tensor slots, torch::Tensor cos_sin, bool neox, torch::Tensor q_out, torch::Tensor kv) {
+  vmc::rope_store(qkv.data_ptr(), qkv.scalar_type() == torch::kFloat32, static_cast<int>(T), static_cast<int>(Hq),
+                  static_cast<int>(Hkv), static_cast<int>(D), ptr<int32_t>(pos), ptr<int32_t>(slots),
+                  ptr<float>(cos_sin), neox, q_out.data_ptr(), kv.data_ptr(), cur_stream());
+}
+
+void swiglu(torch::Tensor gu, int64_t T, int64_t F, bool interleaved, torch::Tensor out) {
+  vmc::swiglu(gu.data_ptr(), gu.scalar_type() == torch::kFloat32, T, static_cast<int>(F), interleaved, out.data_ptr(),
+              cur_stream());
+}
+
+void gather_rows(torch::Tensor src, torch::Tensor idx, int64_t n, int64_t H, torch::Tensor dst) {
+  vmc::gather_rows(src.data_ptr(), ptr<int32_t>(idx), static_cast<int>(n), static_cast<int>(H), dst.data_ptr(),
+                   cur_stream());
+}
+
+void f32_to_bf16(torch::Tensor x, int64_t n, torch::Tensor y) {
+  vmc::f32_to_bf16(ptr<float>(x), n, y.data_ptr(), cur_stream());
+}
+
+void sample(torch::Tensor logits, int64_t S, int64_t V, torch::Tensor params, torch::Tensor out_tok,
+            c10::optional<torch::Tensor> out_lp) {
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "sample: logits must be fp32");
+  vmc::sample(ptr<float>(logits), static_cast<int>(S), static_cast<int>(V), logits.stride(0),
+              reinterpret_cast<const vmc::SampleParams*>(params.data_ptr()), ptr<int32_t>(out_tok),
+              opt_ptr<float>(out_lp), cur_stream());
+}
+
+void apply_penalties(torch::Tensor logits, torch::Tensor row_of, torch::Tensor tok, torch::Tensor out_count,
+                     torch::Tensor params, int64_t n) {
+  vmc::apply_penalties(ptr<float>(logits), logits.stride(0), ptr<int32_t>(row_of), ptr<int32_t>(tok),
+                       ptr<int32_t>(out_count), reinterpret_cast<const vmc::SampleParams*>(params.data_ptr()),
+                       static_cast<int>(n), cur_stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "vm_c_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("gemm_smem_bytes", &vmc::gemm_smem_bytes);
+  m.def("gemm_pick_bn", &vmc::gemm_pick_bn);
+  m.def("tiled_weight_bytes", &vmc::tiled_weight_bytes);
+  m.def("repack_weight", &repack_weight);
+  m.def("untile_bf16", &untile_bf16);
+  m.def("quantize_blocks", &quantize_blocks);
+  m.def("paged_attention", &paged_attention, py::arg("q"), py::arg("kv"), py::arg("q_start"), py::arg("ctx_len"),
+        py::arg("block_tables"), py::arg("num_reqs"), py::arg("req_offset"), py::arg("max_qlen"),
+        py::arg("total_tokens"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("decode"),
+        py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("out"));
+  m.def("embed", &embed);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("rope_store", &rope_store);
+  m.def("swiglu", &swiglu);
+  m.def("gather_rows", &gather_rows);
+  m.def("f32_to_bf16", &f32_to_bf16);
+  m.def("sample", &sample);
+  m.def("apply_penalties", &apply_penalties);
+  m.attr("OUT_BF16") = static_cast<int>(vmc::kGemmOutBF16);
+  m.attr("OUT_F32") = static_cast<int>(vmc::kGemmOutF32);
+  m.attr("OUT_F32_ADD") = static_cast<int>(vmc::kGemmOutF32Add);
+  m.attr("OUT_SWIGLU") = static_cast<int>(vmc::kGemmOutSwiGLU);
+}

@@ -1,0 +1,378 @@
+"""Llama / Mixtral-architecture model on the sm_100a kernels, with Megatron tensor parallelism.
+
+Forward of one engine step over a flat token batch (decodes first, then prefill chunks), reading
+the step metadata written by the native scheduler (csrc/host/scheduler.cpp build_batch):
+
+  embed (GGUF row dequant) -> [per layer] RMSNorm -> QKV GEMM -> RoPE + paged KV store ->
+  paged attention -> O GEMM -> (TP reduce) -> residual + RMSNorm -> gate/up GEMM with fused SwiGLU
+  (or MoE) -> down GEMM -> (TP reduce) -> residual + RMSNorm -> ... -> final norm on the sampled
+  rows -> vocab-parallel lm_head -> sampler.
+
+This is the graph the reference builds with libllama (src/official/llama/models/llama.cpp:98-253)
+including vm_c's two all-reduce sites after Wo and after the FFN / MoE down projection (:171,196,221).
+Weight sharding follows the reference's layout plan (src/model/weight_layout_plan.cpp:38-81,114-131):
+Q/K/V and gate/up column-parallel (KV heads replicated when n_kv_heads < tp), O and down
+row-parallel, embedding replicated; the lm_head is vocab-parallel here (the reference replicates it).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig, rope_inv_freq
+from ..gguf.constants import GType, blk, row_bytes
+
+
+@dataclass
+class LayerWeights:
+    attn_norm: torch.Tensor
+    ffn_norm: torch.Tensor
+    wqkv: list                     # TiledWeight(s): one fused QKV weight, or [QK, V] when types differ
+    qkv_split: list                # output column offsets of each part
+    wo: ops.TiledWeight
+    w_gate_up: ops.TiledWeight | None = None   # rows interleave gate/up (fused SwiGLU)
+    w_down: ops.TiledWeight | None = None
+    moe: object | None = None      # MoE weights (models/moe.py)
+
+
+@dataclass
+class ModelWeights:
+    cfg: ModelConfig
+    layers: list[LayerWeights]
+    embd: torch.Tensor             # raw GGUF rows [V, row_bytes] (replicated)
+    embd_type: int
+    embd_row_bytes: int
+    output_norm: torch.Tensor
+    lm_head: ops.TiledWeight       # rows [vocab_begin, vocab_end) of the output projection
+    vocab_begin: int = 0
+    vocab_end: int = 0
+    tp_rank: int = 0
+    tp_size: int = 1
+    bytes_total: int = 0
+
+
+# ------------------------------------------------------------------------------------------------
+# Sharding helpers
+
+
+def _kv_heads_local(cfg: ModelConfig, rank: int, tp: int) -> tuple[int, int]:
+    """(first kv head, number of kv heads) held by `rank`."""
+    if cfg.n_kv_heads >= tp:
+        n = cfg.n_kv_heads // tp
+        return rank * n, n
+    return (rank * cfg.n_kv_heads) // tp, 1
+
+
+def check_tp(cfg: ModelConfig, tp: int) -> None:
+    if cfg.n_heads % tp:
+        raise ValueError(f"n_heads {cfg.n_heads} not divisible by tp {tp}")
+    if cfg.n_kv_heads >= tp and cfg.n_kv_heads % tp:
+        raise ValueError(f"n_kv_heads {cfg.n_kv_heads} not divisible by tp {tp}")
+    if cfg.n_kv_heads < tp and tp % cfg.n_kv_heads:
+        raise ValueError(f"tp {tp} not a multiple of n_kv_heads {cfg.n_kv_heads}")
+    if cfg.ffn % tp:
+        raise ValueError(f"ffn {cfg.ffn} not divisible by tp {tp}")
+
+
+def _to_dev(t: torch.Tensor, device) -> torch.Tensor:
+    return t.to(device, non_blocking=False).contiguous()
+
+
+def _col_slice(raw: torch.Tensor, gtype: int, K: int, c0: int, c1: int) -> torch.Tensor:
+    """Columns [c0, c1) (elements) of GGUF rows: a byte slice of every row (block aligned)."""
+    if c0 == 0 and c1 == K:
+        return raw
+    if gtype == GType.F32:
+        return raw[:, c0:c1]
+    b0, b1 = row_bytes(gtype, c0) if c0 else 0, row_bytes(gtype, c1)
+    return raw[:, b0:b1]
+
+
+def _tile(src, name: str, device, r0=0, r1=None, c0=0, c1=None, rows_override=None) -> ops.TiledWeight:
+    spec = src.info(name)
+    K = spec.ne[0]
+    r1 = spec.rows if r1 is None else r1
+    c1 = K if c1 is None else c1
+    raw = _to_dev(src.rows(name, r0, r1), device)
+    raw = _col_slice(raw, spec.gtype, K, c0, c1).contiguous()
+    return _tile_raw(raw, spec.gtype, r1 - r0, c1 - c0)
+
+
+def _tile_raw(raw: torch.Tensor, gtype: int, N: int, K: int) -> ops.TiledWeight:
+    if ops.wf_for_gtype(gtype) is None:
+        # No native GPU format (Q2_K, Q3_K, Q5_K, IQ4, ...): dequantise on the host, tile as bf16.
+        from .. import _native
+        f = _native.host().dequantize(int(gtype), raw.cpu().numpy(), N, K)
+        return ops.tile_weight(torch.from_numpy(f).to(raw.device), int(GType.F32), N, K)
+    return ops.tile_weight(raw, gtype, N, K)
+
+
+def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1) -> ModelWeights:
+    """Load (and shard) the weights of a llama-architecture model from a tensor source."""
+    check_tp(cfg, tp_size)
+    dev = torch.device(device)
+    D = cfg.head_dim
+    hq_local = cfg.n_heads // tp_size
+    kv0, nkv = _kv_heads_local(cfg, tp_rank, tp_size)
+    f_local = cfg.ffn // tp_size
+    layers = []
+    total = 0
+    for i in range(cfg.n_layers):
+        qn, kn, vn = blk(i, "attn_q"), blk(i, "attn_k"), blk(i, "attn_v")
+        q_rows = (tp_rank * hq_local * D, (tp_rank + 1) * hq_local * D)
+        kv_rows = (kv0 * D, (kv0 + nkv) * D)
+        tq, tk, tv = src.info(qn).gtype, src.info(kn).gtype, src.info(vn).gtype
+        raw_q = _to_dev(src.rows(qn, *q_rows), dev)
+        raw_k = _to_dev(src.rows(kn, *kv_rows), dev)
+        raw_v = _to_dev(src.rows(vn, *kv_rows), dev)
+        H = cfg.hidden
+        if tq == tk == tv:
+            wqkv = [_tile_raw(torch.cat([raw_q, raw_k, raw_v], 0), tq, (hq_local + 2 * nkv) * D, H)]
+            split = [0]
+        elif tq == tk:
+            wqkv = [_tile_raw(torch.cat([raw_q, raw_k], 0), tq, (hq_local + nkv) * D, H),
+                    _tile_raw(raw_v, tv, nkv * D, H)]
+            split = [0, (hq_local + nkv) * D]
+        else:
+            wqkv = [_tile_raw(raw_q, tq, hq_local * D, H), _tile_raw(raw_k, tk, nkv * D, H),
+                    _tile_raw(raw_v, tv, nkv * D, H)]
+            split = [0, hq_local * D, (hq_local + nkv) * D]
+        del raw_q, raw_k, raw_v
+        on = blk(i, "attn_output")
+        wo = _tile(src, on, dev, c0=tp_rank * hq_local * D, c1=(tp_rank + 1) * hq_local * D)
+        lw = LayerWeights(attn_norm=_to_dev(src.rows(blk(i, "attn_norm")), dev).view(-1).float(),
+                          ffn_norm=_to_dev(src.rows(blk(i, "ffn_norm")), dev).view(-1).float(),
+                          wqkv=wqkv, qkv_split=split, wo=wo)
+        if cfg.is_moe:
+            from .moe import load_moe_layer
+            lw.moe = load_moe_layer(src, cfg, i, dev, tp_rank, tp_size)
+        else:
+            gn, un, dn = blk(i, "ffn_gate"), blk(i, "ffn_up"), blk(i, "ffn_down")
+            fr = (tp_rank * f_local, (tp_rank + 1) * f_local)
+            tg, tu = src.info(gn).gtype, src.info(un).gtype
+            raw_g = _to_dev(src.rows(gn, *fr), dev)
+            raw_u = _to_dev(src.rows(un, *fr), dev)
+            if tg == tu:
+                inter = torch.stack([raw_g, raw_u], 1).reshape(2 * f_local, -1)
+                lw.w_gate_up = _tile_raw(inter, tg, 2 * f_local, H)
+            else:
+                # Mixed types: dequantise both to F32 rows, interleave, tile as bf16.
+                from .. import _native
+                h = _native.host()
+                g = torch.from_numpy(h.dequantize(int(tg), raw_g.cpu().numpy(), f_local, H))
+                u = torch.from_numpy(h.dequantize(int(tu), raw_u.cpu().numpy(), f_local, H))
+                inter = torch.stack([g, u], 1).reshape(2 * f_local, H).to(dev)
+                lw.w_gate_up = ops.tile_weight(inter, int(GType.F32), 2 * f_local, H)
+            lw.w_gate_up.interleaved_swiglu = True
+            del raw_g, raw_u
+            lw.w_down = _tile(src, dn, dev, c0=fr[0], c1=fr[1])
+        layers.append(lw)
+        for w in lw.wqkv + [lw.wo, lw.w_gate_up, lw.w_down]:
+            if w is not None:
+                total += w.nbytes
+    # Embedding (replicated raw rows) and output projection (vocab-parallel).
+    es = src.info("token_embd.weight")
+    embd = _to_dev(src.rows("token_embd.weight"), dev)
+    if es.gtype == GType.F32:
+        embd = embd.view(torch.uint8).reshape(es.ne[1], -1)
+    V = cfg.vocab
+    if V % tp_size:
+        raise ValueError(f"vocab {V} not divisible by tp {tp_size} (vocab-parallel lm_head)")
+    per = V // tp_size
+    v0, v1 = tp_rank * per, min(V, (tp_rank + 1) * per)
+    out_name = "output.weight" if src.has("output.weight") else "token_embd.weight"
+    lm_head = _tile(src, out_name, dev, r0=v0, r1=v1)
+    total += lm_head.nbytes + embd.numel()
+    torch.cuda.synchronize(dev)
+    return ModelWeights(cfg=cfg, layers=layers, embd=embd, embd_type=es.gtype,
+                        embd_row_bytes=row_bytes(es.gtype, cfg.hidden),
+                        output_norm=_to_dev(src.rows("output_norm.weight"), dev).view(-1).float(),
+                        lm_head=lm_head, vocab_begin=v0, vocab_end=v1, tp_rank=tp_rank, tp_size=tp_size,
+                        bytes_total=total)
+
+
+def rope_table(cfg: ModelConfig, max_pos: int, device) -> torch.Tensor:
+    inv = torch.tensor(rope_inv_freq(cfg), dtype=torch.float64)
+    pos = torch.arange(max_pos, dtype=torch.float64)
+    ang = pos[:, None] * inv[None, :]
+    cs = torch.stack([torch.cos(ang), torch.sin(ang)], -1).to(torch.float32)
+    return cs.contiguous().to(device)   # [max_pos, D/2, 2]
+
+
+# ------------------------------------------------------------------------------------------------
+# Forward
+
+
+@dataclass
+class StepMeta:
+    """Device views of one step's metadata (see BatchLayout in csrc/host/scheduler.hpp)."""
+    input_ids: torch.Tensor
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    q_start: torch.Tensor
+    ctx_len: torch.Tensor
+    block_tables: torch.Tensor
+    logits_idx: torch.Tensor
+    T: int            # tokens (including padding rows)
+    R: int            # requests (including padding rows)
+    S: int            # sampled rows
+    num_decode: int   # leading decode requests (one token each)
+    max_qlen: int     # max q_len over the prefill requests
+    decode_qlen: int = 1
+
+
+@dataclass
+class Workspace:
+    resid: torch.Tensor
+    h: torch.Tensor
+    qkv: torch.Tensor      # fp32 (split-K accumulate) or bf16 view on the same storage
+    q: torch.Tensor
+    attn: torch.Tensor
+    o: torch.Tensor        # fp32
+    act: torch.Tensor      # bf16 [T, F_local]
+    down: torch.Tensor     # fp32
+    gu32: torch.Tensor     # fp32 [T, 2F_local] (split-K gate/up)
+    hs: torch.Tensor       # bf16 [S, H]
+    logits: torch.Tensor   # fp32 [S, V_local]
+    part_o: torch.Tensor | None = None
+    part_lse: torch.Tensor | None = None
+
+
+class LlamaModel:
+    def __init__(self, w: ModelWeights, max_tokens: int, max_samples: int, max_model_len: int, comm=None,
+                 attn_splits: int = 0):
+        self.w = w
+        self.cfg = cfg = w.cfg
+        self.dev = w.output_norm.device
+        self.tp = w.tp_size
+        self.comm = comm
+        self.hq = cfg.n_heads // self.tp
+        _, self.hkv = _kv_heads_local(cfg, w.tp_rank, self.tp)
+        self.D = cfg.head_dim
+        self.H = cfg.hidden
+        self.f_local = cfg.ffn // self.tp
+        self.v_local = w.vocab_end - w.vocab_begin
+        self.max_tokens = max_tokens
+        self.max_samples = max_samples
+        self.cos_sin = rope_table(cfg, max_model_len + 1, self.dev)
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.attn_splits = attn_splits
+        T, S = max_tokens, max_samples
+        qkv_n = (self.hq + 2 * self.hkv) * self.D
+        dev = self.dev
+        qkv32 = torch.empty(T, qkv_n, dtype=torch.float32, device=dev)
+        self.ws = Workspace(
+            resid=torch.empty(T, self.H, dtype=torch.float32, device=dev),
+            h=torch.empty(T, self.H, dtype=torch.bfloat16, device=dev),
+            qkv=qkv32,
+            q=torch.empty(T, self.hq * self.D, dtype=torch.bfloat16, device=dev),
+            attn=torch.empty(T, self.hq * self.D, dtype=torch.bfloat16, device=dev),
+            o=torch.empty(T, self.H, dtype=torch.float32, device=dev),
+            act=torch.empty(T, max(self.f_local, 1), dtype=torch.bfloat16, device=dev),
+            down=torch.empty(T, self.H, dtype=torch.float32, device=dev),
+            gu32=torch.empty(T, 2 * max(self.f_local, 1), dtype=torch.float32, device=dev),
+            hs=torch.empty(S, self.H, dtype=torch.bfloat16, device=dev),
+            logits=torch.empty(S, self.v_local, dtype=torch.float32, device=dev),
+        )
+        self.qkv_bf16 = torch.empty(T, qkv_n, dtype=torch.bfloat16, device=dev)
+        if attn_splits > 1:
+            self.ws.part_o = torch.empty(attn_splits, max_samples, self.hq, self.D, dtype=torch.float32, device=dev)
+            self.ws.part_lse = torch.empty(attn_splits, max_samples, self.hq, dtype=torch.float32, device=dev)
+        self.moe_runner = None
+        if cfg.is_moe:
+            from .moe import MoERunner
+            self.moe_runner = MoERunner(self, max_tokens)
+
+    # -- GEMM with the split-K policy: fp32 accumulate output when split --------------------------
+    def _linear(self, x: torch.Tensor, w: ops.TiledWeight, M: int, out32: torch.Tensor,
+                out16: torch.Tensor | None = None, col0: int = 0) -> tuple[torch.Tensor, bool]:
+        splits = ops.pick_splits(w, M)
+        if splits > 1 or out16 is None:
+            view = out32[:M, col0:col0 + w.N]
+            view.zero_() if splits > 1 else None
+            ops.gemm(x, w, view, M, ops.OUT_F32_ADD if splits > 1 else ops.OUT_F32, splits)
+            return out32, True
+        ops.gemm(x, w, out16[:M, col0:col0 + w.N], M, ops.OUT_BF16, 1)
+        return out16, False
+
+    def _qkv(self, lw: LayerWeights, x: torch.Tensor, M: int) -> tuple[torch.Tensor, bool]:
+        ws = self.ws
+        # All parts must land in the same dtype buffer: use fp32 if any part is split.
+        any_split = any(ops.pick_splits(w, M) > 1 for w in lw.wqkv)
+        if any_split:
+            ws.qkv[:M].zero_()
+            for w, c0 in zip(lw.wqkv, lw.qkv_split):
+                s = ops.pick_splits(w, M)
+                ops.gemm(x, w, ws.qkv[:M, c0:c0 + w.N], M, ops.OUT_F32_ADD, s)
+            return ws.qkv, True
+        for w, c0 in zip(lw.wqkv, lw.qkv_split):
+            ops.gemm(x, w, self.qkv_bf16[:M, c0:c0 + w.N], M, ops.OUT_BF16, 1)
+        return self.qkv_bf16, False
+
+    def _mlp(self, lw: LayerWeights, M: int) -> tuple[torch.Tensor, bool]:
+        ws = self.ws
+        if lw.moe is not None:
+            return self.moe_runner.forward(lw.moe, ws.h, M)
+        w = lw.w_gate_up
+        s = ops.pick_splits(w, M)
+        if s > 1:
+            g = ws.gu32[:M, :w.N]
+            g.zero_()
+            ops.gemm(ws.h, w, g, M, ops.OUT_F32_ADD, s)
+            ops.swiglu(g, M, w.N // 2, ws.act, interleaved=True)
+        else:
+            ops.gemm(ws.h, w, ws.act[:M], M, ops.OUT_SWIGLU, 1)
+        return self._linear(ws.act, lw.w_down, M, ws.down)
+
+    def _reduce(self, t: torch.Tensor, M: int) -> None:
+        if self.tp > 1:
+            self.comm.all_reduce(t[:M])
+
+    def forward(self, kv_cache: torch.Tensor, m: StepMeta, params: torch.Tensor, out_tok: torch.Tensor,
+                out_lp: torch.Tensor | None = None, pre_sample=None) -> None:
+        """One step: writes sampled token ids for the m.S sample rows into out_tok."""
+        cfg, ws = self.cfg, self.ws
+        T = m.T
+        ops.embed(m.input_ids, T, self.w.embd, self.w.embd_type, self.w.embd_row_bytes, self.H, resid=ws.resid)
+        layers = self.w.layers
+        ops.add_rmsnorm(ws.resid, layers[0].attn_norm, T, self.H, cfg.rms_eps, out=ws.h)
+        for li, lw in enumerate(layers):
+            qkv, _ = self._qkv(lw, ws.h, T)
+            ops.rope_store(qkv[:T], T, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
+                           cfg.rope_neox, ws.q, kv_cache[li])
+            self._attention(kv_cache[li], m)
+            o, o32 = self._linear(ws.attn, lw.wo, T, ws.o)
+            self._reduce(o, T)
+            ops.add_rmsnorm(ws.resid, lw.ffn_norm, T, self.H, cfg.rms_eps, out=ws.h, delta=o[:T])
+            d, _ = self._mlp(lw, T)
+            self._reduce(d, T)
+            nxt = layers[li + 1].attn_norm if li + 1 < len(layers) else self.w.output_norm
+            ops.add_rmsnorm(ws.resid, nxt, T, self.H, cfg.rms_eps, out=ws.h, delta=d[:T])
+        ops.gather_rows(ws.h, m.logits_idx, m.S, self.H, ws.hs)
+        ops.gemm(ws.hs, self.w.lm_head, ws.logits[:m.S], m.S, ops.OUT_F32, 1)
+        if pre_sample is not None:
+            pre_sample(self)
+        self._sample(m.S, params, out_tok, out_lp)
+
+    def _attention(self, kv_layer: torch.Tensor, m: StepMeta) -> None:
+        ws = self.ws
+        nd = m.num_decode
+        G = self.hq // self.hkv
+        if nd > 0:
+            dec_ok = m.decode_qlen * G <= 16
+            splits = self.attn_splits if (self.attn_splits > 1 and dec_ok and nd <= self.max_samples) else 1
+            ops.paged_attention(ws.q, kv_layer, m.q_start, m.ctx_len, m.block_tables, nd, 0, m.decode_qlen,
+                                nd * m.decode_qlen, self.hq, self.hkv, self.D, self.scale, dec_ok, ws.attn,
+                                splits, ws.part_o if splits > 1 else None, ws.part_lse if splits > 1 else None)
+        if m.R > nd:
+            ops.paged_attention(ws.q, kv_layer, m.q_start, m.ctx_len, m.block_tables, m.R - nd, nd, m.max_qlen,
+                                m.T, self.hq, self.hkv, self.D, self.scale, False, ws.attn)
+
+    def _sample(self, S: int, params: torch.Tensor, out_tok: torch.Tensor, out_lp) -> None:
+        if self.tp > 1:
+            self.comm.sample_vocab_parallel(self, S, params, out_tok, out_lp)
+        else:
+            ops.sample(self.ws.logits, S, self.v_local, params, out_tok, out_lp)

@@ -1,0 +1,211 @@
+"""GPU model runner: owns weights, KV cache, step buffers and the decode CUDA graphs of one rank.
+
+Replaces the reference's per-rank LlamaRuntime + ggml CUDA-graph machinery
+(src/official/llama_runtime.cpp:178-538, ggml-cuda.cu:4308-4520): decode-only steps replay a CUDA
+graph captured per batch-size bucket (the whole layer stack, lm_head and sampler in one graph);
+prefill / mixed steps run the same kernels eagerly. Per step there is one pinned H2D copy of the
+metadata written by the native scheduler, one of the sampling parameters, and one D2H copy of the
+sampled ids followed by an event wait.
+"""
+from __future__ import annotations
+
+import math
+import time
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..config import VmCConfig
+from ..core.engine import ModelRunner, StepCounts
+from ..utils.logging import get_logger
+from .llama import LlamaModel, StepMeta, load_weights
+
+log = get_logger("runner")
+
+GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256]
+
+
+def kv_bytes_per_block(cfg: VmCConfig, hkv_local: int, dtype_bytes: int = 2) -> int:
+    m = cfg.model
+    return m.n_layers * 2 * hkv_local * cfg.cache.block_size * m.head_dim * dtype_bytes
+
+
+class GpuModelRunner(ModelRunner):
+    def __init__(self, cfg: VmCConfig, source, device="cuda", tp_rank: int = 0, tp_size: int = 1, comm=None,
+                 use_graphs: bool = True, weights=None):
+        self.cfg = cfg
+        self.dev = torch.device(device)
+        torch.cuda.set_device(self.dev)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        m = cfg.model
+        t0 = time.perf_counter()
+        self.weights = weights if weights is not None else load_weights(source, m, self.dev, tp_rank, tp_size)
+        log.info("weights loaded: %.2f GB in %.1fs", self.weights.bytes_total / 1e9, time.perf_counter() - t0)
+        s = cfg.scheduler
+        self.max_model_len = m.max_model_len
+        self.max_samples = max(s.max_num_seqs, 1)
+        self.max_tokens = max(s.max_num_batched_tokens, self.max_samples)
+        self.buckets = [b for b in GRAPH_BUCKETS if b <= self.max_samples]
+        if use_graphs and self.buckets and self.buckets[-1] < self.max_samples:
+            self.buckets.append(self.max_samples)
+        self.use_graphs = use_graphs
+        self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len, comm=comm,
+                                attn_splits=16)
+        self.comm = comm
+        # KV cache: [L, num_blocks, 2, Hkv_local, block_size, D] bf16, zero-filled (finite).
+        per_block = kv_bytes_per_block(cfg, self.model.hkv)
+        max_blocks_per_seq = (m.max_model_len + cfg.cache.block_size - 1) // cfg.cache.block_size + 1
+        want = cfg.cache.num_gpu_blocks
+        if want <= 0:
+            torch.cuda.synchronize(self.dev)
+            free, total = torch.cuda.mem_get_info(self.dev)
+            budget = int(total * cfg.cache.gpu_memory_utilization) - (total - free) \
+                - cfg.cache.gpu_safety_margin_mb * (1 << 20) - (1 << 30)
+            want = max(16, budget // per_block)
+            want = min(want, 2 * s.max_num_seqs * max_blocks_per_seq + 1)
+        self.num_kv_blocks = int(want)
+        self.kv = torch.zeros(m.n_layers, self.num_kv_blocks, 2, self.model.hkv, cfg.cache.block_size, m.head_dim,
+                              dtype=torch.bfloat16, device=self.dev)
+        log.info("KV cache: %d blocks x %d tokens (%.2f GB)", self.num_kv_blocks, cfg.cache.block_size,
+                 self.kv.numel() * 2 / 1e9)
+        self.params_dev = torch.zeros(self.max_tokens * 40, dtype=torch.uint8, device=self.dev)
+        self.params_host = torch.zeros(self.max_tokens * 40, dtype=torch.uint8).pin_memory()
+        self.tok_dev = torch.zeros(self.max_tokens, dtype=torch.int32, device=self.dev)
+        self.lp_dev = torch.zeros(self.max_tokens, dtype=torch.float32, device=self.dev)
+        self.tok_host = torch.zeros(self.max_tokens, dtype=torch.int32).pin_memory()
+        self.lp_host = torch.zeros(self.max_tokens, dtype=torch.float32).pin_memory()
+        self.done = torch.cuda.Event()
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: dict[int, int] = {}
+        self.launch_count = 0      # kernels of this framework launched by executed steps
+        self.h2d_bytes = 0         # per-step inputs copied from pinned host memory
+        self.d2h_bytes = 0         # per-step results read back
+        self.meta_dev: Optional[torch.Tensor] = None
+        self.layout = None
+        self.stream = torch.cuda.current_stream(self.dev)
+
+    # -- engine hooks ------------------------------------------------------------------------------
+    def max_graph_batch(self) -> int:
+        return self.buckets[-1] if (self.use_graphs and self.buckets) else 0
+
+    def graph_bucket(self, R: int) -> int:
+        if not self.use_graphs:
+            return 0
+        for b in self.buckets:
+            if b >= R:
+                return b
+        return 0
+
+    def alloc_meta(self, total: int) -> torch.Tensor:
+        self.meta_host = torch.zeros(total, dtype=torch.int32).pin_memory()
+        self.meta_dev = torch.zeros(total, dtype=torch.int32, device=self.dev)
+        return self.meta_host
+
+    def bind_layout(self, layout) -> None:
+        self.layout = layout
+        L = layout
+        md = self.meta_dev
+        self.v_ids = md[L.off_input_ids:L.off_input_ids + L.max_tokens]
+        self.v_pos = md[L.off_positions:L.off_positions + L.max_tokens]
+        self.v_slots = md[L.off_slot_mapping:L.off_slot_mapping + L.max_tokens]
+        self.v_qs = md[L.off_q_start:L.off_q_start + L.max_reqs + 1]
+        self.v_ctx = md[L.off_ctx_len:L.off_ctx_len + L.max_reqs]
+        self.v_lidx = md[L.off_logits_idx:L.off_logits_idx + L.max_reqs]
+        self.v_bt = md[L.off_block_tables:L.off_block_tables + L.max_reqs * L.max_blocks_per_seq].view(
+            L.max_reqs, L.max_blocks_per_seq)
+
+    def _meta(self, T, R, S, nd, max_qlen) -> StepMeta:
+        return StepMeta(self.v_ids, self.v_pos, self.v_slots, self.v_qs, self.v_ctx, self.v_bt, self.v_lidx,
+                        T=T, R=R, S=S, num_decode=nd, max_qlen=max_qlen)
+
+    def _attn_splits(self, nd: int) -> int:
+        ctas = max(1, nd * self.model.hkv)
+        return max(1, min(16, math.ceil(2 * 148 / ctas))) if ctas < 148 else 1
+
+    def _forward(self, m: StepMeta, pen=None) -> None:
+        self.model.attn_splits = self._attn_splits(m.num_decode)
+        params = self.params_dev
+        self.model.forward(self.kv, m, params, self.tok_dev, self.lp_dev, pre_sample=pen)
+
+    def _upload(self, meta: torch.Tensor, params: np.ndarray) -> None:
+        nb = params.nbytes
+        self.params_host[:nb].numpy()[:] = params.view(np.uint8)
+        self.meta_dev.copy_(meta, non_blocking=True)
+        self.params_dev[:nb].copy_(self.params_host[:nb], non_blocking=True)
+
+    def execute(self, meta, counts: StepCounts, params: np.ndarray, penalties=None):
+        if counts.R_pad > 0 and penalties is None and counts.R_pad not in self.graphs:
+            self._capture(counts.R_pad)   # before the upload: capture uses the device buffers
+        self._upload(meta, params)
+        pen = None
+        if penalties is not None:
+            rows, toks, cnts = (torch.from_numpy(a).to(self.dev, non_blocking=True) for a in penalties)
+            n = rows.numel()
+
+            def pen(model):  # applied to the logits before sampling
+                ops.apply_penalties(model.ws.logits, rows, toks, cnts, self.params_dev, n)
+        if counts.R_pad > 0 and pen is None:
+            B = counts.R_pad
+            g = self.graphs.get(B)
+            if g is None:
+                g = self._capture(B)
+            g.replay()
+            self.launch_count += self.graph_launches[B]
+            S = counts.S
+        else:
+            n0 = ops.LAUNCHES[0]
+            self._forward(self._meta(counts.T, counts.R, counts.S, counts.num_decode, counts.max_qlen), pen)
+            self.launch_count += ops.LAUNCHES[0] - n0
+            S = counts.S
+        self.tok_host[:S].copy_(self.tok_dev[:S], non_blocking=True)
+        self.lp_host[:S].copy_(self.lp_dev[:S], non_blocking=True)
+        self.h2d_bytes += meta.numel() * 4 + params.nbytes
+        self.d2h_bytes += S * 8
+        self.done.record()
+        self.done.synchronize()
+        return self.tok_host[:S].numpy(), self.lp_host[:S].numpy()
+
+    # -- CUDA graphs -------------------------------------------------------------------------------
+    def _fake_decode_meta(self, B: int) -> None:
+        """Metadata for a batch of B padding decode rows (no KV writes, empty contexts)."""
+        L = self.layout
+        h = np.zeros(L.total, dtype=np.int32)
+        h[L.off_slot_mapping:L.off_slot_mapping + B] = -1
+        h[L.off_q_start:L.off_q_start + B + 1] = np.arange(B + 1)
+        h[L.off_logits_idx:L.off_logits_idx + B] = np.arange(B)
+        self.meta_dev.copy_(torch.from_numpy(h))
+        self.params_dev.zero_()
+
+    def _capture(self, B: int) -> torch.cuda.CUDAGraph:
+        self._fake_decode_meta(B)
+        m = self._meta(B, B, B, B, 1)
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._forward(m)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        n0 = ops.LAUNCHES[0]
+        with torch.cuda.graph(g, stream=s):
+            self._forward(m)
+        self.graph_launches[B] = ops.LAUNCHES[0] - n0
+        torch.cuda.synchronize(self.dev)
+        self.graphs[B] = g
+        return g
+
+    def warmup(self, capture: bool = True) -> None:
+        """Compile-free warm-up: one eager prefill-shaped step and capture of every decode bucket."""
+        if capture and self.use_graphs:
+            t0 = time.perf_counter()
+            for B in self.buckets:
+                if B not in self.graphs:
+                    self._capture(B)
+            log.info("captured %d decode graphs in %.1fs", len(self.graphs), time.perf_counter() - t0)
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        torch.cuda.synchronize(self.dev)

@@ -1,0 +1,172 @@
+"""Python entry points of the sm_100a kernels (thin wrappers over the ``_cuda`` extension).
+
+Every function launches on the current CUDA stream and writes into caller-provided tensors, so a
+sequence of them can be captured into a CUDA graph. There is no PyTorch fallback: if the CUDA
+extension is missing the first call raises ImportError.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native
+from ..gguf.constants import GType
+
+# Tiled weight formats (csrc/kernels/weight_formats.cuh).
+WF_BF16, WF_Q4K, WF_Q6K, WF_Q8_0 = 0, 1, 2, 3
+OUT_BF16, OUT_F32, OUT_F32_ADD, OUT_SWIGLU = 0, 1, 2, 3
+NUM_SMS = 148
+
+_WF_FOR_GTYPE = {GType.Q4_K: WF_Q4K, GType.Q6_K: WF_Q6K, GType.Q8_0: WF_Q8_0,
+                 GType.F32: WF_BF16, GType.F16: WF_BF16, GType.BF16: WF_BF16}
+_CHUNK = {WF_BF16: 64, WF_Q4K: 256, WF_Q6K: 256, WF_Q8_0: 256}
+_ROWB = {WF_BF16: 128, WF_Q4K: 144, WF_Q6K: 224, WF_Q8_0: 272}
+
+
+def C():
+    return _native.cuda()
+
+
+# Number of kernel launches issued through these wrappers (for the bench's launch count).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+def wf_for_gtype(t: int) -> int | None:
+    return _WF_FOR_GTYPE.get(GType(t))
+
+
+def tiled_bytes(wf: int, N: int, K: int) -> int:
+    return ((N + 127) // 128) * ((K + _CHUNK[wf] - 1) // _CHUNK[wf]) * 128 * _ROWB[wf]
+
+
+@dataclass
+class TiledWeight:
+    """A linear weight [N, K] in a tiled on-device format (see weight_formats.cuh)."""
+    wf: int
+    data: torch.Tensor   # uint8, tiled bytes
+    N: int
+    K: int
+    interleaved_swiglu: bool = False   # rows alternate gate/up (fused SwiGLU epilogue)
+
+    @property
+    def chunks(self) -> int:
+        return (self.K + _CHUNK[self.wf] - 1) // _CHUNK[self.wf]
+
+    @property
+    def nbytes(self) -> int:
+        return self.data.numel()
+
+
+def tile_weight(raw: torch.Tensor, gtype: int, N: int, K: int, wf: int | None = None) -> TiledWeight:
+    """Repack GGUF rows (uint8 bytes, or an F32/F16/BF16 tensor) already on the GPU into tiles."""
+    if wf is None:
+        wf = wf_for_gtype(gtype)
+        if wf is None:
+            raise ValueError(f"no tiled GPU format for GGUF type {GType(gtype).name}; dequantise first")
+    out = torch.empty(tiled_bytes(wf, N, K), dtype=torch.uint8, device=raw.device)
+    C().repack_weight(wf, int(gtype), raw.contiguous(), N, K, out)
+    return TiledWeight(wf, out, N, K)
+
+
+def pick_splits(w: TiledWeight, M: int, bn: int = 0, target_ctas: int = NUM_SMS) -> int:
+    bn = bn or C().gemm_pick_bn(M)
+    ctas = ((w.N + 127) // 128) * ((M + bn - 1) // bn)
+    if ctas >= target_ctas * 0.8 or w.chunks < 2:
+        return 1
+    return max(1, min(w.chunks, math.ceil(target_ctas / ctas)))
+
+
+def gemm(x: torch.Tensor, w: TiledWeight, out: torch.Tensor, M: int, mode: int = OUT_BF16, splits: int = 1,
+         bn: int = 0, err: torch.Tensor | None = None) -> torch.Tensor:
+    """out[:M] (=|+=) x[:M] @ W^T. mode OUT_F32_ADD requires a zeroed fp32 output."""
+    if err is None:
+        err = _err_word(x.device)
+    C().gemm(w.wf, w.data, w.N, w.K, x, M, out, mode, splits, bn, err)
+    _count()
+    return out
+
+
+_ERR: dict = {}
+
+
+def _err_word(device) -> torch.Tensor:
+    key = str(device)
+    if key not in _ERR:
+        _ERR[key] = torch.zeros(4, dtype=torch.int32, device=device)
+    return _ERR[key]
+
+
+def device_error(device="cuda") -> int:
+    """Error code recorded by a kernel whose bounded wait expired (0 = none)."""
+    return int(_err_word(torch.device(device)).max().item())
+
+
+def quantize_blocks(gtype: int, x: torch.Tensor) -> torch.Tensor:
+    """fp32 tensor [..., K] -> GGUF block bytes (uint8) on the device."""
+    x = x.contiguous().float()
+    K = x.shape[-1]
+    rows = x.numel() // K
+    from ..gguf.constants import row_bytes
+    out = torch.empty(rows * row_bytes(gtype, K), dtype=torch.uint8, device=x.device)
+    C().quantize_blocks(int(gtype), x, out)
+    return out.view(rows, -1)
+
+
+def untile_bf16(w: TiledWeight) -> torch.Tensor:
+    out = torch.empty(w.N, w.K, dtype=torch.bfloat16, device=w.data.device)
+    C().untile_bf16(w.data, w.N, w.K, out)
+    return out
+
+
+def embed(ids, T, table, gtype, row_bytes, H, resid=None, out_bf16=None):
+    C().embed(ids, T, table, int(gtype), row_bytes, H, resid, out_bf16)
+    _count()
+
+
+def add_rmsnorm(resid, w, T, H, eps, out=None, delta=None, ndelta=1, delta_stride=0):
+    C().add_rmsnorm(resid, delta, ndelta, delta_stride, w, T, H, eps, out)
+    _count()
+
+
+def rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv):
+    C().rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv)
+    _count()
+
+
+def swiglu(gu, T, F, out, interleaved=False):
+    C().swiglu(gu, T, F, interleaved, out)
+    _count()
+
+
+def gather_rows(src, idx, n, H, dst):
+    C().gather_rows(src, idx, n, H, dst)
+    _count()
+
+
+def paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq, Hkv,
+                    D, scale, decode, out, splits=1, part_o=None, part_lse=None):
+    C().paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq, Hkv,
+                        D, scale, decode, splits, part_o, part_lse, out)
+    _count(2 if (decode and splits > 1) else 1)
+
+
+# Sampling parameters: one 40-byte record per row (csrc/kernels/sampling.h SampleParams).
+SAMPLE_PARAMS_DTYPE = [("temperature", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"), ("min_p", "<f4"),
+                       ("repetition_penalty", "<f4"), ("frequency_penalty", "<f4"), ("presence_penalty", "<f4"),
+                       ("step", "<i4"), ("seed", "<u8")]
+
+
+def sample(logits, S, V, params, out_tok, out_lp=None):
+    C().sample(logits, S, V, params, out_tok, out_lp)
+    _count()
+
+
+def apply_penalties(logits, row_of, tok, out_count, params, n):
+    C().apply_penalties(logits, row_of, tok, out_count, params, n)
+    _count()
