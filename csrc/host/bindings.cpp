@@ -12,6 +12,7 @@
 #include "gguf.hpp"
 #include "quants.hpp"
 #include "scheduler.hpp"
+#include "tokenizer.hpp"
 
 namespace py = pybind11;
 using namespace vmc;
@@ -175,6 +176,21 @@ PYBIND11_MODULE(_host, m) {
     return out;
   }, py::arg("type"), py::arg("src"), py::arg("threads") = 0);
   m.def("can_quantize", [](uint32_t t) { return can_quantize(static_cast<GType>(t)); });
+
+  // ---------------- tokenizer core ----------------
+  py::class_<BpeTokenizer>(m, "BpeTokenizer")
+      .def(py::init([](const std::vector<py::bytes>& toks, const std::vector<float>& scores,
+                       const std::vector<py::bytes>& merges, const std::string& model) {
+        std::vector<std::string> t, mg;
+        t.reserve(toks.size());
+        for (auto& x : toks) t.push_back(x);
+        for (auto& x : merges) mg.push_back(x);
+        return new BpeTokenizer(t, scores, mg, model);
+      }))
+      .def("encode_piece", [](const BpeTokenizer& b, py::bytes text) { return b.encode_piece(text); })
+      .def("token_id", [](const BpeTokenizer& b, py::bytes piece) { return b.token_id(piece); })
+      .def("set_unk", &BpeTokenizer::set_unk)
+      .def_property_readonly("vocab_size", &BpeTokenizer::vocab_size);
 
   // ---------------- block manager ----------------
   py::class_<BlockManager, std::shared_ptr<BlockManager>>(m, "BlockManager")

@@ -12,8 +12,9 @@ namespace {
 
 // ---- per-element GGUF dequant (row-major raw rows; used for embedding gathers) ----------------
 
+// fp16 fields of the GGUF blocks sit at even offsets: one 16-bit load.
 __device__ __forceinline__ float h2f(const uint8_t* p) {
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(p[0] | (p[1] << 8))));
+  return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p)));
 }
 
 __device__ float dq_elem(int type, const uint8_t* row, int k) {

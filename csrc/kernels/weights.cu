@@ -10,9 +10,11 @@
 namespace vmc {
 namespace {
 
+// fp16 / bf16 fields of the block formats always sit at even offsets: use 16-bit accesses.
 __device__ __forceinline__ float ld_half(const uint8_t* p) {
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(p[0] | (p[1] << 8))));
+  return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p)));
 }
+__device__ __forceinline__ void st_u16(uint8_t* p, unsigned short u) { *reinterpret_cast<unsigned short*>(p) = u; }
 
 // ---- repack: GGUF rows -> tiles -------------------------------------------------------------
 
@@ -78,10 +80,7 @@ __global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, int N, int KB
     for (int i = 0; i < 4; ++i) o[128 + 4 * g + i] = static_cast<uint8_t>(V >> (8 * i));
   }
   for (int g = 0; g < 16; ++g) {
-    const __nv_bfloat16 s = __float2bfloat16(d * static_cast<float>(sc[g]));
-    const unsigned short u = __bfloat16_as_ushort(s);
-    o[192 + 2 * g] = static_cast<uint8_t>(u & 0xff);
-    o[192 + 2 * g + 1] = static_cast<uint8_t>(u >> 8);
+    st_u16(o + 192 + 2 * g, __bfloat16_as_ushort(__float2bfloat16(d * static_cast<float>(sc[g]))));
   }
 }
 
@@ -95,14 +94,12 @@ __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ src, int N, int K
   for (int j = 0; j < 8; ++j) {
     const int blk = kc * 8 + j;
     if (n >= N || blk >= K32) {
-      o[2 * j] = o[2 * j + 1] = 0;
+      st_u16(o + 2 * j, 0);
       for (int i = 0; i < 32; ++i) o[16 + 32 * j + i] = 0;
       continue;
     }
     const uint8_t* b = src + (static_cast<int64_t>(n) * K32 + blk) * 34;
-    const unsigned short u = __bfloat16_as_ushort(__float2bfloat16(ld_half(b)));
-    o[2 * j] = static_cast<uint8_t>(u & 0xff);
-    o[2 * j + 1] = static_cast<uint8_t>(u >> 8);
+    st_u16(o + 2 * j, __bfloat16_as_ushort(__float2bfloat16(ld_half(b))));
     for (int g = 0; g < 8; ++g) {
       const uint8_t* q = b + 2 + 4 * g;
       uint8_t* p = o + 16 + 32 * j + 4 * g;
@@ -150,11 +147,7 @@ __global__ void repack_bf16_kernel(const void* __restrict__ src, int src_type, i
 
 // ---- on-device quantisers (GGUF block formats) ------------------------------------------------
 
-__device__ __forceinline__ void st_half(uint8_t* p, float f) {
-  const unsigned short u = __half_as_ushort(__float2half_rn(f));
-  p[0] = static_cast<uint8_t>(u & 0xff);
-  p[1] = static_cast<uint8_t>(u >> 8);
-}
+__device__ __forceinline__ void st_half(uint8_t* p, float f) { st_u16(p, __half_as_ushort(__float2half_rn(f))); }
 __device__ __forceinline__ float rt_half(float f) { return __half2float(__float2half_rn(f)); }
 __device__ __forceinline__ int rne(float x) { return __float2int_rn(x); }
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
