@@ -179,6 +179,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int tota
   constexpr int RB = Frag<D>::RB;
   constexpr int ND = Frag<D>::ND;
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.y;
   const int r = blockIdx.x + p.req_offset;
@@ -295,6 +297,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int tota
 template <int D>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
                                     int64_t rows, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -325,6 +329,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
   constexpr int ND = Frag<D>::ND;
   constexpr int TK = 64;  // keys per tile (4 pages)
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.z + p.req_offset;
   const int kvh = blockIdx.y;
@@ -423,12 +429,11 @@ void launch_decode(const AttnParams& p, int num_reqs, int total_tokens, cudaStre
     cfg = true;
   }
   dim3 grid(num_reqs, p.Hkv, p.splits);
-  attn_decode_kernel<D><<<grid, 128, smem, st>>>(p, total_tokens);
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(attn_decode_kernel<D>, grid, dim3(128), smem, st, p, total_tokens);
   if (p.splits > 1) {
     const int64_t rows = static_cast<int64_t>(total_tokens) * p.Hq;
-    attn_combine_kernel<D><<<static_cast<int>((rows + 3) / 4), 128, 0, st>>>(p.part_o, p.part_lse, p.splits, rows, p.out);
-    VMC_CUDA_CHECK(cudaGetLastError());
+    launch_k(attn_combine_kernel<D>, dim3(static_cast<int>((rows + 3) / 4)), dim3(128), 0, st,
+             static_cast<const float*>(p.part_o), static_cast<const float*>(p.part_lse), p.splits, rows, p.out);
   }
 }
 
@@ -442,8 +447,7 @@ void launch_prefill(const AttnParams& p, int num_reqs, int max_qlen, cudaStream_
     cfg = true;
   }
   dim3 grid((max_qlen * p.G + 63) / 64, p.Hkv, num_reqs);
-  attn_prefill_kernel<D><<<grid, 128, smem, st>>>(p);
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(attn_prefill_kernel<D>, grid, dim3(128), smem, st, p);
 }
 
 }  // namespace

@@ -1,0 +1,150 @@
+// Peer-memory tensor-parallel collectives fused with the adjacent compute (one process per GPU,
+// NVLink 5 / NVSwitch peer access through CUDA IPC mappings).
+//
+// Replaces the reference's NCCL all-reduce at its two per-layer sites (after Wo and after the FFN /
+// MoE down projection: src/distributed/nccl_comm.cu:259-327 via the GGML_OP_VM_C_TP_ALLREDUCE graph
+// op, src/official/llama/models/llama.cpp:171,196,221), which is followed by a separate residual add
+// and RMSNorm in the ggml graph.
+//
+//  * ar_add_rmsnorm_kernel: the row-parallel GEMM of every rank writes its fp32 partial into its
+//    own symmetric buffer; this kernel then (1) signals every peer and waits for every peer's
+//    signal (epoch flags, release/acquire at system scope, bounded spin), (2) reads the partial rows
+//    of all ranks over NVLink in rank order (bit-identical result on every rank), (3) adds the
+//    residual stream, (4) applies RMSNorm and writes the normalised bf16 activations for the next
+//    GEMM. One-shot all-reduce + residual + norm in a single kernel.
+//
+// Synchronisation: CTA b of every rank owns flag slot b; its participation count (epoch) advances
+// identically on all ranks because every rank launches the same sequence of calls with the same
+// grid. The partial buffers alternate between two sites, and a rank rewrites a site only after its
+// next all-reduce has seen every peer start that next all-reduce, so no reader can still be reading.
+#include "comm.h"
+#include "common.cuh"
+
+namespace vmc {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Peer data: bypass L1 so that a line cached by an earlier call is never reused.
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+constexpr int kMaxRanks = 8;
+constexpr int kArThreads = 256;
+constexpr int kMaxPer = 32;  // floats per thread held in registers (H <= 256 * 4 * 8 = 8192)
+
+__global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
+  const int b = blockIdx.x;
+  __shared__ float red[32];
+  __shared__ int ok;
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    const uint32_t e = a.epochs[b] + 1;
+    a.epochs[b] = e;
+    for (int q = 0; q < a.nranks; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
+    int good = 1;
+    for (int q = 0; q < a.nranks && good; ++q) {
+      uint32_t i = 0;
+      while (ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q) < e) {
+        if (++i > kSpinLimit) {
+          atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
+          good = 0;
+          break;
+        }
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int H = a.H;
+  const int nvec = H / 4;
+  for (int row = b; row < a.T; row += gridDim.x) {
+    float v[kMaxPer];
+    float ss = 0.f;
+    const size_t base = static_cast<size_t>(row) * H;
+#pragma unroll
+    for (int j = 0; j < kMaxPer / 4; ++j) {
+      const int vi = threadIdx.x + j * kArThreads;
+      if (vi < nvec) {
+        float4 acc = *reinterpret_cast<const float4*>(a.resid + base + 4 * vi);
+        for (int q = 0; q < a.nranks; ++q) {
+          for (int sp = 0; sp < a.nsplit; ++sp) {
+            const float4 p = ld_cg_f4(a.data[q] + sp * a.split_stride + base + 4 * vi);
+            acc.x += p.x;
+            acc.y += p.y;
+            acc.z += p.z;
+            acc.w += p.w;
+          }
+        }
+        *reinterpret_cast<float4*>(a.resid + base + 4 * vi) = acc;
+        v[4 * j] = acc.x;
+        v[4 * j + 1] = acc.y;
+        v[4 * j + 2] = acc.z;
+        v[4 * j + 3] = acc.w;
+        ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kArThreads / 32 ? red[threadIdx.x] : 0.f;
+      t = warp_sum(t);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / H + a.eps);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kMaxPer / 4; ++j) {
+      const int vi = threadIdx.x + j * kArThreads;
+      if (vi < nvec) {
+        const float4 w = *reinterpret_cast<const float4*>(a.w + 4 * vi);
+        uint2 o;
+        o.x = pack_bf16x2(v[4 * j] * inv * w.x, v[4 * j + 1] * inv * w.y);
+        o.y = pack_bf16x2(v[4 * j + 2] * inv * w.z, v[4 * j + 3] * inv * w.w);
+        *reinterpret_cast<uint2*>(a.out + base + 4 * vi) = o;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
+  VMC_CHECK(a.nranks >= 1 && a.nranks <= kMaxRanks, "ar_add_rmsnorm: 1..8 ranks");
+  VMC_CHECK(a.H % 4 == 0 && a.H <= kArThreads * kMaxPer, "ar_add_rmsnorm: hidden size unsupported");
+  if (a.T <= 0) return;
+  const int grid = a.T < max_ctas ? a.T : max_ctas;
+  launch_k(ar_add_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0, st, a);
+}
+
+// ---- symmetric memory through CUDA IPC ----------------------------------------------------------
+
+uint64_t sym_alloc(size_t bytes, void* handle_out) {
+  void* p = nullptr;
+  VMC_CUDA_CHECK(cudaMalloc(&p, bytes));
+  VMC_CUDA_CHECK(cudaMemset(p, 0, bytes));
+  VMC_CUDA_CHECK(cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), p));
+  return reinterpret_cast<uint64_t>(p);
+}
+
+uint64_t sym_open(const void* handle) {
+  void* p = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  VMC_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<uint64_t>(p);
+}
+
+void sym_close(uint64_t peer_ptr) { VMC_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(peer_ptr))); }
+void sym_free(uint64_t ptr) { VMC_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr))); }
+
+}  // namespace vmc

@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include <stdexcept>
+#include <utility>
 #include <string>
 
 #define VMC_CUDA_CHECK(expr)                                                                     \
@@ -227,6 +228,36 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+}  // namespace vmc
+
+namespace vmc {
+
+// ----------------------------------------------------------------------------------------------
+// Programmatic dependent launch: kernels are launched with the programmatic-serialization
+// attribute so that a kernel's CTAs can start (barrier init, TMEM allocation, weight prefetch)
+// while the previous kernel drains. pdl_wait() blocks until the previous grid has completed and
+// its memory is visible; every kernel calls it before touching data the previous kernel produces
+// (or may still read). pdl_trigger() lets the next kernel be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  VMC_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
 }  // namespace vmc

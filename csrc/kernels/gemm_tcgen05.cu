@@ -4,17 +4,23 @@
 // mul_mat_vec_q, ggml-cuda/mmq.cuh:3542, mmvq.cu:398, and cuBLAS for F16/BF16 weights), which on
 // sm_100 runs as Ampere-class mma.sync / dp4a code.
 //
-// Design ("swap-AB"): the weight tile is the UMMA A operand (M_mma = 128 output features), the
-// activation tile is the B operand (N_mma = BN tokens, 16..256), the fp32 accumulator lives in TMEM.
-// Warp roles in a 320-thread CTA:
-//   warp 0      producer: TMA 2-D loads of activation tiles (128B swizzle, zero fill past M/K) and
-//               one cp.async.bulk per weight tile (tiles are stored contiguously, see
-//               weight_formats.cuh); bf16 weights go straight into the A stage.
+// Design ("swap-AB", persistent, warp-specialised). The weight tile is the UMMA A operand
+// (M_mma = 128 output features), the activation tile is the B operand (N_mma = BN tokens, 16..256),
+// and the fp32 accumulator lives in TMEM, double-buffered so that the epilogue of one work unit
+// overlaps the main loop of the next. A work unit is (128-feature tile, BN-token tile, K split);
+// one CTA per SM walks the units round-robin, so the weight stream never drains between tiles.
+// Warp roles in a 480-thread CTA:
+//   warp 0      weight producer: one cp.async.bulk per weight tile (tiles are stored contiguously,
+//               see weight_formats.cuh) into the raw ring, or straight into the A ring for bf16.
+//               Weights do not depend on the previous kernel, so the first tiles are requested
+//               before the programmatic-dependency wait.
 //   warp 1      allocates TMEM; one elected lane issues tcgen05.mma (K=16 per instruction) and
-//               tcgen05.commit to release stages.
-//   warps 2-9   dequantize GGUF blocks from the raw stage into the swizzled bf16 A stage
-//               (packed bf16x2 integer tricks, see the per-format functions), then run the
-//               epilogue: tcgen05.ld -> bf16 store, fp32 red.add (split-K), or fused SwiGLU.
+//               tcgen05.commit to release ring stages and hand finished accumulators over.
+//   warps 2-9   dequantize GGUF blocks from the raw ring into the 128B-swizzled bf16 A ring
+//               (packed bf16x2 integer tricks, see the per-format functions).
+//   warp 10     activation producer: TMA 2-D loads (128B swizzle, zero fill past M / K).
+//   warps 11-14 epilogue: tcgen05.ld -> bf16 store, fp32 store (per-split partials, no atomics),
+//               fp32 red.add, or the fused SwiGLU (gate / up rows interleaved).
 // Every wait is bounded; on expiry the CTA records an error code and unwinds (TMEM is freed).
 #include <cuda.h>
 
@@ -25,44 +31,48 @@
 namespace vmc {
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 480;
 constexpr int kDequantWarps = 8;
 constexpr int kFirstDqWarp = 2;
+constexpr int kBWarp = 10;
+constexpr int kFirstEpiWarp = 11;
 
 struct GemmSmemPlan {
-  int stages;      // A/B pipeline stages (64-K each)
-  int raw_stages;  // raw quant tile stages (256-K each)
-  int bn;
-  int wf;
-  __host__ __device__ int a_bytes() const { return 128 * 128; }
-  __host__ __device__ int b_bytes() const { return bn * 128; }
-  __host__ __device__ int raw_bytes() const { return wf == kWfBF16 ? 0 : wf_tile_bytes(wf); }
-  __host__ __device__ int off_b() const { return stages * a_bytes(); }
-  __host__ __device__ int off_raw() const { return off_b() + stages * b_bytes(); }
-  __host__ __device__ int off_bar() const { return off_raw() + raw_stages * raw_bytes(); }
-  __host__ __device__ int total() const { return off_bar() + (2 * stages + 2 * raw_stages + 2) * 8 + 16 + 1024; }
+  int stages = 0;      // A/B ring stages (64-K each)
+  int raw_stages = 0;  // raw quant tile stages (one chunk = 256-K each)
+  int bn = 0;
+  int wf = 0;
+  __host__ __device__ constexpr int a_bytes() const { return 128 * 128; }
+  __host__ __device__ constexpr int b_bytes() const { return bn * 128; }
+  __host__ __device__ constexpr int raw_bytes() const { return wf == kWfBF16 ? 0 : wf_tile_bytes(wf); }
+  __host__ __device__ constexpr int off_b() const { return stages * a_bytes(); }
+  __host__ __device__ constexpr int off_raw() const { return off_b() + stages * b_bytes(); }
+  __host__ __device__ constexpr int off_bar() const { return off_raw() + raw_stages * raw_bytes(); }
+  __host__ __device__ constexpr int nbars() const { return 2 * stages + 2 * raw_stages + 4; }
+  __host__ __device__ constexpr int total() const { return off_bar() + nbars() * 8 + 16 + 1024; }
 };
 
-__host__ __device__ inline GemmSmemPlan make_plan(int wf, int bn) {
+// Shared-memory plan for one CTA per SM: at least 2 A/B stages and 2 raw stages, then grow the
+// raw ring (the weight stream) and the A/B ring alternately while the plan fits.
+__host__ __device__ constexpr GemmSmemPlan make_plan(int wf, int bn) {
   GemmSmemPlan p;
   p.bn = bn;
   p.wf = wf;
-  const int budget = 220 * 1024;
-  p.raw_stages = wf == kWfBF16 ? 0 : 2;
+  const int budget = 222 * 1024;
   p.stages = 2;
-  // Grow the A/B ring first, then the raw ring, while the plan fits.
-  while (true) {
-    GemmSmemPlan q = p;
-    q.stages += 1;
-    if (q.stages > 8 || q.total() > budget) break;
-    p = q;
-  }
-  if (wf != kWfBF16) {
-    while (true) {
+  p.raw_stages = wf == kWfBF16 ? 0 : 2;
+  bool grew = true;
+  while (grew) {
+    grew = false;
+    if (wf != kWfBF16 && p.raw_stages < 8) {
       GemmSmemPlan q = p;
       q.raw_stages += 1;
-      if (q.raw_stages > 4 || q.total() > budget) break;
-      p = q;
+      if (q.total() <= budget) { p = q; grew = true; }
+    }
+    if (p.stages < (wf == kWfBF16 ? 8 : 4)) {
+      GemmSmemPlan q = p;
+      q.stages += 1;
+      if (q.total() <= budget) { p = q; grew = true; }
     }
   }
   return p;
@@ -175,17 +185,40 @@ struct GemmArgs {
   int N, K, M;
   int KC;                 // number of K chunks in the tiled weight (ceil(K / chunk))
   int chunks_per_split;
+  int n_tiles, m_tiles, splits;
+  int units;              // n_tiles * m_tiles * splits
   void* out;
   int ldo;                // output row stride in elements
+  int64_t split_stride;   // elements between the per-split output slices (kGemmOutF32Split)
   int out_mode;           // GemmOut
   uint32_t* err;
 };
+
+// Work unit u -> (n tile, m tile, split). m fastest: concurrently running CTAs share a weight tile,
+// so in prefill the tile is fetched from HBM once and re-read from L2 by the other token tiles.
+struct Unit {
+  int nt, mt, split, c0, c1;
+};
+__device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
+  Unit r;
+  r.mt = u % a.m_tiles;
+  const int rest = u / a.m_tiles;
+  r.split = rest % a.splits;
+  r.nt = rest / a.splits;
+  r.c0 = r.split * a.chunks_per_split;
+  r.c1 = min(a.KC, r.c0 + a.chunks_per_split);
+  return r;
+}
 
 template <int WF, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const GemmSmemPlan P = make_plan(WF, BN);
+  constexpr GemmSmemPlan P = make_plan(WF, BN);
+  constexpr int SUBS = (WF == kWfBF16) ? 1 : 4;  // 64-K substeps per chunk
+  constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
+  constexpr uint32_t kTmemCols = 2 * kAccCols;
+  constexpr bool quant = WF != kWfBF16;
   uint8_t* sA = smem;
   uint8_t* sB = smem + P.off_b();
   uint8_t* sRaw = smem + P.off_raw();
@@ -194,30 +227,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint64_t* ab_empty = bars + P.stages;
   uint64_t* raw_full = bars + 2 * P.stages;
   uint64_t* raw_empty = raw_full + P.raw_stages;
-  uint64_t* acc_full = raw_empty + P.raw_stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 2);
+  uint64_t* acc_full = raw_empty + P.raw_stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;             // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nt = blockIdx.x, mt = blockIdx.y;
-  const int c_begin = blockIdx.z * args.chunks_per_split;
-  const int c_end = min(args.KC, c_begin + args.chunks_per_split);
-  const int nchunks = c_end - c_begin;
-  constexpr int SUBS = (WF == kWfBF16) ? 1 : 4;  // 64-K substeps per chunk
-  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
-  const bool quant = WF != kWfBF16;
 
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < P.stages; ++i) {
-      mbar_init(&ab_full[i], 1 + (quant ? kDequantWarps : 0));
+      mbar_init(&ab_full[i], 1 + (quant ? kDequantWarps : 1));
       mbar_init(&ab_empty[i], 1);
     }
     for (int i = 0; i < P.raw_stages; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kDequantWarps);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -229,76 +260,101 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int first = blockIdx.x, step = gridDim.x;
 
-  if (nchunks > 0) {
-    if (warp == 0) {
-      if (lane == 0) {
-        const uint64_t pol = l2_policy_evict_first();
-        int stage = 0;
-        uint32_t phase = 0;
-        int rstage = 0;
-        uint32_t rphase = 0;
-        for (int c = 0; c < nchunks && !*abort_flag; ++c) {
-          const int kc = c_begin + c;
-          const uint8_t* wt = args.w + (static_cast<size_t>(nt) * args.KC + kc) * wf_tile_bytes(WF);
+  if (warp == 0) {
+    // ---------------- weight producer ----------------
+    if (lane == 0) {
+      // Weights are constant: the stream starts before (and never waits on) the programmatic
+      // dependency, so its latency overlaps the previous kernel.
+      const uint64_t pol = l2_policy_evict_first();
+      int st = 0;
+      uint32_t ph = 0;
+      for (int u = first; u < args.units && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        const uint8_t* wbase = args.w + static_cast<size_t>(w.nt) * args.KC * wf_tile_bytes(WF);
+        for (int c = w.c0; c < w.c1; ++c) {
+          const uint8_t* wt = wbase + static_cast<size_t>(c) * wf_tile_bytes(WF);
           if (quant) {
-            if (!mbar_wait(&raw_empty[rstage], rphase ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-            mbar_arrive_expect_tx(&raw_full[rstage], wf_tile_bytes(WF));
-            bulk_load_evict_first(sRaw + rstage * P.raw_bytes(), wt, wf_tile_bytes(WF), &raw_full[rstage], pol);
-            if (++rstage == P.raw_stages) { rstage = 0; rphase ^= 1; }
+            if (!mbar_wait(&raw_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&raw_full[st], wf_tile_bytes(WF));
+            bulk_load_evict_first(sRaw + st * P.raw_bytes(), wt, wf_tile_bytes(WF), &raw_full[st], pol);
+            if (++st == P.raw_stages) { st = 0; ph ^= 1; }
+          } else {
+            if (!mbar_wait(&ab_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&ab_full[st], P.a_bytes());
+            bulk_load_evict_first(sA + st * P.a_bytes(), wt, P.a_bytes(), &ab_full[st], pol);
+            if (++st == P.stages) { st = 0; ph ^= 1; }
           }
+        }
+      }
+    }
+  } else if (warp == kBWarp) {
+    // ---------------- activation producer ----------------
+    if (lane == 0) {
+      pdl_wait();
+      int st = 0;
+      uint32_t ph = 0;
+      for (int u = first; u < args.units && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        for (int c = w.c0; c < w.c1; ++c) {
           for (int sub = 0; sub < SUBS; ++sub) {
-            if (!mbar_wait(&ab_empty[stage], phase ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-            const uint32_t bytes = P.b_bytes() + (quant ? 0 : P.a_bytes());
-            mbar_arrive_expect_tx(&ab_full[stage], bytes);
-            tma_load_2d(sB + stage * P.b_bytes(), &xmap, &ab_full[stage], (kc * SUBS + sub) * 64, mt * BN);
-            if (!quant) bulk_load_evict_first(sA + stage * P.a_bytes(), wt, P.a_bytes(), &ab_full[stage], pol);
-            if (++stage == P.stages) { stage = 0; phase ^= 1; }
+            if (!mbar_wait(&ab_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&ab_full[st], P.b_bytes());
+            tma_load_2d(sB + st * P.b_bytes(), &xmap, &ab_full[st], (c * SUBS + sub) * 64, w.mt * BN);
+            if (++st == P.stages) { st = 0; ph ^= 1; }
           }
         }
       }
-    } else if (warp == 1) {
-      if (lane == 0) {
-        const uint32_t idesc = umma_idesc_bf16(128, BN);
-        int stage = 0;
-        uint32_t phase = 0;
-        const int total = nchunks * SUBS;
-        bool ok = true;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+      int st = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      for (int u = first; u < args.units && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc) * kAccCols;
+        const int total = (w.c1 - w.c0) * SUBS;
         for (int i = 0; i < total; ++i) {
-          if (!mbar_wait(&ab_full[stage], phase, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+          if (!mbar_wait(&ab_full[st], ph, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
           tc_fence_after();
-          const uint64_t a0 = umma_sdesc_sw128(smem_u32(sA + stage * P.a_bytes()));
-          const uint64_t b0 = umma_sdesc_sw128(smem_u32(sB + stage * P.b_bytes()));
+          const uint64_t a0 = umma_sdesc_sw128(smem_u32(sA + st * P.a_bytes()));
+          const uint64_t b0 = umma_sdesc_sw128(smem_u32(sB + st * P.b_bytes()));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            umma_bf16(tmem, a0 + 2 * k, b0 + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&ab_empty[stage]);
-          if (++stage == P.stages) { stage = 0; phase ^= 1; }
+          for (int k = 0; k < 4; ++k) umma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&ab_empty[st]);
+          if (++st == P.stages) { st = 0; ph ^= 1; }
         }
-        (void)ok;
-        umma_commit(acc_full);
+        umma_commit(&acc_full[acc]);
+        if (++acc == 2) { acc = 0; acc_ph ^= 1; }
       }
-    } else {
-      // Dequant warps (quantized formats only).
+    }
+  } else if (warp < kFirstDqWarp + kDequantWarps) {
+    // ---------------- dequant (quantized formats) ----------------
+    if (quant) {
       const int t = threadIdx.x - kFirstDqWarp * 32;  // 0..255
       const int r = t >> 1, h = t & 1;
-      if (quant) {
-        int stage = 0;
-        uint32_t phase = 0;
-        int rstage = 0;
-        uint32_t rphase = 0;
-        for (int c = 0; c < nchunks; ++c) {
-          if (!mbar_wait(&raw_full[rstage], rphase, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-          const uint8_t* row = sRaw + rstage * P.raw_bytes() + r * wf_row_bytes(WF);
-          bool ok = true;
+      int st = 0, rst = 0;
+      uint32_t ph = 0, rph = 0;
+      for (int u = first; u < args.units && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        bool ok = true;
+        for (int c = w.c0; c < w.c1 && ok; ++c) {
+          if (!mbar_wait(&raw_full[rst], rph, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+          const uint8_t* row = sRaw + rst * P.raw_bytes() + r * wf_row_bytes(WF);
           for (int sub = 0; sub < SUBS; ++sub) {
-            if (!mbar_wait(&ab_empty[stage], phase ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+            if (!mbar_wait(&ab_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
             uint32_t o[16];
             if (WF == kWfQ4K) dq_q4k(row, sub, h, o);
             else if (WF == kWfQ6K) dq_q6k(row, sub, h, o);
             else dq_q8_0(row, sub, h, o);
-            uint8_t* a = sA + stage * P.a_bytes();
+            uint8_t* a = sA + st * P.a_bytes();
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
               *reinterpret_cast<uint4*>(a + sw128_offset(r, 4 * h + cc)) =
@@ -306,62 +362,69 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&ab_full[stage]);
-            if (++stage == P.stages) { stage = 0; phase ^= 1; }
+            if (lane == 0) mbar_arrive(&ab_full[st]);
+            if (++st == P.stages) { st = 0; ph ^= 1; }
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&raw_empty[rstage]);
-          if (++rstage == P.raw_stages) { rstage = 0; rphase ^= 1; }
-          if (!ok) break;
+          if (lane == 0) mbar_arrive(&raw_empty[rst]);
+          if (++rst == P.raw_stages) { rst = 0; rph ^= 1; }
         }
+        if (!ok) break;
       }
-      // Epilogue: warps 2..9 -> TMEM lane quarter (warp % 4), column half ((warp - 2) / 4).
-      if (mbar_wait(acc_full, 0, args.err, kErrGemmWait)) {
-        tc_fence_after();
-        const int q = warp & 3;
-        const int half = (warp - kFirstDqWarp) >> 2;
-        const int n_local = 32 * q + lane;
-        constexpr int HALVES = BN >= 32 ? 2 : 1;
-        constexpr int COLS = BN / HALVES;
-        const int col0 = half * COLS;
-        for (int cb = 0; cb < COLS && half < HALVES; cb += 16) {
-          uint32_t v[16];
-          tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(col0 + cb), v);
-          tmem_ld_wait();
-          const int m_base = mt * BN + col0 + cb;
-          if (args.out_mode == kGemmOutSwiGLU) {
-            // Rows interleave gate (even) and up (odd) features of the same output column.
+    }
+  } else {
+    // ---------------- epilogue (warps 11..14 -> TMEM lane quarter warp % 4) ----------------
+    pdl_wait();  // outputs may still be read by the previous kernel
+    const int q = warp & 3;
+    const int n_local = 32 * q + lane;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int u = first; u < args.units && !*abort_flag; u += step) {
+      const Unit w = unit_of(args, u);
+      if (!mbar_wait(&acc_full[acc], acc_ph, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const uint32_t d = tmem + static_cast<uint32_t>(acc) * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
+      float* outf = reinterpret_cast<float*>(args.out);
+      if (args.out_mode == kGemmOutF32Split) outf += w.split * args.split_stride;
+      for (int cb = 0; cb < BN; cb += 16) {
+        uint32_t v[16];
+        tmem_ld16(d + static_cast<uint32_t>(cb), v);
+        tmem_ld_wait();
+        const int m_base = w.mt * BN + cb;
+        if (args.out_mode == kGemmOutSwiGLU) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float mine = __uint_as_float(v[j]);
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            const int m = m_base + j;
+            if ((lane & 1) == 0 && m < args.M) {
+              const float y = mine / (1.f + __expf(-mine)) * other;
+              const int f = w.nt * 64 + (n_local >> 1);
+              if (f < args.N / 2)
+                reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
+            }
+          }
+        } else {
+          const int n = w.nt * 128 + n_local;
+          if (n < args.N) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float mine = __uint_as_float(v[j]);
-              const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
               const int m = m_base + j;
-              if ((lane & 1) == 0 && m < args.M) {
-                const float g = mine, u = other;
-                const float y = g / (1.f + __expf(-g)) * u;
-                const int f = nt * 64 + (n_local >> 1);
-                if (f < args.N / 2)
-                  reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
-              }
-            }
-          } else {
-            const int n = nt * 128 + n_local;
-            if (n < args.N) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int m = m_base + j;
-                if (m < args.M) {
-                  const float y = __uint_as_float(v[j]);
-                  const size_t idx = static_cast<size_t>(m) * args.ldo + n;
-                  if (args.out_mode == kGemmOutF32Add) atomicAdd(reinterpret_cast<float*>(args.out) + idx, y);
-                  else if (args.out_mode == kGemmOutF32) reinterpret_cast<float*>(args.out)[idx] = y;
-                  else reinterpret_cast<__nv_bfloat16*>(args.out)[idx] = __float2bfloat16(y);
-                }
+              if (m < args.M) {
+                const float y = __uint_as_float(v[j]);
+                const size_t idx = static_cast<size_t>(m) * args.ldo + n;
+                if (args.out_mode == kGemmOutF32Add) atomicAdd(outf + idx, y);
+                else if (args.out_mode == kGemmOutBF16) reinterpret_cast<__nv_bfloat16*>(args.out)[idx] = __float2bfloat16(y);
+                else outf[idx] = y;
               }
             }
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_ph ^= 1; }
     }
   }
   tc_fence_before();
@@ -391,27 +454,37 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    VMC_CUDA_CHECK(cudaGetDevice(&dev));
+    VMC_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
 template <int WF, int BN>
-void launch(const CUtensorMap& map, const GemmArgs& a, int splits, cudaStream_t st) {
-  const GemmSmemPlan P = make_plan(WF, BN);
+void launch(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+  constexpr GemmSmemPlan P = make_plan(WF, BN);
+  static_assert(P.total() <= 227 * 1024, "shared memory plan too large");
   static bool configured = false;
   if (!configured) {
     VMC_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel<WF, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, P.total()));
     configured = true;
   }
-  dim3 grid((a.N + 127) / 128, (a.M + BN - 1) / BN, splits);
-  gemm_kernel<WF, BN><<<grid, kThreads, P.total(), st>>>(map, a);
-  VMC_CUDA_CHECK(cudaGetLastError());
+  const int grid = a.units < num_sms() ? a.units : num_sms();
+  launch_k(gemm_kernel<WF, BN>, dim3(grid), dim3(kThreads), P.total(), st, map, a);
 }
 
 template <int WF>
-void dispatch_bn(int bn, const CUtensorMap& map, const GemmArgs& a, int splits, cudaStream_t st) {
+void dispatch_bn(int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   switch (bn) {
-    case 16: launch<WF, 16>(map, a, splits, st); break;
-    case 32: launch<WF, 32>(map, a, splits, st); break;
-    case 64: launch<WF, 64>(map, a, splits, st); break;
-    case 128: launch<WF, 128>(map, a, splits, st); break;
-    case 256: launch<WF, 256>(map, a, splits, st); break;
+    case 16: launch<WF, 16>(map, a, st); break;
+    case 32: launch<WF, 32>(map, a, st); break;
+    case 64: launch<WF, 64>(map, a, st); break;
+    case 128: launch<WF, 128>(map, a, st); break;
+    case 256: launch<WF, 256>(map, a, st); break;
     default: throw std::runtime_error("gemm: unsupported BN");
   }
 }
@@ -440,14 +513,15 @@ int gemm_pick_bn(int M) {
 }
 
 void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
-                  int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st) {
+                  int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride) {
   VMC_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
   if (bn <= 0) bn = gemm_pick_bn(M);
   const int chunk = wf_chunk(wf);
   const int KC = (K + chunk - 1) / chunk;
   if (splits < 1) splits = 1;
   if (splits > KC) splits = KC;
-  VMC_CHECK(splits == 1 || out_mode == kGemmOutF32Add, "gemm: split-K needs the fp32 accumulate output mode");
+  VMC_CHECK(splits == 1 || out_mode == kGemmOutF32Add || out_mode == kGemmOutF32Split,
+            "gemm: split-K needs an fp32 accumulate / per-split output mode");
   GemmArgs a;
   a.w = static_cast<const uint8_t*>(w_tiled);
   a.N = N;
@@ -456,17 +530,22 @@ void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int 
   a.KC = KC;
   a.chunks_per_split = (KC + splits - 1) / splits;
   splits = (KC + a.chunks_per_split - 1) / a.chunks_per_split;
+  a.splits = splits;
+  a.n_tiles = (N + 127) / 128;
+  a.m_tiles = (M + bn - 1) / bn;
+  a.units = a.n_tiles * a.m_tiles * splits;
   a.out = out;
   a.ldo = ldo;
   a.out_mode = out_mode;
+  a.split_stride = split_stride;
   a.err = err;
   CUtensorMap map;
   make_act_tensor_map(&map, x, M, K, ldx, bn);
   switch (wf) {
-    case kWfBF16: dispatch_bn<kWfBF16>(bn, map, a, splits, st); break;
-    case kWfQ4K: dispatch_bn<kWfQ4K>(bn, map, a, splits, st); break;
-    case kWfQ6K: dispatch_bn<kWfQ6K>(bn, map, a, splits, st); break;
-    case kWfQ8_0: dispatch_bn<kWfQ8_0>(bn, map, a, splits, st); break;
+    case kWfBF16: dispatch_bn<kWfBF16>(bn, map, a, st); break;
+    case kWfQ4K: dispatch_bn<kWfQ4K>(bn, map, a, st); break;
+    case kWfQ6K: dispatch_bn<kWfQ6K>(bn, map, a, st); break;
+    case kWfQ8_0: dispatch_bn<kWfQ8_0>(bn, map, a, st); break;
     default: throw std::runtime_error("gemm: unknown weight format");
   }
 }

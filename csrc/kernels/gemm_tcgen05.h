@@ -11,13 +11,14 @@ enum GemmOut : int {
   kGemmOutF32 = 1,     // out[m, n] = acc (fp32)
   kGemmOutF32Add = 2,  // out[m, n] += acc (fp32 red.add; required for split-K; output pre-zeroed)
   kGemmOutSwiGLU = 3,  // rows interleave gate/up: out[m, f] = silu(acc[2f]) * acc[2f+1] (bf16)
+  kGemmOutF32Split = 4,  // out[split][m, n] = partial over this split's K range (fp32, no atomics)
 };
 
 // out = x[M, K] (bf16, row stride ldx) @ W[N, K]^T with W in a tiled format (weight_formats.cuh).
 // splits > 1 partitions K across CTAs (out_mode must be kGemmOutF32Add). bn = 0 picks the token
 // tile from M. `err` receives a DeviceError code if a bounded wait expires.
 void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
-                  int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st);
+                  int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride = 0);
 int gemm_pick_bn(int M);
 int gemm_smem_bytes(int wf, int bn);
 void make_act_tensor_map(CUtensorMap* map, const void* x, int M, int K, int ldx, int box_rows);

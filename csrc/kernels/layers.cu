@@ -49,6 +49,8 @@ __device__ float dq_elem(int type, const uint8_t* row, int k) {
 
 __global__ void embed_kernel(const int32_t* __restrict__ ids, int T, const uint8_t* __restrict__ table, int type,
                              int64_t row_bytes, int H, float* __restrict__ resid, __nv_bfloat16* __restrict__ out_bf16) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   if (t >= T) return;
   const uint8_t* row = table + static_cast<int64_t>(ids[t]) * row_bytes;
@@ -65,6 +67,8 @@ template <typename TD>
 __global__ void add_rmsnorm_kernel(float* __restrict__ resid, const TD* __restrict__ delta, int ndelta,
                                    int64_t delta_stride, const float* __restrict__ w, int H, float eps,
                                    __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   float* x = resid + static_cast<int64_t>(t) * H;
   __shared__ float red[32];
@@ -100,10 +104,12 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ resid, const TD* __restri
 // written to q_out [T, Hq, D]; K heads rotated and V heads copied into the paged cache at the
 // token's slot (skipped when slot < 0). neox = rotate halves (x_i, x_{i+D/2}) instead of pairs.
 template <typename TI>
-__global__ void rope_store_kernel(const TI* __restrict__ qkv, int T, int Hq, int Hkv, int D,
-                                  const int32_t* __restrict__ pos, const int32_t* __restrict__ slots,
+__global__ void rope_store_kernel(const TI* __restrict__ qkv, int nsplit, int64_t split_stride, int T, int Hq, int Hkv,
+                                  int D, const int32_t* __restrict__ pos, const int32_t* __restrict__ slots,
                                   const float2* __restrict__ cs, int neox, __nv_bfloat16* __restrict__ q_out,
                                   __nv_bfloat16* __restrict__ kv) {
+  pdl_trigger();
+  pdl_wait();
   const int warps = blockDim.x >> 5;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -114,8 +120,13 @@ __global__ void rope_store_kernel(const TI* __restrict__ qkv, int T, int Hq, int
   const int p = pos[t];
   const float2* c = cs + static_cast<int64_t>(p) * (D / 2);
   auto ld = [&](int i) -> float {
-    if constexpr (sizeof(TI) == 2) return __bfloat162float(src[i]);
-    else return src[i];
+    if constexpr (sizeof(TI) == 2) {
+      return __bfloat162float(src[i]);
+    } else {
+      float v = src[i];
+      for (int sp = 1; sp < nsplit; ++sp) v += src[sp * split_stride + i];
+      return v;
+    }
   };
   __nv_bfloat16* dst;
   if (h < Hq) {
@@ -145,8 +156,10 @@ __global__ void rope_store_kernel(const TI* __restrict__ qkv, int T, int Hq, int
 // ---- SwiGLU on a [T, 2F] (gate | up) input ---------------------------------------------------
 // interleaved: the row holds (gate_0, up_0, gate_1, up_1, ...) instead of (gate | up).
 template <typename TI>
-__global__ void swiglu_kernel(const TI* __restrict__ gu, int64_t T, int F, int interleaved,
-                              __nv_bfloat16* __restrict__ out) {
+__global__ void swiglu_kernel(const TI* __restrict__ gu, int nsplit, int64_t split_stride, int64_t T, int F,
+                              int interleaved, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= T * F) return;
   const int64_t t = i / F;
@@ -160,6 +173,10 @@ __global__ void swiglu_kernel(const TI* __restrict__ gu, int64_t T, int F, int i
   } else {
     g = gu[ig];
     u = gu[iu];
+    for (int sp = 1; sp < nsplit; ++sp) {
+      g += gu[sp * split_stride + ig];
+      u += gu[sp * split_stride + iu];
+    }
   }
   out[i] = __float2bfloat16(g / (1.f + __expf(-g)) * u);
 }
@@ -167,6 +184,8 @@ __global__ void swiglu_kernel(const TI* __restrict__ gu, int64_t T, int F, int i
 // ---- gather rows (bf16) --------------------------------------------------------------------
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const int32_t* __restrict__ idx, int n,
                                    int H, __nv_bfloat16* __restrict__ dst) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   if (r >= n) return;
   const int64_t s = static_cast<int64_t>(idx[r]) * H;
@@ -181,6 +200,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const 
 
 // ---- fp32 -> bf16 ----------------------------------------------------------------------------
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, int64_t n, __nv_bfloat16* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __float2bfloat16(x[i]);
 }
@@ -192,9 +213,8 @@ inline int nblk(int64_t n, int t) { return static_cast<int>((n + t - 1) / t); }
 void embed(const int32_t* ids, int T, const void* table, int gtype, int64_t row_bytes, int H, float* resid,
            void* out_bf16, cudaStream_t st) {
   if (T <= 0) return;
-  embed_kernel<<<T, 256, 0, st>>>(ids, T, static_cast<const uint8_t*>(table), gtype, row_bytes, H, resid,
-                                  static_cast<__nv_bfloat16*>(out_bf16));
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(embed_kernel, dim3(T), dim3(256), 0, st, ids, T, static_cast<const uint8_t*>(table), gtype, row_bytes, H,
+           resid, static_cast<__nv_bfloat16*>(out_bf16));
 }
 
 void add_rmsnorm(float* resid, const void* delta, bool delta_f32, int ndelta, int64_t delta_stride, const float* w,
@@ -202,51 +222,51 @@ void add_rmsnorm(float* resid, const void* delta, bool delta_f32, int ndelta, in
   if (T <= 0) return;
   const int threads = H >= 2048 ? 512 : 256;
   if (delta_f32 || delta == nullptr)
-    add_rmsnorm_kernel<float><<<T, threads, 0, st>>>(resid, static_cast<const float*>(delta), delta ? ndelta : 0,
-                                                      delta_stride, w, H, eps, static_cast<__nv_bfloat16*>(out));
+    launch_k(add_rmsnorm_kernel<float>, dim3(T), dim3(threads), 0, st, resid, static_cast<const float*>(delta),
+             delta ? ndelta : 0, delta_stride, w, H, eps, static_cast<__nv_bfloat16*>(out));
   else
-    add_rmsnorm_kernel<__nv_bfloat16><<<T, threads, 0, st>>>(resid, static_cast<const __nv_bfloat16*>(delta), ndelta,
-                                                             delta_stride, w, H, eps, static_cast<__nv_bfloat16*>(out));
-  VMC_CUDA_CHECK(cudaGetLastError());
+    launch_k(add_rmsnorm_kernel<__nv_bfloat16>, dim3(T), dim3(threads), 0, st, resid,
+             static_cast<const __nv_bfloat16*>(delta), ndelta, delta_stride, w, H, eps, static_cast<__nv_bfloat16*>(out));
 }
 
-void rope_store(const void* qkv, bool qkv_f32, int T, int Hq, int Hkv, int D, const int32_t* pos, const int32_t* slots,
-                const float* cos_sin, bool neox, void* q_out, void* kv, cudaStream_t st) {
+void rope_store(const void* qkv, bool qkv_f32, int nsplit, int64_t split_stride, int T, int Hq, int Hkv, int D,
+                const int32_t* pos, const int32_t* slots, const float* cos_sin, bool neox, void* q_out, void* kv,
+                cudaStream_t st) {
   if (T <= 0) return;
   const int64_t warps = static_cast<int64_t>(T) * (Hq + 2 * Hkv);
   const int wpb = 8;
   if (qkv_f32)
-    rope_store_kernel<float><<<nblk(warps, wpb), 32 * wpb, 0, st>>>(
-        static_cast<const float*>(qkv), T, Hq, Hkv, D, pos, slots, reinterpret_cast<const float2*>(cos_sin), neox,
-        static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kv));
+    launch_k(rope_store_kernel<float>, dim3(nblk(warps, wpb)), dim3(32 * wpb), 0, st, static_cast<const float*>(qkv),
+             nsplit, split_stride, T, Hq, Hkv, D, pos, slots, reinterpret_cast<const float2*>(cos_sin),
+             static_cast<int>(neox), static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kv));
   else
-    rope_store_kernel<__nv_bfloat16><<<nblk(warps, wpb), 32 * wpb, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(qkv), T, Hq, Hkv, D, pos, slots, reinterpret_cast<const float2*>(cos_sin),
-        neox, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(kv));
-  VMC_CUDA_CHECK(cudaGetLastError());
+    launch_k(rope_store_kernel<__nv_bfloat16>, dim3(nblk(warps, wpb)), dim3(32 * wpb), 0, st,
+             static_cast<const __nv_bfloat16*>(qkv), 1, static_cast<int64_t>(0), T, Hq, Hkv, D, pos, slots,
+             reinterpret_cast<const float2*>(cos_sin), static_cast<int>(neox), static_cast<__nv_bfloat16*>(q_out),
+             static_cast<__nv_bfloat16*>(kv));
 }
 
-void swiglu(const void* gu, bool f32, int64_t T, int F, bool interleaved, void* out, cudaStream_t st) {
+void swiglu(const void* gu, bool f32, int nsplit, int64_t split_stride, int64_t T, int F, bool interleaved, void* out,
+            cudaStream_t st) {
   if (T <= 0) return;
   if (f32)
-    swiglu_kernel<float><<<nblk(T * F, 256), 256, 0, st>>>(static_cast<const float*>(gu), T, F, interleaved,
-                                                           static_cast<__nv_bfloat16*>(out));
+    launch_k(swiglu_kernel<float>, dim3(nblk(T * F, 256)), dim3(256), 0, st, static_cast<const float*>(gu), nsplit,
+             split_stride, T, F, static_cast<int>(interleaved), static_cast<__nv_bfloat16*>(out));
   else
-    swiglu_kernel<__nv_bfloat16><<<nblk(T * F, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gu), T, F,
-                                                                     interleaved, static_cast<__nv_bfloat16*>(out));
-  VMC_CUDA_CHECK(cudaGetLastError());
+    launch_k(swiglu_kernel<__nv_bfloat16>, dim3(nblk(T * F, 256)), dim3(256), 0, st,
+             static_cast<const __nv_bfloat16*>(gu), 1, static_cast<int64_t>(0), T, F, static_cast<int>(interleaved),
+             static_cast<__nv_bfloat16*>(out));
 }
 
 void gather_rows(const void* src, const int32_t* idx, int n, int H, void* dst, cudaStream_t st) {
   if (n <= 0) return;
-  gather_rows_kernel<<<n, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(src), idx, n, H, static_cast<__nv_bfloat16*>(dst));
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(gather_rows_kernel, dim3(n), dim3(128), 0, st, static_cast<const __nv_bfloat16*>(src), idx, n, H,
+           static_cast<__nv_bfloat16*>(dst));
 }
 
 void f32_to_bf16(const float* x, int64_t n, void* y, cudaStream_t st) {
   if (n <= 0) return;
-  f32_to_bf16_kernel<<<nblk(n, 256), 256, 0, st>>>(x, n, static_cast<__nv_bfloat16*>(y));
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(f32_to_bf16_kernel, dim3(nblk(n, 256)), dim3(256), 0, st, x, n, static_cast<__nv_bfloat16*>(y));
 }
 
 }  // namespace vmc

@@ -12,9 +12,12 @@ void embed(const int32_t* ids, int T, const void* table, int gtype, int64_t row_
 void add_rmsnorm(float* resid, const void* delta, bool delta_f32, int ndelta, int64_t delta_stride, const float* w,
                  int T, int H, float eps, void* out, cudaStream_t st);
 // RoPE on Q/K heads of qkv [T, (Hq+2Hkv)*D]; Q -> q_out, K/V -> paged cache at slots[t].
-void rope_store(const void* qkv, bool qkv_f32, int T, int Hq, int Hkv, int D, const int32_t* pos, const int32_t* slots,
-                const float* cos_sin, bool neox, void* q_out, void* kv, cudaStream_t st);
-void swiglu(const void* gu, bool f32, int64_t T, int F, bool interleaved, void* out, cudaStream_t st);
+// qkv may be nsplit fp32 per-split partials `split_stride` elements apart (split-K GEMM output).
+void rope_store(const void* qkv, bool qkv_f32, int nsplit, int64_t split_stride, int T, int Hq, int Hkv, int D,
+                const int32_t* pos, const int32_t* slots, const float* cos_sin, bool neox, void* q_out, void* kv,
+                cudaStream_t st);
+void swiglu(const void* gu, bool f32, int nsplit, int64_t split_stride, int64_t T, int F, bool interleaved, void* out,
+            cudaStream_t st);
 void gather_rows(const void* src, const int32_t* idx, int n, int H, void* dst, cudaStream_t st);
 void f32_to_bf16(const float* x, int64_t n, void* y, cudaStream_t st);
 

@@ -5,6 +5,7 @@
 #include <torch/extension.h>
 
 #include "attention.h"
+#include "comm.h"
 #include "gemm_tcgen05.h"
 #include "layers.h"
 #include "sampling.h"
@@ -27,7 +28,7 @@ T* opt_ptr(const c10::optional<torch::Tensor>& t) {
 }
 
 void gemm(int wf, torch::Tensor w, int64_t N, int64_t K, torch::Tensor x, int64_t M, torch::Tensor out,
-          int64_t out_mode, int64_t splits, int64_t bn, torch::Tensor err) {
+          int64_t out_mode, int64_t splits, int64_t bn, torch::Tensor err, int64_t split_stride) {
   check_cuda(w, "w");
   check_cuda(x, "x");
   check_cuda(out, "out");
@@ -35,13 +36,18 @@ void gemm(int wf, torch::Tensor w, int64_t N, int64_t K, torch::Tensor x, int64_
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "gemm: x must be 2-D with unit inner stride");
   TORCH_CHECK(x.size(0) >= M && x.size(1) >= K, "gemm: x too small");
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= M, "gemm: bad output");
-  const bool f32_out = out_mode == vmc::kGemmOutF32 || out_mode == vmc::kGemmOutF32Add;
+  const bool f32_out =
+      out_mode == vmc::kGemmOutF32 || out_mode == vmc::kGemmOutF32Add || out_mode == vmc::kGemmOutF32Split;
+  if (out_mode == vmc::kGemmOutF32Split)
+    TORCH_CHECK(split_stride >= M * out.stride(0) &&
+                    out.storage().nbytes() >= static_cast<size_t>((splits * split_stride) * 4),
+                "gemm: per-split output buffer too small");
   TORCH_CHECK(out.scalar_type() == (f32_out ? torch::kFloat32 : torch::kBFloat16), "gemm: output dtype mismatch");
   TORCH_CHECK(w.numel() >= vmc::tiled_weight_bytes(wf, N, K), "gemm: weight buffer too small");
   vmc::gemm_tcgen05(wf, w.data_ptr(), static_cast<int>(N), static_cast<int>(K), x.data_ptr(), static_cast<int>(M),
                     static_cast<int>(x.stride(0)), out.data_ptr(), static_cast<int>(out.stride(0)),
                     static_cast<int>(out_mode), static_cast<int>(splits), static_cast<int>(bn),
-                    ptr<uint32_t>(err), cur_stream());
+                    ptr<uint32_t>(err), cur_stream(), split_stride);
 }
 
 void repack_weight(int wf, int src_type, torch::Tensor src, int64_t N, int64_t K, torch::Tensor dst) {
@@ -104,16 +110,19 @@ void add_rmsnorm(torch::Tensor resid, c10::optional<torch::Tensor> delta, int64_
                    static_cast<int>(T), static_cast<int>(H), static_cast<float>(eps), opt_ptr<void>(out), cur_stream());
 }
 
-void rope_store(torch::Tensor qkv, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor pos,
-                torch::Tensor slots, torch::Tensor cos_sin, bool neox, torch::Tensor q_out, torch::Tensor kv) {
-  vmc::rope_store(qkv.data_ptr(), qkv.scalar_type() == torch::kFloat32, static_cast<int>(T), static_cast<int>(Hq),
+void rope_store(torch::Tensor qkv, int64_t nsplit, int64_t split_stride, int64_t T, int64_t Hq, int64_t Hkv,
+                int64_t D, torch::Tensor pos, torch::Tensor slots, torch::Tensor cos_sin, bool neox,
+                torch::Tensor q_out, torch::Tensor kv) {
+  vmc::rope_store(qkv.data_ptr(), qkv.scalar_type() == torch::kFloat32, static_cast<int>(nsplit), split_stride,
+                  static_cast<int>(T), static_cast<int>(Hq),
                   static_cast<int>(Hkv), static_cast<int>(D), ptr<int32_t>(pos), ptr<int32_t>(slots),
                   ptr<float>(cos_sin), neox, q_out.data_ptr(), kv.data_ptr(), cur_stream());
 }
 
-void swiglu(torch::Tensor gu, int64_t T, int64_t F, bool interleaved, torch::Tensor out) {
-  vmc::swiglu(gu.data_ptr(), gu.scalar_type() == torch::kFloat32, T, static_cast<int>(F), interleaved, out.data_ptr(),
-              cur_stream());
+void swiglu(torch::Tensor gu, int64_t nsplit, int64_t split_stride, int64_t T, int64_t F, bool interleaved,
+            torch::Tensor out) {
+  vmc::swiglu(gu.data_ptr(), gu.scalar_type() == torch::kFloat32, static_cast<int>(nsplit), split_stride, T,
+              static_cast<int>(F), interleaved, out.data_ptr(), cur_stream());
 }
 
 void gather_rows(torch::Tensor src, torch::Tensor idx, int64_t n, int64_t H, torch::Tensor dst) {
@@ -140,6 +149,46 @@ void apply_penalties(torch::Tensor logits, torch::Tensor row_of, torch::Tensor t
                        static_cast<int>(n), cur_stream());
 }
 
+void ar_add_rmsnorm(std::vector<int64_t> data, std::vector<int64_t> flags, torch::Tensor epochs, int64_t rank,
+                    int64_t T, int64_t H, int64_t nsplit, int64_t split_stride, torch::Tensor resid, torch::Tensor w,
+                    double eps, torch::Tensor out, torch::Tensor err, int64_t max_ctas) {
+  vmc::ArArgs a;
+  TORCH_CHECK(data.size() == flags.size() && !data.empty() && data.size() <= 8, "ar_add_rmsnorm: bad peer lists");
+  for (size_t i = 0; i < 8; ++i) {
+    a.data[i] = i < data.size() ? reinterpret_cast<const float*>(data[i]) : nullptr;
+    a.flags[i] = i < flags.size() ? reinterpret_cast<uint32_t*>(flags[i]) : nullptr;
+  }
+  a.epochs = ptr<uint32_t>(epochs);
+  a.nranks = static_cast<int>(data.size());
+  a.rank = static_cast<int>(rank);
+  a.T = static_cast<int>(T);
+  a.H = static_cast<int>(H);
+  a.nsplit = static_cast<int>(nsplit);
+  a.split_stride = split_stride;
+  a.resid = ptr<float>(resid);
+  a.w = ptr<float>(w);
+  a.eps = static_cast<float>(eps);
+  a.out = out.data_ptr();
+  a.err = ptr<uint32_t>(err);
+  vmc::ar_add_rmsnorm(a, static_cast<int>(max_ctas), cur_stream());
+}
+
+py::tuple sym_alloc(int64_t bytes) {
+  char h[64];
+  uint64_t p = vmc::sym_alloc(static_cast<size_t>(bytes), h);
+  return py::make_tuple(static_cast<int64_t>(p), py::bytes(h, 64));
+}
+int64_t sym_open(py::bytes handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == 64, "sym_open: handle must be 64 bytes");
+  return static_cast<int64_t>(vmc::sym_open(s.data()));
+}
+// A torch view over raw device memory owned elsewhere (symmetric buffers).
+torch::Tensor wrap_ptr(int64_t p, std::vector<int64_t> sizes, int dtype, int device) {
+  auto opts = torch::TensorOptions().dtype(static_cast<c10::ScalarType>(dtype)).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(p), sizes, opts);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -163,8 +212,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("f32_to_bf16", &f32_to_bf16);
   m.def("sample", &sample);
   m.def("apply_penalties", &apply_penalties);
+  m.def("ar_add_rmsnorm", &ar_add_rmsnorm);
+  m.def("sym_alloc", &sym_alloc);
+  m.def("sym_open", &sym_open);
+  m.def("sym_close", [](int64_t p) { vmc::sym_close(static_cast<uint64_t>(p)); });
+  m.def("sym_free", [](int64_t p) { vmc::sym_free(static_cast<uint64_t>(p)); });
+  m.def("wrap_ptr", &wrap_ptr);
   m.attr("OUT_BF16") = static_cast<int>(vmc::kGemmOutBF16);
   m.attr("OUT_F32") = static_cast<int>(vmc::kGemmOutF32);
   m.attr("OUT_F32_ADD") = static_cast<int>(vmc::kGemmOutF32Add);
   m.attr("OUT_SWIGLU") = static_cast<int>(vmc::kGemmOutSwiGLU);
+  m.attr("OUT_F32_SPLIT") = static_cast<int>(vmc::kGemmOutF32Split);
 }

@@ -144,6 +144,8 @@ __device__ uint32_t radix_kth_largest(const float* x, int V, int k, uint32_t* hi
 __global__ void __launch_bounds__(kThreads) sample_kernel(const float* __restrict__ logits, int V, int64_t ld,
                                                           const SampleParams* __restrict__ params,
                                                           int32_t* __restrict__ out_tok, float* __restrict__ out_lp) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const float* x = logits + row * ld;
   const SampleParams sp = params[row];
@@ -273,6 +275,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const float* __restric
 __global__ void penalties_kernel(float* __restrict__ logits, int64_t ld, const int32_t* __restrict__ row_of,
                                  const int32_t* __restrict__ tok, const int32_t* __restrict__ out_count,
                                  const SampleParams* __restrict__ params, int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int r = row_of[i];
@@ -290,15 +294,13 @@ __global__ void penalties_kernel(float* __restrict__ logits, int64_t ld, const i
 void sample(const float* logits, int S, int V, int64_t ld, const SampleParams* params, int32_t* out_tok, float* out_lp,
             cudaStream_t st) {
   if (S <= 0) return;
-  sample_kernel<<<S, kThreads, 0, st>>>(logits, V, ld, params, out_tok, out_lp);
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(sample_kernel, dim3(S), dim3(kThreads), 0, st, logits, V, ld, params, out_tok, out_lp);
 }
 
 void apply_penalties(float* logits, int64_t ld, const int32_t* row_of, const int32_t* tok, const int32_t* out_count,
                      const SampleParams* params, int n, cudaStream_t st) {
   if (n <= 0) return;
-  penalties_kernel<<<(n + 255) / 256, 256, 0, st>>>(logits, ld, row_of, tok, out_count, params, n);
-  VMC_CUDA_CHECK(cudaGetLastError());
+  launch_k(penalties_kernel, dim3((n + 255) / 256), dim3(256), 0, st, logits, ld, row_of, tok, out_count, params, n);
 }
 
 }  // namespace vmc

@@ -104,3 +104,29 @@ def test_gpu_quantizers_match_host(host, cuda_ext):
         ref = host.quantize(int(gt), x.numpy())
         diff = (dev != ref).mean()
         assert diff < 1e-3, (gt, diff)
+
+
+@pytest.mark.parametrize("gtype", [GType.Q4_K, GType.Q8_0, GType.BF16])
+@pytest.mark.parametrize("M", [1, 64])
+def test_gemm_split_partials(host, cuda_ext, gtype, M):
+    # per-split fp32 partials (no atomics): their sum equals the full product
+    N, K, S = 640, 2048, 3
+    tw, raw = _make(host, gtype, N, K, seed=7)
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    out = torch.full((S, M, N), float("nan"), dtype=torch.float32, device="cuda")
+    ops.gemm(x, tw, out[0], M, ops.OUT_F32_SPLIT, S, split_stride=M * N)
+    torch.cuda.synchronize()
+    ref = _ref(x, host, gtype, raw, N, K)
+    assert (out.sum(0) - ref).abs().max().item() <= 0.01 * ref.abs().max().item() + 1e-3
+
+
+def test_gemm_many_units_persistent(host, cuda_ext):
+    # more work units than SMs: every CTA walks several units with the double-buffered accumulator
+    N, K, M = 128 * 200, 512, 300
+    tw, raw = _make(host, GType.Q4_K, N, K, seed=9)
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, tw, out, M, ops.OUT_BF16, 1)
+    torch.cuda.synchronize()
+    ref = _ref(x, host, GType.Q4_K, raw, N, K)
+    assert (out.float() - ref).abs().max().item() <= 0.02 * ref.abs().max().item() + 1e-3

@@ -9,6 +9,7 @@ reference frees one, engine.cpp:520-532), and sampling is seeded per request.
 """
 from __future__ import annotations
 
+import hashlib
 import itertools
 import threading
 import time
@@ -113,7 +114,9 @@ class LLMEngine:
             raise ValueError(f"prompt token id out of range [0, {V})")
         rid = request_id or f"req-{next(self._ids)}"
         req = Request(rid, list(prompt_token_ids), params, stream_callback=stream_callback, user_data=user_data)
-        req.seed = params.seed if params.seed is not None else (hash(rid) & 0x7fffffffffffffff)
+        # deterministic across processes (every tensor-parallel rank must draw the same samples)
+        req.seed = params.seed if params.seed is not None else \
+            int.from_bytes(hashlib.blake2b(rid.encode(), digest_size=8).digest(), "little") & 0x7fffffffffffffff
         with self._lock:
             self._pending.append(req)
         return req
@@ -243,7 +246,7 @@ class LLMEngine:
             req.output_logprobs.extend([lp_by_id.get(int(iid), 0.0)] * len(new_toks))
             req.token_times.extend([now] * len(new_toks))
             if finished:
-                self._finish(req, FinishReason(reason))
+                self._finish(req, FinishReason(reason), new_toks)
             elif req.stream_callback:
                 req.stream_callback(req, new_toks, False)
             outs.append(req.to_output() if (finished or req.stream_callback is None) else None)
@@ -254,7 +257,7 @@ class LLMEngine:
             self.on_step(plan, counts, dt)
         return [o for o in outs if o is not None]
 
-    def _finish(self, req: Request, reason: FinishReason) -> None:
+    def _finish(self, req: Request, reason: FinishReason, last_tokens: Optional[list[int]] = None) -> None:
         if req.finished:
             return
         req.finished = True
@@ -264,7 +267,7 @@ class LLMEngine:
         self.by_name.pop(req.request_id, None)
         self.metrics.record_finish(req)
         if req.stream_callback:
-            req.stream_callback(req, [], True)
+            req.stream_callback(req, list(last_tokens or []), True)
 
     def finish_request(self, request_id: str, reason: FinishReason = FinishReason.STOP) -> None:
         """Finish a running request from the host (e.g. a stop string matched by the detokenizer)."""

@@ -278,58 +278,88 @@ class LlamaModel:
             logits=torch.empty(S, self.v_local, dtype=torch.float32, device=dev),
         )
         self.qkv_bf16 = torch.empty(T, qkv_n, dtype=torch.bfloat16, device=dev)
+        self.o16 = torch.empty(T, self.H, dtype=torch.bfloat16, device=dev)
+        # Split-K partials: [splits][M][N] fp32, summed by the consumer kernel (no atomics, no memset).
+        self.qkv_n = qkv_n
+        self.split_ws = torch.empty(T * max(qkv_n, 2 * max(self.f_local, 1), self.H), dtype=torch.float32, device=dev)
         if attn_splits > 1:
             self.ws.part_o = torch.empty(attn_splits, max_samples, self.hq, self.D, dtype=torch.float32, device=dev)
             self.ws.part_lse = torch.empty(attn_splits, max_samples, self.hq, dtype=torch.float32, device=dev)
+        self.fused = self.tp > 1 and comm is not None and hasattr(comm, "allreduce_add_rmsnorm") and not cfg.is_moe
+        if self.fused:
+            comm.setup(max_tokens, self.H)
         self.moe_runner = None
         if cfg.is_moe:
             from .moe import MoERunner
             self.moe_runner = MoERunner(self, max_tokens)
 
-    # -- GEMM with the split-K policy: fp32 accumulate output when split --------------------------
-    def _linear(self, x: torch.Tensor, w: ops.TiledWeight, M: int, out32: torch.Tensor,
-                out16: torch.Tensor | None = None, col0: int = 0) -> tuple[torch.Tensor, bool]:
-        splits = ops.pick_splits(w, M)
-        if splits > 1 or out16 is None:
-            view = out32[:M, col0:col0 + w.N]
-            view.zero_() if splits > 1 else None
-            ops.gemm(x, w, view, M, ops.OUT_F32_ADD if splits > 1 else ops.OUT_F32, splits)
-            return out32, True
-        ops.gemm(x, w, out16[:M, col0:col0 + w.N], M, ops.OUT_BF16, 1)
-        return out16, False
+    # -- split-K policy ----------------------------------------------------------------------------
+    def _splits(self, w: ops.TiledWeight, M: int) -> int:
+        s = ops.pick_splits(w, M)
+        while s > 1 and s * M > self.max_tokens:
+            s -= 1
+        return ops.effective_splits(w, s)
 
-    def _qkv(self, lw: LayerWeights, x: torch.Tensor, M: int) -> tuple[torch.Tensor, bool]:
-        ws = self.ws
-        # All parts must land in the same dtype buffer: use fp32 if any part is split.
-        any_split = any(ops.pick_splits(w, M) > 1 for w in lw.wqkv)
-        if any_split:
-            ws.qkv[:M].zero_()
+    def _split_view(self, M: int, N: int) -> torch.Tensor:
+        return self.split_ws[:M * N].view(M, N)
+
+    def _qkv(self, lw: LayerWeights, x: torch.Tensor, M: int, m: StepMeta, kv_layer: torch.Tensor) -> None:
+        """QKV GEMM(s) + RoPE + paged KV store."""
+        s = self._splits(lw.wqkv[0], M)
+        if s > 1:
+            out = self._split_view(M, self.qkv_n)
             for w, c0 in zip(lw.wqkv, lw.qkv_split):
-                s = ops.pick_splits(w, M)
-                ops.gemm(x, w, ws.qkv[:M, c0:c0 + w.N], M, ops.OUT_F32_ADD, s)
-            return ws.qkv, True
+                ops.gemm(x, w, out[:, c0:c0 + w.N], M, ops.OUT_F32_SPLIT, s, split_stride=M * self.qkv_n)
+            ops.rope_store(out, M, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
+                           self.cfg.rope_neox, self.ws.q, kv_layer, nsplit=s, split_stride=M * self.qkv_n)
+            return
         for w, c0 in zip(lw.wqkv, lw.qkv_split):
             ops.gemm(x, w, self.qkv_bf16[:M, c0:c0 + w.N], M, ops.OUT_BF16, 1)
-        return self.qkv_bf16, False
+        ops.rope_store(self.qkv_bf16[:M], M, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
+                       self.cfg.rope_neox, self.ws.q, kv_layer)
 
-    def _mlp(self, lw: LayerWeights, M: int) -> tuple[torch.Tensor, bool]:
-        ws = self.ws
-        if lw.moe is not None:
-            return self.moe_runner.forward(lw.moe, ws.h, M)
-        w = lw.w_gate_up
-        s = ops.pick_splits(w, M)
+    def _row_parallel_norm(self, x: torch.Tensor, w: ops.TiledWeight, M: int, norm_w: torch.Tensor) -> None:
+        """Row-parallel GEMM, (TP reduce), residual add + RMSNorm into ws.h."""
+        ws, eps = self.ws, self.cfg.rms_eps
+        if self.tp > 1:
+            # NCCL baseline: one fp32 partial, all-reduced in place.
+            s = self._splits(w, M)
+            o = ws.o[:M]
+            if s > 1:
+                o.zero_()
+            ops.gemm(x, w, o, M, ops.OUT_F32_ADD if s > 1 else ops.OUT_F32, s)
+            self.comm.all_reduce(o)
+            ops.add_rmsnorm(ws.resid, norm_w, M, self.H, eps, out=ws.h, delta=o)
+            return
+        s = self._splits(w, M)
         if s > 1:
-            g = ws.gu32[:M, :w.N]
-            g.zero_()
-            ops.gemm(ws.h, w, g, M, ops.OUT_F32_ADD, s)
-            ops.swiglu(g, M, w.N // 2, ws.act, interleaved=True)
+            out = self._split_view(M, self.H)
+            ops.gemm(x, w, out, M, ops.OUT_F32_SPLIT, s, split_stride=M * self.H)
+            ops.add_rmsnorm(ws.resid, norm_w, M, self.H, eps, out=ws.h, delta=out, ndelta=s, delta_stride=M * self.H)
+        else:
+            ops.gemm(x, w, self.o16[:M], M, ops.OUT_BF16, 1)
+            ops.add_rmsnorm(ws.resid, norm_w, M, self.H, eps, out=ws.h, delta=self.o16[:M])
+
+    def _row_parallel_fused(self, site: int, x: torch.Tensor, w: ops.TiledWeight, M: int,
+                            norm_w: torch.Tensor) -> None:
+        """Row-parallel GEMM into this rank's symmetric partial buffer, then one kernel that
+        all-reduces over NVLink, adds the residual and applies the next RMSNorm."""
+        s = self._splits(w, M)
+        part = self.comm.partial(site).view(-1)[:s * M * self.H].view(s * M, self.H)
+        ops.gemm(x, w, part[:M], M, ops.OUT_F32_SPLIT if s > 1 else ops.OUT_F32, s, split_stride=M * self.H)
+        self.comm.allreduce_add_rmsnorm(site, M, self.ws.resid, norm_w, self.cfg.rms_eps, self.ws.h, nsplit=s,
+                                        split_stride=M * self.H)
+
+    def _gate_up(self, lw: LayerWeights, M: int) -> None:
+        ws = self.ws
+        w = lw.w_gate_up
+        s = self._splits(w, M)
+        if s > 1:
+            out = self._split_view(M, w.N)
+            ops.gemm(ws.h, w, out, M, ops.OUT_F32_SPLIT, s, split_stride=M * w.N)
+            ops.swiglu(out, M, w.N // 2, ws.act, interleaved=True, nsplit=s, split_stride=M * w.N)
         else:
             ops.gemm(ws.h, w, ws.act[:M], M, ops.OUT_SWIGLU, 1)
-        return self._linear(ws.act, lw.w_down, M, ws.down)
-
-    def _reduce(self, t: torch.Tensor, M: int) -> None:
-        if self.tp > 1:
-            self.comm.all_reduce(t[:M])
 
     def forward(self, kv_cache: torch.Tensor, m: StepMeta, params: torch.Tensor, out_tok: torch.Tensor,
                 out_lp: torch.Tensor | None = None, pre_sample=None) -> None:
@@ -340,17 +370,23 @@ class LlamaModel:
         layers = self.w.layers
         ops.add_rmsnorm(ws.resid, layers[0].attn_norm, T, self.H, cfg.rms_eps, out=ws.h)
         for li, lw in enumerate(layers):
-            qkv, _ = self._qkv(lw, ws.h, T)
-            ops.rope_store(qkv[:T], T, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
-                           cfg.rope_neox, ws.q, kv_cache[li])
+            self._qkv(lw, ws.h, T, m, kv_cache[li])
             self._attention(kv_cache[li], m)
-            o, o32 = self._linear(ws.attn, lw.wo, T, ws.o)
-            self._reduce(o, T)
-            ops.add_rmsnorm(ws.resid, lw.ffn_norm, T, self.H, cfg.rms_eps, out=ws.h, delta=o[:T])
-            d, _ = self._mlp(lw, T)
-            self._reduce(d, T)
             nxt = layers[li + 1].attn_norm if li + 1 < len(layers) else self.w.output_norm
-            ops.add_rmsnorm(ws.resid, nxt, T, self.H, cfg.rms_eps, out=ws.h, delta=d[:T])
+            if self.fused:
+                self._row_parallel_fused(0, ws.attn, lw.wo, T, lw.ffn_norm)
+                self._gate_up(lw, T)
+                self._row_parallel_fused(1, ws.act, lw.w_down, T, nxt)
+                continue
+            self._row_parallel_norm(ws.attn, lw.wo, T, lw.ffn_norm)
+            if lw.moe is not None:
+                d, _ = self.moe_runner.forward(lw.moe, ws.h, T)
+                if self.tp > 1:
+                    self.comm.all_reduce(d[:T])
+                ops.add_rmsnorm(ws.resid, nxt, T, self.H, cfg.rms_eps, out=ws.h, delta=d[:T])
+                continue
+            self._gate_up(lw, T)
+            self._row_parallel_norm(ws.act, lw.w_down, T, nxt)
         ops.gather_rows(ws.h, m.logits_idx, m.S, self.H, ws.hs)
         ops.gemm(ws.hs, self.w.lm_head, ws.logits[:m.S], m.S, ops.OUT_F32, 1)
         if pre_sample is not None:

@@ -16,7 +16,7 @@ from ..gguf.constants import GType
 
 # Tiled weight formats (csrc/kernels/weight_formats.cuh).
 WF_BF16, WF_Q4K, WF_Q6K, WF_Q8_0 = 0, 1, 2, 3
-OUT_BF16, OUT_F32, OUT_F32_ADD, OUT_SWIGLU = 0, 1, 2, 3
+OUT_BF16, OUT_F32, OUT_F32_ADD, OUT_SWIGLU, OUT_F32_SPLIT = 0, 1, 2, 3, 4
 NUM_SMS = 148
 
 _WF_FOR_GTYPE = {GType.Q4_K: WF_Q4K, GType.Q6_K: WF_Q6K, GType.Q8_0: WF_Q8_0,
@@ -74,20 +74,48 @@ def tile_weight(raw: torch.Tensor, gtype: int, N: int, K: int, wf: int | None = 
     return TiledWeight(wf, out, N, K)
 
 
-def pick_splits(w: TiledWeight, M: int, bn: int = 0, target_ctas: int = NUM_SMS) -> int:
-    bn = bn or C().gemm_pick_bn(M)
-    ctas = ((w.N + 127) // 128) * ((M + bn - 1) // bn)
-    if ctas >= target_ctas * 0.8 or w.chunks < 2:
+def pick_bn(M: int) -> int:
+    for b in (16, 32, 64, 128):
+        if M <= b:
+            return b
+    return 256
+
+
+def pick_splits(w: TiledWeight, M: int, bn: int = 0, sms: int = NUM_SMS, max_splits: int = 8) -> int:
+    """K splits for the persistent GEMM: minimise (weight bytes + partial-sum traffic) divided by the
+    SM-balance efficiency of the resulting work units. Multi-token-tile problems are not split."""
+    bn = bn or pick_bn(M)
+    m_tiles = (M + bn - 1) // bn
+    if m_tiles > 1 or w.chunks < 2:
         return 1
-    return max(1, min(w.chunks, math.ceil(target_ctas / ctas)))
+    base = (w.N + 127) // 128
+    wbytes = w.nbytes
+
+    def cost(s: int) -> float:
+        units = base * s
+        eff = units / (math.ceil(units / sms) * sms)
+        partial = (s * M * w.N * 8) if s > 1 else M * w.N * 2
+        return (wbytes + partial) / eff
+
+    best = min(range(1, min(max_splits, w.chunks) + 1), key=lambda s: (cost(s), s))
+    return effective_splits(w, best)
+
+
+def effective_splits(w: TiledWeight, s: int) -> int:
+    """The split count the kernel actually runs for `s` requested splits (each split covers
+    ceil(chunks / s) chunks, so trailing splits can vanish). Consumers must sum exactly this many."""
+    s = max(1, min(s, w.chunks))
+    per = (w.chunks + s - 1) // s
+    return (w.chunks + per - 1) // per
 
 
 def gemm(x: torch.Tensor, w: TiledWeight, out: torch.Tensor, M: int, mode: int = OUT_BF16, splits: int = 1,
-         bn: int = 0, err: torch.Tensor | None = None) -> torch.Tensor:
-    """out[:M] (=|+=) x[:M] @ W^T. mode OUT_F32_ADD requires a zeroed fp32 output."""
+         bn: int = 0, err: torch.Tensor | None = None, split_stride: int = 0) -> torch.Tensor:
+    """out[:M] (=|+=) x[:M] @ W^T. OUT_F32_ADD requires a zeroed fp32 output; OUT_F32_SPLIT writes
+    one fp32 partial per K split, `split_stride` elements apart (consumers sum them)."""
     if err is None:
         err = _err_word(x.device)
-    C().gemm(w.wf, w.data, w.N, w.K, x, M, out, mode, splits, bn, err)
+    C().gemm(w.wf, w.data, w.N, w.K, x, M, out, mode, splits, bn, err, split_stride)
     _count()
     return out
 
@@ -134,13 +162,13 @@ def add_rmsnorm(resid, w, T, H, eps, out=None, delta=None, ndelta=1, delta_strid
     _count()
 
 
-def rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv):
-    C().rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv)
+def rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv, nsplit=1, split_stride=0):
+    C().rope_store(qkv, nsplit, split_stride, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv)
     _count()
 
 
-def swiglu(gu, T, F, out, interleaved=False):
-    C().swiglu(gu, T, F, interleaved, out)
+def swiglu(gu, T, F, out, interleaved=False, nsplit=1, split_stride=0):
+    C().swiglu(gu, nsplit, split_stride, T, F, interleaved, out)
     _count()
 
 
