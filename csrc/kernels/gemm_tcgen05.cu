@@ -38,40 +38,53 @@ constexpr int kBWarp = 10;
 constexpr int kFirstEpiWarp = 11;
 
 struct GemmSmemPlan {
-  int stages = 0;      // A/B ring stages (64-K each)
+  int a_stages = 0;    // A (weights, bf16 swizzled) ring stages, 64-K each
+  int b_stages = 0;    // B (activations) ring stages, 64-K each
   int raw_stages = 0;  // raw quant tile stages (one chunk = 256-K each)
   int bn = 0;
   int wf = 0;
   __host__ __device__ constexpr int a_bytes() const { return 128 * 128; }
   __host__ __device__ constexpr int b_bytes() const { return bn * 128; }
   __host__ __device__ constexpr int raw_bytes() const { return wf == kWfBF16 ? 0 : wf_tile_bytes(wf); }
-  __host__ __device__ constexpr int off_b() const { return stages * a_bytes(); }
-  __host__ __device__ constexpr int off_raw() const { return off_b() + stages * b_bytes(); }
+  __host__ __device__ constexpr int off_b() const { return a_stages * a_bytes(); }
+  __host__ __device__ constexpr int off_raw() const { return off_b() + b_stages * b_bytes(); }
   __host__ __device__ constexpr int off_bar() const { return off_raw() + raw_stages * raw_bytes(); }
-  __host__ __device__ constexpr int nbars() const { return 2 * stages + 2 * raw_stages + 4; }
+  __host__ __device__ constexpr int nbars() const { return 2 * a_stages + 2 * b_stages + 2 * raw_stages + 4; }
   __host__ __device__ constexpr int total() const { return off_bar() + nbars() * 8 + 16 + 1024; }
 };
 
-// Shared-memory plan for one CTA per SM: at least 2 A/B stages and 2 raw stages, then grow the
-// raw ring (the weight stream) and the A/B ring alternately while the plan fits.
+// Shared-memory plan for one CTA per SM. The A and B rings are independent so that each can be as
+// deep as its producer's latency needs: the activation ring (TMA from L2) is made deep for
+// decode-sized tiles, the raw weight ring (HBM) next, and the dequantised A ring stays short
+// because its producer (the dequant warps) sits next to the consumer.
 __host__ __device__ constexpr GemmSmemPlan make_plan(int wf, int bn) {
   GemmSmemPlan p;
   p.bn = bn;
   p.wf = wf;
   const int budget = 222 * 1024;
-  p.stages = 2;
-  p.raw_stages = wf == kWfBF16 ? 0 : 2;
+  const bool quant = wf != kWfBF16;
+  p.b_stages = 2;
+  p.raw_stages = quant ? 2 : 0;
+  // Quantized formats fill A in whole chunks (4 stages); two chunks double-buffer when they fit.
+  p.a_stages = quant ? 8 : 2;
+  if (quant && p.total() > budget) p.a_stages = 4;
+  const int b_cap = bn <= 64 ? 16 : 6;
   bool grew = true;
   while (grew) {
     grew = false;
-    if (wf != kWfBF16 && p.raw_stages < 8) {
+    if (p.b_stages < b_cap) {
+      GemmSmemPlan q = p;
+      q.b_stages += 1;
+      if (q.total() <= budget) { p = q; grew = true; }
+    }
+    if (quant && p.raw_stages < 6) {
       GemmSmemPlan q = p;
       q.raw_stages += 1;
       if (q.total() <= budget) { p = q; grew = true; }
     }
-    if (p.stages < (wf == kWfBF16 ? 8 : 4)) {
+    if (!quant && p.a_stages < 8) {
       GemmSmemPlan q = p;
-      q.stages += 1;
+      q.a_stages += 1;
       if (q.total() <= budget) { p = q; grew = true; }
     }
   }
@@ -123,6 +136,49 @@ __device__ __forceinline__ void dq_q4k(const uint8_t* row, int s, int h, uint32_
   for (int i = 0; i < 8; ++i) {
     uint32_t p01 = ((w[i] >> sh0) & 0x000f000fu) | kMagic128x2;
     uint32_t p23 = ((w[i] >> sh1) & 0x000f000fu) | kMagic128x2;
+    o[2 * i] = bf2_fma(bf2_sub(p01, kMagic128x2), ds2, ndm2);
+    o[2 * i + 1] = bf2_fma(bf2_sub(p23, kMagic128x2), ds2, ndm2);
+  }
+}
+
+// Per-chunk Q4_K state of thread (row, half): bf16x2 scale and negated min of its four sub-blocks
+// j = 2s + h (s = 0..3), decoded once per 256-K chunk instead of once per 64-K substep.
+struct Q4KChunk {
+  uint32_t ds2[4], ndm2[4];
+};
+__device__ __forceinline__ void q4k_prep(const uint8_t* row, int h, Q4KChunk& c) {
+  const uint32_t dd = *reinterpret_cast<const uint32_t*>(row);
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu)));
+  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16)));
+  const uint32_t s0 = *reinterpret_cast<const uint32_t*>(row + 4);
+  const uint32_t s1 = *reinterpret_cast<const uint32_t*>(row + 8);
+  const uint32_t s2 = *reinterpret_cast<const uint32_t*>(row + 12);
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int j = 2 * s + h;
+    int scv, mv;
+    if (s < 2) {  // j < 4
+      scv = (s0 >> (8 * j)) & 63;
+      mv = (s1 >> (8 * j)) & 63;
+    } else {      // j >= 4
+      const int k = j - 4;
+      scv = ((s2 >> (8 * k)) & 0x0f) | (((s0 >> (8 * k + 6)) & 3) << 4);
+      mv = ((s2 >> (8 * k + 4)) & 0x0f) | (((s1 >> (8 * k + 6)) & 3) << 4);
+    }
+    c.ds2[s] = bf2_splat(d * static_cast<float>(scv));
+    c.ndm2[s] = bf2_splat(-dmin * static_cast<float>(mv));
+  }
+}
+__device__ __forceinline__ void q4k_sub(const uint8_t* row, int s, int h, const Q4KChunk& c, uint32_t (&o)[16]) {
+  const uint4* q = reinterpret_cast<const uint4*>(row + 16 + 32 * s);
+  const uint4 w0 = q[0], w1 = q[1];
+  const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const uint32_t ds2 = c.ds2[s], ndm2 = c.ndm2[s];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t lo = h ? (w[i] >> 4) : w[i];
+    const uint32_t p01 = (lo & 0x000f000fu) | kMagic128x2;
+    const uint32_t p23 = ((lo >> 8) & 0x000f000fu) | kMagic128x2;
     o[2 * i] = bf2_fma(bf2_sub(p01, kMagic128x2), ds2, ndm2);
     o[2 * i + 1] = bf2_fma(bf2_sub(p23, kMagic128x2), ds2, ndm2);
   }
@@ -192,7 +248,12 @@ struct GemmArgs {
   int64_t split_stride;   // elements between the per-split output slices (kGemmOutF32Split)
   int out_mode;           // GemmOut
   uint32_t* err;
+  unsigned long long* trace;  // optional per-role timestamps of CTA 0 (diagnostics), else null
 };
+
+__device__ __forceinline__ void trace_at(const GemmArgs& a, int slot) {
+  if (a.trace != nullptr && blockIdx.x == 0 && slot < 512) a.trace[slot] = clock64();
+}
 
 // Work unit u -> (n tile, m tile, split). m fastest: concurrently running CTAs share a weight tile,
 // so in prefill the tile is fetched from HBM once and re-read from L2 by the other token tiles.
@@ -212,8 +273,10 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
 
 template <int WF, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs args) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Align to 1024 B (128B-swizzle atoms) by offsetting the shared pointer itself: rounding through
+  // an integer would drop the shared address space and turn every ring access into a generic one.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr GemmSmemPlan P = make_plan(WF, BN);
   constexpr int SUBS = (WF == kWfBF16) ? 1 : 4;  // 64-K substeps per chunk
   constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
@@ -223,9 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint8_t* sB = smem + P.off_b();
   uint8_t* sRaw = smem + P.off_raw();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_bar());
-  uint64_t* ab_full = bars;
-  uint64_t* ab_empty = bars + P.stages;
-  uint64_t* raw_full = bars + 2 * P.stages;
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = a_full + P.a_stages;
+  uint64_t* b_full = a_empty + P.a_stages;
+  uint64_t* b_empty = b_full + P.b_stages;
+  uint64_t* raw_full = b_empty + P.b_stages;
   uint64_t* raw_empty = raw_full + P.raw_stages;
   uint64_t* acc_full = raw_empty + P.raw_stages;  // [2]
   uint64_t* acc_empty = acc_full + 2;             // [2]
@@ -237,9 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 
   pdl_trigger();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < P.stages; ++i) {
-      mbar_init(&ab_full[i], 1 + (quant ? kDequantWarps : 1));
-      mbar_init(&ab_empty[i], 1);
+    for (int i = 0; i < P.a_stages; ++i) {
+      mbar_init(&a_full[i], quant ? kDequantWarps : 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < P.b_stages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < P.raw_stages; ++i) {
       mbar_init(&raw_full[i], 1);
@@ -278,13 +347,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           if (quant) {
             if (!mbar_wait(&raw_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
             mbar_arrive_expect_tx(&raw_full[st], wf_tile_bytes(WF));
+            trace_at(args, 224 + (c - w.c0));
             bulk_load_evict_first(sRaw + st * P.raw_bytes(), wt, wf_tile_bytes(WF), &raw_full[st], pol);
             if (++st == P.raw_stages) { st = 0; ph ^= 1; }
           } else {
-            if (!mbar_wait(&ab_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-            mbar_arrive_expect_tx(&ab_full[st], P.a_bytes());
-            bulk_load_evict_first(sA + st * P.a_bytes(), wt, P.a_bytes(), &ab_full[st], pol);
-            if (++st == P.stages) { st = 0; ph ^= 1; }
+            if (!mbar_wait(&a_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&a_full[st], P.a_bytes());
+            bulk_load_evict_first(sA + st * P.a_bytes(), wt, P.a_bytes(), &a_full[st], pol);
+            if (++st == P.a_stages) { st = 0; ph ^= 1; }
           }
         }
       }
@@ -299,10 +369,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const Unit w = unit_of(args, u);
         for (int c = w.c0; c < w.c1; ++c) {
           for (int sub = 0; sub < SUBS; ++sub) {
-            if (!mbar_wait(&ab_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-            mbar_arrive_expect_tx(&ab_full[st], P.b_bytes());
-            tma_load_2d(sB + st * P.b_bytes(), &xmap, &ab_full[st], (c * SUBS + sub) * 64, w.mt * BN);
-            if (++st == P.stages) { st = 0; ph ^= 1; }
+            if (!mbar_wait(&b_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&b_full[st], P.b_bytes());
+            trace_at(args, 256 + (c - w.c0) * SUBS + sub);
+            tma_load_2d(sB + st * P.b_bytes(), &xmap, &b_full[st], (c * SUBS + sub) * 64, w.mt * BN);
+            if (++st == P.b_stages) { st = 0; ph ^= 1; }
           }
         }
       }
@@ -311,8 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
-      int st = 0;
-      uint32_t ph = 0;
+      int ast = 0, bst = 0;
+      uint32_t aph = 0, bph = 0;
       int acc = 0;
       uint32_t acc_ph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
@@ -322,14 +393,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const uint32_t d = tmem + static_cast<uint32_t>(acc) * kAccCols;
         const int total = (w.c1 - w.c0) * SUBS;
         for (int i = 0; i < total; ++i) {
-          if (!mbar_wait(&ab_full[st], ph, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+          if (!mbar_wait(&b_full[bst], bph, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+          trace_at(args, 64 + i);
+          if (!mbar_wait(&a_full[ast], aph, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+          trace_at(args, i);
           tc_fence_after();
-          const uint64_t a0 = umma_sdesc_sw128(smem_u32(sA + st * P.a_bytes()));
-          const uint64_t b0 = umma_sdesc_sw128(smem_u32(sB + st * P.b_bytes()));
+          const uint64_t a0 = umma_sdesc_sw128(smem_u32(sA + ast * P.a_bytes()));
+          const uint64_t b0 = umma_sdesc_sw128(smem_u32(sB + bst * P.b_bytes()));
 #pragma unroll
           for (int k = 0; k < 4; ++k) umma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&ab_empty[st]);
-          if (++st == P.stages) { st = 0; ph ^= 1; }
+          umma_commit(&a_empty[ast]);
+          umma_commit(&b_empty[bst]);
+          if (++ast == P.a_stages) { ast = 0; aph ^= 1; }
+          if (++bst == P.b_stages) { bst = 0; bph ^= 1; }
         }
         umma_commit(&acc_full[acc]);
         if (++acc == 2) { acc = 0; acc_ph ^= 1; }
@@ -337,9 +413,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   } else if (warp < kFirstDqWarp + kDequantWarps) {
     // ---------------- dequant (quantized formats) ----------------
-    if (quant) {
+    // Each warp owns 16 rows of the tile for a whole 256-K chunk (4 A stages): one proxy fence per
+    // chunk instead of one per 64-K stage keeps the fence latency off the per-stage critical path.
+    if constexpr (quant) {
+      static_assert(P.a_stages % 4 == 0, "quantized plans use whole chunks of A stages");
       const int t = threadIdx.x - kFirstDqWarp * 32;  // 0..255
       const int r = t >> 1, h = t & 1;
+      uint32_t sw_off[4];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) sw_off[cc] = sw128_offset(r, 4 * h + cc);
       int st = 0, rst = 0;
       uint32_t ph = 0, rph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
@@ -347,26 +429,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         bool ok = true;
         for (int c = w.c0; c < w.c1 && ok; ++c) {
           if (!mbar_wait(&raw_full[rst], rph, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+          if (warp == kFirstDqWarp && lane == 0) trace_at(args, 128 + (c - w.c0));
           const uint8_t* row = sRaw + rst * P.raw_bytes() + r * wf_row_bytes(WF);
+          // All four A stages of this chunk must be free (the MMA consumes them in order).
+#pragma unroll 1
           for (int sub = 0; sub < SUBS; ++sub) {
-            if (!mbar_wait(&ab_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+            if (!mbar_wait(&a_empty[st + sub], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+          }
+          if (!ok) break;
+          uint8_t* a0 = sA + st * P.a_bytes();
+          Q4KChunk qc;
+          if constexpr (WF == kWfQ4K) q4k_prep(row, h, qc);
+#pragma unroll
+          for (int sub = 0; sub < SUBS; ++sub) {
             uint32_t o[16];
-            if (WF == kWfQ4K) dq_q4k(row, sub, h, o);
-            else if (WF == kWfQ6K) dq_q6k(row, sub, h, o);
+            if constexpr (WF == kWfQ4K) q4k_sub(row, sub, h, qc, o);
+            else if constexpr (WF == kWfQ6K) dq_q6k(row, sub, h, o);
             else dq_q8_0(row, sub, h, o);
-            uint8_t* a = sA + st * P.a_bytes();
+            uint8_t* a = a0 + sub * P.a_bytes();
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-              *reinterpret_cast<uint4*>(a + sw128_offset(r, 4 * h + cc)) =
-                  make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
+              *reinterpret_cast<uint4*>(a + sw_off[cc]) = make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ab_full[st]);
-            if (++st == P.stages) { st = 0; ph ^= 1; }
           }
+          if (!ok) break;
+          if (warp == kFirstDqWarp && lane == 0) trace_at(args, 160 + (c - w.c0));
+          fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&raw_empty[rst]);
+          if (warp == kFirstDqWarp && lane == 0) trace_at(args, 192 + (c - w.c0));
+          if (lane == 0) {
+#pragma unroll
+            for (int sub = 0; sub < SUBS; ++sub) mbar_arrive(&a_full[st + sub]);
+            mbar_arrive(&raw_empty[rst]);
+          }
+          st += SUBS;
+          if (st == P.a_stages) { st = 0; ph ^= 1; }
           if (++rst == P.raw_stages) { rst = 0; rph ^= 1; }
         }
         if (!ok) break;
@@ -504,6 +601,9 @@ void make_act_tensor_map(CUtensorMap* map, const void* x, int M, int K, int ldx,
   VMC_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed for the activation map");
 }
 
+unsigned long long* g_gemm_trace = nullptr;
+void gemm_set_trace(unsigned long long* buf) { g_gemm_trace = buf; }
+
 int gemm_pick_bn(int M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
@@ -539,6 +639,7 @@ void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int 
   a.out_mode = out_mode;
   a.split_stride = split_stride;
   a.err = err;
+  a.trace = g_gemm_trace;
   CUtensorMap map;
   make_act_tensor_map(&map, x, M, K, ldx, bn);
   switch (wf) {

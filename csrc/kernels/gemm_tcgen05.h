@@ -20,6 +20,8 @@ enum GemmOut : int {
 void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
                   int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride = 0);
 int gemm_pick_bn(int M);
+// Diagnostics: when set, CTA 0 of every GEMM writes per-role clock64 stamps into buf[512].
+void gemm_set_trace(unsigned long long* buf);
 int gemm_smem_bytes(int wf, int bn);
 void make_act_tensor_map(CUtensorMap* map, const void* x, int M, int K, int ldx, int box_rows);
 

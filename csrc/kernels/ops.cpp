@@ -195,6 +195,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vm_c_b200 sm_100a kernels";
   m.def("gemm", &gemm);
   m.def("gemm_smem_bytes", &vmc::gemm_smem_bytes);
+  m.def("gemm_set_trace", [](c10::optional<torch::Tensor> t) {
+    vmc::gemm_set_trace(t.has_value() && t->defined() ? reinterpret_cast<unsigned long long*>(t->data_ptr()) : nullptr);
+  });
   m.def("gemm_pick_bn", &vmc::gemm_pick_bn);
   m.def("tiled_weight_bytes", &vmc::tiled_weight_bytes);
   m.def("repack_weight", &repack_weight);

@@ -40,11 +40,6 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   const uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
-__device__ __forceinline__ float key_to_float(uint32_t k) {
-  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
-  return __uint_as_float(u);
-}
-
 struct ArgMax {
   float v;
   int i;
@@ -84,21 +79,6 @@ __device__ float block_sum(float v, float* sh) {
   if (w == 0) {
     v = (threadIdx.x < nw) ? sh[threadIdx.x] : 0.f;
     v = warp_sum(v);
-    if (threadIdx.x == 0) sh[0] = v;
-  }
-  __syncthreads();
-  return sh[0];
-}
-
-__device__ float block_max(float v, float* sh) {
-  v = warp_max(v);
-  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) sh[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    v = (threadIdx.x < nw) ? sh[threadIdx.x] : -INFINITY;
-    v = warp_max(v);
     if (threadIdx.x == 0) sh[0] = v;
   }
   __syncthreads();
@@ -156,21 +136,43 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const float* __restric
   __shared__ int cand_i[kMaxCand];
   __shared__ int n_cand;
 
-  // Raw log-softmax normaliser (logprob of the chosen token is reported on the raw logits).
-  float lmax = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) lmax = fmaxf(lmax, x[i]);
-  lmax = block_max(lmax, sh_f);
-  float lsum = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) lsum += __expf(x[i] - lmax);
+  // One pass: running max / argmax and the rescaled sum of exponentials (online softmax), giving
+  // the raw log-softmax normaliser (the reported logprob) and the greedy choice together.
+  ArgMax best{-INFINITY, 0x7fffffff};
+  float run_sum = 0.f;
+  const bool vec = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  auto visit = [&](float v, int i) {
+    if (v == -INFINITY) return;
+    if (v > best.v) {
+      run_sum = run_sum * __expf(best.v - v) + 1.f;
+      best = ArgMax{v, i};
+    } else {
+      run_sum += __expf(v - best.v);
+      if (v == best.v && i < best.i) best.i = i;
+    }
+  };
+  if (vec) {
+    for (int i = threadIdx.x * 4; i < V; i += blockDim.x * 4) {
+      const float4 q = *reinterpret_cast<const float4*>(x + i);
+      visit(q.x, i);
+      visit(q.y, i + 1);
+      visit(q.z, i + 2);
+      visit(q.w, i + 3);
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) visit(x[i], i);
+  }
+  const float my_max = best.v;
+  const ArgMax am = block_argmax(best, sh_am);
+  const float lmax = am.v;
+  float lsum = (my_max == -INFINITY) ? 0.f : run_sum * __expf(my_max - lmax);
   lsum = block_sum(lsum, sh_f);
   const float log_z = lmax + __logf(lsum);
 
   const bool greedy = sp.temperature <= 0.f || sp.top_k == 1;
   int chosen;
   if (greedy) {
-    ArgMax a{-INFINITY, 0x7fffffff};
-    for (int i = threadIdx.x; i < V; i += blockDim.x) a = better(a, ArgMax{x[i], i});
-    chosen = block_argmax(a, sh_am).i;
+    chosen = am.i;
   } else {
     const float inv_t = 1.f / sp.temperature;
     const uint2 key = make_uint2(static_cast<uint32_t>(sp.seed), static_cast<uint32_t>(sp.seed >> 32));

@@ -1,0 +1,52 @@
+"""Tensor parallelism: TP=2 (NCCL baseline and fused peer-memory all-reduce) must produce the same
+greedy tokens as TP=1 on the same checkpoint. Needs >= 2 GPUs."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from vm_c_b200.core.sampling_params import SamplingParams
+from vm_c_b200.gguf.random_init import preset, write_random_gguf
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.fixture(scope="module")
+def tiny(tmp_path_factory):
+    p = tmp_path_factory.mktemp("tp") / "tiny.gguf"
+    write_random_gguf(str(p), preset("tiny-llama"), "Q8_0", seed=0)
+    return str(p)
+
+
+def run_tp(model, backend, tmp_path, n=2):
+    out = tmp_path / f"tp_{backend}.json"
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29631",
+           os.path.join(HERE, "tp_worker.py"), model, backend, str(out)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return json.load(open(out))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("backend", ["nccl", "fused"])
+def test_tp2_matches_tp1(tiny, tmp_path, backend):
+    from vm_c_b200.llm import LLM
+    llm = LLM(tiny, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256)
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
+    ref = [o.output_token_ids for o in llm.generate(prompts, SamplingParams.greedy_params(max_tokens=12,
+                                                                                          ignore_eos=True))]
+    llm.shutdown()
+    got = run_tp(tiny, backend, tmp_path)
+    assert got["err"] == 0
+    agree = sum(a == b for r, g in zip(ref, got["tokens"]) for a, b in zip(r, g))
+    total = sum(len(r) for r in ref)
+    # fp32 reduction order differs between TP=1 and TP=2: allow a late divergence only
+    assert agree >= 0.9 * total, (ref, got["tokens"])

@@ -1,0 +1,41 @@
+"""Worker for the tensor-parallel GPU test (launched by torch.distributed.run, one rank per GPU)."""
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from vm_c_b200.core.sampling_params import SamplingParams  # noqa: E402
+from vm_c_b200.llm import LLM  # noqa: E402
+from vm_c_b200.parallel.comm import NcclComm, init_distributed  # noqa: E402
+
+
+def main():
+    model, backend, out = sys.argv[1], sys.argv[2], sys.argv[3]
+    rank, world, local = init_distributed(timeout_s=60)
+    torch.cuda.set_device(local)
+    if backend == "fused":
+        from vm_c_b200.parallel.fused import FusedComm
+        comm = FusedComm()
+    else:
+        comm = NcclComm()
+    llm = LLM(model, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256,
+              tp_rank=rank, tp_size=world, comm=comm, device=f"cuda:{local}")
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
+    outs = llm.generate(prompts, SamplingParams.greedy_params(max_tokens=12, ignore_eos=True))
+    err = int(comm.device_error()) if hasattr(comm, "device_error") else 0
+    if rank == 0:
+        json.dump({"tokens": [o.output_token_ids for o in outs], "err": err}, open(out, "w"))
+    llm.shutdown()
+    if hasattr(comm, "close"):
+        comm.close()
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
