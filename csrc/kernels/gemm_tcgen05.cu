@@ -109,6 +109,29 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 __device__ __forceinline__ uint32_t bf2_splat(float f) { return pack_bf16x2(f, f); }
+// Single-instruction forms for the dequant inner loops. Measured on B200: the bit operations and
+// the packed bf16 ops each issue at 2 warp-instructions per cycle per SM, and the generic
+// __nv_bfloat162 helpers above cost the integer pipe extra instructions on this toolchain.
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t x, uint32_t m, uint32_t c) {  // (x & m) | c
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(m), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
 
 constexpr uint32_t kMagic128x2 = 0x43004300u;  // bf16 (128, 128); 128 + q is exact for q < 128
 
@@ -207,7 +230,7 @@ __device__ __forceinline__ void dq_q6k(const uint8_t* row, int s, int h, uint32_
       const int sh = 2 * k - 4;
       const uint32_t hb = (sh >= 0 ? (V >> sh) : (V << (-sh))) & 0x00300030u;
       const uint32_t x = nib[p] | hb | kMagic128x2;
-      o[4 * i + p] = bf2_mul(bf2_sub(x, kOff), scale);
+      o[4 * i + p] = bmul2(bsub2(x, kOff), scale);
     }
   }
 }
@@ -229,8 +252,8 @@ __device__ __forceinline__ void dq_q8_0(const uint8_t* row, int s, int h, uint32
     const uint32_t z01 = (x01 & 0x00800080u) | kMagic128x2;
     const uint32_t y23 = (x23 & 0x007f007fu) | kMagic128x2;
     const uint32_t z23 = (x23 & 0x00800080u) | kMagic128x2;
-    o[2 * i] = bf2_mul(bf2_sub(y01, z01), d2);
-    o[2 * i + 1] = bf2_mul(bf2_sub(y23, z23), d2);
+    o[2 * i] = bmul2(bsub2(y01, z01), d2);
+    o[2 * i + 1] = bmul2(bsub2(y23, z23), d2);
   }
 }
 
@@ -251,8 +274,34 @@ struct GemmArgs {
   unsigned long long* trace;  // optional per-role timestamps of CTA 0 (diagnostics), else null
 };
 
+// Per-role timestamps of CTA 0 and per-phase cycle totals for pipeline diagnostics; compiled in only
+// with -DVMC_GEMM_TRACE=1 (the default build has no timing code in the hot loops).
+#ifndef VMC_GEMM_TRACE
+#define VMC_GEMM_TRACE 0
+#endif
 __device__ __forceinline__ void trace_at(const GemmArgs& a, int slot) {
-  if (a.trace != nullptr && blockIdx.x == 0 && slot < 512) a.trace[slot] = clock64();
+  if constexpr (VMC_GEMM_TRACE != 0) {
+    if (a.trace != nullptr && blockIdx.x == 0 && slot < 512) a.trace[slot] = clock64();
+  }
+}
+struct PhaseClock {
+  long long t = 0;
+  __device__ __forceinline__ void start() {
+    if constexpr (VMC_GEMM_TRACE != 0) t = clock64();
+  }
+  __device__ __forceinline__ long long lap() {
+    if constexpr (VMC_GEMM_TRACE != 0) {
+      const long long n = clock64(), d = n - t;
+      t = n;
+      return d;
+    }
+    return 0;
+  }
+};
+__device__ __forceinline__ void phase_add(const GemmArgs& a, int slot, long long v) {
+  if constexpr (VMC_GEMM_TRACE != 0) {
+    if (a.trace != nullptr) atomicAdd(a.trace + 768 + slot, static_cast<unsigned long long>(v));
+  }
 }
 
 // Work unit u -> (n tile, m tile, split). m fastest: concurrently running CTAs share a weight tile,
@@ -533,6 +582,400 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------
+// Decode-width tiles (BN <= 64): dequantised A operand in TMEM, two independent substep groups.
+//
+// With both operands in shared memory every 256-K chunk moves ~230 KB through the SM's shared
+// memory (raw tile in and out, bf16 A written by the dequant warps and read by the MMA, activation
+// tile in and out), more than the chunk's HBM bytes take to arrive. Here the dequant warps write
+// the bf16 A operand straight into TMEM (tcgen05.st) and the MMA reads it from there
+// (tcgen05.mma with A in tensor memory), which removes the 128 KB of A traffic.
+//
+// Measured on B200: a 128xNx16 MMA with N <= 64 takes ~45 cycles, and each mbarrier wait or
+// commit in an issuing thread's loop stalls its issue stream for about as long, so a pipeline in
+// which one MMA thread waits for all dequant warps (and they for it) leaves the tensor pipe idle.
+// The 16 dequant warps therefore form two groups; group G owns K substeps 2G and 2G+1 (128 K) of
+// every chunk, writes them into its own TMEM A slots (three, so the dequant runs up to two chunks
+// ahead of the MMA) and has its own MMA-issuing warp accumulating into its own TMEM accumulator;
+// the epilogue adds the two. One group's handshakes overlap the other group's MMAs.
+// TMEM: accumulators [0, 128), A slots [128, 512) (64 columns = 128 K each).
+//
+// Warp roles in a 768-thread CTA:
+//   warp 0       weight producer (raw ring, one cp.async.bulk per tile) and TMEM allocation
+//   warp 1       activation producer (one chunk-wide stage = 4 TMA boxes)
+//   warps 2, 3   MMA issuers of groups 0, 1
+//   warps 4-19   dequant: group (w - 4) / 8, substep 2 * group + ((w - 4) / 4) % 2, lane quarter w % 4
+//   warps 20-23  epilogue (lane quarter w % 4)
+
+constexpr int kDThreads = 768;
+constexpr int kDFirstDq = 4;
+constexpr int kDFirstEpi = 20;
+constexpr int kDSlots = 3;
+constexpr uint32_t kDACol = 128;
+
+// Q4_K scale / negated min of sub-block J (bf16x2 splats) from the 16-byte block header (fp16 d,
+// fp16 dmin, 12 bytes of packed 6-bit scales and mins); J is a compile-time constant so the
+// bit-field offsets fold.
+template <int J>
+__device__ __forceinline__ void q4k_scale_c(const uint4& hdr, uint32_t& ds2, uint32_t& ndm2) {
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x & 0xffffu)));
+  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x >> 16)));
+  uint32_t scv, mv;
+  if constexpr (J < 4) {
+    scv = (hdr.y >> (8 * J)) & 63u;
+    mv = (hdr.z >> (8 * J)) & 63u;
+  } else {
+    constexpr int k = J - 4;
+    scv = ((hdr.w >> (8 * k)) & 0x0fu) | (((hdr.y >> (8 * k + 6)) & 3u) << 4);
+    mv = ((hdr.w >> (8 * k + 4)) & 0x0fu) | (((hdr.z >> (8 * k + 6)) & 3u) << 4);
+  }
+  ds2 = bf2_splat(d * static_cast<float>(scv));
+  ndm2 = bf2_splat(-dmin * static_cast<float>(mv));
+}
+
+// 64 K-values of substep S of one Q4_K row: o[0..15] = sub-block 2S, o[16..31] = sub-block 2S + 1
+// (bf16 pairs in K order). Per 8 values: 3 shifts + 4 lop3 on the integer pipe, 4 sub + 4 fma.
+template <int S>
+__device__ __forceinline__ void q4k_row64(const uint8_t* row, uint32_t (&o)[32]) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(row);
+  uint32_t ds_lo, dm_lo, ds_hi, dm_hi;
+  q4k_scale_c<2 * S>(hdr, ds_lo, dm_lo);
+  q4k_scale_c<2 * S + 1>(hdr, ds_hi, dm_hi);
+  const uint4* q = reinterpret_cast<const uint4*>(row + 16 + 32 * S);
+  const uint4 w0 = q[0], w1 = q[1];
+  const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t a = lop_and_or(w[i], 0x000f000fu, kMagic128x2);
+    const uint32_t b = lop_and_or(w[i] >> 8, 0x000f000fu, kMagic128x2);
+    const uint32_t c = lop_and_or(w[i] >> 4, 0x000f000fu, kMagic128x2);
+    const uint32_t e = lop_and_or(w[i] >> 12, 0x000f000fu, kMagic128x2);
+    o[2 * i] = bfma2(bsub2(a, kMagic128x2), ds_lo, dm_lo);
+    o[2 * i + 1] = bfma2(bsub2(b, kMagic128x2), ds_lo, dm_lo);
+    o[16 + 2 * i] = bfma2(bsub2(c, kMagic128x2), ds_hi, dm_hi);
+    o[16 + 2 * i + 1] = bfma2(bsub2(e, kMagic128x2), ds_hi, dm_hi);
+  }
+}
+
+// 64 K-values of substep s (0..3, warp-uniform) of one row of a quantized tile.
+template <int WF>
+__device__ __forceinline__ void dq_row64(const uint8_t* row, int s, uint32_t (&o)[32]) {
+  if constexpr (WF == kWfQ4K) {
+    switch (s) {
+      case 0: q4k_row64<0>(row, o); break;
+      case 1: q4k_row64<1>(row, o); break;
+      case 2: q4k_row64<2>(row, o); break;
+      default: q4k_row64<3>(row, o); break;
+    }
+  } else {
+    uint32_t (&lo)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[0]);
+    uint32_t (&hi)[16] = *reinterpret_cast<uint32_t(*)[16]>(&o[16]);
+    if constexpr (WF == kWfQ6K) {
+      dq_q6k(row, s, 0, lo);
+      dq_q6k(row, s, 1, hi);
+    } else {
+      dq_q8_0(row, s, 0, lo);
+      dq_q8_0(row, s, 1, hi);
+    }
+  }
+}
+
+struct GemmDPlan {
+  int b_stages = 0;
+  int raw_stages = 0;
+  int bn = 0;
+  int wf = 0;
+  __host__ __device__ constexpr int b_box() const { return bn * 128; }
+  __host__ __device__ constexpr int b_bytes() const { return 4 * b_box(); }
+  __host__ __device__ constexpr int raw_bytes() const { return wf_tile_bytes(wf); }
+  __host__ __device__ constexpr int off_raw() const { return b_stages * b_bytes(); }
+  __host__ __device__ constexpr int off_bar() const { return off_raw() + raw_stages * raw_bytes(); }
+  // a_full[6], slot_free[6], acc_full[2], acc_empty, b_full/b_empty, raw_full/raw_empty
+  __host__ __device__ constexpr int nbars() const { return 15 + 2 * b_stages + 2 * raw_stages; }
+  __host__ __device__ constexpr int total() const { return off_bar() + nbars() * 8 + 16 + 1024; }
+};
+
+// Activation stages first (a chunk-wide stage is read by both groups, which may be a chunk apart),
+// then raw weight stages for HBM latency.
+__host__ __device__ constexpr GemmDPlan make_dplan(int wf, int bn) {
+  GemmDPlan p;
+  p.bn = bn;
+  p.wf = wf;
+  const int budget = 222 * 1024;
+  p.b_stages = 2;
+  p.raw_stages = 2;
+  while (p.b_stages < 4) {
+    GemmDPlan q = p;
+    q.b_stages += 1;
+    if (q.total() > budget) break;
+    p = q;
+  }
+  while (p.raw_stages < 8) {
+    GemmDPlan q = p;
+    q.raw_stages += 1;
+    if (q.total() > budget) break;
+    p = q;
+  }
+  return p;
+}
+
+template <int WF, int BN>
+__global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs args) {
+  static_assert(BN <= 64, "decode-width kernel");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr GemmDPlan P = make_dplan(WF, BN);
+  constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
+  static_assert(2 * kAccCols <= kDACol && kDACol + 2 * kDSlots * 64 <= 512, "TMEM plan");
+  uint8_t* sB = smem;
+  uint8_t* sRaw = smem + P.off_raw();
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_bar());
+  uint64_t* a_full = bars;                       // [group * kDSlots + slot], 8 dequant-warp arrivals
+  uint64_t* slot_free = a_full + 2 * kDSlots;    // [group * kDSlots + slot], MMA commit
+  uint64_t* acc_full = slot_free + 2 * kDSlots;  // [group], MMA commit at the end of a unit
+  uint64_t* acc_empty = acc_full + 2;            // 4 epilogue-warp arrivals
+  uint64_t* b_full = acc_empty + 1;
+  uint64_t* b_empty = b_full + P.b_stages;       // one commit per group
+  uint64_t* raw_full = b_empty + P.b_stages;
+  uint64_t* raw_empty = raw_full + P.raw_stages;  // 16 dequant-warp arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw_empty + P.raw_stages);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2 * kDSlots; ++i) {
+      mbar_init(&a_full[i], 8);
+      mbar_init(&slot_free[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) mbar_init(&acc_full[i], 1);
+    mbar_init(acc_empty, 4);
+    for (int i = 0; i < P.b_stages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 2);
+    }
+    for (int i = 0; i < P.raw_stages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 16);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int first = blockIdx.x, step = gridDim.x;
+
+  if (warp == 0) {
+    // ---------------- weight producer (weights are constant: starts before the PDL wait) -------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int st = 0;
+      uint32_t ph = 0;
+      for (int u = first; u < args.units && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        const uint8_t* wbase = args.w + static_cast<size_t>(w.nt) * args.KC * wf_tile_bytes(WF);
+        for (int c = w.c0; c < w.c1; ++c) {
+          if (!mbar_wait(&raw_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+          mbar_arrive_expect_tx(&raw_full[st], wf_tile_bytes(WF));
+          bulk_load_evict_first(sRaw + st * P.raw_bytes(), wbase + static_cast<size_t>(c) * wf_tile_bytes(WF),
+                                wf_tile_bytes(WF), &raw_full[st], pol);
+          if (++st == P.raw_stages) { st = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- activation producer ----------------
+    if (lane == 0) {
+      pdl_wait();
+      int st = 0;
+      uint32_t ph = 0;
+      for (int u = first; u < args.units && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        for (int c = w.c0; c < w.c1; ++c) {
+          if (!mbar_wait(&b_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
+          mbar_arrive_expect_tx(&b_full[st], P.b_bytes());
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            tma_load_2d(sB + st * P.b_bytes() + i * P.b_box(), &xmap, &b_full[st], (c * 4 + i) * 64, w.mt * BN);
+          if (++st == P.b_stages) { st = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ---------------- MMA issuer of group G ----------------
+    if (lane == 0) {
+      const int G = warp - 2;
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+      const uint32_t d = tmem + static_cast<uint32_t>(G) * kAccCols;
+      int g = 0;  // CTA-wide chunk counter
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      PhaseClock pc;
+      long long ph_acc = 0, ph_a = 0, ph_b = 0, ph_mma = 0;
+      pc.start();
+      for (int u = first; u < args.units && ok && !*abort_flag; u += step) {
+        const Unit w = unit_of(args, u);
+        if (!mbar_wait(acc_empty, acc_ph ^ 1, args.err, kErrGemmWait)) { ok = false; break; }
+        ph_acc += pc.lap();
+        tc_fence_after();
+        for (int c = w.c0; c < w.c1; ++c, ++g) {
+          const int k = g % kDSlots;
+          const int bst = g % P.b_stages;
+          ph_mma += pc.lap();
+          if (!mbar_wait(&a_full[G * kDSlots + k], (g / kDSlots) & 1, args.err, kErrGemmWait)) { ok = false; break; }
+          ph_a += pc.lap();
+          if (!mbar_wait(&b_full[bst], (g / P.b_stages) & 1, args.err, kErrGemmWait)) { ok = false; break; }
+          ph_b += pc.lap();
+          tc_fence_after();
+          const uint32_t a0 = tmem + kDACol + static_cast<uint32_t>(G * kDSlots + k) * 64;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t b0 = umma_sdesc_sw128(smem_u32(sB + bst * P.b_bytes() + (2 * G + h) * P.b_box()));
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              umma_bf16_ts(d, a0 + h * 32 + 8 * k4, b0 + 2 * k4, idesc, (c > w.c0 || h > 0 || k4 > 0) ? 1u : 0u);
+          }
+          umma_commit(&slot_free[G * kDSlots + k]);
+          umma_commit(&b_empty[bst]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[G]);
+        acc_ph ^= 1;
+      }
+      if (!ok) *abort_flag = 1;
+      ph_mma += pc.lap();
+      phase_add(args, 8, ph_acc);
+      phase_add(args, 9, ph_a);
+      phase_add(args, 10, ph_b);
+      phase_add(args, 11, ph_mma);
+      phase_add(args, 12, g);
+    }
+  } else if (warp >= kDFirstDq && warp < kDFirstEpi) {
+    // ---------------- dequant -> TMEM ----------------
+    const int q = warp & 3;
+    const int G = (warp - kDFirstDq) >> 3;
+    const int h = ((warp - kDFirstDq) >> 2) & 1;
+    const int s = 2 * G + h;  // K substep of this warp
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+    int rst = 0;
+    uint32_t rph = 0;
+    int g = 0;
+    PhaseClock pc;
+    long long ph_raw = 0, ph_dq = 0, ph_slot = 0, ph_st = 0, ph_rest = 0;
+    pc.start();
+    for (int u = first; u < args.units && !*abort_flag; u += step) {
+      const Unit w = unit_of(args, u);
+      bool ok = true;
+      for (int c = w.c0; c < w.c1; ++c, ++g) {
+        ph_rest += pc.lap();
+        if (!mbar_wait(&raw_full[rst], rph, args.err, kErrGemmWait)) { ok = false; break; }
+        ph_raw += pc.lap();
+        const uint8_t* row = sRaw + rst * P.raw_bytes() + (32 * q + lane) * wf_row_bytes(WF);
+        uint32_t o[32];
+        dq_row64<WF>(row, s, o);
+        __syncwarp();
+        ph_dq += pc.lap();
+        if (lane == 0) mbar_arrive(&raw_empty[rst]);
+        const int k = g % kDSlots;
+        if (!mbar_wait(&slot_free[G * kDSlots + k], ((g / kDSlots) & 1) ^ 1, args.err, kErrGemmWait)) { ok = false; break; }
+        ph_slot += pc.lap();
+        tc_fence_after();
+        const uint32_t ta = tmem + lane_base + kDACol + static_cast<uint32_t>(G * kDSlots + k) * 64 + h * 32;
+        tmem_st16(ta, o);
+        tmem_st16(ta + 16, o + 16);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        ph_st += pc.lap();
+        if (lane == 0) mbar_arrive(&a_full[G * kDSlots + k]);
+        if (++rst == P.raw_stages) { rst = 0; rph ^= 1; }
+      }
+      if (!ok) { *abort_flag = 1; break; }
+    }
+    if (lane == 0) {
+      phase_add(args, 0, ph_raw);
+      phase_add(args, 1, ph_dq);
+      phase_add(args, 2, ph_slot);
+      phase_add(args, 3, ph_st);
+      phase_add(args, 4, ph_rest);
+      phase_add(args, 5, g);
+    }
+  } else if (warp >= kDFirstEpi && warp < kDFirstEpi + 4) {
+    // ---------------- epilogue: sum of the two group accumulators ----------------
+    pdl_wait();  // outputs may still be read by the previous kernel
+    const int q = warp & 3;
+    const int n_local = 32 * q + lane;
+    uint32_t acc_ph = 0;
+    for (int u = first; u < args.units && !*abort_flag; u += step) {
+      const Unit w = unit_of(args, u);
+      const bool ok = mbar_wait(&acc_full[0], acc_ph, args.err, kErrGemmWait) &&
+                      mbar_wait(&acc_full[1], acc_ph, args.err, kErrGemmWait);
+      if (!ok) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const uint32_t d = tmem + (static_cast<uint32_t>(32 * q) << 16);
+      float* outf = reinterpret_cast<float*>(args.out);
+      if (args.out_mode == kGemmOutF32Split) outf += w.split * args.split_stride;
+#pragma unroll 1
+      for (int cb = 0; cb < BN; cb += 16) {
+        uint32_t v[16], t[16];
+        tmem_ld16(d + static_cast<uint32_t>(cb), v);
+        tmem_ld16(d + kAccCols + static_cast<uint32_t>(cb), t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
+        const int m_base = w.mt * BN + cb;
+        if (args.out_mode == kGemmOutSwiGLU) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float mine = __uint_as_float(v[j]);
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            const int m = m_base + j;
+            if ((lane & 1) == 0 && m < args.M) {
+              const float y = mine / (1.f + __expf(-mine)) * other;
+              const int f = w.nt * 64 + (n_local >> 1);
+              if (f < args.N / 2)
+                reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
+            }
+          }
+        } else {
+          const int nn = w.nt * 128 + n_local;
+          if (nn < args.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = m_base + j;
+              if (m < args.M) {
+                const float y = __uint_as_float(v[j]);
+                const size_t idx = static_cast<size_t>(m) * args.ldo + nn;
+                if (args.out_mode == kGemmOutF32Add) atomicAdd(outf + idx, y);
+                else if (args.out_mode == kGemmOutBF16) reinterpret_cast<__nv_bfloat16*>(args.out)[idx] = __float2bfloat16(y);
+                else outf[idx] = y;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      acc_ph ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -574,14 +1017,38 @@ void launch(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   launch_k(gemm_kernel<WF, BN>, dim3(grid), dim3(kThreads), P.total(), st, map, a);
 }
 
+template <int WF, int BN>
+void launch_qd(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+  constexpr GemmDPlan P = make_dplan(WF, BN);
+  static_assert(P.total() <= 227 * 1024, "shared memory plan too large");
+  // More than half the SM's shared memory: no second CTA (and no second 512-column TMEM
+  // allocation) can be resident on the SM.
+  static_assert(P.total() > 114 * 1024, "the TMEM plan assumes one CTA per SM");
+  static bool configured = false;
+  if (!configured) {
+    VMC_CUDA_CHECK(cudaFuncSetAttribute(gemm_qd_kernel<WF, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, P.total()));
+    configured = true;
+  }
+  const int grid = a.units < num_sms() ? a.units : num_sms();
+  launch_k(gemm_qd_kernel<WF, BN>, dim3(grid), dim3(kDThreads), P.total(), st, map, a);
+}
+
+// Quantized weights with decode-width token tiles take the TMEM-A kernel; bf16 weights and wide
+// (prefill) tiles the shared-memory kernel.
+template <int WF, int BN>
+void launch_any(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+  if constexpr (WF != kWfBF16 && BN <= 64) launch_qd<WF, BN>(map, a, st);
+  else launch<WF, BN>(map, a, st);
+}
+
 template <int WF>
 void dispatch_bn(int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   switch (bn) {
-    case 16: launch<WF, 16>(map, a, st); break;
-    case 32: launch<WF, 32>(map, a, st); break;
-    case 64: launch<WF, 64>(map, a, st); break;
-    case 128: launch<WF, 128>(map, a, st); break;
-    case 256: launch<WF, 256>(map, a, st); break;
+    case 16: launch_any<WF, 16>(map, a, st); break;
+    case 32: launch_any<WF, 32>(map, a, st); break;
+    case 64: launch_any<WF, 64>(map, a, st); break;
+    case 128: launch_any<WF, 128>(map, a, st); break;
+    case 256: launch_any<WF, 256>(map, a, st); break;
     default: throw std::runtime_error("gemm: unsupported BN");
   }
 }
@@ -651,6 +1118,8 @@ void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int 
   }
 }
 
-int gemm_smem_bytes(int wf, int bn) { return make_plan(wf, bn).total(); }
+int gemm_smem_bytes(int wf, int bn) {
+  return (wf != kWfBF16 && bn <= 64) ? make_dplan(wf, bn).total() : make_plan(wf, bn).total();
+}
 
 }  // namespace vmc
