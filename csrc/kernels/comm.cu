@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
         uint2 o;
         o.x = pack_bf16x2(v[4 * j] * inv * w.x, v[4 * j + 1] * inv * w.y);
         o.y = pack_bf16x2(v[4 * j + 2] * inv * w.z, v[4 * j + 3] * inv * w.w);
-        *reinterpret_cast<uint2*>(a.out + base + 4 * vi) = o;
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out) + base + 4 * vi) = o;
       }
     }
   }
