@@ -1,0 +1,170 @@
+"""Kernel microbenchmarks at the shapes of the Llama-3-8B serving config (one GPU).
+
+    python -m vm_c_b200.ops.bench [case ...] [--reps N]
+
+Cases: gemm:<name> (decode / prefill projections of the 8B model, see GEMM_CASES), attn:decode,
+attn:prefill, norm, rope, swiglu, sample. Each case is timed with CUDA events on the current stream
+after warm-up, with a 256 MB buffer written between repetitions so that every repetition reads its
+inputs from HBM; the median is reported with the achieved bandwidth / FLOP rate. These are the
+cases the committed ncu summaries were captured on.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from . import (OUT_BF16, OUT_F32_SPLIT, OUT_SWIGLU, add_rmsnorm, device_error, effective_splits, gemm,
+               paged_attention, pick_splits, quantize_blocks, rope_store, sample, swiglu, tile_weight)
+from ..gguf.constants import GType
+
+# name: (weight type, N, K, tokens M, output mode)
+GEMM_CASES = {
+    "dec_qkv": (GType.Q4_K, 6144, 4096, 64, OUT_F32_SPLIT),
+    "dec_o": (GType.Q4_K, 4096, 4096, 64, OUT_F32_SPLIT),
+    "dec_gu": (GType.Q4_K, 28672, 4096, 64, OUT_SWIGLU),
+    "dec_down": (GType.Q4_K, 4096, 14336, 64, OUT_F32_SPLIT),
+    "dec_down6": (GType.Q6_K, 4096, 14336, 64, OUT_F32_SPLIT),
+    "dec_lm": (GType.Q6_K, 128256, 4096, 64, OUT_F32_SPLIT),
+    "dec1_gu": (GType.Q4_K, 28672, 4096, 1, OUT_SWIGLU),
+    "pre_qkv": (GType.Q4_K, 6144, 4096, 2048, OUT_BF16),
+    "pre_gu": (GType.Q4_K, 28672, 4096, 2048, OUT_SWIGLU),
+    "pre_bf16": (GType.BF16, 8192, 4096, 2048, OUT_BF16),
+}
+
+
+def _time(fn, reps: int, flush: torch.Tensor) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    return sorted(ts)[len(ts) // 2]
+
+
+def bench_gemm(name: str, reps: int, flush: torch.Tensor) -> str:
+    gt, N, K, M, mode = GEMM_CASES[name]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x32 = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    raw = x32.bfloat16() if gt == GType.BF16 else quantize_blocks(int(gt), x32)
+    del x32
+    w = tile_weight(raw, int(gt), N, K)
+    del raw
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    s = effective_splits(w, pick_splits(w, M)) if mode == OUT_F32_SPLIT else 1
+    if mode == OUT_SWIGLU:
+        out = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
+    elif mode == OUT_BF16:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    else:
+        out = torch.empty(s * M, N, dtype=torch.float32, device="cuda")
+    t = _time(lambda: gemm(x, w, out[:M] if mode == OUT_F32_SPLIT else out, M, mode, s, split_stride=M * N),
+              reps, flush)
+    return (f"gemm:{name:9s} M={M:5d} N={N:6d} K={K:6d} splits={s} {t:8.1f} us  weight bytes {w.nbytes / t / 1e6:5.2f} TB/s"
+            f"  {2 * M * N * K / t / 1e6:7.1f} TFLOP/s")
+
+
+def _paged_setup(ctx, qlen, Hq=32, Hkv=8, D=128, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    nblocks = sum((c + 15) // 16 for c in ctx) + 1
+    kv = (torch.randn(nblocks, 2, Hkv, 16, D, device="cuda", generator=g) * 0.5).bfloat16()
+    maxb = max((c + 15) // 16 for c in ctx)
+    bt = torch.zeros(len(ctx), maxb, dtype=torch.int32)
+    o = 1
+    for r, c in enumerate(ctx):
+        nb = (c + 15) // 16
+        bt[r, :nb] = torch.arange(o, o + nb, dtype=torch.int32)
+        o += nb
+    T = sum(qlen)
+    q = torch.randn(T, Hq, D, device="cuda", generator=g).bfloat16()
+    qs = torch.tensor([0] + list(torch.cumsum(torch.tensor(qlen), 0)), dtype=torch.int32, device="cuda")
+    return kv, bt.cuda(), q, qs, torch.tensor(ctx, dtype=torch.int32, device="cuda"), T
+
+
+def bench_attn(kind: str, reps: int, flush: torch.Tensor) -> str:
+    Hq, Hkv, D = 32, 8, 128
+    if kind == "decode":
+        ctx, ql = [1280] * 64, [1] * 64
+    else:
+        ctx, ql = [2048], [2048]
+    kv, bt, q, qs, cl, T = _paged_setup(ctx, ql, Hq, Hkv, D)
+    out = torch.empty_like(q)
+    dec = kind == "decode"
+    t = _time(lambda: paged_attention(q, kv, qs, cl, bt, len(ctx), 0, max(ql), T, Hq, Hkv, D, 1 / math.sqrt(D), dec,
+                                      out), reps, flush)
+    kv_bytes = sum(ctx) * Hkv * D * 2 * 2
+    flops = sum(4 * q_ * c * Hq * D for q_, c in zip(ql, ctx)) / (1 if dec else 2)
+    return (f"attn:{kind:7s} reqs={len(ctx)} ctx={ctx[0]} qlen={ql[0]} {t:8.1f} us  KV {kv_bytes / t / 1e6:5.2f} TB/s"
+            f"  {flops / t / 1e6:7.1f} TFLOP/s")
+
+
+def bench_small(kind: str, reps: int, flush: torch.Tensor) -> str:
+    T, H, F = 2048, 4096, 14336
+    dev = "cuda"
+    if kind == "norm":
+        resid = torch.randn(T, H, device=dev)
+        delta = torch.randn(T, H, device=dev)
+        w = torch.randn(H, device=dev)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        t = _time(lambda: add_rmsnorm(resid, w, T, H, 1e-5, out=out, delta=delta), reps, flush)
+        nbytes = T * H * (4 + 4 + 4 + 2)
+    elif kind == "swiglu":
+        gu = torch.randn(T, 2 * F, device=dev).bfloat16()
+        out = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+        t = _time(lambda: swiglu(gu, T, F, out, interleaved=True), reps, flush)
+        nbytes = T * F * 2 * 3
+    elif kind == "rope":
+        Hq, Hkv, D = 32, 8, 128
+        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev).bfloat16()
+        pos = torch.arange(T, dtype=torch.int32, device=dev)
+        slots = torch.arange(T, dtype=torch.int32, device=dev)
+        inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, dtype=torch.float64) / D))
+        ang = torch.arange(4096, dtype=torch.float64)[:, None] * inv[None, :]
+        cos_sin = torch.stack([ang.cos(), ang.sin()], -1).float().to(dev).contiguous()
+        q_out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
+        kv = torch.zeros(T // 16 + 1, 2, Hkv, 16, D, dtype=torch.bfloat16, device=dev)
+        t = _time(lambda: rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, False, q_out, kv), reps, flush)
+        nbytes = T * (Hq + 2 * Hkv) * D * 2 * 2
+    else:  # sample: greedy over a 128K vocabulary for 64 rows
+        from . import SAMPLE_PARAMS_DTYPE
+        import numpy as np
+        S, V = 64, 128256
+        logits = torch.randn(S, V, device=dev)
+        p = np.zeros(S, dtype=SAMPLE_PARAMS_DTYPE)
+        params = torch.from_numpy(p.view(np.uint8)).to(dev)
+        tok = torch.empty(S, dtype=torch.int32, device=dev)
+        t = _time(lambda: sample(logits, S, V, params, tok), reps, flush)
+        nbytes = S * V * 4
+    return f"{kind:12s} {t:8.1f} us  {nbytes / t / 1e6:5.2f} TB/s"
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("cases", nargs="*", default=["all"])
+    ap.add_argument("--reps", type=int, default=20)
+    a = ap.parse_args(argv)
+    cases = a.cases
+    if cases == ["all"]:
+        cases = [f"gemm:{k}" for k in GEMM_CASES] + ["attn:decode", "attn:prefill", "norm", "rope", "swiglu", "sample"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for c in cases:
+        if c.startswith("gemm:"):
+            line = bench_gemm(c[5:], a.reps, flush)
+        elif c.startswith("attn:"):
+            line = bench_attn(c[5:], a.reps, flush)
+        else:
+            line = bench_small(c, a.reps, flush)
+        print(line, flush=True)
+    print("device error word:", device_error())
+
+
+if __name__ == "__main__":
+    main()
