@@ -210,20 +210,28 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int tota
   auto sK = [&](int s) { return wsm + s * (2 * kBS * RB); };
   auto sV = [&](int s) { return wsm + s * (2 * kBS * RB) + kBS * RB; };
   const int64_t page_elems = static_cast<int64_t>(kBS) * D;
-  auto issue = [&](int b, int s) {
-    const int blk = bt[b];
+  // Block ids of this warp's pages (b0 + warp + 4j), 32 at a time in one coalesced load, so that a
+  // page's copy never waits on its own dependent block-table load.
+  int ids = 0;
+  auto fetch_ids = [&](int j0) {
+    const int bj = b0 + warp + 4 * (j0 + lane);
+    ids = bj < b1 ? bt[bj] : 0;
+  };
+  auto issue = [&](int j, int s) {  // j = index of the page among this warp's pages
+    if ((j & 31) == 0) fetch_ids(j);
+    const int blk = __shfl_sync(0xffffffffu, ids, j & 31);
     const __nv_bfloat16* kp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + kvh) * page_elems;
     const __nv_bfloat16* vp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + p.Hkv + kvh) * page_elems;
     load_page_warp<D>(sK(s), 0, kp, lane);
     load_page_warp<D>(sV(s), 0, vp, lane);
   };
   int b = b0 + warp;
-  int stage = 0;
-  if (b < b1) issue(b, 0);
+  int stage = 0, j = 0;
+  if (b < b1) issue(0, 0);
   cp_async_commit();
-  for (; b < b1; b += 4) {
+  for (; b < b1; b += 4, ++j) {
     const int nb = b + 4;
-    if (nb < b1) issue(nb, stage ^ 1);
+    if (nb < b1) issue(j + 1, stage ^ 1);
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
@@ -418,16 +426,35 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
 }
 
 template <int D>
-void launch_decode(const AttnParams& p, int num_reqs, int total_tokens, cudaStream_t st) {
+constexpr int decode_smem() {
   constexpr int RB = Frag<D>::RB;
-  const int smem_pipe = 4 * 2 * 2 * kBS * RB;
-  const int smem_merge = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
-  const int smem = smem_pipe > smem_merge ? smem_pipe : smem_merge;
+  constexpr int smem_pipe = 4 * 2 * 2 * kBS * RB;
+  constexpr int smem_merge = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
+  return smem_pipe > smem_merge ? smem_pipe : smem_merge;
+}
+
+template <int D>
+void config_decode() {
   static bool cfg = false;
   if (!cfg) {
-    VMC_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    VMC_CUDA_CHECK(
+        cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<D>()));
     cfg = true;
   }
+}
+
+template <int D>
+int decode_ctas_per_sm() {
+  config_decode<D>();
+  int n = 0;
+  VMC_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_kernel<D>, 128, decode_smem<D>()));
+  return n;
+}
+
+template <int D>
+void launch_decode(const AttnParams& p, int num_reqs, int total_tokens, cudaStream_t st) {
+  const int smem = decode_smem<D>();
+  config_decode<D>();
   dim3 grid(num_reqs, p.Hkv, p.splits);
   launch_k(attn_decode_kernel<D>, grid, dim3(128), smem, st, p, total_tokens);
   if (p.splits > 1) {
@@ -487,6 +514,15 @@ void paged_attention(const AttnLaunch& a, cudaStream_t st) {
       case 128: launch_prefill<128>(p, a.num_reqs, a.max_qlen, st); break;
       default: throw std::runtime_error("attention: unsupported head dim");
     }
+  }
+}
+
+int attn_decode_ctas_per_sm(int D) {
+  switch (D) {
+    case 32: return decode_ctas_per_sm<32>();
+    case 64: return decode_ctas_per_sm<64>();
+    case 128: return decode_ctas_per_sm<128>();
+    default: throw std::runtime_error("attention: unsupported head dim");
   }
 }
 

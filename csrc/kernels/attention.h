@@ -27,4 +27,7 @@ struct AttnLaunch {
 
 void paged_attention(const AttnLaunch& a, cudaStream_t st);
 
+// Resident decode CTAs per SM (occupancy of the decode kernel for head dim D).
+int attn_decode_ctas_per_sm(int D);
+
 }  // namespace vmc

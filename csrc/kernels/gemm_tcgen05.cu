@@ -272,6 +272,14 @@ struct GemmArgs {
   int out_mode;           // GemmOut
   uint32_t* err;
   unsigned long long* trace;  // optional per-role timestamps of CTA 0 (diagnostics), else null
+  int bn;                     // token tile width
+  // Grouped mode (groups > 0, e.g. MoE experts): group g owns rows [offset[g], offset[g] + count[g])
+  // of X and of the output (device arrays, read by the kernel) and the weight at w + g * w_stride.
+  // m_tiles is then the per-group tile bound; units past a group's count are skipped by every role.
+  int groups;
+  const int32_t* grp_count;
+  const int32_t* grp_offset;
+  int64_t grp_w_stride;  // bytes
 };
 
 // Per-role timestamps of CTA 0 and per-phase cycle totals for pipeline diagnostics; compiled in only
@@ -304,19 +312,44 @@ __device__ __forceinline__ void phase_add(const GemmArgs& a, int slot, long long
   }
 }
 
-// Work unit u -> (n tile, m tile, split). m fastest: concurrently running CTAs share a weight tile,
-// so in prefill the tile is fetched from HBM once and re-read from L2 by the other token tiles.
+// Work unit u -> (group, n tile, m tile, split). m fastest: concurrently running CTAs share a weight
+// tile, so in prefill the tile is fetched from HBM once and re-read from L2 by the other token
+// tiles. `rows` <= 0 marks a unit past the end of its group (grouped mode); every role skips it.
 struct Unit {
   int nt, mt, split, c0, c1;
+  int row0;     // first row of X / of the output covered by the tile
+  int rows;     // valid rows of the tile
+  size_t wtile; // byte offset of the unit's first weight tile (chunk 0)
 };
-__device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
+__device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u, int tile_bytes) {
   Unit r;
-  r.mt = u % a.m_tiles;
-  const int rest = u / a.m_tiles;
-  r.split = rest % a.splits;
-  r.nt = rest / a.splits;
+  int g = 0;
+  if (a.groups > 0) {
+    // Grouped: n fastest, then m, then group, so the (usually non-empty) first m tile of every
+    // group spreads over consecutive CTAs instead of landing on every m_tiles-th one.
+    r.nt = u % a.n_tiles;
+    const int rest = u / a.n_tiles;
+    r.mt = rest % a.m_tiles;
+    g = rest / a.m_tiles;
+    r.split = 0;
+  } else {
+    r.mt = u % a.m_tiles;
+    const int rest = u / a.m_tiles;
+    r.split = rest % a.splits;
+    r.nt = rest / a.splits;
+  }
   r.c0 = r.split * a.chunks_per_split;
   r.c1 = min(a.KC, r.c0 + a.chunks_per_split);
+  r.wtile = static_cast<size_t>(r.nt) * a.KC * tile_bytes;
+  if (a.groups > 0) {
+    const int cnt = a.grp_count[g];
+    r.row0 = a.grp_offset[g] + r.mt * a.bn;
+    r.rows = min(a.bn, cnt - r.mt * a.bn);
+    r.wtile += static_cast<size_t>(g) * a.grp_w_stride;
+  } else {
+    r.row0 = r.mt * a.bn;
+    r.rows = min(a.bn, a.M - r.row0);
+  }
   return r;
 }
 
@@ -379,6 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int first = blockIdx.x, step = gridDim.x;
+  // Grouped mode: the unit list depends on row counts written by the previous kernels, so every
+  // role (the weight producer included) waits for them before enumerating its units.
+  if (args.groups > 0) pdl_wait();
 
   if (warp == 0) {
     // ---------------- weight producer ----------------
@@ -389,8 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       int st = 0;
       uint32_t ph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
-        const uint8_t* wbase = args.w + static_cast<size_t>(w.nt) * args.KC * wf_tile_bytes(WF);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
+        const uint8_t* wbase = args.w + w.wtile;
         for (int c = w.c0; c < w.c1; ++c) {
           const uint8_t* wt = wbase + static_cast<size_t>(c) * wf_tile_bytes(WF);
           if (quant) {
@@ -415,13 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       int st = 0;
       uint32_t ph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
         for (int c = w.c0; c < w.c1; ++c) {
           for (int sub = 0; sub < SUBS; ++sub) {
             if (!mbar_wait(&b_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
             mbar_arrive_expect_tx(&b_full[st], P.b_bytes());
             trace_at(args, 256 + (c - w.c0) * SUBS + sub);
-            tma_load_2d(sB + st * P.b_bytes(), &xmap, &b_full[st], (c * SUBS + sub) * 64, w.mt * BN);
+            tma_load_2d(sB + st * P.b_bytes(), &xmap, &b_full[st], (c * SUBS + sub) * 64, w.row0);
             if (++st == P.b_stages) { st = 0; ph ^= 1; }
           }
         }
@@ -436,7 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       int acc = 0;
       uint32_t acc_ph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
         if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(acc) * kAccCols;
@@ -474,7 +513,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       int st = 0, rst = 0;
       uint32_t ph = 0, rph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
         bool ok = true;
         for (int c = w.c0; c < w.c1 && ok; ++c) {
           if (!mbar_wait(&raw_full[rst], rph, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
@@ -526,7 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int u = first; u < args.units && !*abort_flag; u += step) {
-      const Unit w = unit_of(args, u);
+      const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
       if (!mbar_wait(&acc_full[acc], acc_ph, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t d = tmem + static_cast<uint32_t>(acc) * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
@@ -536,14 +577,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         uint32_t v[16];
         tmem_ld16(d + static_cast<uint32_t>(cb), v);
         tmem_ld_wait();
-        const int m_base = w.mt * BN + cb;
+        const int m_base = w.row0 + cb;
+        const int m_end = w.row0 + w.rows;
         if (args.out_mode == kGemmOutSwiGLU) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float mine = __uint_as_float(v[j]);
             const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
             const int m = m_base + j;
-            if ((lane & 1) == 0 && m < args.M) {
+            if ((lane & 1) == 0 && m < m_end) {
               const float y = mine / (1.f + __expf(-mine)) * other;
               const int f = w.nt * 64 + (n_local >> 1);
               if (f < args.N / 2)
@@ -556,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = m_base + j;
-              if (m < args.M) {
+              if (m < m_end) {
                 const float y = __uint_as_float(v[j]);
                 const size_t idx = static_cast<size_t>(m) * args.ldo + n;
                 if (args.out_mode == kGemmOutF32Add) atomicAdd(outf + idx, y);
@@ -771,6 +813,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int first = blockIdx.x, step = gridDim.x;
+  // Grouped mode: the unit list depends on row counts written by the previous kernels, so every
+  // role (the weight producer included) waits for them before enumerating its units.
+  if (args.groups > 0) pdl_wait();
 
   if (warp == 0) {
     // ---------------- weight producer (weights are constant: starts before the PDL wait) -------
@@ -779,8 +824,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       int st = 0;
       uint32_t ph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
-        const uint8_t* wbase = args.w + static_cast<size_t>(w.nt) * args.KC * wf_tile_bytes(WF);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
+        const uint8_t* wbase = args.w + w.wtile;
         for (int c = w.c0; c < w.c1; ++c) {
           if (!mbar_wait(&raw_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
           mbar_arrive_expect_tx(&raw_full[st], wf_tile_bytes(WF));
@@ -797,13 +843,14 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       int st = 0;
       uint32_t ph = 0;
       for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
         for (int c = w.c0; c < w.c1; ++c) {
           if (!mbar_wait(&b_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
           mbar_arrive_expect_tx(&b_full[st], P.b_bytes());
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            tma_load_2d(sB + st * P.b_bytes() + i * P.b_box(), &xmap, &b_full[st], (c * 4 + i) * 64, w.mt * BN);
+            tma_load_2d(sB + st * P.b_bytes() + i * P.b_box(), &xmap, &b_full[st], (c * 4 + i) * 64, w.row0);
           if (++st == P.b_stages) { st = 0; ph ^= 1; }
         }
       }
@@ -821,7 +868,8 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       long long ph_acc = 0, ph_a = 0, ph_b = 0, ph_mma = 0;
       pc.start();
       for (int u = first; u < args.units && ok && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u);
+        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
         if (!mbar_wait(acc_empty, acc_ph ^ 1, args.err, kErrGemmWait)) { ok = false; break; }
         ph_acc += pc.lap();
         tc_fence_after();
@@ -871,7 +919,8 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
     long long ph_raw = 0, ph_dq = 0, ph_slot = 0, ph_st = 0, ph_rest = 0;
     pc.start();
     for (int u = first; u < args.units && !*abort_flag; u += step) {
-      const Unit w = unit_of(args, u);
+      const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
       bool ok = true;
       for (int c = w.c0; c < w.c1; ++c, ++g) {
         ph_rest += pc.lap();
@@ -914,7 +963,8 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
     const int n_local = 32 * q + lane;
     uint32_t acc_ph = 0;
     for (int u = first; u < args.units && !*abort_flag; u += step) {
-      const Unit w = unit_of(args, u);
+      const Unit w = unit_of(args, u, wf_tile_bytes(WF));
+        if (w.rows <= 0) continue;
       const bool ok = mbar_wait(&acc_full[0], acc_ph, args.err, kErrGemmWait) &&
                       mbar_wait(&acc_full[1], acc_ph, args.err, kErrGemmWait);
       if (!ok) { *abort_flag = 1; break; }
@@ -930,14 +980,15 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
-        const int m_base = w.mt * BN + cb;
+        const int m_base = w.row0 + cb;
+        const int m_end = w.row0 + w.rows;
         if (args.out_mode == kGemmOutSwiGLU) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float mine = __uint_as_float(v[j]);
             const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
             const int m = m_base + j;
-            if ((lane & 1) == 0 && m < args.M) {
+            if ((lane & 1) == 0 && m < m_end) {
               const float y = mine / (1.f + __expf(-mine)) * other;
               const int f = w.nt * 64 + (n_local >> 1);
               if (f < args.N / 2)
@@ -950,7 +1001,7 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = m_base + j;
-              if (m < args.M) {
+              if (m < m_end) {
                 const float y = __uint_as_float(v[j]);
                 const size_t idx = static_cast<size_t>(m) * args.ldo + nn;
                 if (args.out_mode == kGemmOutF32Add) atomicAdd(outf + idx, y);
@@ -1053,6 +1104,16 @@ void dispatch_bn(int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t
   }
 }
 
+void dispatch_wf(int wf, int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+  switch (wf) {
+    case kWfBF16: dispatch_bn<kWfBF16>(bn, map, a, st); break;
+    case kWfQ4K: dispatch_bn<kWfQ4K>(bn, map, a, st); break;
+    case kWfQ6K: dispatch_bn<kWfQ6K>(bn, map, a, st); break;
+    case kWfQ8_0: dispatch_bn<kWfQ8_0>(bn, map, a, st); break;
+    default: throw std::runtime_error("gemm: unknown weight format");
+  }
+}
+
 }  // namespace
 
 void make_act_tensor_map(CUtensorMap* map, const void* x, int M, int K, int ldx, int box_rows) {
@@ -1107,16 +1168,52 @@ void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int 
   a.split_stride = split_stride;
   a.err = err;
   a.trace = g_gemm_trace;
+  a.bn = bn;
+  a.groups = 0;
+  a.grp_count = nullptr;
+  a.grp_offset = nullptr;
+  a.grp_w_stride = 0;
   CUtensorMap map;
   make_act_tensor_map(&map, x, M, K, ldx, bn);
-  switch (wf) {
-    case kWfBF16: dispatch_bn<kWfBF16>(bn, map, a, st); break;
-    case kWfQ4K: dispatch_bn<kWfQ4K>(bn, map, a, st); break;
-    case kWfQ6K: dispatch_bn<kWfQ6K>(bn, map, a, st); break;
-    case kWfQ8_0: dispatch_bn<kWfQ8_0>(bn, map, a, st); break;
-    default: throw std::runtime_error("gemm: unknown weight format");
-  }
+  dispatch_wf(wf, bn, map, a, st);
 }
+
+void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, int N, int K, const void* x,
+                          int rows_total, int ldx, void* out, int ldo, int out_mode, int groups,
+                          const int32_t* counts, const int32_t* offsets, int max_rows, int bn, uint32_t* err,
+                          cudaStream_t st) {
+  VMC_CHECK(rows_total > 0 && N > 0 && K > 0 && groups > 0 && max_rows > 0, "gemm_grouped: empty problem");
+  VMC_CHECK(out_mode == kGemmOutBF16 || out_mode == kGemmOutF32 || out_mode == kGemmOutSwiGLU,
+            "gemm_grouped: bf16, fp32 or SwiGLU output");
+  if (bn <= 0) bn = gemm_pick_bn(max_rows);
+  const int chunk = wf_chunk(wf);
+  GemmArgs a;
+  a.w = static_cast<const uint8_t*>(w_tiled);
+  a.N = N;
+  a.K = K;
+  a.M = rows_total;
+  a.KC = (K + chunk - 1) / chunk;
+  a.chunks_per_split = a.KC;
+  a.splits = 1;
+  a.n_tiles = (N + 127) / 128;
+  a.m_tiles = (max_rows + bn - 1) / bn;
+  a.units = groups * a.n_tiles * a.m_tiles;
+  a.out = out;
+  a.ldo = ldo;
+  a.out_mode = out_mode;
+  a.split_stride = 0;
+  a.err = err;
+  a.trace = g_gemm_trace;
+  a.bn = bn;
+  a.groups = groups;
+  a.grp_count = counts;
+  a.grp_offset = offsets;
+  a.grp_w_stride = w_group_stride;
+  CUtensorMap map;
+  make_act_tensor_map(&map, x, rows_total, K, ldx, bn);
+  dispatch_wf(wf, bn, map, a, st);
+}
+
 
 int gemm_smem_bytes(int wf, int bn) {
   return (wf != kWfBF16 && bn <= 64) ? make_dplan(wf, bn).total() : make_plan(wf, bn).total();

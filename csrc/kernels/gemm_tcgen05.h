@@ -19,6 +19,14 @@ enum GemmOut : int {
 // tile from M. `err` receives a DeviceError code if a bounded wait expires.
 void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
                   int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride = 0);
+// Grouped GEMM (MoE experts): for every group g with rows [offsets[g], offsets[g] + counts[g]) of
+// x (device arrays, at most max_rows rows per group), out[rows] = x[rows] @ W_g^T where W_g starts
+// w_group_stride bytes after W_{g-1}. One launch for all groups; no host synchronisation on the
+// counts. out_mode: kGemmOutBF16, kGemmOutF32 or kGemmOutSwiGLU.
+void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, int N, int K, const void* x,
+                          int rows_total, int ldx, void* out, int ldo, int out_mode, int groups,
+                          const int32_t* counts, const int32_t* offsets, int max_rows, int bn, uint32_t* err,
+                          cudaStream_t st);
 int gemm_pick_bn(int M);
 // Diagnostics: when set, CTA 0 of every GEMM writes per-role clock64 stamps into buf[512].
 void gemm_set_trace(unsigned long long* buf);

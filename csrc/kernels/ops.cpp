@@ -8,6 +8,7 @@
 #include "comm.h"
 #include "gemm_tcgen05.h"
 #include "layers.h"
+#include "moe.h"
 #include "sampling.h"
 #include "weights.h"
 
@@ -48,6 +49,63 @@ void gemm(int wf, torch::Tensor w, int64_t N, int64_t K, torch::Tensor x, int64_
                     static_cast<int>(x.stride(0)), out.data_ptr(), static_cast<int>(out.stride(0)),
                     static_cast<int>(out_mode), static_cast<int>(splits), static_cast<int>(bn),
                     ptr<uint32_t>(err), cur_stream(), split_stride);
+}
+
+void gemm_grouped(int wf, torch::Tensor w, int64_t w_group_stride, int64_t N, int64_t K, torch::Tensor x,
+                  int64_t rows_total, torch::Tensor out, int64_t out_mode, int64_t groups, torch::Tensor counts,
+                  torch::Tensor offsets, int64_t max_rows, int64_t bn, torch::Tensor err) {
+  check_cuda(w, "w");
+  check_cuda(x, "x");
+  check_cuda(out, "out");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_grouped: bad x");
+  TORCH_CHECK(x.size(0) >= rows_total && x.size(1) >= K, "gemm_grouped: x too small");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= rows_total, "gemm_grouped: bad output");
+  TORCH_CHECK(counts.scalar_type() == torch::kInt32 && offsets.scalar_type() == torch::kInt32 &&
+                  counts.numel() >= groups && offsets.numel() >= groups,
+              "gemm_grouped: counts / offsets must be int32 [groups]");
+  TORCH_CHECK(w.numel() >= static_cast<int64_t>(groups - 1) * w_group_stride + vmc::tiled_weight_bytes(wf, N, K),
+              "gemm_grouped: weight buffer too small");
+  const bool f32_out = out_mode == vmc::kGemmOutF32;
+  TORCH_CHECK(out.scalar_type() == (f32_out ? torch::kFloat32 : torch::kBFloat16), "gemm_grouped: output dtype");
+  vmc::gemm_tcgen05_grouped(wf, w.data_ptr(), w_group_stride, static_cast<int>(N), static_cast<int>(K), x.data_ptr(),
+                            static_cast<int>(rows_total), static_cast<int>(x.stride(0)), out.data_ptr(),
+                            static_cast<int>(out.stride(0)), static_cast<int>(out_mode), static_cast<int>(groups),
+                            ptr<int32_t>(counts), ptr<int32_t>(offsets), static_cast<int>(max_rows),
+                            static_cast<int>(bn), ptr<uint32_t>(err), cur_stream());
+}
+
+void moe_route(torch::Tensor logits, int64_t T, int64_t E, int64_t k, bool norm_topk, int64_t e0, int64_t e_local,
+               torch::Tensor topk_id, torch::Tensor topk_w, torch::Tensor counts, torch::Tensor offsets,
+               torch::Tensor sorted_src, torch::Tensor slot_row, torch::Tensor total_rows) {
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "moe_route: fp32 logits");
+  TORCH_CHECK(topk_id.numel() >= T * k && topk_w.numel() >= T * k && slot_row.numel() >= T * k &&
+                  sorted_src.numel() >= T * k && counts.numel() >= e_local && offsets.numel() >= e_local,
+              "moe_route: output buffers too small");
+  vmc::MoeRouteArgs a;
+  a.logits = ptr<float>(logits);
+  a.ld_logits = static_cast<int>(logits.stride(0));
+  a.T = static_cast<int>(T);
+  a.E = static_cast<int>(E);
+  a.k = static_cast<int>(k);
+  a.norm_topk = norm_topk ? 1 : 0;
+  a.e0 = static_cast<int>(e0);
+  a.e_local = static_cast<int>(e_local);
+  a.topk_id = ptr<int32_t>(topk_id);
+  a.topk_w = ptr<float>(topk_w);
+  a.counts = ptr<int32_t>(counts);
+  a.offsets = ptr<int32_t>(offsets);
+  a.sorted_src = ptr<int32_t>(sorted_src);
+  a.slot_row = ptr<int32_t>(slot_row);
+  a.total_rows = ptr<int32_t>(total_rows);
+  vmc::moe_route(a, cur_stream());
+}
+
+void moe_combine(torch::Tensor y, torch::Tensor slot_row, torch::Tensor topk_w, int64_t T, int64_t k, int64_t H,
+                 torch::Tensor out) {
+  TORCH_CHECK(y.scalar_type() == torch::kFloat32 && out.scalar_type() == torch::kFloat32, "moe_combine: fp32");
+  vmc::moe_combine(ptr<float>(y), static_cast<int>(y.stride(0)), ptr<int32_t>(slot_row), ptr<float>(topk_w),
+                   static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), ptr<float>(out),
+                   static_cast<int>(out.stride(0)), cur_stream());
 }
 
 void repack_weight(int wf, int src_type, torch::Tensor src, int64_t N, int64_t K, torch::Tensor dst) {
@@ -194,6 +252,9 @@ torch::Tensor wrap_ptr(int64_t p, std::vector<int64_t> sizes, int dtype, int dev
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vm_c_b200 sm_100a kernels";
   m.def("gemm", &gemm);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_route", &moe_route);
+  m.def("moe_combine", &moe_combine);
   m.def("gemm_smem_bytes", &vmc::gemm_smem_bytes);
   m.def("gemm_set_trace", [](c10::optional<torch::Tensor> t) {
     vmc::gemm_set_trace(t.has_value() && t->defined() ? reinterpret_cast<unsigned long long*>(t->data_ptr()) : nullptr);
@@ -213,6 +274,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu", &swiglu);
   m.def("gather_rows", &gather_rows);
   m.def("f32_to_bf16", &f32_to_bf16);
+  m.def("attn_decode_ctas_per_sm", &vmc::attn_decode_ctas_per_sm);
   m.def("sample", &sample);
   m.def("apply_penalties", &apply_penalties);
   m.def("ar_add_rmsnorm", &ar_add_rmsnorm);

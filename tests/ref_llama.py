@@ -23,11 +23,31 @@ def load_dense(src, cfg):
 
     W = {"embd": get("token_embd.weight"), "norm": get("output_norm.weight").view(-1),
          "out": get("output.weight") if src.has("output.weight") else get("token_embd.weight"), "layers": []}
+    ffn = ["ffn_gate_inp", "ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"] if cfg.is_moe else \
+        ["ffn_gate", "ffn_up", "ffn_down"]
     for i in range(cfg.n_layers):
-        W["layers"].append({k: get(blk(i, k)) for k in
-                            ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
-                             "ffn_up", "ffn_down"]})
+        L = {k: get(blk(i, k)) for k in ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm"] + ffn}
+        if cfg.is_moe:
+            E, F, H = cfg.n_experts, cfg.ffn, cfg.hidden
+            L["ffn_gate_exps"] = L["ffn_gate_exps"].reshape(E, F, H)
+            L["ffn_up_exps"] = L["ffn_up_exps"].reshape(E, F, H)
+            L["ffn_down_exps"] = L["ffn_down_exps"].reshape(E, H, F)
+        W["layers"].append(L)
     return W
+
+
+def moe_ffn(L, cfg, h):
+    """Mixtral FFN: softmax router, top-k, renormalised weights, weighted sum of SwiGLU experts."""
+    probs = torch.softmax(h @ L["ffn_gate_inp"].T, -1)
+    w, idx = torch.topk(probs, cfg.n_experts_used, -1)
+    w = w / w.sum(-1, keepdim=True)
+    out = torch.zeros_like(h)
+    for t in range(h.shape[0]):
+        for j in range(cfg.n_experts_used):
+            e = int(idx[t, j])
+            g = torch.nn.functional.silu(h[t] @ L["ffn_gate_exps"][e].T) * (h[t] @ L["ffn_up_exps"][e].T)
+            out[t] += w[t, j] * (g @ L["ffn_down_exps"][e].T)
+    return out
 
 
 def rope(x, pos, inv, neox):
@@ -70,7 +90,10 @@ def forward_logits(W, cfg, tokens: list[int]) -> torch.Tensor:
         a = torch.einsum("hts,shd->thd", torch.softmax(s, -1), v).reshape(T, Hq * D)
         x = x + a @ L["attn_output"].T
         h = rms(x, L["ffn_norm"])
-        x = x + (torch.nn.functional.silu(h @ L["ffn_gate"].T) * (h @ L["ffn_up"].T)) @ L["ffn_down"].T
+        if cfg.is_moe:
+            x = x + moe_ffn(L, cfg, h)
+        else:
+            x = x + (torch.nn.functional.silu(h @ L["ffn_gate"].T) * (h @ L["ffn_up"].T)) @ L["ffn_down"].T
     return rms(x, W["norm"]) @ W["out"].T
 
 

@@ -39,6 +39,10 @@ PRESETS: dict[str, ModelConfig] = {
     "mixtral-8x7b": ModelConfig(name="mixtral-8x7b", n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128,
                                 ffn=14336, vocab=32000, rms_eps=1e-5, rope_theta=1000000.0, context_length=32768,
                                 n_experts=8, n_experts_used=2, bos_token_id=1, eos_token_ids=[2]),
+    # small Mixtral-architecture model for tests (4 experts, top-2)
+    "tiny-mixtral": ModelConfig(name="tiny-mixtral", n_layers=2, hidden=256, n_heads=8, n_kv_heads=4, head_dim=32,
+                                ffn=512, vocab=32000, rms_eps=1e-5, rope_theta=10000.0, context_length=2048,
+                                n_experts=4, n_experts_used=2, bos_token_id=1, eos_token_ids=[2]),
     # config 5 draft model
     "draft-16l-2048": ModelConfig(name="draft-16l-2048", n_layers=16, hidden=2048, n_heads=32, n_kv_heads=8,
                                   head_dim=64, ffn=8192, vocab=128256, rms_eps=1e-5, rope_theta=500000.0,

@@ -110,7 +110,7 @@ def _tile_raw(raw: torch.Tensor, gtype: int, N: int, K: int) -> ops.TiledWeight:
     return ops.tile_weight(raw, gtype, N, K)
 
 
-def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1) -> ModelWeights:
+def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1, ep_size: int = 1) -> ModelWeights:
     """Load (and shard) the weights of a llama-architecture model from a tensor source."""
     check_tp(cfg, tp_size)
     dev = torch.device(device)
@@ -148,7 +148,7 @@ def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int =
                           wqkv=wqkv, qkv_split=split, wo=wo)
         if cfg.is_moe:
             from .moe import load_moe_layer
-            lw.moe = load_moe_layer(src, cfg, i, dev, tp_rank, tp_size)
+            lw.moe = load_moe_layer(src, cfg, i, dev, tp_rank, tp_size, ep_size)
         else:
             gn, un, dn = blk(i, "ffn_gate"), blk(i, "ffn_up"), blk(i, "ffn_down")
             fr = (tp_rank * f_local, (tp_rank + 1) * f_local)
@@ -173,6 +173,8 @@ def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int =
         for w in lw.wqkv + [lw.wo, lw.w_gate_up, lw.w_down]:
             if w is not None:
                 total += w.nbytes
+        if lw.moe is not None:
+            total += lw.moe.router.nbytes + lw.moe.gate_up.nbytes + lw.moe.down.nbytes
     # Embedding (replicated raw rows) and output projection (vocab-parallel).
     es = src.info("token_embd.weight")
     embd = _to_dev(src.rows("token_embd.weight"), dev)
@@ -285,7 +287,7 @@ class LlamaModel:
         if attn_splits > 1:
             self.ws.part_o = torch.empty(attn_splits, max_samples, self.hq, self.D, dtype=torch.float32, device=dev)
             self.ws.part_lse = torch.empty(attn_splits, max_samples, self.hq, dtype=torch.float32, device=dev)
-        self.fused = self.tp > 1 and comm is not None and hasattr(comm, "allreduce_add_rmsnorm") and not cfg.is_moe
+        self.fused = self.tp > 1 and comm is not None and hasattr(comm, "allreduce_add_rmsnorm")
         if self.fused:
             comm.setup(max_tokens, self.H)
         self.moe_runner = None
@@ -375,6 +377,11 @@ class LlamaModel:
             nxt = layers[li + 1].attn_norm if li + 1 < len(layers) else self.w.output_norm
             if self.fused:
                 self._row_parallel_fused(0, ws.attn, lw.wo, T, lw.ffn_norm)
+                if lw.moe is not None:
+                    part = self.comm.partial(1).view(-1)[:T * self.H].view(T, self.H)
+                    self.moe_runner.forward(lw.moe, ws.h, T, out=part)
+                    self.comm.allreduce_add_rmsnorm(1, T, ws.resid, nxt, cfg.rms_eps, ws.h)
+                    continue
                 self._gate_up(lw, T)
                 self._row_parallel_fused(1, ws.act, lw.w_down, T, nxt)
                 continue

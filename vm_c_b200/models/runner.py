@@ -41,7 +41,8 @@ class GpuModelRunner(ModelRunner):
         self.tp_rank, self.tp_size = tp_rank, tp_size
         m = cfg.model
         t0 = time.perf_counter()
-        self.weights = weights if weights is not None else load_weights(source, m, self.dev, tp_rank, tp_size)
+        self.weights = weights if weights is not None else load_weights(source, m, self.dev, tp_rank, tp_size,
+                                                                                 cfg.parallel.expert_parallel_size)
         log.info("weights loaded: %.2f GB in %.1fs", self.weights.bytes_total / 1e9, time.perf_counter() - t0)
         s = cfg.scheduler
         self.max_model_len = m.max_model_len
@@ -54,6 +55,8 @@ class GpuModelRunner(ModelRunner):
         self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len, comm=comm,
                                 attn_splits=16)
         self.comm = comm
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        self._decode_slots = sms * max(1, ops.C().attn_decode_ctas_per_sm(self.model.D))
         # KV cache: [L, num_blocks, 2, Hkv_local, block_size, D] bf16, zero-filled (finite).
         per_block = kv_bytes_per_block(cfg, self.model.hkv)
         max_blocks_per_seq = (m.max_model_len + cfg.cache.block_size - 1) // cfg.cache.block_size + 1
@@ -121,8 +124,7 @@ class GpuModelRunner(ModelRunner):
                         T=T, R=R, S=S, num_decode=nd, max_qlen=max_qlen)
 
     def _attn_splits(self, nd: int) -> int:
-        ctas = max(1, nd * self.model.hkv)
-        return max(1, min(16, math.ceil(2 * 148 / ctas))) if ctas < 148 else 1
+        return ops.decode_splits(nd * self.model.hkv, self._decode_slots)
 
     def _forward(self, m: StepMeta, pen=None) -> None:
         self.model.attn_splits = self._attn_splits(m.num_decode)

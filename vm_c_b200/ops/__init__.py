@@ -120,6 +120,32 @@ def gemm(x: torch.Tensor, w: TiledWeight, out: torch.Tensor, M: int, mode: int =
     return out
 
 
+def gemm_grouped(x: torch.Tensor, w: TiledWeight, groups: int, group_stride: int, rows_total: int,
+                 counts: torch.Tensor, offsets: torch.Tensor, max_rows: int, out: torch.Tensor,
+                 mode: int = OUT_BF16, bn: int = 0, err: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-group GEMM in one launch (MoE experts): rows [offsets[g], offsets[g] + counts[g]) of x
+    times expert g's weight (``group_stride`` bytes after expert g-1 in ``w.data``; ``w`` describes
+    one expert). Counts and offsets stay on the device."""
+    if err is None:
+        err = _err_word(x.device)
+    C().gemm_grouped(w.wf, w.data, group_stride, w.N, w.K, x, rows_total, out, mode, groups, counts, offsets,
+                     max_rows, bn, err)
+    _count()
+    return out
+
+
+def moe_route(logits, T, E, k, norm_topk, e0, e_local, topk_id, topk_w, counts, offsets, sorted_src, slot_row,
+              total_rows):
+    C().moe_route(logits, T, E, k, norm_topk, e0, e_local, topk_id, topk_w, counts, offsets, sorted_src, slot_row,
+                  total_rows)
+    _count()
+
+
+def moe_combine(y, slot_row, topk_w, T, k, H, out):
+    C().moe_combine(y, slot_row, topk_w, T, k, H, out)
+    _count()
+
+
 _ERR: dict = {}
 
 
@@ -188,6 +214,23 @@ def paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset,
 SAMPLE_PARAMS_DTYPE = [("temperature", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"), ("min_p", "<f4"),
                        ("repetition_penalty", "<f4"), ("frequency_penalty", "<f4"), ("presence_penalty", "<f4"),
                        ("step", "<i4"), ("seed", "<u8")]
+
+
+def decode_splits(ctas: int, slots: int, max_splits: int = 16) -> int:
+    """Split-KV factor for decode attention with `ctas` (request, KV head) pairs on a GPU with
+    `slots` resident CTA slots. Splitting only pays when the pairs alone leave SMs idle: measured on
+    the 8B shapes, filling the last wave of a >1-wave grid with splits gains nothing."""
+    sms = slots // max(1, slots // 148) if slots >= 148 else slots
+    ctas = max(1, ctas)
+    if ctas >= sms:
+        return 1
+    return max(1, min(max_splits, math.ceil(2 * sms / ctas)))
+
+
+def decode_slots(D: int) -> int:
+    """Resident decode-attention CTAs on the whole GPU for head dim D."""
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return sms * max(1, C().attn_decode_ctas_per_sm(D))
 
 
 def sample(logits, S, V, params, out_tok, out_lp=None):

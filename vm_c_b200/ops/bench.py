@@ -15,8 +15,9 @@ import math
 
 import torch
 
-from . import (OUT_BF16, OUT_F32_SPLIT, OUT_SWIGLU, add_rmsnorm, device_error, effective_splits, gemm,
-               paged_attention, pick_splits, quantize_blocks, rope_store, sample, swiglu, tile_weight)
+from . import (OUT_BF16, OUT_F32_SPLIT, OUT_SWIGLU, add_rmsnorm, decode_slots, decode_splits, device_error,
+               effective_splits, gemm, paged_attention, pick_splits, quantize_blocks, rope_store, sample, swiglu,
+               tile_weight)
 from ..gguf.constants import GType
 
 # name: (weight type, N, K, tokens M, output mode)
@@ -98,11 +99,14 @@ def bench_attn(kind: str, reps: int, flush: torch.Tensor) -> str:
     kv, bt, q, qs, cl, T = _paged_setup(ctx, ql, Hq, Hkv, D)
     out = torch.empty_like(q)
     dec = kind == "decode"
+    s = decode_splits(len(ctx) * Hkv, decode_slots(D)) if dec else 1
+    po = torch.empty(s, T, Hq, D, device="cuda") if s > 1 else None
+    pl = torch.empty(s, T, Hq, device="cuda") if s > 1 else None
     t = _time(lambda: paged_attention(q, kv, qs, cl, bt, len(ctx), 0, max(ql), T, Hq, Hkv, D, 1 / math.sqrt(D), dec,
-                                      out), reps, flush)
+                                      out, s, po, pl), reps, flush)
     kv_bytes = sum(ctx) * Hkv * D * 2 * 2
     flops = sum(4 * q_ * c * Hq * D for q_, c in zip(ql, ctx)) / (1 if dec else 2)
-    return (f"attn:{kind:7s} reqs={len(ctx)} ctx={ctx[0]} qlen={ql[0]} {t:8.1f} us  KV {kv_bytes / t / 1e6:5.2f} TB/s"
+    return (f"attn:{kind:7s} reqs={len(ctx)} ctx={ctx[0]} qlen={ql[0]} splits={s} {t:8.1f} us  KV {kv_bytes / t / 1e6:5.2f} TB/s"
             f"  {flops / t / 1e6:7.1f} TFLOP/s")
 
 
