@@ -13,6 +13,7 @@
 #include "quants.hpp"
 #include "scheduler.hpp"
 #include "tokenizer.hpp"
+#include "turboquant.hpp"
 
 namespace py = pybind11;
 using namespace vmc;
@@ -152,6 +153,25 @@ PYBIND11_MODULE(_host, m) {
   m.def("row_bytes", [](uint32_t t, int64_t n) { return gtype_row_bytes(static_cast<GType>(t), n); });
 
   // ---------------- quant codecs ----------------
+  m.def("tq_layout", [](const std::string& method, int head_dim) {
+    const vmc::TqLayout l = vmc::TqLayout::from_method(head_dim, method);
+    py::dict d;
+    d["head_dim"] = l.head_dim;
+    d["key_bits"] = l.key_bits;
+    d["value_bits"] = l.value_bits;
+    d["norm_correction"] = l.norm_correction;
+    d["key_fp8"] = l.key_fp8;
+    d["n_centroids"] = l.n_centroids;
+    d["mse_bytes"] = l.mse_bytes;
+    d["key_packed"] = l.key_packed;
+    d["val_bytes"] = l.val_bytes;
+    d["value_packed"] = l.value_packed;
+    d["slot"] = l.slot;
+    d["slot_aligned"] = l.slot_aligned;
+    return d;
+  });
+  m.def("is_turboquant_method", &vmc::is_turboquant_method);
+  m.def("lloyd_max_gaussian", &vmc::lloyd_max_gaussian, py::arg("bits"), py::arg("sigma"));
   m.def("dequantize", [](uint32_t type, py::buffer src, int64_t rows, int64_t row_elems, int threads) {
     py::buffer_info bi = src.request();
     size_t need = gtype_row_bytes(static_cast<GType>(type), row_elems) * static_cast<size_t>(rows);

@@ -20,6 +20,7 @@
 //                          causal mask against each row's absolute position.
 #include "attention.h"
 #include "common.cuh"
+#include "turboquant.cuh"
 
 namespace vmc {
 namespace {
@@ -48,6 +49,7 @@ struct AttnParams {
   float* part_o;            // [splits, T, Hq, D] (split-KV only)
   float* part_lse;          // [splits, T, Hq]
   int req_offset;           // first request index handled by this launch
+  TqDev tq;                 // TurboQuant cache of this layer (tq.cache == nullptr: bf16 pages in kv)
 };
 
 // Copy one 16 x D page (K or V) into a padded smem tile (rows 16*slot .. 16*slot+15).
@@ -171,77 +173,109 @@ __device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV
   }
 }
 
-// ---------------------------------------------------------------------------------------------
-// Decode: one CTA = (request, kv head, split); 16 packed rows; 4 warps split the pages.
-
-template <int D>
-__global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int total_tokens) {
-  constexpr int RB = Frag<D>::RB;
-  constexpr int ND = Frag<D>::ND;
-  extern __shared__ __align__(16) uint8_t smem[];
-  pdl_trigger();
-  pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = blockIdx.y;
-  const int r = blockIdx.x + p.req_offset;
-  const int split = blockIdx.z;
-  const int qs = p.q_start[r], qlen = p.q_start[r + 1] - qs;
-  const int ctx = p.ctx_len[r];
-  if (qlen <= 0) return;
-  const int nblocks = (ctx + kBS - 1) / kBS;
-  const int per_split = (nblocks + p.splits - 1) / p.splits;
-  const int b0 = split * per_split, b1 = min(nblocks, b0 + per_split);
-  const int32_t* bt = p.block_tables + static_cast<int64_t>(r) * p.max_blocks;
-
-  uint32_t qa[Frag<D>::KD][4];
-  load_q_frags<D>(p, qs, qlen, kvh, 0, lane, qa);
-  const int rows = qlen * p.G;
-  const int pr_lo = lane >> 2, pr_hi = pr_lo + 8;
-  const int qpos_lo = pr_lo < rows ? ctx - qlen + pr_lo / p.G : -1;
-  const int qpos_hi = pr_hi < rows ? ctx - qlen + pr_hi / p.G : -1;
-
-  float o[ND][4];
+// TurboQuant: dequantise half (dims [half * D/2, (half + 1) * D/2)) of one key's K and V slot into
+// bf16 rows of the padded smem tiles. Lanes 2k and 2k+1 of a warp hold the two halves of one key
+// (the norm correction needs the squared norm over all D dims). KB: key bits (3, 4; 8 = fp8 e4m3),
+// VB: value bits. Invalid keys (past the context) get zero rows.
+template <int D, int KB, int VB>
+__device__ __forceinline__ void tq_dequant_half(const AttnParams& p, int blk, int off, int kvh, int half, bool valid,
+                                                uint8_t* k_row, uint8_t* v_row, const float* s_cent) {
+  constexpr int HD = D / 2;
+  const TqDev& t = p.tq;
+  const uint16_t* sp = reinterpret_cast<const uint16_t*>(t.cache + tq_slot_offset(t, valid ? blk : 0, off, kvh, p.Hkv));
+  uint32_t* kr = reinterpret_cast<uint32_t*>(k_row + half * HD * 2);
+  if constexpr (KB == 8) {
 #pragma unroll
-  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-
-  // Per-warp double buffer: stage s holds K rows [0,16) and V rows [0,16) of one page.
-  uint8_t* wsm = smem + warp * (2 * 2 * kBS * RB);
-  auto sK = [&](int s) { return wsm + s * (2 * kBS * RB); };
-  auto sV = [&](int s) { return wsm + s * (2 * kBS * RB) + kBS * RB; };
-  const int64_t page_elems = static_cast<int64_t>(kBS) * D;
-  // Block ids of this warp's pages (b0 + warp + 4j), 32 at a time in one coalesced load, so that a
-  // page's copy never waits on its own dependent block-table load.
-  int ids = 0;
-  auto fetch_ids = [&](int j0) {
-    const int bj = b0 + warp + 4 * (j0 + lane);
-    ids = bj < b1 ? bt[bj] : 0;
-  };
-  auto issue = [&](int j, int s) {  // j = index of the page among this warp's pages
-    if ((j & 31) == 0) fetch_ids(j);
-    const int blk = __shfl_sync(0xffffffffu, ids, j & 31);
-    const __nv_bfloat16* kp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + kvh) * page_elems;
-    const __nv_bfloat16* vp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + p.Hkv + kvh) * page_elems;
-    load_page_warp<D>(sK(s), 0, kp, lane);
-    load_page_warp<D>(sV(s), 0, vp, lane);
-  };
-  int b = b0 + warp;
-  int stage = 0, j = 0;
-  if (b < b1) issue(0, 0);
-  cp_async_commit();
-  for (; b < b1; b += 4, ++j) {
-    const int nb = b + 4;
-    if (nb < b1) issue(j + 1, stage ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncwarp();
-    attn_step16<D>(sK(stage), sV(stage), 0, b * kBS, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane);
-    __syncwarp();
-    stage ^= 1;
+    for (int w = 0; w < HD / 2; ++w) {
+      const uint16_t b2 = valid ? __ldg(sp + half * (HD / 2) + w) : 0;
+      uint32_t h2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(b2));
+      const __half2 hv = *reinterpret_cast<const __half2*>(&h2);
+      kr[w] = valid ? pack_bf16x2(__low2float(hv), __high2float(hv)) : 0u;
+    }
+  } else {
+    // Packed indices stay in registers: one pass for the squared norm of the reconstruction (norm
+    // correction), one to write the scaled centroids.
+    constexpr int NW = KB == 4 ? HD / 4 : HD / 16;  // 16-bit words (4-bit) or 48-bit groups (3-bit)
+    uint64_t pk[NW];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if constexpr (KB == 4) {
+        pk[w] = valid ? __ldg(sp + half * (HD / 4) + w) : 0;
+      } else {
+        const uint16_t* gp = sp + half * (HD / 16) * 3 + w * 3;
+        pk[w] = valid ? (static_cast<uint64_t>(__ldg(gp)) | (static_cast<uint64_t>(__ldg(gp + 1)) << 16) |
+                         (static_cast<uint64_t>(__ldg(gp + 2)) << 32))
+                      : 0ull;
+      }
+    }
+    constexpr int PER = KB == 4 ? 4 : 16;
+    constexpr uint32_t MASK = (1u << KB) - 1u;
+    float ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+#pragma unroll
+      for (int n = 0; n < PER; ++n) {
+        const float c = s_cent[(pk[w] >> (KB * n)) & MASK];
+        ss += c * c;
+      }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    const float norm = valid ? bf16_bits_to_float(__ldg(sp + t.mse_bytes / 2)) : 0.f;
+    const float factor = t.norm_correction ? norm * rsqrtf(ss + 1e-16f) : norm;
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+#pragma unroll
+      for (int n = 0; n < PER; n += 2) {
+        const float c0 = s_cent[(pk[w] >> (KB * n)) & MASK], c1 = s_cent[(pk[w] >> (KB * (n + 1))) & MASK];
+        kr[(w * PER + n) / 2] = valid ? pack_bf16x2(c0 * factor, c1 * factor) : 0u;
+      }
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  // V
+  const uint16_t* vp = sp + t.key_packed / 2;
+  const float vs = valid ? bf16_bits_to_float(__ldg(vp + t.val_bytes / 2)) : 0.f;
+  const float vm = valid ? bf16_bits_to_float(__ldg(vp + t.val_bytes / 2 + 1)) : 0.f;
+  uint32_t* vr = reinterpret_cast<uint32_t*>(v_row + half * HD * 2);
+  if constexpr (VB == 4) {
+#pragma unroll
+    for (int w = 0; w < HD / 4; ++w) {
+      const uint32_t b2 = valid ? __ldg(vp + half * (HD / 4) + w) : 0;
+      const float a0 = static_cast<float>(b2 & 15u) * vs + vm, a1 = static_cast<float>((b2 >> 4) & 15u) * vs + vm;
+      const float a2 = static_cast<float>((b2 >> 8) & 15u) * vs + vm, a3 = static_cast<float>((b2 >> 12) & 15u) * vs + vm;
+      vr[2 * w] = valid ? pack_bf16x2(a0, a1) : 0u;
+      vr[2 * w + 1] = valid ? pack_bf16x2(a2, a3) : 0u;
+    }
+  } else {
+#pragma unroll
+    for (int g = 0; g < HD / 16; ++g) {
+      const uint16_t* gp = vp + half * (HD / 16) * 3 + g * 3;
+      const uint64_t bits = valid ? (static_cast<uint64_t>(__ldg(gp)) | (static_cast<uint64_t>(__ldg(gp + 1)) << 16) |
+                                     (static_cast<uint64_t>(__ldg(gp + 2)) << 32))
+                                  : 0ull;
+#pragma unroll
+      for (int n = 0; n < 16; n += 2) {
+        const float a0 = static_cast<float>((bits >> (3 * n)) & 7u) * vs + vm;
+        const float a1 = static_cast<float>((bits >> (3 * n + 3)) & 7u) * vs + vm;
+        vr[8 * g + n / 2] = valid ? pack_bf16x2(a0, a1) : 0u;
+      }
+    }
+  }
+}
 
+// Centroid table of the TurboQuant keys into shared memory (all threads; followed by a barrier).
+__device__ __forceinline__ void tq_load_centroids(const AttnParams& p, float* s_cent) {
+  const int n = p.tq.key_fp8 ? 0 : (1 << p.tq.key_bits);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s_cent[i] = p.tq.centroids[i];
+  __syncthreads();
+}
+
+// Merge the 4 warps of a decode CTA (each holds o, m, l for the same 16 packed rows over disjoint
+// keys) through shared memory and write the output rows, or this split's partial O and LSE.
+template <int D>
+__device__ __forceinline__ void decode_merge_store(const AttnParams& p, uint8_t* smem, const float (&o)[Frag<D>::ND][4],
+                                                   const float (&m)[2], const float (&l)[2], int rows, int qs, int kvh,
+                                                   int split, int total_tokens) {
+  constexpr int ND = Frag<D>::ND;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Merge the 4 warps: each writes (m, l, o) for its 16 rows to smem; warp 0 combines.
   float* mo = reinterpret_cast<float*>(smem);           // [4][16][D]
   float* ml = mo + 4 * 16 * D;                          // [4][16][2]
@@ -301,6 +335,88 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int tota
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Decode: one CTA = (request, kv head, split); 16 packed rows; 4 warps split the pages.
+
+template <int D, int KQ>
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int total_tokens) {
+  constexpr int RB = Frag<D>::RB;
+  constexpr int ND = Frag<D>::ND;
+  extern __shared__ __align__(16) uint8_t smem[];
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y;
+  const int r = blockIdx.x + p.req_offset;
+  const int split = blockIdx.z;
+  const int qs = p.q_start[r], qlen = p.q_start[r + 1] - qs;
+  const int ctx = p.ctx_len[r];
+  if (qlen <= 0) return;
+  const int nblocks = (ctx + kBS - 1) / kBS;
+  const int per_split = (nblocks + p.splits - 1) / p.splits;
+  const int b0 = split * per_split, b1 = min(nblocks, b0 + per_split);
+  const int32_t* bt = p.block_tables + static_cast<int64_t>(r) * p.max_blocks;
+
+  uint32_t qa[Frag<D>::KD][4];
+  load_q_frags<D>(p, qs, qlen, kvh, 0, lane, qa);
+  const int rows = qlen * p.G;
+  const int pr_lo = lane >> 2, pr_hi = pr_lo + 8;
+  const int qpos_lo = pr_lo < rows ? ctx - qlen + pr_lo / p.G : -1;
+  const int qpos_hi = pr_hi < rows ? ctx - qlen + pr_hi / p.G : -1;
+
+  float o[ND][4];
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+
+  // Per-warp double buffer: stage s holds K rows [0,16) and V rows [0,16) of one page.
+  uint8_t* wsm = smem + warp * (2 * 2 * kBS * RB);
+  auto sK = [&](int s) { return wsm + s * (2 * kBS * RB); };
+  auto sV = [&](int s) { return wsm + s * (2 * kBS * RB) + kBS * RB; };
+  const int64_t page_elems = static_cast<int64_t>(kBS) * D;
+  // Block ids of this warp's pages (b0 + warp + 4j), 32 at a time in one coalesced load, so that a
+  // page's copy never waits on its own dependent block-table load.
+  int ids = 0;
+  auto fetch_ids = [&](int j0) {
+    const int bj = b0 + warp + 4 * (j0 + lane);
+    ids = bj < b1 ? bt[bj] : 0;
+  };
+  __shared__ float s_cent[KQ ? 16 : 1];
+  if constexpr (KQ != 0) tq_load_centroids(p, s_cent);
+  auto issue = [&](int j, int s) {  // j = index of the page among this warp's pages
+    if ((j & 31) == 0) fetch_ids(j);
+    const int blk = __shfl_sync(0xffffffffu, ids, j & 31);
+    if constexpr (KQ == 0) {
+      const __nv_bfloat16* kp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + kvh) * page_elems;
+      const __nv_bfloat16* vp = p.kv + (static_cast<int64_t>(blk) * 2 * p.Hkv + p.Hkv + kvh) * page_elems;
+      load_page_warp<D>(sK(s), 0, kp, lane);
+      load_page_warp<D>(sV(s), 0, vp, lane);
+    } else {
+      const int key = lane >> 1;
+      const bool valid = (b0 + warp + 4 * j) * kBS + key < ctx;
+      tq_dequant_half<D, KQ / 10, KQ % 10>(p, blk, key, kvh, lane & 1, valid, sK(s) + key * RB, sV(s) + key * RB,
+                                           s_cent);
+    }
+  };
+  int b = b0 + warp;
+  int stage = 0, j = 0;
+  if (b < b1) issue(0, 0);
+  cp_async_commit();
+  for (; b < b1; b += 4, ++j) {
+    const int nb = b + 4;
+    if (nb < b1) issue(j + 1, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    attn_step16<D>(sK(stage), sV(stage), 0, b * kBS, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane);
+    __syncwarp();
+    stage ^= 1;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  decode_merge_store<D>(p, smem, o, m, l, rows, qs, kvh, split, total_tokens);
+}
+
 // Merge split-KV partials: one warp per (token, head).
 template <int D>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
@@ -331,7 +447,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
 // ---------------------------------------------------------------------------------------------
 // Prefill / extend: one CTA = (64 packed rows, kv head, request). 64-key tiles shared by warps.
 
-template <int D>
+template <int D, int KQ>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
   constexpr int RB = Frag<D>::RB;
   constexpr int ND = Frag<D>::ND;
@@ -372,7 +488,19 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
   auto sV = [&](int s) { return smem + s * (2 * TK * RB) + TK * RB; };
   const int64_t page_elems = static_cast<int64_t>(kBS) * D;
   constexpr int CH = D / 8;
+  __shared__ float s_cent[KQ ? 16 : 1];
+  if constexpr (KQ != 0) tq_load_centroids(p, s_cent);
   auto issue = [&](int tile, int s) {
+    if constexpr (KQ != 0) {
+      // One thread per (key, half) of the 64-key tile: dequantise into the bf16 tiles.
+      const int key = threadIdx.x >> 1;
+      const int b = tile * 4 + (key >> 4);
+      const bool valid = tile * TK + key < kmax;
+      const int blk = valid ? bt[b] : 0;
+      tq_dequant_half<D, KQ / 10, KQ % 10>(p, blk, key & 15, kvh, threadIdx.x & 1, valid, sK(s) + key * RB,
+                                           sV(s) + key * RB, s_cent);
+      return;
+    }
     // 4 pages x (K, V) x 16 rows x CH chunks, spread over 128 threads.
     constexpr int TOTAL = 4 * 2 * kBS * CH;
     for (int i = threadIdx.x; i < TOTAL; i += 128) {
@@ -433,30 +561,30 @@ constexpr int decode_smem() {
   return smem_pipe > smem_merge ? smem_pipe : smem_merge;
 }
 
-template <int D>
+template <int D, int KQ>
 void config_decode() {
   static bool cfg = false;
   if (!cfg) {
-    VMC_CUDA_CHECK(
-        cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<D>()));
+    VMC_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<D, KQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        decode_smem<D>()));
     cfg = true;
   }
 }
 
 template <int D>
 int decode_ctas_per_sm() {
-  config_decode<D>();
+  config_decode<D, 0>();
   int n = 0;
-  VMC_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_kernel<D>, 128, decode_smem<D>()));
+  VMC_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_kernel<D, 0>, 128, decode_smem<D>()));
   return n;
 }
 
-template <int D>
+template <int D, int KQ>
 void launch_decode(const AttnParams& p, int num_reqs, int total_tokens, cudaStream_t st) {
   const int smem = decode_smem<D>();
-  config_decode<D>();
+  config_decode<D, KQ>();
   dim3 grid(num_reqs, p.Hkv, p.splits);
-  launch_k(attn_decode_kernel<D>, grid, dim3(128), smem, st, p, total_tokens);
+  launch_k(attn_decode_kernel<D, KQ>, grid, dim3(128), smem, st, p, total_tokens);
   if (p.splits > 1) {
     const int64_t rows = static_cast<int64_t>(total_tokens) * p.Hq;
     launch_k(attn_combine_kernel<D>, dim3(static_cast<int>((rows + 3) / 4)), dim3(128), 0, st,
@@ -464,17 +592,40 @@ void launch_decode(const AttnParams& p, int num_reqs, int total_tokens, cudaStre
   }
 }
 
-template <int D>
+template <int D, int KQ>
 void launch_prefill(const AttnParams& p, int num_reqs, int max_qlen, cudaStream_t st) {
   constexpr int RB = Frag<D>::RB;
   const int smem = 2 * 2 * 64 * RB;
   static bool cfg = false;
   if (!cfg) {
-    VMC_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    VMC_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<D, KQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cfg = true;
   }
   dim3 grid((max_qlen * p.G + 63) / 64, p.Hkv, num_reqs);
-  launch_k(attn_prefill_kernel<D>, grid, dim3(128), smem, st, p);
+  launch_k(attn_prefill_kernel<D, KQ>, grid, dim3(128), smem, st, p);
+}
+
+// KV format code: 0 = bf16 pages; TurboQuant: 10 * key bits + value bits (fp8 keys: 8).
+template <int D, int KQ>
+void launch_any(const AttnParams& p, const AttnLaunch& a, cudaStream_t st) {
+  if (a.decode) launch_decode<D, KQ>(p, a.num_reqs, a.total_tokens, st);
+  else launch_prefill<D, KQ>(p, a.num_reqs, a.max_qlen, st);
+}
+
+template <int D>
+void dispatch_kv(const AttnParams& p, const AttnLaunch& a, cudaStream_t st) {
+  if (!a.tq) {
+    launch_any<D, 0>(p, a, st);
+    return;
+  }
+  const int kb = a.tq->key_fp8 ? 8 : a.tq->key_bits, vb = a.tq->value_bits;
+  switch (kb * 10 + vb) {
+    case 44: launch_any<D, 44>(p, a, st); break;
+    case 34: launch_any<D, 34>(p, a, st); break;
+    case 33: launch_any<D, 33>(p, a, st); break;
+    case 84: launch_any<D, 84>(p, a, st); break;
+    default: throw std::runtime_error("attention: unsupported TurboQuant variant");
+  }
 }
 
 }  // namespace
@@ -497,23 +648,18 @@ void paged_attention(const AttnLaunch& a, cudaStream_t st) {
   p.part_o = a.part_o;
   p.part_lse = a.part_lse;
   p.req_offset = a.req_offset;
+  if (a.tq) p.tq = *a.tq;
+  else p.tq.cache = nullptr;
   if (a.num_reqs <= 0) return;
   if (a.decode) {
     VMC_CHECK(a.max_qlen * p.G <= 16, "attention: decode path needs q_len * group <= 16");
     VMC_CHECK(p.splits == 1 || (a.part_o && a.part_lse), "attention: split-KV needs partial buffers");
-    switch (a.D) {
-      case 32: launch_decode<32>(p, a.num_reqs, a.total_tokens, st); break;
-      case 64: launch_decode<64>(p, a.num_reqs, a.total_tokens, st); break;
-      case 128: launch_decode<128>(p, a.num_reqs, a.total_tokens, st); break;
-      default: throw std::runtime_error("attention: unsupported head dim");
-    }
-  } else {
-    switch (a.D) {
-      case 32: launch_prefill<32>(p, a.num_reqs, a.max_qlen, st); break;
-      case 64: launch_prefill<64>(p, a.num_reqs, a.max_qlen, st); break;
-      case 128: launch_prefill<128>(p, a.num_reqs, a.max_qlen, st); break;
-      default: throw std::runtime_error("attention: unsupported head dim");
-    }
+  }
+  switch (a.D) {
+    case 32: dispatch_kv<32>(p, a, st); break;
+    case 64: dispatch_kv<64>(p, a, st); break;
+    case 128: dispatch_kv<128>(p, a, st); break;
+    default: throw std::runtime_error("attention: unsupported head dim");
   }
 }
 

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "turboquant_types.h"
+
 namespace vmc {
 
 struct AttnLaunch {
@@ -23,6 +25,7 @@ struct AttnLaunch {
   float* part_o;             // [splits, total_tokens, Hq, D] fp32 (splits > 1)
   float* part_lse;           // [splits, total_tokens, Hq] fp32
   void* out;                 // bf16 [T, Hq, D]
+  const TqDev* tq = nullptr; // TurboQuant cache of this layer instead of bf16 pages (kv unused)
 };
 
 void paged_attention(const AttnLaunch& a, cudaStream_t st);

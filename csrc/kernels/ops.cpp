@@ -10,6 +10,7 @@
 #include "layers.h"
 #include "moe.h"
 #include "sampling.h"
+#include "turboquant_ops.h"
 #include "weights.h"
 
 namespace {
@@ -126,11 +127,51 @@ void quantize_blocks(int gtype, torch::Tensor x, torch::Tensor out) {
   vmc::quantize_blocks(gtype, ptr<float>(x), x.numel(), out.data_ptr(), cur_stream());
 }
 
+// TurboQuant layer description from Python: meta = [slot, mse_bytes, key_packed, val_bytes, key_bits,
+// value_bits, norm_correction, key_fp8, rot_seed, layer].
+vmc::TqDev make_tq(torch::Tensor cache, const std::vector<int64_t>& meta, torch::Tensor centroids,
+                   torch::Tensor midpoints) {
+  TORCH_CHECK(meta.size() == 10, "turboquant: meta must have 10 entries");
+  TORCH_CHECK(cache.scalar_type() == torch::kUInt8 && cache.is_cuda(), "turboquant: cache must be uint8 CUDA");
+  TORCH_CHECK(centroids.scalar_type() == torch::kFloat32 && midpoints.scalar_type() == torch::kFloat32,
+              "turboquant: fp32 centroid tables");
+  vmc::TqDev t;
+  t.cache = cache.data_ptr<uint8_t>();
+  t.slot = static_cast<int>(meta[0]);
+  t.mse_bytes = static_cast<int>(meta[1]);
+  t.key_packed = static_cast<int>(meta[2]);
+  t.val_bytes = static_cast<int>(meta[3]);
+  t.key_bits = static_cast<int>(meta[4]);
+  t.value_bits = static_cast<int>(meta[5]);
+  t.norm_correction = static_cast<int>(meta[6]);
+  t.key_fp8 = static_cast<int>(meta[7]);
+  t.rot_seed = static_cast<uint32_t>(meta[8]);
+  t.layer = static_cast<int>(meta[9]);
+  t.centroids = centroids.data_ptr<float>();
+  t.midpoints = midpoints.data_ptr<float>();
+  return t;
+}
+
+void rope_store_tq(torch::Tensor qkv, int64_t nsplit, int64_t split_stride, int64_t T, int64_t Hq, int64_t Hkv,
+                   int64_t D, torch::Tensor pos, torch::Tensor slots, torch::Tensor cos_sin, bool neox,
+                   torch::Tensor q_out, torch::Tensor cache, std::vector<int64_t> meta, torch::Tensor centroids,
+                   torch::Tensor midpoints) {
+  const vmc::TqDev t = make_tq(cache, meta, centroids, midpoints);
+  vmc::rope_store_tq(qkv.data_ptr(), qkv.scalar_type() == torch::kFloat32, static_cast<int>(nsplit), split_stride,
+                     static_cast<int>(T), static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(D),
+                     ptr<int32_t>(pos), ptr<int32_t>(slots), ptr<float>(cos_sin), neox, q_out.data_ptr(), t,
+                     cur_stream());
+}
+
 void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, torch::Tensor ctx_len,
                      torch::Tensor block_tables, int64_t num_reqs, int64_t req_offset, int64_t max_qlen,
                      int64_t total_tokens, int64_t Hq, int64_t Hkv, int64_t D, double scale, bool decode,
                      int64_t splits, c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse,
-                     torch::Tensor out) {
+                     torch::Tensor out, c10::optional<torch::Tensor> tq_cache, std::vector<int64_t> tq_meta,
+                     c10::optional<torch::Tensor> tq_centroids, c10::optional<torch::Tensor> tq_midpoints) {
+  vmc::TqDev tq;
+  const bool use_tq = tq_cache.has_value() && tq_cache->defined();
+  if (use_tq) tq = make_tq(*tq_cache, tq_meta, *tq_centroids, *tq_midpoints);
   vmc::AttnLaunch a;
   a.q = q.data_ptr();
   a.kv = kv.data_ptr();
@@ -151,6 +192,7 @@ void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, t
   a.part_o = opt_ptr<float>(part_o);
   a.part_lse = opt_ptr<float>(part_lse);
   a.out = out.data_ptr();
+  a.tq = use_tq ? &tq : nullptr;
   vmc::paged_attention(a, cur_stream());
 }
 
@@ -267,7 +309,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention", &paged_attention, py::arg("q"), py::arg("kv"), py::arg("q_start"), py::arg("ctx_len"),
         py::arg("block_tables"), py::arg("num_reqs"), py::arg("req_offset"), py::arg("max_qlen"),
         py::arg("total_tokens"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("decode"),
-        py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("out"));
+        py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("out"), py::arg("tq_cache") = py::none(),
+        py::arg("tq_meta") = std::vector<int64_t>{}, py::arg("tq_centroids") = py::none(),
+        py::arg("tq_midpoints") = py::none());
+  m.def("rope_store_tq", &rope_store_tq);
   m.def("embed", &embed);
   m.def("add_rmsnorm", &add_rmsnorm);
   m.def("rope_store", &rope_store);

@@ -27,6 +27,9 @@ def build_parser() -> argparse.ArgumentParser:
                     choices=["auto", "float16", "bfloat16", "fp8_e4m3", "fp8_e5m2", "int8_per_token_head",
                              "fp8_per_token_head", "nvfp4", "turboquant_4bit_nc", "turboquant_k8v4",
                              "turboquant_k3v4_nc", "turboquant_3bit_nc"])
+    ap.add_argument("--tq-rotation-seed", type=int, default=0,
+                    help="TurboQuant: 0 = normalised Hadamard rotation; otherwise random sign flips per layer and "
+                         "KV head before it (a seeded random orthogonal rotation)")
     ap.add_argument("--max-model-len", type=int, default=0)
     ap.add_argument("--gpu-memory-utilization", type=float, default=0.90)
     ap.add_argument("--gpu-safety-margin-mb", type=int, default=256)
@@ -75,6 +78,7 @@ def config_from_args(a) -> VmCConfig:
     cfg.model.max_model_len = a.max_model_len
     c = cfg.cache
     c.kv_cache_dtype = a.kv_cache_dtype
+    c.tq_rotation_seed = a.tq_rotation_seed
     c.gpu_memory_utilization = a.gpu_memory_utilization
     c.gpu_safety_margin_mb = a.gpu_safety_margin_mb
     c.num_gpu_blocks = a.num_gpu_blocks

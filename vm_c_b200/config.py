@@ -72,6 +72,7 @@ class CacheConfig:
     gpu_memory_utilization: float = 0.90
     gpu_safety_margin_mb: int = 256
     kv_cache_dtype: str = "auto"
+    tq_rotation_seed: int = 0        # TurboQuant: 0 = plain Hadamard; else random signs per layer / KV head
     num_gpu_blocks: int = 0          # 0: size from free memory
     enable_prefix_caching: bool = True
     cpu_offload_gb: float = 0.0

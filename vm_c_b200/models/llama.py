@@ -36,6 +36,7 @@ class LayerWeights:
     w_gate_up: ops.TiledWeight | None = None   # rows interleave gate/up (fused SwiGLU)
     w_down: ops.TiledWeight | None = None
     moe: object | None = None      # MoE weights (models/moe.py)
+    index: int = 0                 # layer number
 
 
 @dataclass
@@ -145,7 +146,7 @@ def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int =
         wo = _tile(src, on, dev, c0=tp_rank * hq_local * D, c1=(tp_rank + 1) * hq_local * D)
         lw = LayerWeights(attn_norm=_to_dev(src.rows(blk(i, "attn_norm")), dev).view(-1).float(),
                           ffn_norm=_to_dev(src.rows(blk(i, "ffn_norm")), dev).view(-1).float(),
-                          wqkv=wqkv, qkv_split=split, wo=wo)
+                          wqkv=wqkv, qkv_split=split, wo=wo, index=i)
         if cfg.is_moe:
             from .moe import load_moe_layer
             lw.moe = load_moe_layer(src, cfg, i, dev, tp_rank, tp_size, ep_size)
@@ -291,6 +292,7 @@ class LlamaModel:
         if self.fused:
             comm.setup(max_tokens, self.H)
         self.moe_runner = None
+        self.tq = None  # TurboQuant tables when the KV cache is compressed (set by the runner)
         if cfg.is_moe:
             from .moe import MoERunner
             self.moe_runner = MoERunner(self, max_tokens)
@@ -312,13 +314,21 @@ class LlamaModel:
             out = self._split_view(M, self.qkv_n)
             for w, c0 in zip(lw.wqkv, lw.qkv_split):
                 ops.gemm(x, w, out[:, c0:c0 + w.N], M, ops.OUT_F32_SPLIT, s, split_stride=M * self.qkv_n)
-            ops.rope_store(out, M, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
-                           self.cfg.rope_neox, self.ws.q, kv_layer, nsplit=s, split_stride=M * self.qkv_n)
+            self._rope_store(out, M, m, kv_layer, lw.index, nsplit=s, split_stride=M * self.qkv_n)
             return
         for w, c0 in zip(lw.wqkv, lw.qkv_split):
             ops.gemm(x, w, self.qkv_bf16[:M, c0:c0 + w.N], M, ops.OUT_BF16, 1)
-        ops.rope_store(self.qkv_bf16[:M], M, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
-                       self.cfg.rope_neox, self.ws.q, kv_layer)
+        self._rope_store(self.qkv_bf16[:M], M, m, kv_layer, lw.index)
+
+    def _rope_store(self, qkv, M: int, m: StepMeta, kv_layer: torch.Tensor, layer: int, nsplit=1,
+                    split_stride=0) -> None:
+        if self.tq is None:
+            ops.rope_store(qkv, M, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
+                           self.cfg.rope_neox, self.ws.q, kv_layer, nsplit=nsplit, split_stride=split_stride)
+        else:
+            ops.rope_store_tq(qkv, M, self.hq, self.hkv, self.D, m.positions, m.slot_mapping, self.cos_sin,
+                              self.cfg.rope_neox, self.ws.q, kv_layer, self.tq, layer, nsplit=nsplit,
+                              split_stride=split_stride)
 
     def _row_parallel_norm(self, x: torch.Tensor, w: ops.TiledWeight, M: int, norm_w: torch.Tensor) -> None:
         """Row-parallel GEMM, (TP reduce), residual add + RMSNorm into ws.h."""
@@ -402,6 +412,7 @@ class LlamaModel:
 
     def _attention(self, kv_layer: torch.Tensor, m: StepMeta) -> None:
         ws = self.ws
+        tq = None if self.tq is None else (kv_layer, self.tq)
         nd = m.num_decode
         G = self.hq // self.hkv
         if nd > 0:
@@ -409,10 +420,11 @@ class LlamaModel:
             splits = self.attn_splits if (self.attn_splits > 1 and dec_ok and nd <= self.max_samples) else 1
             ops.paged_attention(ws.q, kv_layer, m.q_start, m.ctx_len, m.block_tables, nd, 0, m.decode_qlen,
                                 nd * m.decode_qlen, self.hq, self.hkv, self.D, self.scale, dec_ok, ws.attn,
-                                splits, ws.part_o if splits > 1 else None, ws.part_lse if splits > 1 else None)
+                                splits, ws.part_o if splits > 1 else None, ws.part_lse if splits > 1 else None,
+                                tq=tq)
         if m.R > nd:
             ops.paged_attention(ws.q, kv_layer, m.q_start, m.ctx_len, m.block_tables, m.R - nd, nd, m.max_qlen,
-                                m.T, self.hq, self.hkv, self.D, self.scale, False, ws.attn)
+                                m.T, self.hq, self.hkv, self.D, self.scale, False, ws.attn, tq=tq)
 
     def _sample(self, S: int, params: torch.Tensor, out_tok: torch.Tensor, out_lp) -> None:
         if self.tp > 1:

@@ -29,7 +29,23 @@ GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224
 
 def kv_bytes_per_block(cfg: VmCConfig, hkv_local: int, dtype_bytes: int = 2) -> int:
     m = cfg.model
+    if is_turboquant(cfg.cache.kv_cache_dtype):
+        from .. import _native
+        slot = _native.host().tq_layout(cfg.cache.kv_cache_dtype, m.head_dim)["slot_aligned"]
+        return m.n_layers * cfg.cache.block_size * hkv_local * slot
     return m.n_layers * 2 * hkv_local * cfg.cache.block_size * m.head_dim * dtype_bytes
+
+
+def is_turboquant(kv_cache_dtype: str) -> bool:
+    return kv_cache_dtype.startswith("turboquant")
+
+
+def check_kv_cache_dtype(kv_cache_dtype: str) -> None:
+    """bf16 pages (auto / bfloat16) and the four TurboQuant layouts are implemented; the other
+    names the reference's flag accepts are rejected here instead of silently served as bf16."""
+    ok = ("auto", "bfloat16", "turboquant_4bit_nc", "turboquant_k8v4", "turboquant_k3v4_nc", "turboquant_3bit_nc")
+    if kv_cache_dtype not in ok:
+        raise ValueError(f"--kv-cache-dtype {kv_cache_dtype!r} is not supported (supported: {', '.join(ok)})")
 
 
 class GpuModelRunner(ModelRunner):
@@ -57,7 +73,13 @@ class GpuModelRunner(ModelRunner):
         self.comm = comm
         sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
         self._decode_slots = sms * max(1, ops.C().attn_decode_ctas_per_sm(self.model.D))
-        # KV cache: [L, num_blocks, 2, Hkv_local, block_size, D] bf16, zero-filled (finite).
+        # KV cache: bf16 [L, num_blocks, 2, Hkv_local, block_size, D], or TurboQuant slots
+        # uint8 [L, num_blocks, block_size, Hkv_local, slot]; zero-filled (finite).
+        check_kv_cache_dtype(cfg.cache.kv_cache_dtype)
+        self.tq = None
+        if is_turboquant(cfg.cache.kv_cache_dtype):
+            self.tq = ops.TqTables(cfg.cache.kv_cache_dtype, m.head_dim, self.dev, rot_seed=cfg.cache.tq_rotation_seed)
+        self.model.tq = self.tq
         per_block = kv_bytes_per_block(cfg, self.model.hkv)
         max_blocks_per_seq = (m.max_model_len + cfg.cache.block_size - 1) // cfg.cache.block_size + 1
         want = cfg.cache.num_gpu_blocks
@@ -69,10 +91,16 @@ class GpuModelRunner(ModelRunner):
             want = max(16, budget // per_block)
             want = min(want, 2 * s.max_num_seqs * max_blocks_per_seq + 1)
         self.num_kv_blocks = int(want)
-        self.kv = torch.zeros(m.n_layers, self.num_kv_blocks, 2, self.model.hkv, cfg.cache.block_size, m.head_dim,
-                              dtype=torch.bfloat16, device=self.dev)
-        log.info("KV cache: %d blocks x %d tokens (%.2f GB)", self.num_kv_blocks, cfg.cache.block_size,
-                 self.kv.numel() * 2 / 1e9)
+        if self.tq is None:
+            self.kv = torch.zeros(m.n_layers, self.num_kv_blocks, 2, self.model.hkv, cfg.cache.block_size,
+                                  m.head_dim, dtype=torch.bfloat16, device=self.dev)
+        else:
+            self.kv = torch.zeros(m.n_layers, self.num_kv_blocks, cfg.cache.block_size, self.model.hkv,
+                                  self.tq.slot_bytes, dtype=torch.uint8, device=self.dev)
+        self.kv_bytes_per_token = per_block // cfg.cache.block_size
+        log.info("KV cache (%s): %d blocks x %d tokens (%.2f GB, %d bytes/token on this rank)",
+                 cfg.cache.kv_cache_dtype, self.num_kv_blocks, cfg.cache.block_size,
+                 self.kv.numel() * self.kv.element_size() / 1e9, self.kv_bytes_per_token)
         self.params_dev = torch.zeros(self.max_tokens * 40, dtype=torch.uint8, device=self.dev)
         self.params_host = torch.zeros(self.max_tokens * 40, dtype=torch.uint8).pin_memory()
         self.tok_dev = torch.zeros(self.max_tokens, dtype=torch.int32, device=self.dev)

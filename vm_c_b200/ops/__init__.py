@@ -193,6 +193,47 @@ def rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv, nsplit=
     _count()
 
 
+class TqTables:
+    """TurboQuant layout of one model (csrc/host/turboquant.hpp) and its Lloyd-Max tables on the
+    device. ``layer`` selects the random rotation of a layer (set per call through ``for_layer``)."""
+
+    def __init__(self, method: str, head_dim: int, device, rot_seed: int = 0):
+        from .. import _native
+        h = _native.host()
+        self.method = method
+        self.layout = dict(h.tq_layout(method, head_dim))
+        self.head_dim = head_dim
+        self.rot_seed = int(rot_seed) & 0xFFFFFFFF
+        L = self.layout
+        if L["key_fp8"]:
+            cent = [0.0]
+        else:
+            cent = list(h.lloyd_max_gaussian(L["key_bits"], 1.0 / math.sqrt(head_dim)))
+        mids = [(a + b) / 2 for a, b in zip(cent[:-1], cent[1:])] or [0.0]
+        self.centroids = torch.tensor(cent, dtype=torch.float32, device=device)
+        self.midpoints = torch.tensor(mids, dtype=torch.float32, device=device)
+        self.layer = 0
+
+    @property
+    def slot_bytes(self) -> int:
+        return self.layout["slot_aligned"]
+
+    def meta(self) -> list[int]:
+        L = self.layout
+        return [L["slot_aligned"], L["mse_bytes"], L["key_packed"], L["val_bytes"], L["key_bits"], L["value_bits"],
+                int(L["norm_correction"]), int(L["key_fp8"]), self.rot_seed, self.layer]
+
+
+def rope_store_tq(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, cache, tab: TqTables, layer: int,
+                  nsplit=1, split_stride=0):
+    """RoPE + rotation of Q (written to q_out) and TurboQuant quantisation of K / V into ``cache``
+    (one layer: uint8 [num_blocks, 16, Hkv, slot])."""
+    tab.layer = layer
+    C().rope_store_tq(qkv, nsplit, split_stride, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, cache, tab.meta(),
+                      tab.centroids, tab.midpoints)
+    _count()
+
+
 def swiglu(gu, T, F, out, interleaved=False, nsplit=1, split_stride=0):
     C().swiglu(gu, nsplit, split_stride, T, F, interleaved, out)
     _count()
@@ -204,9 +245,17 @@ def gather_rows(src, idx, n, H, dst):
 
 
 def paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq, Hkv,
-                    D, scale, decode, out, splits=1, part_o=None, part_lse=None):
-    C().paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq, Hkv,
-                        D, scale, decode, splits, part_o, part_lse, out)
+                    D, scale, decode, out, splits=1, part_o=None, part_lse=None, tq=None):
+    """Paged attention over bf16 pages ``kv``, or over a TurboQuant cache layer when ``tq`` is a
+    (cache layer, TqTables) pair (``kv`` is then ignored)."""
+    if tq is None:
+        C().paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq,
+                            Hkv, D, scale, decode, splits, part_o, part_lse, out)
+    else:
+        cache, tab = tq
+        C().paged_attention(q, cache, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens,
+                            Hq, Hkv, D, scale, decode, splits, part_o, part_lse, out, cache, tab.meta(),
+                            tab.centroids, tab.midpoints)
     _count(2 if (decode and splits > 1) else 1)
 
 
