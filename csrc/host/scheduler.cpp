@@ -379,6 +379,9 @@ std::vector<StepEvent> Scheduler::update(const Plan& plan, const std::vector<std
     s.num_computed = e.start + e.num_tokens;
     if (was_prefill && s.num_computed >= static_cast<int64_t>(s.prompt.size())) cache_prompt_blocks(s);
     if (!toks) continue;
+    // Speculative decoding: a decode entry that returns m > 1 tokens had m - 1 of them verified in
+    // the same step (their KV is written); only the last one still has to be processed.
+    if (!was_prefill && toks->size() > 1) s.num_computed += static_cast<int64_t>(toks->size()) - 1;
     StepEvent ev{s.id, {}, false, FinishReason::NONE};
     for (int32_t tok : *toks) {
       s.output.push_back(tok);

@@ -214,30 +214,44 @@ class LLMEngine:
     def step(self) -> list[RequestOutput]:
         """Run one scheduler step; returns outputs of requests that produced tokens or finished."""
         self._drain()
+        spec = getattr(self.runner, "spec", None)
         plan = self.sched.schedule()
         for iid in plan.preempted:
             self.metrics.preemptions += 1
+            if spec is not None:
+                spec.forget(int(iid))
         if len(plan) == 0:
             return []
         t0 = time.perf_counter()
         pen = self._penalties(plan, plan.num_sample)
         all_decode = plan.num_decode == len(plan)
+        sample_ids = plan.sample_ids()
+        # Speculate on all-decode steps whose requests are all greedy and penalty-free.
+        speculate = spec is not None and all_decode and pen is None and \
+            all(self.requests[int(i)].params.greedy for i in sample_ids)
         pad = 0
-        if all_decode and pen is None and hasattr(self.runner, "graph_bucket"):
+        if all_decode and pen is None and not speculate and hasattr(self.runner, "graph_bucket"):
             pad = self.runner.graph_bucket(len(plan))
         self.sched.build_batch(plan, self.layout, self.meta_addr, pad)
         counts = self._counts()
         if not pad:
             counts.R_pad = 0
-        params = self._sample_params(plan, counts.S, counts.R_pad)
-        toks, lps = self.runner.execute(self.meta, counts, params, pen)
-        events = self.sched.update(plan, toks[:counts.S])
+        lp_by_id = {}
+        if speculate:
+            new = spec.step(sample_ids, counts)
+            flat = np.fromiter((t for row in new for t in row), dtype=np.int32)
+            events = self.sched.update(plan, flat, [len(row) for row in new])
+        else:
+            params = self._sample_params(plan, counts.S, counts.R_pad)
+            toks, lps = self.runner.execute(self.meta, counts, params, pen)
+            if spec is not None:  # keep the draft's cache in step with the target's
+                spec.set_batch([e.id for e in plan.entries])
+                spec.shadow(counts)
+            events = self.sched.update(plan, toks[:counts.S])
+            for k, iid in enumerate(sample_ids):
+                lp_by_id[int(iid)] = float(lps[k]) if lps is not None else 0.0
         now = time.perf_counter()
         outs = []
-        lp_by_id = {}
-        sample_ids = plan.sample_ids()
-        for k, iid in enumerate(sample_ids):
-            lp_by_id[int(iid)] = float(lps[k]) if lps is not None else 0.0
         for iid, new_toks, finished, reason in events:
             req = self.requests.get(int(iid))
             if req is None:
@@ -263,6 +277,9 @@ class LLMEngine:
         req.finished = True
         req.finish_reason = reason
         self.sched.release(req.int_id)
+        spec = getattr(self.runner, "spec", None)
+        if spec is not None:
+            spec.forget(req.int_id)
         self.requests.pop(req.int_id, None)
         self.by_name.pop(req.request_id, None)
         self.metrics.record_finish(req)

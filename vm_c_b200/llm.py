@@ -32,7 +32,8 @@ class LLM:
                  enable_prefix_caching: bool = True, enable_chunked_prefill: bool = True,
                  long_prefill_token_threshold: int = 0, scheduling_policy: str = "decode_first",
                  use_cuda_graphs: bool = True, device: Optional[str] = None, tp_rank: int = 0, tp_size: int = 1,
-                 ep_size: int = 1, kv_cache_dtype: str = "auto", tq_rotation_seed: int = 0, comm=None, config: Optional[VmCConfig] = None, warmup: bool = True):
+                 ep_size: int = 1, kv_cache_dtype: str = "auto", tq_rotation_seed: int = 0, draft_model: str = "",
+                 num_speculative_tokens: int = 5, comm=None, config: Optional[VmCConfig] = None, warmup: bool = True):
         import torch
         dev = device or (f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cuda")
         src, mcfg = make_source(model, dev)
@@ -52,6 +53,10 @@ class LLM:
             cfg.cache.kv_cache_dtype = kv_cache_dtype
         if config is None or tq_rotation_seed:
             cfg.cache.tq_rotation_seed = tq_rotation_seed
+        if draft_model:
+            cfg.spec.method = "draft"
+            cfg.spec.draft_model = draft_model
+            cfg.spec.draft_n_max = num_speculative_tokens
         cfg.parallel.tensor_parallel_size = tp_size
         cfg.parallel.expert_parallel_size = ep_size
         cfg.finalize()

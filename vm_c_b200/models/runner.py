@@ -62,13 +62,21 @@ class GpuModelRunner(ModelRunner):
         log.info("weights loaded: %.2f GB in %.1fs", self.weights.bytes_total / 1e9, time.perf_counter() - t0)
         s = cfg.scheduler
         self.max_model_len = m.max_model_len
-        self.max_samples = max(s.max_num_seqs, 1)
+        sp = cfg.spec
+        if sp.method == "mtp":
+            raise ValueError("--spec-method mtp needs next-n prediction layers, which the supported model "
+                             "families do not have; use --spec-method draft --draft-model <gguf>")
+        self.spec_k = sp.draft_n_max if sp.method == "draft" else 0
+        self.num_lookahead_tokens = self.spec_k
+        max_seqs = max(s.max_num_seqs, 1)
+        # Sampled rows: one per request, or k + 1 per request when speculative verification runs.
+        self.max_samples = max_seqs * (1 + self.spec_k)
         self.max_tokens = max(s.max_num_batched_tokens, self.max_samples)
-        self.buckets = [b for b in GRAPH_BUCKETS if b <= self.max_samples]
-        if use_graphs and self.buckets and self.buckets[-1] < self.max_samples:
-            self.buckets.append(self.max_samples)
+        self.buckets = [b for b in GRAPH_BUCKETS if b <= max_seqs]
+        if use_graphs and self.buckets and self.buckets[-1] < max_seqs:
+            self.buckets.append(max_seqs)
         self.use_graphs = use_graphs
-        self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len, comm=comm,
+        self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len + self.spec_k, comm=comm,
                                 attn_splits=16)
         self.comm = comm
         sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
@@ -136,6 +144,8 @@ class GpuModelRunner(ModelRunner):
 
     def bind_layout(self, layout) -> None:
         self.layout = layout
+        if self.spec_k and self.spec is None:
+            self._init_spec()
         L = layout
         md = self.meta_dev
         self.v_ids = md[L.off_input_ids:L.off_input_ids + L.max_tokens]
@@ -146,6 +156,23 @@ class GpuModelRunner(ModelRunner):
         self.v_lidx = md[L.off_logits_idx:L.off_logits_idx + L.max_reqs]
         self.v_bt = md[L.off_block_tables:L.off_block_tables + L.max_reqs * L.max_blocks_per_seq].view(
             L.max_reqs, L.max_blocks_per_seq)
+
+    # -- speculative decoding ------------------------------------------------------------------------
+    spec = None
+
+    def _init_spec(self) -> None:
+        from .. import _native
+        from ..llm import make_source
+        from ..speculative.draft import DraftSpeculator
+        sp = self.cfg.spec
+        if not sp.draft_model:
+            raise ValueError("--spec-method draft needs --draft-model")
+        src, dcfg = make_source(sp.draft_model, str(self.dev))
+        spec_layout = _native.host().BatchLayout(self.max_tokens, self.max_samples, self.layout.max_blocks_per_seq)
+        self.tok_spec = torch.zeros(self.max_samples, dtype=torch.int32, device=self.dev)
+        self.tok_spec_host = torch.zeros(self.max_samples, dtype=torch.int32).pin_memory()
+        self.spec = DraftSpeculator(self, src, dcfg, self.spec_k, comm=self.comm, layout=spec_layout)
+        log.info("speculative decoding: draft %s, k = %d", sp.draft_model, self.spec_k)
 
     def _meta(self, T, R, S, nd, max_qlen) -> StepMeta:
         return StepMeta(self.v_ids, self.v_pos, self.v_slots, self.v_qs, self.v_ctx, self.v_bt, self.v_lidx,
