@@ -102,12 +102,19 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
       : "memory");
   return ok != 0;
 }
+#ifndef VMC_MBAR_SLEEP_NS
+#define VMC_MBAR_SLEEP_NS 20000
+#endif
 // Bounded wait (about 2 s of SM clock): returns false (and records `code` in *err) when it expires.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    if constexpr (VMC_MBAR_SLEEP_NS > 0) {
+      if (mbar_try_wait_sleep(bar, parity, VMC_MBAR_SLEEP_NS)) return true;
+    } else {
+      if (mbar_try_wait(bar, parity)) return true;
+    }
     if (clock64() - t0 > (4ll << 30)) break;
   }
   if (err) atomicCAS(err, 0u, code);

@@ -292,6 +292,15 @@ __device__ __forceinline__ void trace_at(const GemmArgs& a, int slot) {
     if (a.trace != nullptr && blockIdx.x == 0 && slot < 512) a.trace[slot] = clock64();
   }
 }
+// Diagnostic builds (-DVMC_GEMM_SKIP=mask) drop stages of the decode kernel to expose how much of
+// its time each stage costs: 1 dequant arithmetic, 2 MMAs, 4 weight loads, 8 TMEM stores. The
+// outputs of such builds are meaningless; the default build skips nothing. 16 leaves the kernel
+// right after its set-up (the fixed cost of a launch); 32 drops the activation loads, 64 the
+// epilogue's reads and stores.
+#ifndef VMC_GEMM_SKIP
+#define VMC_GEMM_SKIP 0
+#endif
+
 struct PhaseClock {
   long long t = 0;
   __device__ __forceinline__ void start() {
@@ -320,6 +329,13 @@ struct Unit {
   int row0;     // first row of X / of the output covered by the tile
   int rows;     // valid rows of the tile
   size_t wtile; // byte offset of the unit's first weight tile (chunk 0)
+  int rot;      // the decode kernel walks chunks c0 + (i + rot) % (c1 - c0), i = 0 .. c1 - c0 - 1
+  __device__ __forceinline__ int nchunks() const { return c1 - c0; }
+  __device__ __forceinline__ int chunk(int i) const {
+    const int n = c1 - c0;
+    const int j = i + rot;
+    return c0 + (j >= n ? j - n : j);
+  }
 };
 __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u, int tile_bytes) {
   Unit r;
@@ -350,6 +366,10 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u, int tile_bytes
     r.row0 = r.mt * a.bn;
     r.rows = min(a.bn, a.M - r.row0);
   }
+  // Units that run at the same time start at different K chunks, so that the CTAs do not all read
+  // the same activation tile from L2 at once.
+  const int n = r.c1 - r.c0;
+  r.rot = n > 0 ? u % n : 0;
   return r;
 }
 
@@ -586,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
             const int m = m_base + j;
             if ((lane & 1) == 0 && m < m_end) {
-              const float y = mine / (1.f + __expf(-mine)) * other;
+              const float y = __fdividef(mine, 1.f + __expf(-mine)) * other;
               const int f = w.nt * 64 + (n_local >> 1);
               if (f < args.N / 2)
                 reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
@@ -636,10 +656,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // commit in an issuing thread's loop stalls its issue stream for about as long, so a pipeline in
 // which one MMA thread waits for all dequant warps (and they for it) leaves the tensor pipe idle.
 // The 16 dequant warps therefore form two groups; group G owns K substeps 2G and 2G+1 (128 K) of
-// every chunk, writes them into its own TMEM A slots (three, so the dequant runs up to two chunks
-// ahead of the MMA) and has its own MMA-issuing warp accumulating into its own TMEM accumulator;
-// the epilogue adds the two. One group's handshakes overlap the other group's MMAs.
-// TMEM: accumulators [0, 128), A slots [128, 512) (64 columns = 128 K each).
+// every chunk, writes them into its own TMEM A slots (two, so the dequant runs a chunk ahead of the
+// MMA) and has its own MMA-issuing warp accumulating into its own TMEM accumulator;
+// the epilogue adds the two. One group's handshakes overlap the other group's MMAs. Accumulators
+// are double-buffered per group, so a unit's epilogue (measured at ~5 us for the SwiGLU output of
+// a 128-row unit while the dequant warps share the SM) overlaps the next unit's MMAs.
+// TMEM: accumulators [0, 256) (buffer b, group G at (2b + G) * 64), A slots [256, 512)
+// (64 columns = 128 K each).
 //
 // Warp roles in a 768-thread CTA:
 //   warp 0       weight producer (raw ring, one cp.async.bulk per tile) and TMEM allocation
@@ -651,8 +674,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 constexpr int kDThreads = 768;
 constexpr int kDFirstDq = 4;
 constexpr int kDFirstEpi = 20;
-constexpr int kDSlots = 3;
-constexpr uint32_t kDACol = 128;
+constexpr int kDSlots = 2;
+constexpr uint32_t kDACol = 256;
 
 // Q4_K scale / negated min of sub-block J (bf16x2 splats) from the 16-byte block header (fp16 d,
 // fp16 dmin, 12 bytes of packed 6-bit scales and mins); J is a compile-time constant so the
@@ -731,8 +754,9 @@ struct GemmDPlan {
   __host__ __device__ constexpr int raw_bytes() const { return wf_tile_bytes(wf); }
   __host__ __device__ constexpr int off_raw() const { return b_stages * b_bytes(); }
   __host__ __device__ constexpr int off_bar() const { return off_raw() + raw_stages * raw_bytes(); }
-  // a_full[6], slot_free[6], acc_full[2], acc_empty, b_full/b_empty, raw_full/raw_empty
-  __host__ __device__ constexpr int nbars() const { return 15 + 2 * b_stages + 2 * raw_stages; }
+  // a_full[2 * kDSlots], slot_free[2 * kDSlots], acc_full[4], acc_empty[2], b_full/b_empty,
+  // raw_full/raw_empty
+  __host__ __device__ constexpr int nbars() const { return 4 * kDSlots + 6 + 2 * b_stages + 2 * raw_stages; }
   __host__ __device__ constexpr int total() const { return off_bar() + nbars() * 8 + 16 + 1024; }
 };
 
@@ -767,15 +791,15 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr GemmDPlan P = make_dplan(WF, BN);
   constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
-  static_assert(2 * kAccCols <= kDACol && kDACol + 2 * kDSlots * 64 <= 512, "TMEM plan");
+  static_assert(4 * kAccCols <= kDACol && kDACol + 2 * kDSlots * 64 <= 512, "TMEM plan");
   uint8_t* sB = smem;
   uint8_t* sRaw = smem + P.off_raw();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_bar());
   uint64_t* a_full = bars;                       // [group * kDSlots + slot], 8 dequant-warp arrivals
   uint64_t* slot_free = a_full + 2 * kDSlots;    // [group * kDSlots + slot], MMA commit
-  uint64_t* acc_full = slot_free + 2 * kDSlots;  // [group], MMA commit at the end of a unit
-  uint64_t* acc_empty = acc_full + 2;            // 4 epilogue-warp arrivals
-  uint64_t* b_full = acc_empty + 1;
+  uint64_t* acc_full = slot_free + 2 * kDSlots;  // [buffer * 2 + group], MMA commit at the end of a unit
+  uint64_t* acc_empty = acc_full + 4;            // [buffer], 4 epilogue-warp arrivals
+  uint64_t* b_full = acc_empty + 2;
   uint64_t* b_empty = b_full + P.b_stages;       // one commit per group
   uint64_t* raw_full = b_empty + P.b_stages;
   uint64_t* raw_empty = raw_full + P.raw_stages;  // 16 dequant-warp arrivals
@@ -791,8 +815,8 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       mbar_init(&a_full[i], 8);
       mbar_init(&slot_free[i], 1);
     }
-    for (int i = 0; i < 2; ++i) mbar_init(&acc_full[i], 1);
-    mbar_init(acc_empty, 4);
+    for (int i = 0; i < 4; ++i) mbar_init(&acc_full[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&acc_empty[i], 4);
     for (int i = 0; i < P.b_stages; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 2);
@@ -812,7 +836,7 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int first = blockIdx.x, step = gridDim.x;
+  const int first = (VMC_GEMM_SKIP & 16) != 0 ? args.units : static_cast<int>(blockIdx.x), step = gridDim.x;
   // Grouped mode: the unit list depends on row counts written by the previous kernels, so every
   // role (the weight producer included) waits for them before enumerating its units.
   if (args.groups > 0) pdl_wait();
@@ -827,11 +851,16 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
         const Unit w = unit_of(args, u, wf_tile_bytes(WF));
         if (w.rows <= 0) continue;
         const uint8_t* wbase = args.w + w.wtile;
-        for (int c = w.c0; c < w.c1; ++c) {
+        for (int i = 0; i < w.nchunks(); ++i) {
+          const int c = w.chunk(i);
           if (!mbar_wait(&raw_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-          mbar_arrive_expect_tx(&raw_full[st], wf_tile_bytes(WF));
-          bulk_load_evict_first(sRaw + st * P.raw_bytes(), wbase + static_cast<size_t>(c) * wf_tile_bytes(WF),
-                                wf_tile_bytes(WF), &raw_full[st], pol);
+          if constexpr ((VMC_GEMM_SKIP & 4) != 0) {
+            mbar_arrive(&raw_full[st]);
+          } else {
+            mbar_arrive_expect_tx(&raw_full[st], wf_tile_bytes(WF));
+            bulk_load_evict_first(sRaw + st * P.raw_bytes(), wbase + static_cast<size_t>(c) * wf_tile_bytes(WF),
+                                  wf_tile_bytes(WF), &raw_full[st], pol);
+          }
           if (++st == P.raw_stages) { st = 0; ph ^= 1; }
         }
       }
@@ -845,12 +874,17 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       for (int u = first; u < args.units && !*abort_flag; u += step) {
         const Unit w = unit_of(args, u, wf_tile_bytes(WF));
         if (w.rows <= 0) continue;
-        for (int c = w.c0; c < w.c1; ++c) {
+        for (int i = 0; i < w.nchunks(); ++i) {
+          const int c = w.chunk(i);
           if (!mbar_wait(&b_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
-          mbar_arrive_expect_tx(&b_full[st], P.b_bytes());
+          if constexpr ((VMC_GEMM_SKIP & 32) != 0) {
+            mbar_arrive(&b_full[st]);
+          } else {
+            mbar_arrive_expect_tx(&b_full[st], P.b_bytes());
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            tma_load_2d(sB + st * P.b_bytes() + i * P.b_box(), &xmap, &b_full[st], (c * 4 + i) * 64, w.row0);
+            for (int i = 0; i < 4; ++i)
+              tma_load_2d(sB + st * P.b_bytes() + i * P.b_box(), &xmap, &b_full[st], (c * 4 + i) * 64, w.row0);
+          }
           if (++st == P.b_stages) { st = 0; ph ^= 1; }
         }
       }
@@ -860,9 +894,8 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
     if (lane == 0) {
       const int G = warp - 2;
       constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
-      const uint32_t d = tmem + static_cast<uint32_t>(G) * kAccCols;
-      int g = 0;  // CTA-wide chunk counter
-      uint32_t acc_ph = 0;
+      int g = 0;   // CTA-wide chunk counter
+      int ui = 0;  // units of this CTA so far: accumulator buffer ui & 1
       bool ok = true;
       PhaseClock pc;
       long long ph_acc = 0, ph_a = 0, ph_b = 0, ph_mma = 0;
@@ -870,10 +903,12 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       for (int u = first; u < args.units && ok && !*abort_flag; u += step) {
         const Unit w = unit_of(args, u, wf_tile_bytes(WF));
         if (w.rows <= 0) continue;
-        if (!mbar_wait(acc_empty, acc_ph ^ 1, args.err, kErrGemmWait)) { ok = false; break; }
+        const int buf = ui & 1;
+        if (!mbar_wait(&acc_empty[buf], ((ui >> 1) & 1) ^ 1, args.err, kErrGemmWait)) { ok = false; break; }
         ph_acc += pc.lap();
         tc_fence_after();
-        for (int c = w.c0; c < w.c1; ++c, ++g) {
+        const uint32_t d = tmem + static_cast<uint32_t>(2 * buf + G) * kAccCols;
+        for (int i = 0; i < w.nchunks(); ++i, ++g) {
           const int k = g % kDSlots;
           const int bst = g % P.b_stages;
           ph_mma += pc.lap();
@@ -888,14 +923,15 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
             const uint64_t b0 = umma_sdesc_sw128(smem_u32(sB + bst * P.b_bytes() + (2 * G + h) * P.b_box()));
 #pragma unroll
             for (int k4 = 0; k4 < 4; ++k4)
-              umma_bf16_ts(d, a0 + h * 32 + 8 * k4, b0 + 2 * k4, idesc, (c > w.c0 || h > 0 || k4 > 0) ? 1u : 0u);
+              if constexpr ((VMC_GEMM_SKIP & 2) == 0)
+                umma_bf16_ts(d, a0 + h * 32 + 8 * k4, b0 + 2 * k4, idesc, (i > 0 || h > 0 || k4 > 0) ? 1u : 0u);
           }
           umma_commit(&slot_free[G * kDSlots + k]);
           umma_commit(&b_empty[bst]);
         }
         if (!ok) break;
-        umma_commit(&acc_full[G]);
-        acc_ph ^= 1;
+        umma_commit(&acc_full[2 * buf + G]);
+        ++ui;
       }
       if (!ok) *abort_flag = 1;
       ph_mma += pc.lap();
@@ -922,13 +958,22 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       const Unit w = unit_of(args, u, wf_tile_bytes(WF));
         if (w.rows <= 0) continue;
       bool ok = true;
-      for (int c = w.c0; c < w.c1; ++c, ++g) {
+      for (int i = 0; i < w.nchunks(); ++i, ++g) {
         ph_rest += pc.lap();
         if (!mbar_wait(&raw_full[rst], rph, args.err, kErrGemmWait)) { ok = false; break; }
         ph_raw += pc.lap();
         const uint8_t* row = sRaw + rst * P.raw_bytes() + (32 * q + lane) * wf_row_bytes(WF);
         uint32_t o[32];
-        dq_row64<WF>(row, s, o);
+        if constexpr ((VMC_GEMM_SKIP & 1) != 0) {
+          const uint4* r4 = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 v = r4[i & 3];
+            o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
+          }
+        } else {
+          dq_row64<WF>(row, s, o);
+        }
         __syncwarp();
         ph_dq += pc.lap();
         if (lane == 0) mbar_arrive(&raw_empty[rst]);
@@ -937,9 +982,13 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
         ph_slot += pc.lap();
         tc_fence_after();
         const uint32_t ta = tmem + lane_base + kDACol + static_cast<uint32_t>(G * kDSlots + k) * 64 + h * 32;
-        tmem_st16(ta, o);
-        tmem_st16(ta + 16, o + 16);
-        tmem_st_wait();
+        if constexpr ((VMC_GEMM_SKIP & 8) == 0) {
+          tmem_st16(ta, o);
+          tmem_st16(ta + 16, o + 16);
+          tmem_st_wait();
+        } else {
+          if (o[0] == 0x7fffffffu && o[31] == 0x7fffffffu) args.err[0] = o[7];  // keeps the loads live
+        }
         tc_fence_before();
         __syncwarp();
         ph_st += pc.lap();
@@ -961,23 +1010,30 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
     pdl_wait();  // outputs may still be read by the previous kernel
     const int q = warp & 3;
     const int n_local = 32 * q + lane;
-    uint32_t acc_ph = 0;
+    int ui = 0;
+    PhaseClock pc;
+    long long ph_ew = 0, ph_ld = 0, ph_out = 0;
+    pc.start();
     for (int u = first; u < args.units && !*abort_flag; u += step) {
       const Unit w = unit_of(args, u, wf_tile_bytes(WF));
         if (w.rows <= 0) continue;
-      const bool ok = mbar_wait(&acc_full[0], acc_ph, args.err, kErrGemmWait) &&
-                      mbar_wait(&acc_full[1], acc_ph, args.err, kErrGemmWait);
+      const int buf = ui & 1;
+      const uint32_t acc_ph = (ui >> 1) & 1;
+      const bool ok = mbar_wait(&acc_full[2 * buf], acc_ph, args.err, kErrGemmWait) &&
+                      mbar_wait(&acc_full[2 * buf + 1], acc_ph, args.err, kErrGemmWait);
       if (!ok) { *abort_flag = 1; break; }
+      ph_ew += pc.lap();
       tc_fence_after();
-      const uint32_t d = tmem + (static_cast<uint32_t>(32 * q) << 16);
+      const uint32_t d = tmem + static_cast<uint32_t>(2 * buf) * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
       float* outf = reinterpret_cast<float*>(args.out);
       if (args.out_mode == kGemmOutF32Split) outf += w.split * args.split_stride;
 #pragma unroll 1
-      for (int cb = 0; cb < BN; cb += 16) {
+      for (int cb = 0; cb < ((VMC_GEMM_SKIP & 64) != 0 ? 0 : BN); cb += 16) {
         uint32_t v[16], t[16];
         tmem_ld16(d + static_cast<uint32_t>(cb), v);
         tmem_ld16(d + kAccCols + static_cast<uint32_t>(cb), t);
         tmem_ld_wait();
+        ph_ld += pc.lap();
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
         const int m_base = w.row0 + cb;
@@ -989,7 +1045,7 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
             const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
             const int m = m_base + j;
             if ((lane & 1) == 0 && m < m_end) {
-              const float y = mine / (1.f + __expf(-mine)) * other;
+              const float y = __fdividef(mine, 1.f + __expf(-mine)) * other;
               const int f = w.nt * 64 + (n_local >> 1);
               if (f < args.N / 2)
                 reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
@@ -1014,8 +1070,14 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
-      acc_ph ^= 1;
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      ++ui;
+      ph_out += pc.lap();
+    }
+    if (lane == 0) {
+      phase_add(args, 13, ph_ew);
+      phase_add(args, 14, ph_ld);
+      phase_add(args, 15, ph_out);
     }
   }
   tc_fence_before();

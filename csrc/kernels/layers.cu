@@ -178,7 +178,7 @@ __global__ void swiglu_kernel(const TI* __restrict__ gu, int nsplit, int64_t spl
       u += gu[sp * split_stride + iu];
     }
   }
-  out[i] = __float2bfloat16(g / (1.f + __expf(-g)) * u);
+  out[i] = __float2bfloat16(__fdividef(g, 1.f + __expf(-g)) * u);
 }
 
 // ---- gather rows (bf16) --------------------------------------------------------------------

@@ -64,7 +64,7 @@ def build_cuda(verbose: bool = False):
                                 "-Xptxas=-v" if os.environ.get("VMC_PTXAS_VERBOSE") else "-Xptxas=-O3",
                                 "-DNDEBUG", "-U__CUDA_NO_HALF_OPERATORS__",
                                 "-U__CUDA_NO_HALF_CONVERSIONS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
-                                "-U__CUDA_NO_HALF2_OPERATORS__"]
+                                "-U__CUDA_NO_HALF2_OPERATORS__"] + os.environ.get("VMC_NVCC_EXTRA", "").split()
     return load(name="_cuda", sources=cuda_sources(),
                 extra_cflags=["-O3", "-std=c++17"], extra_cuda_cflags=cuda_flags,
                 extra_include_paths=[str(CSRC / "kernels"), str(CSRC / "host")],
