@@ -65,8 +65,10 @@ __host__ __device__ constexpr GemmSmemPlan make_plan(int wf, int bn) {
   const bool quant = wf != kWfBF16;
   p.b_stages = 2;
   p.raw_stages = quant ? 2 : 0;
-  // Quantized formats fill A in whole chunks (4 stages); two chunks double-buffer when they fit.
+  // Quantized formats: the dequant warps fill A one 64-K stage at a time, so any ring of at least
+  // one chunk (4 stages) works; 6 stages let the next chunk start while the MMA drains this one.
   p.a_stages = quant ? 8 : 2;
+  if (quant && p.total() > budget) p.a_stages = 6;
   if (quant && p.total() > budget) p.a_stages = 4;
   const int b_cap = bn <= 64 ? 16 : 6;
   bool grew = true;
@@ -521,10 +523,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   } else if (warp < kFirstDqWarp + kDequantWarps) {
     // ---------------- dequant (quantized formats) ----------------
-    // Each warp owns 16 rows of the tile for a whole 256-K chunk (4 A stages): one proxy fence per
-    // chunk instead of one per 64-K stage keeps the fence latency off the per-stage critical path.
+    // Each warp owns 16 rows of the tile. A stages are filled and handed to the MMA one at a time
+    // (one proxy fence per 64-K stage), so the dequant of the next chunk overlaps the MMAs of the
+    // current one instead of waiting for its whole chunk of stages to drain.
     if constexpr (quant) {
-      static_assert(P.a_stages % 4 == 0, "quantized plans use whole chunks of A stages");
+      static_assert(P.a_stages >= 4, "a chunk needs four A stages");
       const int t = threadIdx.x - kFirstDqWarp * 32;  // 0..255
       const int r = t >> 1, h = t & 1;
       uint32_t sw_off[4];
@@ -540,13 +543,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           if (!mbar_wait(&raw_full[rst], rph, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
           if (warp == kFirstDqWarp && lane == 0) trace_at(args, 128 + (c - w.c0));
           const uint8_t* row = sRaw + rst * P.raw_bytes() + r * wf_row_bytes(WF);
-          // All four A stages of this chunk must be free (the MMA consumes them in order).
-#pragma unroll 1
-          for (int sub = 0; sub < SUBS; ++sub) {
-            if (!mbar_wait(&a_empty[st + sub], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
-          }
-          if (!ok) break;
-          uint8_t* a0 = sA + st * P.a_bytes();
           Q4KChunk qc;
           if constexpr (WF == kWfQ4K) q4k_prep(row, h, qc);
 #pragma unroll
@@ -555,24 +551,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             if constexpr (WF == kWfQ4K) q4k_sub(row, sub, h, qc, o);
             else if constexpr (WF == kWfQ6K) dq_q6k(row, sub, h, o);
             else dq_q8_0(row, sub, h, o);
-            uint8_t* a = a0 + sub * P.a_bytes();
+            if (!mbar_wait(&a_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; ok = false; break; }
+            uint8_t* a = sA + st * P.a_bytes();
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
               *reinterpret_cast<uint4*>(a + sw_off[cc]) = make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&a_full[st]);
+              if (sub == SUBS - 1) mbar_arrive(&raw_empty[rst]);
+            }
+            if (++st == P.a_stages) { st = 0; ph ^= 1; }
           }
           if (!ok) break;
           if (warp == kFirstDqWarp && lane == 0) trace_at(args, 160 + (c - w.c0));
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (warp == kFirstDqWarp && lane == 0) trace_at(args, 192 + (c - w.c0));
-          if (lane == 0) {
-#pragma unroll
-            for (int sub = 0; sub < SUBS; ++sub) mbar_arrive(&a_full[st + sub]);
-            mbar_arrive(&raw_empty[rst]);
-          }
-          st += SUBS;
-          if (st == P.a_stages) { st = 0; ph ^= 1; }
           if (++rst == P.raw_stages) { rst = 0; rph ^= 1; }
         }
         if (!ok) break;
