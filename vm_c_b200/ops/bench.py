@@ -3,7 +3,7 @@
     python -m vm_c_b200.ops.bench [case ...] [--reps N]
 
 Cases: gemm:<name> (decode / prefill projections of the 8B model, see GEMM_CASES), attn:decode,
-attn:prefill, norm, rope, swiglu, sample. Each case is timed with CUDA events on the current stream
+attn:prefill (one 2048-token prompt), attn:prefill2 (two 1024-token prompts), norm, rope, swiglu, sample. Each case is timed with CUDA events on the current stream
 after warm-up, with a 256 MB buffer written between repetitions so that every repetition reads its
 inputs from HBM; the median is reported with the achieved bandwidth / FLOP rate. These are the
 cases the committed ncu summaries were captured on.
@@ -31,6 +31,9 @@ GEMM_CASES = {
     "dec1_gu": (GType.Q4_K, 28672, 4096, 1, OUT_SWIGLU),
     "pre_qkv": (GType.Q4_K, 6144, 4096, 2048, OUT_BF16),
     "pre_gu": (GType.Q4_K, 28672, 4096, 2048, OUT_SWIGLU),
+    "pre_o": (GType.Q4_K, 4096, 4096, 2048, OUT_F32_SPLIT),
+    "pre_down": (GType.Q4_K, 4096, 14336, 2048, OUT_F32_SPLIT),
+    "pre_down6": (GType.Q6_K, 4096, 14336, 2048, OUT_F32_SPLIT),
     "pre_bf16": (GType.BF16, 8192, 4096, 2048, OUT_BF16),
 }
 
@@ -94,6 +97,8 @@ def bench_attn(kind: str, reps: int, flush: torch.Tensor) -> str:
     Hq, Hkv, D = 32, 8, 128
     if kind == "decode":
         ctx, ql = [1280] * 64, [1] * 64
+    elif kind == "prefill2":  # two 1024-token prompts: the 2048-token chunked-prefill step of serving
+        ctx, ql = [1024, 1024], [1024, 1024]
     else:
         ctx, ql = [2048], [2048]
     kv, bt, q, qs, cl, T = _paged_setup(ctx, ql, Hq, Hkv, D)
@@ -157,7 +162,8 @@ def main(argv=None) -> None:
     a = ap.parse_args(argv)
     cases = a.cases
     if cases == ["all"]:
-        cases = [f"gemm:{k}" for k in GEMM_CASES] + ["attn:decode", "attn:prefill", "norm", "rope", "swiglu", "sample"]
+        cases = [f"gemm:{k}" for k in GEMM_CASES] + ["attn:decode", "attn:prefill", "attn:prefill2", "norm", "rope",
+                                                      "swiglu", "sample"]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for c in cases:
         if c.startswith("gemm:"):
