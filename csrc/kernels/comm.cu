@@ -6,12 +6,13 @@
 // op, src/official/llama/models/llama.cpp:171,196,221), which is followed by a separate residual add
 // and RMSNorm in the ggml graph.
 //
-//  * ar_add_rmsnorm_kernel: the row-parallel GEMM of every rank writes its fp32 partial into its
-//    own symmetric buffer; this kernel then (1) signals every peer and waits for every peer's
-//    signal (epoch flags, release/acquire at system scope, bounded spin), (2) reads the partial rows
-//    of all ranks over NVLink in rank order (bit-identical result on every rank), (3) adds the
-//    residual stream, (4) applies RMSNorm and writes the normalised bf16 activations for the next
-//    GEMM. One-shot all-reduce + residual + norm in a single kernel.
+//  * ar_add_rmsnorm_kernel: the row-parallel GEMM of every rank writes its fp32 split-K partials
+//    into its own symmetric buffer; this kernel then (1) sums this rank's splits locally into split
+//    slice 0, (2) signals every peer and waits for every peer's signal (epoch flags,
+//    release/acquire at system scope, bounded spin), (3) reads slice 0 of all ranks over NVLink and
+//    adds them in rank order (bit-identical result on every rank), (4) adds the residual stream,
+//    (5) applies RMSNorm and writes the normalised bf16 activations for the next GEMM. One-shot
+//    all-reduce + residual + norm in a single kernel.
 //
 // Synchronisation: CTA b of every rank owns flag slot b; its participation count (epoch) advances
 // identically on all ranks because every rank launches the same sequence of calls with the same
@@ -38,18 +39,50 @@ constexpr int kMaxRanks = 8;
 constexpr int kArThreads = 256;
 constexpr int kMaxPer = 32;  // floats per thread held in registers (H <= 256 * 4 * 8 = 8192)
 
+// NR = number of ranks (compile-time, so that the loads of all ranks' partials are issued
+// back to back before the first add).
+//
+// Two phases around one flag exchange. (1) Each CTA sums this rank's split-K partials of its rows
+// (local memory) into split slice 0 of its own symmetric buffer, then publishes with a system-scope
+// release. (2) After every peer's CTA b has published, it reads slice 0 of every rank for its rows
+// (one fp32 partial per rank crosses NVLink, whatever the split count), adds them in rank order
+// (the same sum on every rank), adds the residual and applies RMSNorm. Rows are assigned to CTAs
+// identically on every rank (row = b + k * grid), so CTA b only ever waits for the CTAs b of its
+// peers, which wrote exactly the rows it reads.
+template <int NR>
 __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
   const int b = blockIdx.x;
   __shared__ float red[32];
   __shared__ int ok;
   pdl_trigger();
   pdl_wait();
+  const int H = a.H;
+  const int nvec = H / 4;
+  float* mine = const_cast<float*>(a.data[a.rank]);
+  if (a.nsplit > 1) {
+    for (int row = b; row < a.T; row += gridDim.x) {
+      const size_t base = static_cast<size_t>(row) * H;
+      for (int vi = threadIdx.x; vi < nvec; vi += kArThreads) {
+        float4 acc = *reinterpret_cast<const float4*>(mine + base + 4 * vi);
+        for (int sp = 1; sp < a.nsplit; ++sp) {
+          const float4 p = *reinterpret_cast<const float4*>(mine + sp * a.split_stride + base + 4 * vi);
+          acc.x += p.x;
+          acc.y += p.y;
+          acc.z += p.z;
+          acc.w += p.w;
+        }
+        *reinterpret_cast<float4*>(mine + base + 4 * vi) = acc;
+      }
+    }
+    __syncthreads();
+  }
   if (threadIdx.x == 0) {
     const uint32_t e = a.epochs[b] + 1;
     a.epochs[b] = e;
-    for (int q = 0; q < a.nranks; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
+    __threadfence_system();
+    for (int q = 0; q < NR; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
     int good = 1;
-    for (int q = 0; q < a.nranks && good; ++q) {
+    for (int q = 0; q < NR && good; ++q) {
       uint32_t i = 0;
       while (ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q) < e) {
         if (++i > kSpinLimit) {
@@ -63,8 +96,6 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
   }
   __syncthreads();
   if (!ok) return;
-  const int H = a.H;
-  const int nvec = H / 4;
   for (int row = b; row < a.T; row += gridDim.x) {
     float v[kMaxPer];
     float ss = 0.f;
@@ -74,14 +105,15 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
       const int vi = threadIdx.x + j * kArThreads;
       if (vi < nvec) {
         float4 acc = *reinterpret_cast<const float4*>(a.resid + base + 4 * vi);
-        for (int q = 0; q < a.nranks; ++q) {
-          for (int sp = 0; sp < a.nsplit; ++sp) {
-            const float4 p = ld_cg_f4(a.data[q] + sp * a.split_stride + base + 4 * vi);
-            acc.x += p.x;
-            acc.y += p.y;
-            acc.z += p.z;
-            acc.w += p.w;
-          }
+        float4 p[NR];
+#pragma unroll
+        for (int q = 0; q < NR; ++q) p[q] = ld_cg_f4(a.data[q] + base + 4 * vi);
+#pragma unroll
+        for (int q = 0; q < NR; ++q) {  // rank order: the same sum on every rank
+          acc.x += p[q].x;
+          acc.y += p[q].y;
+          acc.z += p[q].z;
+          acc.w += p[q].w;
         }
         *reinterpret_cast<float4*>(a.resid + base + 4 * vi) = acc;
         v[4 * j] = acc.x;
@@ -123,7 +155,16 @@ void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
   VMC_CHECK(a.H % 4 == 0 && a.H <= kArThreads * kMaxPer, "ar_add_rmsnorm: hidden size unsupported");
   if (a.T <= 0) return;
   const int grid = a.T < max_ctas ? a.T : max_ctas;
-  launch_k(ar_add_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0, st, a);
+  switch (a.nranks) {
+    case 1: launch_k(ar_add_rmsnorm_kernel<1>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    case 2: launch_k(ar_add_rmsnorm_kernel<2>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    case 3: launch_k(ar_add_rmsnorm_kernel<3>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    case 4: launch_k(ar_add_rmsnorm_kernel<4>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    case 5: launch_k(ar_add_rmsnorm_kernel<5>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    case 6: launch_k(ar_add_rmsnorm_kernel<6>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    case 7: launch_k(ar_add_rmsnorm_kernel<7>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+    default: launch_k(ar_add_rmsnorm_kernel<8>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+  }
 }
 
 // ---- symmetric memory through CUDA IPC ----------------------------------------------------------

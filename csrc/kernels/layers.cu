@@ -62,7 +62,112 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, int T, const uint8
 }
 
 // ---- residual add + RMSNorm ------------------------------------------------------------------
-// resid (fp32) += delta (bf16 or fp32, may be null); out = rmsnorm(resid) * w (bf16).
+// resid (fp32) += sum_j delta_j (bf16 or fp32, ndelta slices delta_stride apart; may be null);
+// out = rmsnorm(resid) * w (bf16). One CTA per row. Vector path (H % 4 == 0, H <= 16 * threads):
+// every load of the row (residual and all delta slices) is issued before the first add, and the
+// row stays in registers between the sum of squares and the output, so a decode-sized call costs
+// about one memory round trip.
+constexpr int kNormMaxVec = 4;    // float4 per thread
+constexpr int kNormMaxDelta = 8;  // delta slices summed with unrolled loads
+
+template <typename TD>
+__device__ __forceinline__ float4 ld_delta4(const TD* p, int64_t i4) {
+  if constexpr (sizeof(TD) == 2) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p + 4 * i4);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+  } else {
+    return *reinterpret_cast<const float4*>(p + 4 * i4);
+  }
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+template <typename TD>
+__global__ void add_rmsnorm_vec_kernel(float* __restrict__ resid, const TD* __restrict__ delta, int ndelta,
+                                       int64_t delta_stride, const float* __restrict__ w, int H, float eps,
+                                       __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int nvec = H >> 2;
+  float4* x = reinterpret_cast<float4*>(resid + static_cast<int64_t>(t) * H);
+  __shared__ float red[32];
+  float4 v[kNormMaxVec];
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int k = threadIdx.x + i * blockDim.x;
+    v[i] = k < nvec ? x[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (delta != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kNormMaxDelta; ++j) {
+      if (j < ndelta) {
+        const TD* dj = delta + j * delta_stride + static_cast<int64_t>(t) * H;
+#pragma unroll
+        for (int i = 0; i < kNormMaxVec; ++i) {
+          const int k = threadIdx.x + i * blockDim.x;
+          if (k < nvec) {
+            const float4 d = ld_delta4(dj, k);
+            v[i].x += d.x;
+            v[i].y += d.y;
+            v[i].z += d.z;
+            v[i].w += d.w;
+          }
+        }
+      }
+    }
+    for (int j = kNormMaxDelta; j < ndelta; ++j) {
+      const TD* dj = delta + j * delta_stride + static_cast<int64_t>(t) * H;
+      for (int i = 0; i < kNormMaxVec; ++i) {
+        const int k = threadIdx.x + i * blockDim.x;
+        if (k < nvec) {
+          const float4 d = ld_delta4(dj, k);
+          v[i].x += d.x;
+          v[i].y += d.y;
+          v[i].z += d.z;
+          v[i].w += d.w;
+        }
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int k = threadIdx.x + i * blockDim.x;
+    if (k < nvec) {
+      if (delta != nullptr) x[k] = v[i];
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / H + eps);
+  if (out) {
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * H);
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int k = threadIdx.x + i * blockDim.x;
+      if (k < nvec) {
+        const float4 g = w4[k];
+        o[k] = make_uint2(pack_bf16x2(v[i].x * inv * g.x, v[i].y * inv * g.y),
+                          pack_bf16x2(v[i].z * inv * g.z, v[i].w * inv * g.w));
+      }
+    }
+  }
+}
+
+// Scalar path for hidden sizes the vector path does not cover.
 template <typename TD>
 __global__ void add_rmsnorm_kernel(float* __restrict__ resid, const TD* __restrict__ delta, int ndelta,
                                    int64_t delta_stride, const float* __restrict__ w, int H, float eps,
@@ -83,16 +188,7 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ resid, const TD* __restri
     x[k] = v;
     ss += v * v;
   }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    v = warp_sum(v);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float inv = rsqrtf(red[0] / H + eps);
+  const float inv = rsqrtf(block_sum(ss, red) / H + eps);
   if (out) {
     for (int k = threadIdx.x; k < H; k += blockDim.x)
       out[static_cast<int64_t>(t) * H + k] = __float2bfloat16(x[k] * inv * w[k]);
@@ -100,9 +196,25 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ resid, const TD* __restri
 }
 
 // ---- RoPE + KV store -----------------------------------------------------------------------
-// qkv: [T, (Hq + 2 Hkv) * D] (bf16 or fp32). One warp per (token, head). Q heads are rotated and
-// written to q_out [T, Hq, D]; K heads rotated and V heads copied into the paged cache at the
-// token's slot (skipped when slot < 0). neox = rotate halves (x_i, x_{i+D/2}) instead of pairs.
+// qkv: [T, (Hq + 2 Hkv) * D] (bf16 or fp32; fp32 input may be nsplit split-K partials
+// split_stride apart). One warp per (token, head); each lane owns groups of 4 dimensions: 4
+// consecutive ones (two adjacent rotation pairs), or with neox (pairs x_i, x_{i + D/2}) dimensions
+// 2q, 2q+1 and their partners. Q heads are rotated into q_out [T, Hq, D]; K heads rotated and V
+// heads copied into the paged cache at the token's slot (skipped when slot < 0). All partial loads
+// of a lane are issued before the first add.
+template <typename TI>
+__device__ __forceinline__ void ld2(const TI* p, int64_t i, float& a, float& b) {
+  if constexpr (sizeof(TI) == 2) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p + i);
+    a = __uint_as_float(u << 16);
+    b = __uint_as_float(u & 0xffff0000u);
+  } else {
+    const float2 f = *reinterpret_cast<const float2*>(p + i);
+    a = f.x;
+    b = f.y;
+  }
+}
+
 template <typename TI>
 __global__ void rope_store_kernel(const TI* __restrict__ qkv, int nsplit, int64_t split_stride, int T, int Hq, int Hkv,
                                   int D, const int32_t* __restrict__ pos, const int32_t* __restrict__ slots,
@@ -119,16 +231,8 @@ __global__ void rope_store_kernel(const TI* __restrict__ qkv, int nsplit, int64_
   const TI* src = qkv + static_cast<int64_t>(t) * H * D + static_cast<int64_t>(h) * D;
   const int p = pos[t];
   const float2* c = cs + static_cast<int64_t>(p) * (D / 2);
-  auto ld = [&](int i) -> float {
-    if constexpr (sizeof(TI) == 2) {
-      return __bfloat162float(src[i]);
-    } else {
-      float v = src[i];
-      for (int sp = 1; sp < nsplit; ++sp) v += src[sp * split_stride + i];
-      return v;
-    }
-  };
   __nv_bfloat16* dst;
+  bool rotate = true;
   if (h < Hq) {
     dst = q_out + (static_cast<int64_t>(t) * Hq + h) * D;
   } else {
@@ -138,18 +242,62 @@ __global__ void rope_store_kernel(const TI* __restrict__ qkv, int nsplit, int64_
     const int kvsel = h < Hq + Hkv ? 0 : 1;
     const int kvh = h - Hq - kvsel * Hkv;
     dst = kv + ((static_cast<int64_t>(blk) * 2 + kvsel) * Hkv + kvh) * 16 * D + static_cast<int64_t>(off) * D;
-    if (kvsel == 1) {
-      for (int i = lane; i < D; i += 32) dst[i] = __float2bfloat16(ld(i));
-      return;
-    }
+    rotate = kvsel == 0;
   }
-  for (int i = lane; i < D / 2; i += 32) {
-    const float2 cv = c[i];
-    const int i0 = neox ? i : 2 * i;
-    const int i1 = neox ? i + D / 2 : 2 * i + 1;
-    const float x0 = ld(i0), x1 = ld(i1);
-    dst[i0] = __float2bfloat16(x0 * cv.x - x1 * cv.y);
-    dst[i1] = __float2bfloat16(x0 * cv.y + x1 * cv.x);
+  const int half = D / 2;
+  for (int q = lane; q < D / 4; q += 32) {
+    // element indices of this lane's two rotation pairs: (a0, a1) and (b0, b1)
+    const int a0 = neox ? 2 * q : 4 * q, a1 = neox ? 2 * q + half : 4 * q + 1;
+    const int b0 = neox ? 2 * q + 1 : 4 * q + 2, b1 = neox ? 2 * q + 1 + half : 4 * q + 3;
+    // two contiguous element pairs to load: neox (a0, b0) and (a1, b1); else (a0, a1) and (b0, b1)
+    const int l0 = a0, l1 = neox ? a1 : b0;
+    float x[4];  // values at a0, a1, b0, b1
+    float u0, u1, u2, u3;
+    ld2(src, l0, u0, u1);
+    ld2(src, l1, u2, u3);
+    if constexpr (sizeof(TI) == 4) {
+#pragma unroll
+      for (int sp = 1; sp < 8; ++sp) {
+        if (sp < nsplit) {
+          float w0, w1, w2, w3;
+          ld2(src + sp * split_stride, l0, w0, w1);
+          ld2(src + sp * split_stride, l1, w2, w3);
+          u0 += w0;
+          u1 += w1;
+          u2 += w2;
+          u3 += w3;
+        }
+      }
+      for (int sp = 8; sp < nsplit; ++sp) {
+        float w0, w1, w2, w3;
+        ld2(src + sp * split_stride, l0, w0, w1);
+        ld2(src + sp * split_stride, l1, w2, w3);
+        u0 += w0;
+        u1 += w1;
+        u2 += w2;
+        u3 += w3;
+      }
+    }
+    if (neox) { x[0] = u0; x[2] = u1; x[1] = u2; x[3] = u3; }
+    else { x[0] = u0; x[1] = u1; x[2] = u2; x[3] = u3; }
+    float y[4];
+    if (rotate) {
+      const int ia = neox ? 2 * q : 2 * q, ib = ia + 1;  // rotation pair indices in the table
+      const float2 ca = c[ia], cb = c[ib];
+      y[0] = x[0] * ca.x - x[1] * ca.y;
+      y[1] = x[0] * ca.y + x[1] * ca.x;
+      y[2] = x[2] * cb.x - x[3] * cb.y;
+      y[3] = x[2] * cb.y + x[3] * cb.x;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = x[i];
+    }
+    if (neox) {
+      *reinterpret_cast<uint32_t*>(dst + a0) = pack_bf16x2(y[0], y[2]);
+      *reinterpret_cast<uint32_t*>(dst + a1) = pack_bf16x2(y[1], y[3]);
+    } else {
+      *reinterpret_cast<uint2*>(dst + a0) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+    }
   }
 }
 
@@ -221,6 +369,16 @@ void add_rmsnorm(float* resid, const void* delta, bool delta_f32, int ndelta, in
                  int T, int H, float eps, void* out, cudaStream_t st) {
   if (T <= 0) return;
   const int threads = H >= 2048 ? 512 : 256;
+  if (H % 4 == 0 && H <= 4 * kNormMaxVec * threads) {
+    if (delta_f32 || delta == nullptr)
+      launch_k(add_rmsnorm_vec_kernel<float>, dim3(T), dim3(threads), 0, st, resid, static_cast<const float*>(delta),
+               delta ? ndelta : 0, delta_stride, w, H, eps, static_cast<__nv_bfloat16*>(out));
+    else
+      launch_k(add_rmsnorm_vec_kernel<__nv_bfloat16>, dim3(T), dim3(threads), 0, st, resid,
+               static_cast<const __nv_bfloat16*>(delta), ndelta, delta_stride, w, H, eps,
+               static_cast<__nv_bfloat16*>(out));
+    return;
+  }
   if (delta_f32 || delta == nullptr)
     launch_k(add_rmsnorm_kernel<float>, dim3(T), dim3(threads), 0, st, resid, static_cast<const float*>(delta),
              delta ? ndelta : 0, delta_stride, w, H, eps, static_cast<__nv_bfloat16*>(out));
@@ -233,6 +391,7 @@ void rope_store(const void* qkv, bool qkv_f32, int nsplit, int64_t split_stride,
                 const int32_t* pos, const int32_t* slots, const float* cos_sin, bool neox, void* q_out, void* kv,
                 cudaStream_t st) {
   if (T <= 0) return;
+  VMC_CHECK(D % 8 == 0, "rope_store: head dim must be a multiple of 8");
   const int64_t warps = static_cast<int64_t>(T) * (Hq + 2 * Hkv);
   const int wpb = 8;
   if (qkv_f32)

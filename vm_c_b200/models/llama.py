@@ -385,7 +385,7 @@ class LlamaModel:
             self._qkv(lw, ws.h, T, m, kv_cache[li])
             self._attention(kv_cache[li], m)
             nxt = layers[li + 1].attn_norm if li + 1 < len(layers) else self.w.output_norm
-            if self.fused:
+            if self.fused and T <= self.comm.max_fused_tokens:
                 self._row_parallel_fused(0, ws.attn, lw.wo, T, lw.ffn_norm)
                 if lw.moe is not None:
                     part = self.comm.partial(1).view(-1)[:T * self.H].view(T, self.H)

@@ -21,8 +21,15 @@ _MAX_RANKS = 8
 
 
 class FusedComm(NcclComm):
-    def __init__(self, group=None, max_ctas: int = 148):
+    """`max_fused_tokens`: steps with more tokens (prefill chunks) take the NCCL all-reduce and a
+    separate residual + RMSNorm kernel instead: a one-shot all-reduce reads every peer's whole
+    partial, (world - 1) times the data, where NCCL's bandwidth-optimal algorithms move about twice
+    the data whatever the world size; decode-sized steps are latency-bound and take the fused
+    kernel."""
+
+    def __init__(self, group=None, max_ctas: int = 148, max_fused_tokens: int = 512):
         super().__init__(group)
+        self.max_fused_tokens = max_fused_tokens
         if self.world > _MAX_RANKS:
             raise ValueError("fused communication supports up to 8 ranks")
         self.max_ctas = min(max_ctas, _FLAG_SLOTS)
