@@ -77,3 +77,21 @@ def test_sampling_seeded(llm):
     a = llm.generate([p], sp)[0].output_token_ids
     b = llm.generate([p], sp)[0].output_token_ids
     assert a == b and len(a) == 10
+
+
+def test_hidden_tracer_does_not_change_tokens(tiny, llm, monkeypatch):
+    from vm_c_b200.llm import LLM
+    monkeypatch.setenv("VMC_LOG_HIDDEN", "1")
+    monkeypatch.setenv("VMC_LOG_LOGITS", "1")
+    traced = LLM(tiny, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256)
+    lines = []
+    traced.runner.tracer.sink = lines.append
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, 32000, 12).tolist()
+    sp = SamplingParams.greedy_params(max_tokens=4, ignore_eos=True)
+    a = traced.generate([prompt], sp)[0].output_token_ids
+    b = llm.generate([prompt], sp)[0].output_token_ids
+    traced.shutdown()
+    assert a == b
+    assert any(" hidden inp_embd " in ln for ln in lines) and any("logits_top5" in ln for ln in lines)
+    assert any(" hidden l_out-1 " in ln for ln in lines)

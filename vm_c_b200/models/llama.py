@@ -293,6 +293,7 @@ class LlamaModel:
             comm.setup(max_tokens, self.H)
         self.moe_runner = None
         self.tq = None  # TurboQuant tables when the KV cache is compressed (set by the runner)
+        self.tracer = None  # utils.trace.HiddenTracer when VMC_LOG_HIDDEN / VMC_LOG_LOGITS is set
         if cfg.is_moe:
             from .moe import MoERunner
             self.moe_runner = MoERunner(self, max_tokens)
@@ -378,36 +379,65 @@ class LlamaModel:
         """One step: writes sampled token ids for the m.S sample rows into out_tok."""
         cfg, ws = self.cfg, self.ws
         T = m.T
+        tr = self.tracer
         ops.embed(m.input_ids, T, self.w.embd, self.w.embd_type, self.w.embd_row_bytes, self.H, resid=ws.resid)
+        if tr:
+            tr.probe("inp_embd", ws.resid[:T])
         layers = self.w.layers
         ops.add_rmsnorm(ws.resid, layers[0].attn_norm, T, self.H, cfg.rms_eps, out=ws.h)
         for li, lw in enumerate(layers):
+            if tr:
+                tr.probe(f"attn_norm-{li}", ws.h[:T])
             self._qkv(lw, ws.h, T, m, kv_cache[li])
             self._attention(kv_cache[li], m)
+            if tr:
+                tr.probe(f"kqv_out-{li}", ws.attn[:T])
             nxt = layers[li + 1].attn_norm if li + 1 < len(layers) else self.w.output_norm
             if self.fused and T <= self.comm.max_fused_tokens:
                 self._row_parallel_fused(0, ws.attn, lw.wo, T, lw.ffn_norm)
+                if tr:
+                    tr.probe(f"ffn_inp-{li}", ws.resid[:T])
                 if lw.moe is not None:
                     part = self.comm.partial(1).view(-1)[:T * self.H].view(T, self.H)
                     self.moe_runner.forward(lw.moe, ws.h, T, out=part)
                     self.comm.allreduce_add_rmsnorm(1, T, ws.resid, nxt, cfg.rms_eps, ws.h)
+                    if tr:
+                        tr.probe(f"l_out-{li}", ws.resid[:T])
                     continue
                 self._gate_up(lw, T)
+                if tr:
+                    tr.probe(f"ffn_swiglu-{li}", ws.act[:T])
                 self._row_parallel_fused(1, ws.act, lw.w_down, T, nxt)
+                if tr:
+                    tr.probe(f"l_out-{li}", ws.resid[:T])
                 continue
             self._row_parallel_norm(ws.attn, lw.wo, T, lw.ffn_norm)
+            if tr:
+                tr.probe(f"ffn_inp-{li}", ws.resid[:T])
             if lw.moe is not None:
                 d, _ = self.moe_runner.forward(lw.moe, ws.h, T)
                 if self.tp > 1:
                     self.comm.all_reduce(d[:T])
                 ops.add_rmsnorm(ws.resid, nxt, T, self.H, cfg.rms_eps, out=ws.h, delta=d[:T])
+                if tr:
+                    tr.probe(f"l_out-{li}", ws.resid[:T])
                 continue
             self._gate_up(lw, T)
+            if tr:
+                tr.probe(f"ffn_swiglu-{li}", ws.act[:T])
             self._row_parallel_norm(ws.act, lw.w_down, T, nxt)
+            if tr:
+                tr.probe(f"l_out-{li}", ws.resid[:T])
         ops.gather_rows(ws.h, m.logits_idx, m.S, self.H, ws.hs)
+        if tr:
+            tr.probe("result_norm", ws.hs[:m.S])
         ops.gemm(ws.hs, self.w.lm_head, ws.logits[:m.S], m.S, ops.OUT_F32, 1)
         if pre_sample is not None:
             pre_sample(self)
+        if tr:
+            tr.probe("result_output", ws.logits[:m.S])
+            if self.tp == 1:
+                tr.probe_logits(ws.logits, m.S)
         self._sample(m.S, params, out_tok, out_lp)
 
     def _attention(self, kv_layer: torch.Tensor, m: StepMeta) -> None:

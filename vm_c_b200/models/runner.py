@@ -75,6 +75,11 @@ class GpuModelRunner(ModelRunner):
         self.buckets = [b for b in GRAPH_BUCKETS if b <= max_seqs]
         if use_graphs and self.buckets and self.buckets[-1] < max_seqs:
             self.buckets.append(max_seqs)
+        from ..utils.trace import HiddenTracer
+        self.tracer = HiddenTracer.from_env()
+        if self.tracer is not None and use_graphs:
+            log.warning("VMC_LOG_HIDDEN / VMC_LOG_LOGITS set: decode steps run eagerly (no CUDA graphs)")
+            use_graphs = False
         self.use_graphs = use_graphs
         self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len + self.spec_k, comm=comm,
                                 attn_splits=16)
@@ -88,6 +93,7 @@ class GpuModelRunner(ModelRunner):
         if is_turboquant(cfg.cache.kv_cache_dtype):
             self.tq = ops.TqTables(cfg.cache.kv_cache_dtype, m.head_dim, self.dev, rot_seed=cfg.cache.tq_rotation_seed)
         self.model.tq = self.tq
+        self.model.tracer = self.tracer
         per_block = kv_bytes_per_block(cfg, self.model.hkv)
         max_blocks_per_seq = (m.max_model_len + cfg.cache.block_size - 1) // cfg.cache.block_size + 1
         want = cfg.cache.num_gpu_blocks
@@ -216,6 +222,8 @@ class GpuModelRunner(ModelRunner):
             self._forward(self._meta(counts.T, counts.R, counts.S, counts.num_decode, counts.max_qlen), pen)
             self.launch_count += ops.LAUNCHES[0] - n0
             S = counts.S
+        if self.tracer is not None:
+            self.tracer.flush()
         self.tok_host[:S].copy_(self.tok_dev[:S], non_blocking=True)
         self.lp_host[:S].copy_(self.lp_dev[:S], non_blocking=True)
         self.h2d_bytes += meta.numel() * 4 + params.nbytes
