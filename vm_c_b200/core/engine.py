@@ -286,6 +286,17 @@ class LLMEngine:
         if req.stream_callback:
             req.stream_callback(req, list(last_tokens or []), True)
 
+    def fail_all(self, reason: FinishReason = FinishReason.ERROR) -> int:
+        """Finish every queued and running request with `reason` (after a rank or device failure).
+        Returns how many requests were failed."""
+        self._drain()
+        reqs = list(self.requests.values())
+        for req in reqs:
+            if self.sched.abort_request(req.int_id):
+                pass
+            self._finish(req, reason)
+        return len(reqs)
+
     def finish_request(self, request_id: str, reason: FinishReason = FinishReason.STOP) -> None:
         """Finish a running request from the host (e.g. a stop string matched by the detokenizer)."""
         iid = self.by_name.get(request_id)

@@ -7,6 +7,12 @@ CPU (gloo) group, the requests added, aborted or finished on the host since the 
 Every rank then applies the same commands in the same order and runs the same step, so the
 schedules, the collectives and the sampled tokens stay identical without any per-step device sync.
 Followers wait with a bounded timeout; rank 0 sends a heartbeat while idle.
+
+Failure detection (parallel/health.py): every rank publishes a heartbeat into the process group's
+store; before each control collective a rank checks its peers' heartbeats and raises RankFailure
+instead of entering a collective that a dead peer will never join. A peer that is alive but stuck
+is caught by the control group's timeout, and the error names the stalled rank. VMC_FAULT injects
+host-side faults at step boundaries for testing.
 """
 from __future__ import annotations
 
@@ -17,17 +23,63 @@ from datetime import timedelta
 import torch.distributed as dist
 
 from ..core.sampling_params import FinishReason, SamplingParams
+from .health import FaultPlan, Heartbeats, RankFailure
 
 
 class StepDriver:
-    def __init__(self, engine, heartbeat_s: float = 0.05, timeout_s: float = 300.0):
+    def __init__(self, engine, heartbeat_s: float = 0.05, timeout_s: float = 300.0, peer_timeout_s: float = 10.0,
+                 faults: FaultPlan | None = None):
         self.engine = engine
         self.rank = dist.get_rank()
         self.world = dist.get_world_size()
+        self.timeout_s = timeout_s
         self.group = dist.new_group(backend="gloo", timeout=timedelta(seconds=timeout_s))
         self.heartbeat_s = heartbeat_s
         self._finish: list[tuple[str, int]] = []
         self.stopped = False
+        self.faults = faults if faults is not None else FaultPlan.from_env()
+        self.health = None
+        if self.world > 1:
+            store = dist.distributed_c10d._get_default_store()
+            # progress = control collectives entered: a peer behind us never joined the current one
+            self.health = Heartbeats(store, self.rank, self.world, interval_s=min(0.2, peer_timeout_s / 10),
+                                     timeout_s=peer_timeout_s, progress=lambda: self.ncoll)
+    ncoll = 0
+
+    # every rank, before each control collective ------------------------------------------------
+    def _pre_collective(self) -> None:
+        if self.faults is not None:
+            self.faults.fire(self.rank, self.engine.step_id)
+        if self.health is not None:
+            self.health.check()
+
+    def _broadcast(self, obj: list) -> None:
+        self._pre_collective()
+        self.ncoll += 1
+        try:
+            dist.broadcast_object_list(obj, src=0, group=self.group)
+        except RuntimeError as e:  # the control group's timeout, or a peer's connection went away
+            self._diagnose(e)
+            raise
+
+    def _diagnose(self, e: BaseException) -> None:
+        """After a failed control collective: name the peer that died (its heartbeat goes stale
+        within the peer timeout) or that is alive but never joined this collective."""
+        if self.health is None:
+            return
+        deadline = time.time() + self.health.timeout_s + 1.0
+        while True:
+            try:
+                self.health.check()
+            except RankFailure as f:
+                raise f from e
+            behind = [r for r in range(self.world)
+                      if r != self.rank and (hb := self.health.read(r)) is not None and hb[1] < self.ncoll]
+            if time.time() >= deadline:
+                if behind:
+                    raise RankFailure(behind[0], f"is alive but stopped taking steps ({e})") from e
+                return
+            time.sleep(0.05)
 
     # rank 0 ----------------------------------------------------------------------------------
     def finish(self, request_id: str, reason: FinishReason) -> None:
@@ -49,7 +101,7 @@ class StepDriver:
             time.sleep(self.heartbeat_s)
         cmds = self._collect()
         obj = [cmds]
-        dist.broadcast_object_list(obj, src=0, group=self.group)
+        self._broadcast(obj)
         self._apply_finish(cmds)
         if eng.has_unfinished():
             eng.step()
@@ -58,15 +110,21 @@ class StepDriver:
         self.stopped = True
         obj = [{"add": [], "abort": [], "finish": [], "stop": True}]
         dist.broadcast_object_list(obj, src=0, group=self.group)
+        self.close()
+
+    def close(self) -> None:
+        if self.health is not None:
+            self.health.stop()
 
     # followers ---------------------------------------------------------------------------------
     def follow(self) -> None:
         eng = self.engine
         while True:
             obj = [None]
-            dist.broadcast_object_list(obj, src=0, group=self.group)
+            self._broadcast(obj)
             cmds = obj[0]
             if cmds["stop"]:
+                self.close()
                 break
             for rid, prompt, params in cmds["add"]:
                 eng.add_request(prompt, SamplingParams(**params), request_id=rid)

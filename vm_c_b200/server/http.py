@@ -35,7 +35,7 @@ VERSION = "vm_c_b200 0.1.0"
 class EngineLoop(threading.Thread):
     """Steps the engine whenever it has work; sleeps on a condition variable otherwise."""
 
-    def __init__(self, engine, poll_s: float = 0.01, driver=None):
+    def __init__(self, engine, poll_s: float = 0.01, driver=None, step_timeout_s: float = 120.0):
         super().__init__(daemon=True, name="engine-loop")
         self.engine = engine
         self.poll_s = poll_s
@@ -43,14 +43,23 @@ class EngineLoop(threading.Thread):
         self.cv = threading.Condition()
         self.stop_flag = False
         self.error: Optional[BaseException] = None
+        self.failed = False           # a rank failed: the server answers 503 from now on
+        from ..parallel.health import StepWatchdog
+        self.watchdog = StepWatchdog(step_timeout_s, self._step_timeout) if step_timeout_s > 0 else None
+
+    def _step_timeout(self, step: int, dt: float) -> None:
+        log.error("engine step %d stuck for %.1f s; in-flight requests will be failed when it returns", step, dt)
 
     def wake(self) -> None:
         with self.cv:
             self.cv.notify()
 
     def run(self) -> None:
+        from ..parallel.health import RankFailure
         while not self.stop_flag:
             try:
+                if self.watchdog is not None:
+                    self.watchdog.begin(self.engine.step_id)
                 if self.driver is not None:
                     self.driver.step()
                     continue
@@ -59,13 +68,25 @@ class EngineLoop(threading.Thread):
                 else:
                     with self.cv:
                         self.cv.wait(self.poll_s)
+            except RankFailure as e:  # a peer rank is gone: no further collective can complete
+                log.error("stopping the engine: %s", e)
+                self.error, self.failed = e, True
+                n = self.engine.fail_all(FinishReason.ERROR)
+                log.error("failed %d in-flight requests", n)
+                break
             except Exception as e:  # keep serving; fail the in-flight requests
                 log.exception("engine step failed: %s", e)
                 self.error = e
+                self.engine.fail_all(FinishReason.ERROR)
                 time.sleep(0.1)
+            finally:
+                if self.watchdog is not None:
+                    self.watchdog.end()
 
     def shutdown(self) -> None:
         self.stop_flag = True
+        if self.watchdog is not None:
+            self.watchdog.stop()
         self.wake()
 
 
