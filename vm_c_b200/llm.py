@@ -33,7 +33,8 @@ class LLM:
                  long_prefill_token_threshold: int = 0, scheduling_policy: str = "decode_first",
                  use_cuda_graphs: bool = True, device: Optional[str] = None, tp_rank: int = 0, tp_size: int = 1,
                  ep_size: int = 1, kv_cache_dtype: str = "auto", tq_rotation_seed: int = 0, draft_model: str = "",
-                 num_speculative_tokens: int = 5, comm=None, config: Optional[VmCConfig] = None, warmup: bool = True):
+                 num_speculative_tokens: int = 5, cpu_offload_gb: float = 0.0, cpu_offload_params=(),
+                 comm=None, config: Optional[VmCConfig] = None, warmup: bool = True):
         import torch
         dev = device or (f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cuda")
         src, mcfg = make_source(model, dev)
@@ -49,6 +50,9 @@ class LLM:
         cfg.cache.num_gpu_blocks = num_gpu_blocks
         cfg.cache.gpu_memory_utilization = gpu_memory_utilization
         cfg.cache.enable_prefix_caching = enable_prefix_caching
+        if cpu_offload_gb:
+            cfg.cache.cpu_offload_gb = cpu_offload_gb
+            cfg.cache.cpu_offload_params = list(cpu_offload_params)
         if config is None or kv_cache_dtype != "auto":
             cfg.cache.kv_cache_dtype = kv_cache_dtype
         if config is None or tq_rotation_seed:

@@ -37,6 +37,7 @@ class LayerWeights:
     w_down: ops.TiledWeight | None = None
     moe: object | None = None      # MoE weights (models/moe.py)
     index: int = 0                 # layer number
+    offload: list = field(default_factory=list)  # (pinned host tensor, device view) copied before the layer
 
 
 @dataclass
@@ -386,6 +387,8 @@ class LlamaModel:
         layers = self.w.layers
         ops.add_rmsnorm(ws.resid, layers[0].attn_norm, T, self.H, cfg.rms_eps, out=ws.h)
         for li, lw in enumerate(layers):
+            for host, dev in lw.offload:  # CPU-offloaded weights of this layer into the staging buffer
+                dev.copy_(host, non_blocking=True)
             if tr:
                 tr.probe(f"attn_norm-{li}", ws.h[:T])
             self._qkv(lw, ws.h, T, m, kv_cache[li])

@@ -60,6 +60,8 @@ class GpuModelRunner(ModelRunner):
         self.weights = weights if weights is not None else load_weights(source, m, self.dev, tp_rank, tp_size,
                                                                                  cfg.parallel.expert_parallel_size)
         log.info("weights loaded: %.2f GB in %.1fs", self.weights.bytes_total / 1e9, time.perf_counter() - t0)
+        from .offload import apply_offload
+        self.offload = apply_offload(self.weights, cfg.cache.cpu_offload_gb, cfg.cache.cpu_offload_params, self.dev)
         s = cfg.scheduler
         self.max_model_len = m.max_model_len
         sp = cfg.spec
