@@ -50,6 +50,10 @@ struct AttnParams {
   float* part_lse;          // [splits, T, Hq]
   int req_offset;           // first request index handled by this launch
   TqDev tq;                 // TurboQuant cache of this layer (tq.cache == nullptr: bf16 pages in kv)
+  // Token trees (prefill kernel): per query token, which of the request's last tree_span key
+  // positions it may attend to (bit i = key at position ctx - tree_span + i); null = causal.
+  const uint64_t* tree_mask;
+  int tree_span;
 };
 
 // Copy one 16 x D page (K or V) into a padded smem tile (rows 16*slot .. 16*slot+15).
@@ -91,7 +95,8 @@ template <int D>
 __device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV, int key0, int kpos0,
                                             const uint32_t (&qa)[Frag<D>::KD][4], int qpos_lo, int qpos_hi,
                                             float scale_log2, float (&o)[Frag<D>::ND][4], float (&m)[2],
-                                            float (&l)[2], int lane) {
+                                            float (&l)[2], int lane, bool tree = false, int tbase = 0,
+                                            uint64_t tm_lo = 0, uint64_t tm_hi = 0) {
   constexpr int RB = Frag<D>::RB;
   float s[2][4];
 #pragma unroll
@@ -119,6 +124,7 @@ __device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV
       const int qp = (e < 2) ? qpos_lo : qpos_hi;
       float v = s[j][e] * scale_log2;
       if (kp > qp) v = -INFINITY;
+      else if (tree && kp >= tbase && !((((e < 2) ? tm_lo : tm_hi) >> (kp - tbase)) & 1ull)) v = -INFINITY;
       s[j][e] = v;
       mx[e >> 1] = fmaxf(mx[e >> 1], v);
     }
@@ -471,6 +477,9 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
   const int pr_lo = prow0 + (lane >> 2), pr_hi = pr_lo + 8;
   const int qpos_lo = pr_lo < rows ? ctx - qlen + pr_lo / p.G : -1;
   const int qpos_hi = pr_hi < rows ? ctx - qlen + pr_hi / p.G : -1;
+  const bool tree = p.tree_mask != nullptr;
+  const uint64_t tm_lo = (tree && pr_lo < rows) ? p.tree_mask[qs + pr_lo / p.G] : 0ull;
+  const uint64_t tm_hi = (tree && pr_hi < rows) ? p.tree_mask[qs + pr_hi / p.G] : 0ull;
   // Keys needed by this CTA: up to the largest query position among its rows.
   const int last_row = min(rows, prow_cta + 64) - 1;
   const int kmax = ctx - qlen + last_row / p.G + 1;  // exclusive
@@ -530,7 +539,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
       for (int sub = 0; sub < TK / 16; ++sub) {
         const int kpos0 = tile * TK + sub * 16;
         if (kpos0 <= warp_qmax && kpos0 < kmax)
-          attn_step16<D>(sK(s), sV(s), sub * 16, kpos0, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane);
+          attn_step16<D>(sK(s), sV(s), sub * 16, kpos0, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane, tree,
+                         ctx - p.tree_span, tm_lo, tm_hi);
       }
     }
     __syncthreads();
@@ -628,7 +638,70 @@ void dispatch_kv(const AttnParams& p, const AttnLaunch& a, cudaStream_t st) {
   }
 }
 
+// One warp per (request, layer, K/V, kv head): the lanes hold the request's rows (16-byte pieces,
+// lane-strided) in registers, then write them, so sources and destinations may overlap.
+constexpr int kMoveMax = 16;
+template <int D>
+__global__ void kv_move_kernel(__nv_bfloat16* cache, int L, int64_t layer_elems, int Hkv, const int32_t* src,
+                               const int32_t* dst, const int32_t* cnt, int num_reqs, int max_moves) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int kVec = D / 8;                      // 16-byte pieces per row
+  constexpr int kPer = (kVec + 31) / 32;           // pieces per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t per_req = static_cast<int64_t>(L) * 2 * Hkv;
+  if (w >= per_req * num_reqs) return;
+  const int r = static_cast<int>(w / per_req);
+  int rest = static_cast<int>(w % per_req);
+  const int l = rest / (2 * Hkv);
+  rest %= 2 * Hkv;
+  const int kvsel = rest / Hkv, h = rest % Hkv;
+  const int n = min(cnt[r], kMoveMax);
+  __nv_bfloat16* base = cache + l * layer_elems;
+  auto row = [&](int slot) {
+    const int blk = slot / 16, off = slot % 16;
+    return reinterpret_cast<uint4*>(base + ((static_cast<int64_t>(blk) * 2 + kvsel) * Hkv + h) * 16 * D +
+                                    static_cast<int64_t>(off) * D);
+  };
+  uint4 v[kMoveMax][kPer];
+#pragma unroll
+  for (int i = 0; i < kMoveMax; ++i) {
+    if (i < n) {
+      const uint4* s = row(src[r * max_moves + i]);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j)
+        if (lane + 32 * j < kVec) v[i][j] = s[lane + 32 * j];
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < kMoveMax; ++i) {
+    if (i < n) {
+      uint4* d = row(dst[r * max_moves + i]);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j)
+        if (lane + 32 * j < kVec) d[lane + 32 * j] = v[i][j];
+    }
+  }
+}
+
 }  // namespace
+
+void kv_move(void* cache, int L, int64_t layer_elems, int Hkv, int D, const int32_t* src, const int32_t* dst,
+             const int32_t* cnt, int num_reqs, int max_moves, cudaStream_t st) {
+  VMC_CHECK(max_moves <= kMoveMax, "kv_move: at most 16 moves per request");
+  if (num_reqs <= 0) return;
+  const int64_t warps = static_cast<int64_t>(num_reqs) * L * 2 * Hkv;
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8));
+  auto* c = static_cast<__nv_bfloat16*>(cache);
+  switch (D) {
+    case 32: launch_k(kv_move_kernel<32>, grid, dim3(256), 0, st, c, L, layer_elems, Hkv, src, dst, cnt, num_reqs, max_moves); break;
+    case 64: launch_k(kv_move_kernel<64>, grid, dim3(256), 0, st, c, L, layer_elems, Hkv, src, dst, cnt, num_reqs, max_moves); break;
+    case 128: launch_k(kv_move_kernel<128>, grid, dim3(256), 0, st, c, L, layer_elems, Hkv, src, dst, cnt, num_reqs, max_moves); break;
+    default: throw std::runtime_error("kv_move: unsupported head dim");
+  }
+}
 
 void paged_attention(const AttnLaunch& a, cudaStream_t st) {
   VMC_CHECK(a.Hq % a.Hkv == 0, "attention: Hq must be a multiple of Hkv");
@@ -650,6 +723,10 @@ void paged_attention(const AttnLaunch& a, cudaStream_t st) {
   p.req_offset = a.req_offset;
   if (a.tq) p.tq = *a.tq;
   else p.tq.cache = nullptr;
+  p.tree_mask = a.tree_mask;
+  p.tree_span = a.tree_span;
+  VMC_CHECK(!(a.decode && a.tree_mask), "attention: tree masks need the prefill path");
+  VMC_CHECK(!a.tree_mask || (a.tree_span >= 1 && a.tree_span <= 64), "attention: tree span must be 1..64");
   if (a.num_reqs <= 0) return;
   if (a.decode) {
     VMC_CHECK(a.max_qlen * p.G <= 16, "attention: decode path needs q_len * group <= 16");

@@ -26,9 +26,18 @@ struct AttnLaunch {
   float* part_lse;           // [splits, total_tokens, Hq] fp32
   void* out;                 // bf16 [T, Hq, D]
   const TqDev* tq = nullptr; // TurboQuant cache of this layer instead of bf16 pages (kv unused)
+  const uint64_t* tree_mask = nullptr;  // [T] tree-verification masks (prefill path only), or null
+  int tree_span = 0;         // bit 0 of a mask is the key at position ctx - tree_span
 };
 
 void paged_attention(const AttnLaunch& a, cudaStream_t st);
+
+// Move KV rows inside a bf16 paged cache [L, num_blocks, 2, Hkv, 16, D] (all layers, K and V, all
+// KV heads): request r moves cnt[r] rows, src[r * max_moves + i] -> dst[r * max_moves + i] (slot
+// indices). All rows of a request are read before any is written, so a destination may be another
+// move's source (tree verification compacting the accepted branch).
+void kv_move(void* cache, int L, int64_t layer_elems, int Hkv, int D, const int32_t* src, const int32_t* dst,
+             const int32_t* cnt, int num_reqs, int max_moves, cudaStream_t st);
 
 // Resident decode CTAs per SM (occupancy of the decode kernel for head dim D).
 int attn_decode_ctas_per_sm(int D);

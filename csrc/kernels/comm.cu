@@ -32,6 +32,17 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+#ifndef VMC_AR_SYNC
+#define VMC_AR_SYNC 0
+#endif
 // Peer data: bypass L1 so that a line cached by an earlier call is never reused.
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
@@ -63,37 +74,61 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
     for (int row = b; row < a.T; row += gridDim.x) {
       const size_t base = static_cast<size_t>(row) * H;
       for (int vi = threadIdx.x; vi < nvec; vi += kArThreads) {
-        float4 acc = *reinterpret_cast<const float4*>(mine + base + 4 * vi);
-        for (int sp = 1; sp < a.nsplit; ++sp) {
-          const float4 p = *reinterpret_cast<const float4*>(mine + sp * a.split_stride + base + 4 * vi);
-          acc.x += p.x;
-          acc.y += p.y;
-          acc.z += p.z;
-          acc.w += p.w;
+        float4 p[8];  // splits 0..7 loaded together, then added in split order
+#pragma unroll
+        for (int sp = 0; sp < 8; ++sp)
+          if (sp < a.nsplit) p[sp] = *reinterpret_cast<const float4*>(mine + sp * a.split_stride + base + 4 * vi);
+        float4 acc = p[0];
+#pragma unroll
+        for (int sp = 1; sp < 8; ++sp) {
+          if (sp < a.nsplit) {
+            acc.x += p[sp].x;
+            acc.y += p[sp].y;
+            acc.z += p[sp].z;
+            acc.w += p[sp].w;
+          }
+        }
+        for (int sp = 8; sp < a.nsplit; ++sp) {
+          const float4 q = *reinterpret_cast<const float4*>(mine + sp * a.split_stride + base + 4 * vi);
+          acc.x += q.x;
+          acc.y += q.y;
+          acc.z += q.z;
+          acc.w += q.w;
         }
         *reinterpret_cast<float4*>(mine + base + 4 * vi) = acc;
       }
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && VMC_AR_SYNC != 4) {
     const uint32_t e = a.epochs[b] + 1;
     a.epochs[b] = e;
-    __threadfence_system();
-    for (int q = 0; q < NR; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
+    if constexpr (VMC_AR_SYNC == 0) __threadfence_system();
+    if constexpr (VMC_AR_SYNC == 5) {
+      __threadfence();
+      for (int q = 0; q < NR; ++q) st_relaxed_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
+    } else {
+      for (int q = 0; q < NR; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
+    }
     int good = 1;
-    for (int q = 0; q < NR && good; ++q) {
-      uint32_t i = 0;
-      while (ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q) < e) {
-        if (++i > kSpinLimit) {
-          atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
-          good = 0;
-          break;
+    if constexpr (VMC_AR_SYNC != 3) {
+      for (int q = 0; q < NR && good; ++q) {
+        uint32_t i = 0;
+        while ((VMC_AR_SYNC == 0 ? ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q)
+                                 : ld_relaxed_sys(a.flags[a.rank] + b * kMaxRanks + q)) < e) {
+          if (++i > kSpinLimit) {
+            atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
+            good = 0;
+            break;
+          }
         }
       }
+      if constexpr (VMC_AR_SYNC == 5) __threadfence();
+      else if constexpr (VMC_AR_SYNC != 0) __threadfence_system();
     }
     ok = good;
   }
+  if (VMC_AR_SYNC == 4 && threadIdx.x == 0) ok = 1;
   __syncthreads();
   if (!ok) return;
   for (int row = b; row < a.T; row += gridDim.x) {

@@ -168,7 +168,8 @@ void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, t
                      int64_t total_tokens, int64_t Hq, int64_t Hkv, int64_t D, double scale, bool decode,
                      int64_t splits, c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse,
                      torch::Tensor out, c10::optional<torch::Tensor> tq_cache, std::vector<int64_t> tq_meta,
-                     c10::optional<torch::Tensor> tq_centroids, c10::optional<torch::Tensor> tq_midpoints) {
+                     c10::optional<torch::Tensor> tq_centroids, c10::optional<torch::Tensor> tq_midpoints,
+                     c10::optional<torch::Tensor> tree_mask, int64_t tree_span) {
   vmc::TqDev tq;
   const bool use_tq = tq_cache.has_value() && tq_cache->defined();
   if (use_tq) tq = make_tq(*tq_cache, tq_meta, *tq_centroids, *tq_midpoints);
@@ -193,7 +194,22 @@ void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, t
   a.part_lse = opt_ptr<float>(part_lse);
   a.out = out.data_ptr();
   a.tq = use_tq ? &tq : nullptr;
+  if (tree_mask.has_value() && tree_mask->defined()) {
+    TORCH_CHECK(tree_mask->scalar_type() == torch::kInt64 && tree_mask->numel() >= total_tokens,
+                "paged_attention: tree_mask must be int64 [T]");
+    a.tree_mask = reinterpret_cast<const uint64_t*>(tree_mask->data_ptr());
+    a.tree_span = static_cast<int>(tree_span);
+  }
   vmc::paged_attention(a, cur_stream());
+}
+
+void kv_move(torch::Tensor cache, int64_t Hkv, int64_t D, torch::Tensor src, torch::Tensor dst, torch::Tensor cnt,
+             int64_t num_reqs, int64_t max_moves) {
+  check_cuda(cache, "cache");
+  TORCH_CHECK(cache.scalar_type() == torch::kBFloat16 && cache.dim() == 6, "kv_move: bf16 [L, blocks, 2, Hkv, 16, D]");
+  vmc::kv_move(cache.data_ptr(), static_cast<int>(cache.size(0)), cache.stride(0), static_cast<int>(Hkv),
+               static_cast<int>(D), ptr<int32_t>(src), ptr<int32_t>(dst), ptr<int32_t>(cnt), static_cast<int>(num_reqs),
+               static_cast<int>(max_moves), cur_stream());
 }
 
 void embed(torch::Tensor ids, int64_t T, torch::Tensor table, int gtype, int64_t row_bytes, int64_t H,
@@ -311,7 +327,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("total_tokens"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("decode"),
         py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("out"), py::arg("tq_cache") = py::none(),
         py::arg("tq_meta") = std::vector<int64_t>{}, py::arg("tq_centroids") = py::none(),
-        py::arg("tq_midpoints") = py::none());
+        py::arg("tq_midpoints") = py::none(), py::arg("tree_mask") = py::none(), py::arg("tree_span") = 0);
+  m.def("kv_move", &kv_move);
   m.def("rope_store_tq", &rope_store_tq);
   m.def("embed", &embed);
   m.def("add_rmsnorm", &add_rmsnorm);

@@ -96,3 +96,60 @@ def test_mixed_offsets(cuda_ext):
     torch.cuda.synchronize()
     ref = _ref(kv, bt, q, qs, cl, Hq, Hkv, D)
     assert (out.float() - ref).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("span_extra", [0, 3])
+def test_prefill_tree_mask(cuda_ext, span_extra):
+    # Queries are the last q_len positions; the tree spans the last q_len + span_extra positions
+    # (span_extra > 0: earlier tree levels that are keys only, as in the draft's per-depth passes).
+    from vm_c_b200.speculative.tree import TokenTree
+    tree = TokenTree([2, 2, 1])
+    Hq, Hkv, D = 32, 8, 128
+    span = tree.N
+    ql = span - span_extra
+    ctx = [40 + span, 300 + span]
+    kv, bt, q, qs, cl, T = _setup(ctx, [ql, ql], Hq, Hkv, D, seed=4)
+    masks = torch.tensor(list(tree.masks[span_extra:span]) * 2, dtype=torch.int64, device="cuda")
+    out = torch.empty_like(q)
+    ops.paged_attention(q, kv, qs, cl, bt, 2, 0, ql, T, Hq, Hkv, D, 1 / math.sqrt(D), False, out,
+                        tree_mask=masks, tree_span=span)
+    torch.cuda.synchronize()
+    G = Hq // Hkv
+    ref = torch.zeros_like(q, dtype=torch.float32)
+    for r in range(2):
+        c = ctx[r]; a = int(qs[r])
+        nb = (c + 15) // 16
+        blocks = bt[r, :nb].long()
+        K = kv[blocks, 0].permute(1, 0, 2, 3).reshape(Hkv, nb * 16, D)[:, :c].float()
+        V = kv[blocks, 1].permute(1, 0, 2, 3).reshape(Hkv, nb * 16, D)[:, :c].float()
+        allow = torch.ones(ql, c, dtype=torch.bool, device="cuda")
+        base = c - span
+        for t in range(ql):
+            m = int(tree.masks[span_extra + t]) & ((1 << 64) - 1)
+            for i in range(span):
+                allow[t, base + i] = bool((m >> i) & 1)
+        for h in range(Hq):
+            s = q[a:a + ql, h].float() @ K[h // G].T / math.sqrt(D)
+            s = s.masked_fill(~allow, float("-inf"))
+            ref[a:a + ql, h] = torch.softmax(s, -1) @ V[h // G]
+    assert (out.float() - ref).abs().max().item() < 2e-2
+
+
+def test_kv_move_reads_before_writes(cuda_ext):
+    L, nb, Hkv, D = 3, 8, 2, 64
+    cache = torch.randn(L, nb, 2, Hkv, 16, D, device="cuda").bfloat16()
+    before = cache.clone()
+    # request 0: 20 -> 17, 23 -> 18 (18's old content is not a source); request 1: 34 -> 33, 36 -> 34
+    src = torch.tensor([[20, 23] + [0] * 14, [34, 36] + [0] * 14], dtype=torch.int32, device="cuda")
+    dst = torch.tensor([[17, 18] + [0] * 14, [33, 34] + [0] * 14], dtype=torch.int32, device="cuda")
+    cnt = torch.tensor([2, 2], dtype=torch.int32, device="cuda")
+    ops.kv_move(cache, Hkv, D, src, dst, cnt, 2, 16)
+    torch.cuda.synchronize()
+
+    def row(c, s):
+        return c[:, s // 16, :, :, s % 16]
+
+    for s_, d_ in ((20, 17), (23, 18), (34, 33), (36, 34)):
+        assert torch.equal(row(cache, d_), row(before, s_))
+    for s_ in (20, 23, 36, 0, 5):
+        assert torch.equal(row(cache, s_), row(before, s_))

@@ -128,3 +128,17 @@ def test_sampled_requests_take_the_plain_path():
     eng = make(k=4, bad=lambda p: False)
     eng.generate([[1, 2]], SamplingParams(temperature=0.8, max_tokens=6, ignore_eos=True, seed=1))
     assert eng.runner.spec.steps == 0 and eng.runner.spec.shadows >= 6
+
+
+def test_token_tree_layout():
+    from vm_c_b200.speculative.tree import TokenTree
+    t = TokenTree([2, 2, 1])
+    assert t.N == 11 and t.D == 3
+    assert t.parent.tolist() == [-1, 0, 0, 1, 1, 2, 2, 3, 4, 5, 6]
+    assert t.depth.tolist() == [0, 1, 1, 2, 2, 2, 2, 3, 3, 3, 3]
+    assert [list(t.level(d)) for d in range(4)] == [[0], [1, 2], [3, 4, 5, 6], [7, 8, 9, 10]]
+    m = [int(x) & ((1 << 64) - 1) for x in t.masks]
+    assert m[0] == 1 and m[3] == 0b1011 and m[10] == (1 | 1 << 2 | 1 << 6 | 1 << 10)
+    import pytest
+    with pytest.raises(ValueError):
+        TokenTree([8, 8])  # 73 nodes

@@ -64,3 +64,30 @@ def test_spec_equals_plain_greedy(models, which):
         assert st["tokens_per_step"] > 3.5, st
     else:
         assert st["acceptance_rate"] < 0.2, st
+
+
+def _gen_tree(path, prompts, n, draft, tree):
+    from vm_c_b200.llm import LLM
+    llm = LLM(path, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256,
+              enable_prefix_caching=False, draft_model=draft, spec_tree=tree)
+    outs = llm.generate(prompts, SamplingParams.greedy_params(max_tokens=n, ignore_eos=True))
+    stats = llm.runner.spec.stats.as_dict()
+    llm.shutdown()
+    return [o.output_token_ids for o in outs], stats
+
+
+@pytest.mark.parametrize("which,tree", [("self", "2,2,1"), ("other", "3,2"), ("other", "1,1,1,1")])
+def test_tree_spec_equals_plain_greedy(models, which, tree):
+    tgt, other = models
+    src = GgufSource(tgt)
+    cfg = src.model_config()
+    W = load_dense(src, cfg)
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (7, 33, 16, 70)]
+    n = 20
+    plain, _ = _gen(tgt, prompts, n)
+    spec, st = _gen_tree(tgt, prompts, n, tgt if which == "self" else other, tree)
+    _same_up_to_ties(W, cfg, prompts, spec, plain)
+    assert st["steps"] > 0
+    if which == "self":
+        assert st["tokens_per_step"] > 3.0, st

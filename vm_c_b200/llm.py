@@ -33,7 +33,8 @@ class LLM:
                  long_prefill_token_threshold: int = 0, scheduling_policy: str = "decode_first",
                  use_cuda_graphs: bool = True, device: Optional[str] = None, tp_rank: int = 0, tp_size: int = 1,
                  ep_size: int = 1, kv_cache_dtype: str = "auto", tq_rotation_seed: int = 0, draft_model: str = "",
-                 num_speculative_tokens: int = 5, cpu_offload_gb: float = 0.0, cpu_offload_params=(),
+                 num_speculative_tokens: int = 5, spec_tree: str = "", cpu_offload_gb: float = 0.0,
+                 cpu_offload_params=(),
                  comm=None, config: Optional[VmCConfig] = None, warmup: bool = True):
         import torch
         dev = device or (f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cuda")
@@ -61,6 +62,7 @@ class LLM:
             cfg.spec.method = "draft"
             cfg.spec.draft_model = draft_model
             cfg.spec.draft_n_max = num_speculative_tokens
+            cfg.spec.tree = spec_tree
         cfg.parallel.tensor_parallel_size = tp_size
         cfg.parallel.expert_parallel_size = ep_size
         cfg.finalize()

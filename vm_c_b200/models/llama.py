@@ -226,6 +226,8 @@ class StepMeta:
     num_decode: int   # leading decode requests (one token each)
     max_qlen: int     # max q_len over the prefill requests
     decode_qlen: int = 1
+    tree_mask: torch.Tensor | None = None  # int64 [T]: token-tree masks (prefill path)
+    tree_span: int = 0                     # bit 0 of a mask = key at position ctx - tree_span
 
 
 @dataclass
@@ -457,7 +459,8 @@ class LlamaModel:
                                 tq=tq)
         if m.R > nd:
             ops.paged_attention(ws.q, kv_layer, m.q_start, m.ctx_len, m.block_tables, m.R - nd, nd, m.max_qlen,
-                                m.T, self.hq, self.hkv, self.D, self.scale, False, ws.attn, tq=tq)
+                                m.T, self.hq, self.hkv, self.D, self.scale, False, ws.attn, tq=tq,
+                                tree_mask=m.tree_mask, tree_span=m.tree_span)
 
     def _sample(self, S: int, params: torch.Tensor, out_tok: torch.Tensor, out_lp) -> None:
         if self.tp > 1:

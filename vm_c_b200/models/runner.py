@@ -68,7 +68,12 @@ class GpuModelRunner(ModelRunner):
         if sp.method == "mtp":
             raise ValueError("--spec-method mtp needs next-n prediction layers, which the supported model "
                              "families do not have; use --spec-method draft --draft-model <gguf>")
-        self.spec_k = sp.draft_n_max if sp.method == "draft" else 0
+        self.spec_tree = [int(x) for x in sp.tree.split(",") if x.strip()] if (sp.method == "draft" and sp.tree) else []
+        if self.spec_tree:
+            from ..speculative.tree import TokenTree
+            self.spec_k = TokenTree(self.spec_tree).N - 1   # look-ahead slots: every non-root tree node
+        else:
+            self.spec_k = sp.draft_n_max if sp.method == "draft" else 0
         self.num_lookahead_tokens = self.spec_k
         max_seqs = max(s.max_num_seqs, 1)
         # Sampled rows: one per request, or k + 1 per request when speculative verification runs.
@@ -172,6 +177,7 @@ class GpuModelRunner(ModelRunner):
         from .. import _native
         from ..llm import make_source
         from ..speculative.draft import DraftSpeculator
+        from ..speculative.tree import TreeSpeculator
         sp = self.cfg.spec
         if not sp.draft_model:
             raise ValueError("--spec-method draft needs --draft-model")
@@ -179,8 +185,15 @@ class GpuModelRunner(ModelRunner):
         spec_layout = _native.host().BatchLayout(self.max_tokens, self.max_samples, self.layout.max_blocks_per_seq)
         self.tok_spec = torch.zeros(self.max_samples, dtype=torch.int32, device=self.dev)
         self.tok_spec_host = torch.zeros(self.max_samples, dtype=torch.int32).pin_memory()
-        self.spec = DraftSpeculator(self, src, dcfg, self.spec_k, comm=self.comm, layout=spec_layout)
-        log.info("speculative decoding: draft %s, k = %d", sp.draft_model, self.spec_k)
+        if self.spec_tree:
+            if self.tq is not None:
+                raise ValueError("token-tree speculation needs a bf16 KV cache (the accepted branch is moved in place)")
+            self.spec = TreeSpeculator(self, src, dcfg, self.spec_tree, comm=self.comm, layout=spec_layout)
+            log.info("speculative decoding: draft %s, token tree %s (%d nodes)", sp.draft_model, self.spec_tree,
+                     self.spec_k + 1)
+        else:
+            self.spec = DraftSpeculator(self, src, dcfg, self.spec_k, comm=self.comm, layout=spec_layout)
+            log.info("speculative decoding: draft %s, k = %d", sp.draft_model, self.spec_k)
 
     def _meta(self, T, R, S, nd, max_qlen) -> StepMeta:
         return StepMeta(self.v_ids, self.v_pos, self.v_slots, self.v_qs, self.v_ctx, self.v_bt, self.v_lidx,

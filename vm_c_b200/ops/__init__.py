@@ -245,18 +245,29 @@ def gather_rows(src, idx, n, H, dst):
 
 
 def paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq, Hkv,
-                    D, scale, decode, out, splits=1, part_o=None, part_lse=None, tq=None):
+                    D, scale, decode, out, splits=1, part_o=None, part_lse=None, tq=None, tree_mask=None,
+                    tree_span=0):
     """Paged attention over bf16 pages ``kv``, or over a TurboQuant cache layer when ``tq`` is a
-    (cache layer, TqTables) pair (``kv`` is then ignored)."""
+    (cache layer, TqTables) pair (``kv`` is then ignored). ``tree_mask`` (int64 [T], prefill path):
+    bit i of a token's mask lets it attend to the key at position ctx - tree_span + i of its
+    request (token trees; keys before that are context, visible to all); null = causal."""
     if tq is None:
         C().paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq,
-                            Hkv, D, scale, decode, splits, part_o, part_lse, out)
+                            Hkv, D, scale, decode, splits, part_o, part_lse, out, tree_mask=tree_mask,
+                            tree_span=tree_span)
     else:
         cache, tab = tq
         C().paged_attention(q, cache, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens,
                             Hq, Hkv, D, scale, decode, splits, part_o, part_lse, out, cache, tab.meta(),
-                            tab.centroids, tab.midpoints)
+                            tab.centroids, tab.midpoints, tree_mask, tree_span)
     _count(2 if (decode and splits > 1) else 1)
+
+
+def kv_move(cache, Hkv, D, src, dst, cnt, num_reqs, max_moves):
+    """Move KV rows (all layers, K and V) of a bf16 paged cache [L, blocks, 2, Hkv, 16, D]: request r
+    moves cnt[r] slots src[r, i] -> dst[r, i]; all reads happen before the writes."""
+    C().kv_move(cache, Hkv, D, src, dst, cnt, num_reqs, max_moves)
+    _count()
 
 
 # Sampling parameters: one 40-byte record per row (csrc/kernels/sampling.h SampleParams).
