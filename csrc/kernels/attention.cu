@@ -26,6 +26,10 @@ namespace vmc {
 namespace {
 
 constexpr int kBS = 16;  // tokens per KV block
+#ifndef VMC_DEC_STAGES
+#define VMC_DEC_STAGES 3
+#endif
+constexpr int kDecStages = VMC_DEC_STAGES;  // KV pages in flight per decode warp (ring depth)
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -375,8 +379,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int tota
   for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
 
-  // Per-warp double buffer: stage s holds K rows [0,16) and V rows [0,16) of one page.
-  uint8_t* wsm = smem + warp * (2 * 2 * kBS * RB);
+  // Per-warp ring of kDecStages pages: stage s holds K rows [0,16) and V rows [0,16) of one page.
+  uint8_t* wsm = smem + warp * (kDecStages * 2 * kBS * RB);
   auto sK = [&](int s) { return wsm + s * (2 * kBS * RB); };
   auto sV = [&](int s) { return wsm + s * (2 * kBS * RB) + kBS * RB; };
   const int64_t page_elems = static_cast<int64_t>(kBS) * D;
@@ -405,18 +409,21 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p, int tota
     }
   };
   int b = b0 + warp;
-  int stage = 0, j = 0;
-  if (b < b1) issue(0, 0);
-  cp_async_commit();
-  for (; b < b1; b += 4, ++j) {
-    const int nb = b + 4;
-    if (nb < b1) issue(j + 1, stage ^ 1);
+  int j = 0;
+#pragma unroll
+  for (int s = 0; s < kDecStages - 1; ++s) {
+    if (b + 4 * s < b1) issue(s, s);
     cp_async_commit();
-    cp_async_wait<1>();
+  }
+  for (; b < b1; b += 4, ++j) {
+    const int ahead = j + kDecStages - 1;
+    if (b + 4 * (kDecStages - 1) < b1) issue(ahead, ahead % kDecStages);
+    cp_async_commit();
+    cp_async_wait<kDecStages - 1>();
     __syncwarp();
+    const int stage = j % kDecStages;
     attn_step16<D>(sK(stage), sV(stage), 0, b * kBS, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane);
     __syncwarp();
-    stage ^= 1;
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -566,7 +573,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
 template <int D>
 constexpr int decode_smem() {
   constexpr int RB = Frag<D>::RB;
-  constexpr int smem_pipe = 4 * 2 * 2 * kBS * RB;
+  constexpr int smem_pipe = 4 * kDecStages * 2 * kBS * RB;
   constexpr int smem_merge = 4 * 16 * D * 4 + 4 * 16 * 2 * 4;
   return smem_pipe > smem_merge ? smem_pipe : smem_merge;
 }

@@ -3,9 +3,10 @@
     python -m vm_c_b200.ops.bench [case ...] [--reps N]
 
 Cases: gemm:<name> (decode / prefill projections of the 8B model, see GEMM_CASES), attn:decode,
-attn:prefill (one 2048-token prompt), attn:prefill2 (two 1024-token prompts), norm, rope, swiglu, sample. Each case is timed with CUDA events on the current stream
-after warm-up, with a 256 MB buffer written between repetitions so that every repetition reads its
-inputs from HBM; the median is reported with the achieved bandwidth / FLOP rate. These are the
+attn:prefill (one 2048-token prompt), attn:prefill2 (two 1024-token prompts), norm, rope, swiglu,
+sample. Each case is captured in a CUDA graph after warm-up and timed with CUDA events around the
+graph replay (no host launch overhead, as in the engine's decode graphs), with a 256 MB buffer
+written between repetitions so that every repetition reads its inputs from HBM; the median is reported with the achieved bandwidth / FLOP rate. These are the
 cases the committed ncu summaries were captured on.
 """
 from __future__ import annotations
@@ -39,7 +40,16 @@ GEMM_CASES = {
 
 
 def _time(fn, reps: int, flush: torch.Tensor) -> float:
+    """Median device time of `fn` in microseconds. `fn` is captured once in a CUDA graph and the
+    graph is replayed between two events, so host launch overhead (argument marshalling, tensor-map
+    encoding) is not in the number, as in the engine's decode graphs."""
     for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
         fn()
     torch.cuda.synchronize()
     ts = []
@@ -47,10 +57,11 @@ def _time(fn, reps: int, flush: torch.Tensor) -> float:
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        fn()
+        g.replay()
         e1.record()
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1) * 1e3)
+    del g
     return sorted(ts)[len(ts) // 2]
 
 
