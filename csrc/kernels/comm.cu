@@ -40,6 +40,10 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Flag protocol. 0: system-scope fence + release store / acquire loads. 1: GPU-scope fences around
+// relaxed system-scope flag accesses — a peer reads this GPU's partial through this GPU's L2 over
+// NVLink, so the data only has to be visible at GPU scope before the flag goes out; measured
+// ~2x cheaper per call than 0 (the system-scope fence dominates a decode-sized all-reduce).
 #ifndef VMC_AR_SYNC
 #define VMC_AR_SYNC 0
 #endif
@@ -100,35 +104,33 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0 && VMC_AR_SYNC != 4) {
+  if (threadIdx.x == 0) {
     const uint32_t e = a.epochs[b] + 1;
     a.epochs[b] = e;
-    if constexpr (VMC_AR_SYNC == 0) __threadfence_system();
-    if constexpr (VMC_AR_SYNC == 5) {
+    // Publish: the partial rows this CTA's peers will read are in this GPU's memory (written by the
+    // previous kernel or by phase 1 above); then one flag store per rank.
+    if constexpr (VMC_AR_SYNC == 0) {
+      __threadfence_system();
+      for (int q = 0; q < NR; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
+    } else {
       __threadfence();
       for (int q = 0; q < NR; ++q) st_relaxed_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
-    } else {
-      for (int q = 0; q < NR; ++q) st_release_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
     }
     int good = 1;
-    if constexpr (VMC_AR_SYNC != 3) {
-      for (int q = 0; q < NR && good; ++q) {
-        uint32_t i = 0;
-        while ((VMC_AR_SYNC == 0 ? ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q)
-                                 : ld_relaxed_sys(a.flags[a.rank] + b * kMaxRanks + q)) < e) {
-          if (++i > kSpinLimit) {
-            atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
-            good = 0;
-            break;
-          }
+    for (int q = 0; q < NR && good; ++q) {
+      uint32_t i = 0;
+      while ((VMC_AR_SYNC == 0 ? ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q)
+                               : ld_relaxed_sys(a.flags[a.rank] + b * kMaxRanks + q)) < e) {
+        if (++i > kSpinLimit) {
+          atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
+          good = 0;
+          break;
         }
       }
-      if constexpr (VMC_AR_SYNC == 5) __threadfence();
-      else if constexpr (VMC_AR_SYNC != 0) __threadfence_system();
     }
+    if constexpr (VMC_AR_SYNC != 0) __threadfence();
     ok = good;
   }
-  if (VMC_AR_SYNC == 4 && threadIdx.x == 0) ok = 1;
   __syncthreads();
   if (!ok) return;
   for (int row = b; row < a.T; row += gridDim.x) {
