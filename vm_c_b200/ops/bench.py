@@ -4,7 +4,7 @@
 
 Cases: gemm:<name> (decode / prefill projections of the 8B model, see GEMM_CASES), attn:decode,
 attn:prefill (one 2048-token prompt), attn:prefill2 (two 1024-token prompts), norm, rope, swiglu,
-sample. Each case is captured in a CUDA graph after warm-up and timed with CUDA events around the
+sample, and step:decode (a whole engine decode step; not part of "all"). Each case is captured in a CUDA graph after warm-up and timed with CUDA events around the
 graph replay (no host launch overhead, as in the engine's decode graphs), with a 256 MB buffer
 written between repetitions so that every repetition reads its inputs from HBM; the median is reported with the achieved bandwidth / FLOP rate. These are the
 cases the committed ncu summaries were captured on.
@@ -166,6 +166,44 @@ def bench_small(kind: str, reps: int, flush: torch.Tensor) -> str:
     return f"{kind:12s} {t:8.1f} us  {nbytes / t / 1e6:5.2f} TB/s"
 
 
+def bench_step(kind: str, reps: int) -> str:
+    """Whole engine steps of the 8B serving config (random-init Q4_K_M weights, 64 requests with
+    1024-token prompts): run until every request decodes, time `reps` decode steps (wall clock
+    around a synchronised step; the step replays a CUDA graph), then run one more step between
+    cudaProfilerStart / Stop so that `ncu --profile-from-start off` captures exactly one step."""
+    import time
+
+    import numpy as np
+
+    from ..core.sampling_params import SamplingParams
+    from ..llm import LLM
+    R, P = 64, 1024
+    llm = LLM("random:llama3-8b:Q4_K_M:0", max_model_len=2048, max_num_seqs=R, max_num_batched_tokens=2048,
+              num_gpu_blocks=R * ((P + 300) // 16) + 64)
+    eng = llm.engine
+    rng = np.random.default_rng(0)
+    sp = SamplingParams.greedy_params(max_tokens=64, ignore_eos=True)
+    for _ in range(R):
+        eng.add_request(rng.integers(0, llm.cfg.model.vocab, P).tolist(), sp)
+    while eng.sched.num_waiting or any(len(r.output_token_ids) < 2 for r in eng.requests.values()):
+        eng.step()
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        eng.step()
+        torch.cuda.synchronize()
+        ts.append((time.perf_counter() - t0) * 1e3)
+    torch.cuda.profiler.start()
+    eng.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    llm.shutdown()
+    return f"step:decode  64 requests, context ~{P + 8}  median {sorted(ts)[len(ts) // 2]:.3f} ms  ({len(ts)} steps)"
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("cases", nargs="*", default=["all"])
@@ -179,6 +217,8 @@ def main(argv=None) -> None:
     for c in cases:
         if c.startswith("gemm:"):
             line = bench_gemm(c[5:], a.reps, flush)
+        elif c.startswith("step:"):
+            line = bench_step(c[5:], min(a.reps, 10))
         elif c.startswith("attn:"):
             line = bench_attn(c[5:], a.reps, flush)
         else:
