@@ -30,6 +30,10 @@ constexpr int kBS = 16;  // tokens per KV block
 #define VMC_DEC_STAGES 3
 #endif
 constexpr int kDecStages = VMC_DEC_STAGES;  // KV pages in flight per decode warp (ring depth)
+#ifndef VMC_PRE_NS
+#define VMC_PRE_NS 1
+#endif
+constexpr int kPreNS = VMC_PRE_NS;  // 16-key sub-blocks per softmax update on unmasked prefill tiles
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -92,43 +96,50 @@ __device__ __forceinline__ void load_q_frags(const AttnParams& p, int qs, int ql
   }
 }
 
-// One 16-key step of attention for a warp's 16 rows. K/V rows key0..key0+15 of the smem tiles.
-// kpos0: absolute position of the first key; qpos_lo/hi: absolute positions of this thread's two
-// rows (or -1 for invalid rows); klimit: number of valid keys (context length).
-template <int D>
-__device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV, int key0, int kpos0,
-                                            const uint32_t (&qa)[Frag<D>::KD][4], int qpos_lo, int qpos_hi,
-                                            float scale_log2, float (&o)[Frag<D>::ND][4], float (&m)[2],
-                                            float (&l)[2], int lane, bool tree = false, int tbase = 0,
-                                            uint64_t tm_lo = 0, uint64_t tm_hi = 0) {
+// One step of attention over NS x 16 keys for a warp's 16 rows: S = Q K^T for all NS sub-blocks,
+// one online-softmax update (one rescale of O) for the whole step, then O += P V. K/V rows
+// key0 .. key0 + 16 NS - 1 of the smem tiles. kpos0: absolute position of the first key;
+// qpos_lo/hi: absolute positions of this thread's two rows (-1 for invalid rows); keys past a row's
+// position are masked (and, with a tree mask, keys at or after tbase that are not its ancestors).
+template <int D, int NS, bool MASK = true>
+__device__ __forceinline__ void attn_step(const uint8_t* sK, const uint8_t* sV, int key0, int kpos0,
+                                          const uint32_t (&qa)[Frag<D>::KD][4], int qpos_lo, int qpos_hi,
+                                          float scale_log2, float (&o)[Frag<D>::ND][4], float (&m)[2], float (&l)[2],
+                                          int lane, bool tree = false, int tbase = 0, uint64_t tm_lo = 0,
+                                          uint64_t tm_hi = 0) {
   constexpr int RB = Frag<D>::RB;
-  float s[2][4];
+  float s[2 * NS][4];
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
+  for (int j = 0; j < 2 * NS; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
-  // S = Q K^T over 16 keys (two n-tiles of 8).
+  // S = Q K^T: two n-tiles of 8 keys per sub-block.
 #pragma unroll
-  for (int kd = 0; kd < Frag<D>::KD; ++kd) {
-    uint32_t b[4];
-    const int i = lane;
-    const int key = key0 + (i & 7) + 8 * (i >> 4);
-    const int dim = 16 * kd + 8 * ((i >> 3) & 1);
-    ldmatrix_x4(b, smem_u32(sK + key * RB + dim * 2));
-    mma_bf16_16816(s[0], qa[kd], b[0], b[1]);
-    mma_bf16_16816(s[1], qa[kd], b[2], b[3]);
+  for (int sb = 0; sb < NS; ++sb) {
+#pragma unroll
+    for (int kd = 0; kd < Frag<D>::KD; ++kd) {
+      uint32_t b[4];
+      const int i = lane;
+      const int key = key0 + 16 * sb + (i & 7) + 8 * (i >> 4);
+      const int dim = 16 * kd + 8 * ((i >> 3) & 1);
+      ldmatrix_x4(b, smem_u32(sK + key * RB + dim * 2));
+      mma_bf16_16816(s[2 * sb], qa[kd], b[0], b[1]);
+      mma_bf16_16816(s[2 * sb + 1], qa[kd], b[2], b[3]);
+    }
   }
   // Mask + online softmax. Thread holds rows (lane/4) [e=0,1] and (lane/4 + 8) [e=2,3].
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
+  for (int j = 0; j < 2 * NS; ++j) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int kp = kpos0 + 8 * j + 2 * (lane & 3) + (e & 1);
       const int qp = (e < 2) ? qpos_lo : qpos_hi;
       float v = s[j][e] * scale_log2;
-      if (kp > qp) v = -INFINITY;
-      else if (tree && kp >= tbase && !((((e < 2) ? tm_lo : tm_hi) >> (kp - tbase)) & 1ull)) v = -INFINITY;
+      if constexpr (MASK) {
+        if (kp > qp) v = -INFINITY;
+        else if (tree && kp >= tbase && !((((e < 2) ? tm_lo : tm_hi) >> (kp - tbase)) & 1ull)) v = -INFINITY;
+      }
       s[j][e] = v;
       mx[e >> 1] = fmaxf(mx[e >> 1], v);
     }
@@ -143,9 +154,9 @@ __device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV
     m[h] = mnew;
   }
   float rs[2] = {0.f, 0.f};
-  uint32_t pa[4];
+  uint32_t pa[NS][4];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
+  for (int j = 0; j < 2 * NS; ++j) {
     float pv[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -153,9 +164,9 @@ __device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV
       pv[e] = (mm == -INFINITY) ? 0.f : exp2f(s[j][e] - mm);
       rs[e >> 1] += pv[e];
     }
-    // A fragment of P (16 rows x 16 keys): a0/a1 from n-tile 0, a2/a3 from n-tile 1.
-    pa[2 * j] = pack_bf16x2(pv[0], pv[1]);
-    pa[2 * j + 1] = pack_bf16x2(pv[2], pv[3]);
+    // A fragment of P (16 rows x 16 keys) of sub-block j / 2: a0/a1 from its n-tile 0, a2/a3 from 1.
+    pa[j >> 1][2 * (j & 1)] = pack_bf16x2(pv[0], pv[1]);
+    pa[j >> 1][2 * (j & 1) + 1] = pack_bf16x2(pv[2], pv[3]);
   }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -170,17 +181,28 @@ __device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV
     o[nd][2] *= corr[1];
     o[nd][3] *= corr[1];
   }
-  // O += P V (16 keys = one k-step).
+  // O += P V, one k-step of 16 keys per sub-block.
 #pragma unroll
-  for (int nd = 0; nd < Frag<D>::ND; nd += 2) {
-    uint32_t b[4];
-    const int i = lane;
-    const int key = key0 + (i & 7) + 8 * ((i >> 3) & 1);
-    const int dim = 8 * nd + 8 * (i >> 4);
-    ldmatrix_x4_trans(b, smem_u32(sV + key * RB + dim * 2));
-    mma_bf16_16816(o[nd], pa, b[0], b[1]);
-    mma_bf16_16816(o[nd + 1], pa, b[2], b[3]);
+  for (int sb = 0; sb < NS; ++sb) {
+#pragma unroll
+    for (int nd = 0; nd < Frag<D>::ND; nd += 2) {
+      uint32_t b[4];
+      const int i = lane;
+      const int key = key0 + 16 * sb + (i & 7) + 8 * ((i >> 3) & 1);
+      const int dim = 8 * nd + 8 * (i >> 4);
+      ldmatrix_x4_trans(b, smem_u32(sV + key * RB + dim * 2));
+      mma_bf16_16816(o[nd], pa[sb], b[0], b[1]);
+      mma_bf16_16816(o[nd + 1], pa[sb], b[2], b[3]);
+    }
   }
+}
+
+template <int D>
+__device__ __forceinline__ void attn_step16(const uint8_t* sK, const uint8_t* sV, int key0, int kpos0,
+                                            const uint32_t (&qa)[Frag<D>::KD][4], int qpos_lo, int qpos_hi,
+                                            float scale_log2, float (&o)[Frag<D>::ND][4], float (&m)[2],
+                                            float (&l)[2], int lane) {
+  attn_step<D, 1>(sK, sV, key0, kpos0, qa, qpos_lo, qpos_hi, scale_log2, o, m, l, lane);
 }
 
 // TurboQuant: dequantise half (dims [half * D/2, (half + 1) * D/2)) of one key's K and V slot into
@@ -345,6 +367,7 @@ __device__ __forceinline__ void decode_merge_store(const AttnParams& p, uint8_t*
   }
 }
 
+
 // ---------------------------------------------------------------------------------------------
 // Decode: one CTA = (request, kv head, split); 16 packed rows; 4 warps split the pages.
 
@@ -494,6 +517,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
   // Rows of this warp that exist at all (skip compute for fully invalid warps).
   const bool warp_active = prow0 < rows;
   const int warp_qmax = warp_active ? (ctx - qlen + (min(rows, prow0 + 16) - 1) / p.G) : -1;
+  const int warp_qmin = ctx - qlen + prow0 / p.G;  // position of the warp's first row
 
   float o[ND][4];
 #pragma unroll
@@ -542,12 +566,22 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnParams p) {
     cp_async_wait<1>();
     __syncthreads();
     if (warp_active) {
+      const int kpos0 = tile * TK;
+      if (!tree && kpos0 + TK - 1 <= warp_qmin) {
+        // every key of the tile precedes every row of the warp: no mask, one softmax update per
+        // kPreNS x 16 keys
 #pragma unroll
-      for (int sub = 0; sub < TK / 16; ++sub) {
-        const int kpos0 = tile * TK + sub * 16;
-        if (kpos0 <= warp_qmax && kpos0 < kmax)
-          attn_step16<D>(sK(s), sV(s), sub * 16, kpos0, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane, tree,
-                         ctx - p.tree_span, tm_lo, tm_hi);
+        for (int sub = 0; sub < TK / 16; sub += kPreNS)
+          attn_step<D, kPreNS, false>(sK(s), sV(s), sub * 16, kpos0 + sub * 16, qa, qpos_lo, qpos_hi, p.scale_log2,
+                                      o, m, l, lane);
+      } else {
+#pragma unroll
+        for (int sub = 0; sub < TK / 16; ++sub) {
+          const int kp0 = kpos0 + sub * 16;
+          if (kp0 <= warp_qmax && kp0 < kmax)
+            attn_step<D, 1>(sK(s), sV(s), sub * 16, kp0, qa, qpos_lo, qpos_hi, p.scale_log2, o, m, l, lane, tree,
+                            ctx - p.tree_span, tm_lo, tm_hi);
+        }
       }
     }
     __syncthreads();
