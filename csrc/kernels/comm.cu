@@ -40,12 +40,13 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Flag protocol. 0: system-scope fence + release store / acquire loads. 1: GPU-scope fences around
-// relaxed system-scope flag accesses — a peer reads this GPU's partial through this GPU's L2 over
-// NVLink, so the data only has to be visible at GPU scope before the flag goes out; measured
-// ~2x cheaper per call than 0 (the system-scope fence dominates a decode-sized all-reduce).
+// Flag protocol. 1 (default): GPU-scope fences around relaxed system-scope flag accesses — a peer
+// reads this GPU's partial through this GPU's L2 over NVLink, so the data only has to be visible at
+// GPU scope before the flag goes out. 0: system-scope fence + release store / acquire loads.
+// Measured on 2 B200s inside CUDA graphs (64 x 4096 fp32, 4 split-K partials): 14.5 us for 1,
+// 24.5 us for 0, 17.9 us for NCCL all-reduce + a separate residual/RMSNorm kernel.
 #ifndef VMC_AR_SYNC
-#define VMC_AR_SYNC 0
+#define VMC_AR_SYNC 1
 #endif
 // Peer data: bypass L1 so that a line cached by an earlier call is never reused.
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
