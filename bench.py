@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--gen-len", type=int, default=256)
     ap.add_argument("--max-num-batched-tokens", type=int, default=2048)
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--comm", default=os.environ.get("VMC_COMM", "nccl"), choices=["nccl", "fused"])
+    ap.add_argument("--comm", default=os.environ.get("VMC_COMM", "fused"), choices=["nccl", "fused"])
     ap.add_argument("--e2e-steps", type=int, default=1)
     return ap.parse_args()
 
