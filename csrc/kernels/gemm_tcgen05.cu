@@ -143,65 +143,21 @@ __device__ __forceinline__ uint32_t bfma2(uint32_t a, uint32_t b, uint32_t c) {
 
 constexpr uint32_t kMagic128x2 = 0x43004300u;  // bf16 (128, 128); 128 + q is exact for q < 128
 
-__device__ __forceinline__ void dq_q4k(const uint8_t* row, int s, int h, uint32_t (&o)[16]) {
-  const uint32_t dd = *reinterpret_cast<const uint32_t*>(row);
-  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu)));
-  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16)));
-  const uint8_t* sc = row + 4;
-  const int j = 2 * s + h;
-  int scv, mv;
-  if (j < 4) {
-    scv = sc[j] & 63;
-    mv = sc[j + 4] & 63;
-  } else {
-    scv = (sc[j + 4] & 0x0f) | ((sc[j - 4] >> 6) << 4);
-    mv = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-  }
-  const uint32_t ds2 = bf2_splat(d * static_cast<float>(scv));
-  const uint32_t ndm2 = bf2_splat(-dmin * static_cast<float>(mv));
-  const uint4* q = reinterpret_cast<const uint4*>(row + 16 + 32 * s);
-  const uint4 w0 = q[0], w1 = q[1];
-  const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-  const int sh0 = h ? 4 : 0, sh1 = h ? 12 : 8;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    uint32_t p01 = ((w[i] >> sh0) & 0x000f000fu) | kMagic128x2;
-    uint32_t p23 = ((w[i] >> sh1) & 0x000f000fu) | kMagic128x2;
-    o[2 * i] = bf2_fma(bf2_sub(p01, kMagic128x2), ds2, ndm2);
-    o[2 * i + 1] = bf2_fma(bf2_sub(p23, kMagic128x2), ds2, ndm2);
-  }
-}
-
 // Per-chunk Q4_K state of thread (row, half): bf16x2 scale and negated min of its four sub-blocks
 // j = 2s + h (s = 0..3), decoded once per 256-K chunk instead of once per 64-K substep.
 struct Q4KChunk {
   uint32_t ds2[4], ndm2[4];
 };
 __device__ __forceinline__ void q4k_prep(const uint8_t* row, int h, Q4KChunk& c) {
-  const uint32_t dd = *reinterpret_cast<const uint32_t*>(row);
-  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu)));
-  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16)));
-  const uint32_t s0 = *reinterpret_cast<const uint32_t*>(row + 4);
-  const uint32_t s1 = *reinterpret_cast<const uint32_t*>(row + 8);
-  const uint32_t s2 = *reinterpret_cast<const uint32_t*>(row + 12);
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
-    const int j = 2 * s + h;
-    int scv, mv;
-    if (s < 2) {  // j < 4
-      scv = (s0 >> (8 * j)) & 63;
-      mv = (s1 >> (8 * j)) & 63;
-    } else {      // j >= 4
-      const int k = j - 4;
-      scv = ((s2 >> (8 * k)) & 0x0f) | (((s0 >> (8 * k + 6)) & 3) << 4);
-      mv = ((s2 >> (8 * k + 4)) & 0x0f) | (((s1 >> (8 * k + 6)) & 3) << 4);
-    }
-    c.ds2[s] = bf2_splat(d * static_cast<float>(scv));
-    c.ndm2[s] = bf2_splat(-dmin * static_cast<float>(mv));
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + 4 * (2 * s + h));  // (ds, ndm) of sub-block j
+    c.ds2[s] = __byte_perm(w, 0u, 0x1010);
+    c.ndm2[s] = __byte_perm(w, 0u, 0x3232);
   }
 }
 __device__ __forceinline__ void q4k_sub(const uint8_t* row, int s, int h, const Q4KChunk& c, uint32_t (&o)[16]) {
-  const uint4* q = reinterpret_cast<const uint4*>(row + 16 + 32 * s);
+  const uint4* q = reinterpret_cast<const uint4*>(row + 32 + 32 * s);
   const uint4 w0 = q[0], w1 = q[1];
   const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
   const uint32_t ds2 = c.ds2[s], ndm2 = c.ndm2[s];
@@ -677,35 +633,14 @@ constexpr int kDFirstEpi = 20;
 constexpr int kDSlots = 2;
 constexpr uint32_t kDACol = 256;
 
-// Q4_K scale / negated min of sub-block J (bf16x2 splats) from the 16-byte block header (fp16 d,
-// fp16 dmin, 12 bytes of packed 6-bit scales and mins); J is a compile-time constant so the
-// bit-field offsets fold.
-template <int J>
-__device__ __forceinline__ void q4k_scale_c(const uint4& hdr, uint32_t& ds2, uint32_t& ndm2) {
-  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x & 0xffffu)));
-  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x >> 16)));
-  uint32_t scv, mv;
-  if constexpr (J < 4) {
-    scv = (hdr.y >> (8 * J)) & 63u;
-    mv = (hdr.z >> (8 * J)) & 63u;
-  } else {
-    constexpr int k = J - 4;
-    scv = ((hdr.w >> (8 * k)) & 0x0fu) | (((hdr.y >> (8 * k + 6)) & 3u) << 4);
-    mv = ((hdr.w >> (8 * k + 4)) & 0x0fu) | (((hdr.z >> (8 * k + 6)) & 3u) << 4);
-  }
-  ds2 = bf2_splat(d * static_cast<float>(scv));
-  ndm2 = bf2_splat(-dmin * static_cast<float>(mv));
-}
-
 // 64 K-values of substep S of one Q4_K row: o[0..15] = sub-block 2S, o[16..31] = sub-block 2S + 1
 // (bf16 pairs in K order). Per 8 values: 3 shifts + 4 lop3 on the integer pipe, 4 sub + 4 fma.
 template <int S>
 __device__ __forceinline__ void q4k_row64(const uint8_t* row, uint32_t (&o)[32]) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(row);
-  uint32_t ds_lo, dm_lo, ds_hi, dm_hi;
-  q4k_scale_c<2 * S>(hdr, ds_lo, dm_lo);
-  q4k_scale_c<2 * S + 1>(hdr, ds_hi, dm_hi);
-  const uint4* q = reinterpret_cast<const uint4*>(row + 16 + 32 * S);
+  const uint2 sc = *reinterpret_cast<const uint2*>(row + 8 * S);  // (ds, ndm) of sub-blocks 2S, 2S + 1
+  const uint32_t ds_lo = __byte_perm(sc.x, 0u, 0x1010), dm_lo = __byte_perm(sc.x, 0u, 0x3232);
+  const uint32_t ds_hi = __byte_perm(sc.y, 0u, 0x1010), dm_hi = __byte_perm(sc.y, 0u, 0x3232);
+  const uint4* q = reinterpret_cast<const uint4*>(row + 32 + 32 * S);
   const uint4 w0 = q[0], w1 = q[1];
   const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll

@@ -24,16 +24,30 @@ __global__ void repack_q4k_kernel(const uint8_t* __restrict__ src, int N, int KB
   const int Np = (N + 127) / 128 * 128;
   if (idx >= static_cast<int64_t>(Np) * KB) return;
   const int n = static_cast<int>(idx / KB), kb = static_cast<int>(idx % KB);
-  uint8_t* o = dst + ((static_cast<int64_t>(n / 128) * KB + kb) * 128 + (n % 128)) * 144;
+  uint8_t* o = dst + ((static_cast<int64_t>(n / 128) * KB + kb) * 128 + (n % 128)) * 160;
   if (n >= N) {
-    for (int i = 0; i < 144; ++i) o[i] = 0;
+    for (int i = 0; i < 160; ++i) o[i] = 0;
     return;
   }
   const uint8_t* s = src + (static_cast<int64_t>(n) * KB + kb) * 144;
-  for (int i = 0; i < 16; ++i) o[i] = s[i];
+  // GGUF Q4_K header: fp16 d, fp16 dmin, 12 bytes packing eight 6-bit (scale, min) pairs.
+  const float d = ld_half(s), dmin = ld_half(s + 2);
+  const uint8_t* sc = s + 4;
+  for (int j = 0; j < 8; ++j) {
+    int scv, mv;
+    if (j < 4) {
+      scv = sc[j] & 63;
+      mv = sc[j + 4] & 63;
+    } else {
+      scv = (sc[j + 4] & 0x0f) | ((sc[j - 4] >> 6) << 4);
+      mv = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    st_u16(o + 4 * j, __bfloat16_as_ushort(__float2bfloat16(d * static_cast<float>(scv))));
+    st_u16(o + 4 * j + 2, __bfloat16_as_ushort(__float2bfloat16(-dmin * static_cast<float>(mv))));
+  }
   for (int g = 0; g < 32; ++g) {  // nibble bytes, 4-byte groups reordered (0,2,1,3)
     const uint8_t* q = s + 16 + 4 * g;
-    uint8_t* p = o + 16 + 4 * g;
+    uint8_t* p = o + 32 + 4 * g;
     p[0] = q[0];
     p[1] = q[2];
     p[2] = q[1];

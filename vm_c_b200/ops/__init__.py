@@ -22,7 +22,7 @@ NUM_SMS = 148
 _WF_FOR_GTYPE = {GType.Q4_K: WF_Q4K, GType.Q6_K: WF_Q6K, GType.Q8_0: WF_Q8_0,
                  GType.F32: WF_BF16, GType.F16: WF_BF16, GType.BF16: WF_BF16}
 _CHUNK = {WF_BF16: 64, WF_Q4K: 256, WF_Q6K: 256, WF_Q8_0: 256}
-_ROWB = {WF_BF16: 128, WF_Q4K: 144, WF_Q6K: 224, WF_Q8_0: 272}
+_ROWB = {WF_BF16: 128, WF_Q4K: 160, WF_Q6K: 224, WF_Q8_0: 272}
 
 
 def C():
