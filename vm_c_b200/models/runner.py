@@ -43,7 +43,8 @@ def is_turboquant(kv_cache_dtype: str) -> bool:
 def check_kv_cache_dtype(kv_cache_dtype: str) -> None:
     """bf16 pages (auto / bfloat16) and the four TurboQuant layouts are implemented; the other
     names the reference's flag accepts are rejected here instead of silently served as bf16."""
-    ok = ("auto", "bfloat16", "turboquant_4bit_nc", "turboquant_k8v4", "turboquant_k3v4_nc", "turboquant_3bit_nc")
+    ok = ("auto", "bfloat16", "bf16", "turboquant_4bit_nc", "turboquant_k8v4", "turboquant_k3v4_nc",
+          "turboquant_3bit_nc")
     if kv_cache_dtype not in ok:
         raise ValueError(f"--kv-cache-dtype {kv_cache_dtype!r} is not supported (supported: {', '.join(ok)})")
 
