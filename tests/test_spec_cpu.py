@@ -142,3 +142,23 @@ def test_token_tree_layout():
     import pytest
     with pytest.raises(ValueError):
         TokenTree([8, 8])  # 73 nodes
+
+
+def test_filtered_probs_matches_sampler_rules():
+    import torch
+    from vm_c_b200.speculative.draft import filtered_probs
+    logits = torch.tensor([[2.0, 1.0, 0.5, 0.0, -1.0, -3.0]] * 5)
+    temp = torch.tensor([1.0, 0.5, 1.0, 1.0, 0.0])
+    top_k = torch.tensor([0, 0, 3, 0, 0])
+    top_p = torch.tensor([1.0, 1.0, 1.0, 0.7, 1.0])
+    min_p = torch.tensor([0.0, 0.0, 0.0, 0.0, 0.0])
+    p = filtered_probs(logits, temp, top_k, top_p, min_p)
+    assert torch.allclose(p[0], torch.softmax(logits[0], -1))
+    assert torch.allclose(p[1], torch.softmax(logits[1] / 0.5, -1))
+    want = torch.softmax(logits[2, :3], -1)
+    assert torch.allclose(p[2, :3], want) and p[2, 3:].sum() == 0
+    full = torch.softmax(logits[3], -1)  # 0.61, 0.22, ...: the top two reach 0.7
+    assert torch.allclose(p[3, :2], full[:2] / full[:2].sum()) and p[3, 2:].sum() == 0
+    assert p[4].tolist() == [1.0, 0, 0, 0, 0, 0]
+    mp = filtered_probs(logits[:1], torch.tensor([1.0]), torch.tensor([0]), torch.tensor([1.0]), torch.tensor([0.3]))
+    assert (mp[0] > 0).sum() == 2  # p_i >= 0.3 * p_max keeps the two largest

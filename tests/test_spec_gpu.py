@@ -91,3 +91,40 @@ def test_tree_spec_equals_plain_greedy(models, which, tree):
     assert st["steps"] > 0
     if which == "self":
         assert st["tokens_per_step"] > 3.0, st
+
+
+def _gen_sampled(path, prompts, n, draft, sp, k=4):
+    from vm_c_b200.llm import LLM
+    llm = LLM(path, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256,
+              enable_prefix_caching=False, draft_model=draft, num_speculative_tokens=k)
+    outs = llm.generate(prompts, sp)
+    stats = llm.runner.spec.stats.as_dict() if llm.runner.spec is not None else None
+    llm.shutdown()
+    return [o.output_token_ids for o in outs], stats
+
+
+def test_speculative_sampling_self_draft_accepts_nearly_all(models):
+    # p and q come from the same weights (decode vs prefill kernels): min(1, p/q) is ~1 everywhere.
+    tgt, _ = models
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, 32000, n).tolist() for n in (9, 40, 20)]
+    sp = SamplingParams(temperature=1.0, top_k=40, top_p=0.95, max_tokens=16, ignore_eos=True, seed=3)
+    toks, st = _gen_sampled(tgt, prompts, 16, tgt, sp)
+    assert all(len(t) == 16 for t in toks)
+    assert st["steps"] > 0 and st["acceptance_rate"] > 0.9, st
+
+
+def test_speculative_sampling_cold_temperature_is_greedy(models):
+    # At a temperature this low both distributions are one-hot at the argmax: rejection sampling
+    # with an unrelated draft must reproduce plain greedy decoding (up to near-ties).
+    tgt, other = models
+    src = GgufSource(tgt)
+    cfg = src.model_config()
+    W = load_dense(src, cfg)
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (7, 33, 16)]
+    plain, _ = _gen(tgt, prompts, 12)
+    sp = SamplingParams(temperature=1e-4, top_k=0, top_p=1.0, max_tokens=12, ignore_eos=True, seed=5)
+    spec, st = _gen_sampled(tgt, prompts, 12, other, sp)
+    assert st["steps"] > 0
+    _same_up_to_ties(W, cfg, prompts, spec, plain)

@@ -226,9 +226,11 @@ class LLMEngine:
         pen = self._penalties(plan, plan.num_sample)
         all_decode = plan.num_decode == len(plan)
         sample_ids = plan.sample_ids()
-        # Speculate on all-decode steps whose requests are all greedy and penalty-free.
+        # Speculate on all-decode, penalty-free steps: greedy batches by exact agreement, batches with
+        # sampled requests by rejection sampling when the speculator supports it.
+        all_greedy = all(self.requests[int(i)].params.greedy for i in sample_ids)
         speculate = spec is not None and all_decode and pen is None and \
-            all(self.requests[int(i)].params.greedy for i in sample_ids)
+            (all_greedy or getattr(spec, "supports_sampling", False))
         pad = 0
         if all_decode and pen is None and not speculate and hasattr(self.runner, "graph_bucket"):
             pad = self.runner.graph_bucket(len(plan))
@@ -237,8 +239,13 @@ class LLMEngine:
         if not pad:
             counts.R_pad = 0
         lp_by_id = {}
-        if speculate:
+        if speculate and all_greedy:
             new = spec.step(sample_ids, counts)
+        elif speculate:
+            reqs = [self.requests[int(i)] for i in sample_ids]
+            seed = hash((self.step_id, tuple(rq.seed for rq in reqs))) & 0x7fffffffffffffff
+            new = spec.sampled_step(sample_ids, counts, [rq.params for rq in reqs], seed)
+        if speculate:
             flat = np.fromiter((t for row in new for t in row), dtype=np.int32)
             events = self.sched.update(plan, flat, [len(row) for row in new])
         else:

@@ -259,3 +259,160 @@ class DraftSpeculator:
         self.stats.draft_s += t1 - t0
         self.stats.verify_s += t2 - t1
         return out
+
+
+# ---------------------------------------------------------------------------------------------------
+# Sampled requests: rejection-sampling verification (speculative sampling).
+#
+# For a request sampled from the filtered distribution p = F(target logits) (temperature, top-k,
+# top-p, min-p applied as the GPU sampler applies them), the draft samples d_{j+1} from its own
+# filtered distribution q_j; the target accepts d_{j+1} with probability min(1, p_j(d) / q_j(d)),
+# and at the first rejection samples from normalize(max(p_j - q_j, 0)); if all k are accepted a
+# bonus token is sampled from p_k. Every emitted token is distributed exactly as plain sampling
+# from the target would be (Leviathan et al., "Fast Inference from Transformers via Speculative
+# Decoding", ICML 2023; Chen et al., "Accelerating Large Language Model Decoding with Speculative
+# Sampling", 2023). Greedy rows of the same batch use one-hot distributions, which reduces to the
+# greedy rule. The random stream differs from the non-speculative sampler's, so individual sampled
+# outputs are not reproduced token for token — their distribution is.
+
+_MAX_CAND = 1024  # candidate cap of the GPU sampler's restricted path
+
+
+def filtered_probs(logits: torch.Tensor, temp: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+                   min_p: torch.Tensor) -> torch.Tensor:
+    """Row-wise sampling distribution of the GPU sampler: temperature, then (when any filter is
+    set) the top-k set (at most 1024 candidates), the top-p prefix of it and the min-p cut;
+    temperature <= 0 or top_k == 1 gives a one-hot at the argmax. fp32 [n, V]."""
+    n, V = logits.shape
+    greedy = (temp <= 0) | (top_k == 1)
+    t = torch.where(greedy, torch.ones_like(temp), temp)
+    x = logits.float() / t[:, None]
+    out = torch.softmax(x, -1)
+    restricted = (top_k > 0) | (top_p < 1) | (min_p > 0)
+    if bool(restricted.any()):
+        kcap = min(_MAX_CAND, V)
+        vals, idx = torch.topk(x, kcap, dim=-1)            # descending
+        k = torch.where(top_k > 0, torch.clamp(top_k, max=kcap), torch.full_like(top_k, kcap))
+        pos = torch.arange(kcap, device=x.device)[None, :]
+        keep = pos < k[:, None]
+        pv = torch.softmax(vals.masked_fill(~keep, float("-inf")), -1)
+        cum = torch.cumsum(pv, -1)
+        # top-p: keep the smallest prefix whose mass reaches top_p
+        keep &= (cum - pv) < top_p[:, None]
+        # min-p: p_i >= min_p * p_max
+        keep &= pv >= (min_p[:, None] * pv[:, :1])
+        keep[:, 0] = True
+        pr = torch.zeros_like(x).scatter_(1, idx, pv.masked_fill(~keep, 0.0))
+        pr = pr / pr.sum(-1, keepdim=True)
+        out = torch.where(restricted[:, None], pr, out)
+    if bool(greedy.any()):
+        onehot = torch.zeros_like(out).scatter_(1, logits.argmax(-1, keepdim=True), 1.0)
+        out = torch.where(greedy[:, None], onehot, out)
+    return out
+
+
+class _RowParams:
+    def __init__(self, params, dev):
+        self.temp = torch.tensor([p.temperature for p in params], dtype=torch.float32, device=dev)
+        self.top_k = torch.tensor([p.top_k for p in params], dtype=torch.int64, device=dev)
+        self.top_p = torch.tensor([p.top_p for p in params], dtype=torch.float32, device=dev)
+        self.min_p = torch.tensor([p.min_p for p in params], dtype=torch.float32, device=dev)
+
+    def probs(self, logits: torch.Tensor, reps: int = 1) -> torch.Tensor:
+        f = (lambda t: t.repeat_interleave(reps)) if reps > 1 else (lambda t: t)
+        return filtered_probs(logits, f(self.temp), f(self.top_k), f(self.top_p), f(self.min_p))
+
+
+def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int]]:
+    """Speculative step with rejection-sampling verification (see the section comment above)."""
+    L, k, r = self.RL, self.k, self.runner
+    if self.model.tp > 1:
+        raise RuntimeError("speculative sampling needs unsharded logits (tensor-parallel size 1)")
+    h = r.meta_host.numpy()
+    R = counts.R
+    ids = [int(x) for x in request_ids]
+    qs = h[L.off_q_start:L.off_q_start + R + 1]
+    x0 = h[L.off_input_ids + qs[:-1]]
+    p0 = h[L.off_positions + qs[:-1]]
+    bt = h[L.off_block_tables:L.off_block_tables + R * L.max_blocks_per_seq].reshape(R, L.max_blocks_per_seq).copy()
+    bs = self.bs
+    dev = self.dev
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed & 0x7fffffffffffffff)
+    rp = _RowParams(params, dev)
+    V = self.model.v_local
+
+    def slot(i, p):
+        return int(bt[i, p // bs]) * bs + p % bs
+
+    t0 = time.perf_counter()
+    toks, pos, slots, qsd = [], [], [], [0]
+    for i in range(R):
+        e = self.extra.pop(ids[i], None)
+        if e is not None:
+            toks.append(e[0]); pos.append(e[1]); slots.append(slot(i, e[1]))
+        toks.append(int(x0[i])); pos.append(int(p0[i])); slots.append(slot(i, int(p0[i])))
+        qsd.append(len(toks))
+    qsd = np.array(qsd)
+    T1 = len(toks)
+    self._upload(np.array(toks), np.array(pos), np.array(slots), qsd, p0 + 1, qsd[1:] - 1, bt)
+    qdist = torch.empty(R, k, V, device=dev)
+    drafts = torch.empty(R, k, dtype=torch.int64, device=dev)
+    self.model.attn_splits = 1
+    self.model.forward(self.kv, self._meta(T1, R, R, 0 if T1 > R else R, int(np.max(np.diff(qsd)))), self.params,
+                       self.tok_dev, None)
+    for j in range(k):
+        qdist[:, j] = rp.probs(self.model.ws.logits[:R])
+        drafts[:, j] = torch.multinomial(qdist[:, j], 1, generator=gen).squeeze(1)
+        if j + 1 < k:
+            pj = p0 + j + 1
+            dj = drafts[:, j].cpu().numpy()
+            self._upload(dj, pj, np.array([slot(i, int(pj[i])) for i in range(R)]), np.arange(R + 1), pj + 1,
+                         np.arange(R), bt)
+            self.model.forward(self.kv, self._meta(R, R, R, R, 1), self.params, self.tok_dev, None)
+    dr = drafts.cpu().numpy()
+    t1 = time.perf_counter()
+    n = k + 1
+    vt = np.concatenate([x0[:, None], dr], 1).reshape(-1)
+    vp = (p0[:, None] + np.arange(n)[None, :]).reshape(-1)
+    vs = np.array([slot(i, int(vp[i * n + j])) for i in range(R) for j in range(n)])
+    self._upload(vt, vp, vs, np.arange(R + 1) * n, p0 + n, np.arange(R * n), bt)
+    r.model.attn_splits = 1
+    r.model.forward(r.kv, self._meta(R * n, R, R * n, 0, n), self.params, r.tok_spec, None)
+    pdist = rp.probs(r.model.ws.logits[:R * n], reps=n).view(R, n, V)
+    # acceptance of d_{j+1} with probability min(1, p_j(d) / q_j(d))
+    pd = torch.gather(pdist[:, :k], 2, drafts[:, :, None]).squeeze(2)
+    qd = torch.gather(qdist, 2, drafts[:, :, None]).squeeze(2)
+    u = torch.rand(R, k, device=dev, generator=gen)
+    acc = (u * qd < pd).cpu().numpy()
+    a_len = np.array([int(np.argmin(row)) if not row.all() else k for row in acc])
+    # the token after the accepted prefix: residual at the first rejection, p_k if all accepted
+    rows = torch.arange(R, device=dev)
+    ja = torch.from_numpy(a_len).to(dev)
+    pj = pdist[rows, ja]
+    qj = torch.where((ja < k)[:, None], qdist[rows, torch.clamp(ja, max=k - 1)], torch.zeros_like(pj))
+    res = torch.clamp(pj - qj, min=0.0)
+    mass = res.sum(-1, keepdim=True)
+    res = torch.where(mass > 0, res / mass.clamp_min(1e-30), pj)
+    nxt = torch.multinomial(res, 1, generator=gen).squeeze(1).cpu().numpy()
+    t2 = time.perf_counter()
+    out = []
+    for i in range(R):
+        a = int(a_len[i])
+        for j in range(a):
+            self.stats.per_pos_accept[j] += 1
+        out.append([int(t) for t in dr[i, :a]] + [int(nxt[i])])
+        if a == k:
+            self.extra[ids[i]] = (int(dr[i, k - 1]), int(p0[i]) + k)
+        self.stats.accepted += a
+        self.stats.emitted += a + 1
+    self.stats.proposed += R * k
+    self.stats.steps += 1
+    self.stats.draft_s += t1 - t0
+    self.stats.verify_s += t2 - t1
+    return out
+
+
+DraftSpeculator.sampled_step = _sampled_step
+# sampled requests need unsharded logits: tensor-parallel size 1
+DraftSpeculator.supports_sampling = property(lambda self: self.model.tp == 1)

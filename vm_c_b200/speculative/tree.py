@@ -71,6 +71,7 @@ class TokenTree:
 
 
 class TreeSpeculator(DraftSpeculator):
+    supports_sampling = False  # greedy verification only: sampled requests take the plain path
     def __init__(self, runner, draft_source, draft_cfg, branching: list[int], comm=None, layout=None):
         self.tree = TokenTree(branching)
         super().__init__(runner, draft_source, draft_cfg, self.tree.N - 1, comm=comm, layout=layout)
