@@ -136,36 +136,72 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const float* __restric
   __shared__ int cand_i[kMaxCand];
   __shared__ int n_cand;
 
-  // One pass: running max / argmax and the rescaled sum of exponentials (online softmax), giving
-  // the raw log-softmax normaliser (the reported logprob) and the greedy choice together.
-  ArgMax best{-INFINITY, 0x7fffffff};
-  float run_sum = 0.f;
+  // Two passes over the row (the second hits L1/L2): the argmax (independent compares, four
+  // running maxima per thread), then the sum of exponentials against the row maximum, giving the
+  // raw log-softmax normaliser (the reported logprob) and the greedy choice.
   const bool vec = (V % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-  auto visit = [&](float v, int i) {
-    if (v == -INFINITY) return;
-    if (v > best.v) {
-      run_sum = run_sum * __expf(best.v - v) + 1.f;
-      best = ArgMax{v, i};
-    } else {
-      run_sum += __expf(v - best.v);
-      if (v == best.v && i < best.i) best.i = i;
-    }
-  };
+  ArgMax b4[4] = {{-INFINITY, 0x7fffffff}, {-INFINITY, 0x7fffffff}, {-INFINITY, 0x7fffffff}, {-INFINITY, 0x7fffffff}};
   if (vec) {
-    for (int i = threadIdx.x * 4; i < V; i += blockDim.x * 4) {
+    // eight loads in flight per thread: one outstanding 16-byte load per thread left a 64-row
+    // batch latency-bound at ~15 GB/s per SM
+    const int step = blockDim.x * 4;
+    int i = threadIdx.x * 4;
+    for (; i + 7 * step < V; i += 8 * step) {
+      float4 q[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q[u] = __ldg(reinterpret_cast<const float4*>(x + i + u * step));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = i + u * step;
+        if (q[u].x > b4[0].v) b4[0] = ArgMax{q[u].x, j};
+        if (q[u].y > b4[1].v) b4[1] = ArgMax{q[u].y, j + 1};
+        if (q[u].z > b4[2].v) b4[2] = ArgMax{q[u].z, j + 2};
+        if (q[u].w > b4[3].v) b4[3] = ArgMax{q[u].w, j + 3};
+      }
+    }
+    for (; i < V; i += step) {
       const float4 q = *reinterpret_cast<const float4*>(x + i);
-      visit(q.x, i);
-      visit(q.y, i + 1);
-      visit(q.z, i + 2);
-      visit(q.w, i + 3);
+      if (q.x > b4[0].v) b4[0] = ArgMax{q.x, i};
+      if (q.y > b4[1].v) b4[1] = ArgMax{q.y, i + 1};
+      if (q.z > b4[2].v) b4[2] = ArgMax{q.z, i + 2};
+      if (q.w > b4[3].v) b4[3] = ArgMax{q.w, i + 3};
     }
   } else {
-    for (int i = threadIdx.x; i < V; i += blockDim.x) visit(x[i], i);
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+      if (x[i] > b4[0].v) b4[0] = ArgMax{x[i], i};
   }
-  const float my_max = best.v;
-  const ArgMax am = block_argmax(best, sh_am);
+  const ArgMax am = block_argmax(better(better(b4[0], b4[1]), better(b4[2], b4[3])), sh_am);
   const float lmax = am.v;
-  float lsum = (my_max == -INFINITY) ? 0.f : run_sum * __expf(my_max - lmax);
+  float lsum = 0.f;
+  if (lmax != -INFINITY) {
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec) {
+      const int step = blockDim.x * 4;
+      int i = threadIdx.x * 4;
+      for (; i + 3 * step < V; i += 4 * step) {
+        float4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = __ldg(reinterpret_cast<const float4*>(x + i + u * step));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          s4[0] += __expf(q[u].x - lmax);
+          s4[1] += __expf(q[u].y - lmax);
+          s4[2] += __expf(q[u].z - lmax);
+          s4[3] += __expf(q[u].w - lmax);
+        }
+      }
+      for (; i < V; i += step) {
+        const float4 q = *reinterpret_cast<const float4*>(x + i);
+        s4[0] += __expf(q.x - lmax);
+        s4[1] += __expf(q.y - lmax);
+        s4[2] += __expf(q.z - lmax);
+        s4[3] += __expf(q.w - lmax);
+      }
+    } else {
+      for (int i = threadIdx.x; i < V; i += blockDim.x) s4[0] += __expf(x[i] - lmax);
+    }
+    lsum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  }
   lsum = block_sum(lsum, sh_f);
   const float log_z = lmax + __logf(lsum);
 
