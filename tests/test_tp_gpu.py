@@ -1,5 +1,6 @@
 """Tensor parallelism: TP=2 (NCCL baseline and fused peer-memory all-reduce) must produce the same
-greedy tokens as TP=1 on the same checkpoint. Needs >= 2 GPUs."""
+greedy tokens as TP=1 on the same checkpoint, for dense Llama and for expert-parallel Mixtral.
+Needs >= 2 GPUs."""
 import json
 import os
 import subprocess
@@ -23,11 +24,11 @@ def tiny(tmp_path_factory):
     return str(p)
 
 
-def run_tp(model, backend, tmp_path, n=2):
-    out = tmp_path / f"tp_{backend}.json"
+def run_tp(model, backend, tmp_path, n=2, ep=1):
+    out = tmp_path / f"tp_{backend}_ep{ep}.json"
     cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29631",
-           os.path.join(HERE, "tp_worker.py"), model, backend, str(out)]
+           os.path.join(HERE, "tp_worker.py"), model, backend, str(out), str(ep)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
@@ -50,3 +51,24 @@ def test_tp2_matches_tp1(tiny, tmp_path, backend):
     total = sum(len(r) for r in ref)
     # fp32 reduction order differs between TP=1 and TP=2: allow a late divergence only
     assert agree >= 0.9 * total, (ref, got["tokens"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("backend", ["nccl", "fused"])
+def test_mixtral_expert_parallel_matches_single_gpu(tmp_path, backend):
+    # Expert parallelism (each rank holds half of the experts, attention tensor-parallel): the
+    # combine of the partial expert sums rides on the layer's all-reduce (fused with residual +
+    # RMSNorm on the peer-memory path).
+    from vm_c_b200.llm import LLM
+    p = str(tmp_path / "tiny-mixtral.gguf")
+    write_random_gguf(p, preset("tiny-mixtral"), "Q8_0", seed=0)
+    llm = LLM(p, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256)
+    rng = np.random.default_rng(2)  # the worker's prompts
+    prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
+    ref = [o.output_token_ids for o in llm.generate(prompts, SamplingParams.greedy_params(max_tokens=12,
+                                                                                          ignore_eos=True))]
+    llm.shutdown()
+    got = run_tp(p, backend, tmp_path, ep=2)
+    assert got["err"] == 0
+    agree = sum(a == b for r, g in zip(ref, got["tokens"]) for a, b in zip(r, g))
+    assert agree >= 0.9 * sum(len(r) for r in ref), (ref, got["tokens"])

@@ -15,6 +15,7 @@ from vm_c_b200.parallel.comm import NcclComm, init_distributed  # noqa: E402
 
 def main():
     model, backend, out = sys.argv[1], sys.argv[2], sys.argv[3]
+    ep = int(sys.argv[4]) if len(sys.argv) > 4 else 1
     rank, world, local = init_distributed(timeout_s=60)
     torch.cuda.set_device(local)
     if backend == "fused":
@@ -23,7 +24,7 @@ def main():
     else:
         comm = NcclComm()
     llm = LLM(model, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256,
-              tp_rank=rank, tp_size=world, comm=comm, device=f"cuda:{local}")
+              tp_rank=rank, tp_size=world, ep_size=ep, comm=comm, device=f"cuda:{local}")
     rng = np.random.default_rng(2)
     prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
     outs = llm.generate(prompts, SamplingParams.greedy_params(max_tokens=12, ignore_eos=True))
