@@ -1,0 +1,143 @@
+"""HuggingFace checkpoints (safetensors + config.json, optionally tokenizer.json) on CPU: the source
+presents them under GGUF names with the same bytes, and the fp32 oracle gives the same logits as on
+the GGUF they were converted from (Q/K in rotate-half order with half-rotation RoPE)."""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from vm_c_b200.gguf.constants import GType
+from vm_c_b200.gguf.random_init import preset, write_random_gguf
+from vm_c_b200.gguf.reader import GgufSource
+from vm_c_b200.hf import HfSource, SafetensorsFile, save_file
+from vm_c_b200.hf.source import gguf_name
+
+from hf_convert import gguf_to_hf
+from ref_llama import forward_logits, load_dense
+
+
+def test_safetensors_roundtrip(tmp_path):
+    p = str(tmp_path / "a.safetensors")
+    t = {"x": torch.randn(3, 5), "y": torch.randn(4, 8).to(torch.bfloat16), "z": torch.arange(7, dtype=torch.int32),
+         "h": torch.randn(2, 2).half()}
+    save_file(t, p, metadata={"k": "v"})
+    f = SafetensorsFile(p)
+    assert f.metadata == {"k": "v"}
+    assert set(f.entries) == set(t)
+    for n, v in t.items():
+        raw = np.array(f.raw(n))
+        assert raw.tobytes() == v.contiguous().view(torch.uint8).numpy().tobytes(), n
+        assert f.entries[n].shape == list(v.shape)
+    assert np.array(f.rows_bytes("y", 1, 3)).tobytes() == t["y"][1:3].contiguous().view(torch.uint8).numpy().tobytes()
+
+
+def test_truncated_file_is_rejected(tmp_path):
+    p = tmp_path / "bad.safetensors"
+    save_file({"x": torch.randn(16, 16)}, str(p))
+    p.write_bytes(p.read_bytes()[:-4])
+    with pytest.raises(ValueError):
+        SafetensorsFile(str(p))
+
+
+def test_name_map():
+    assert gguf_name("model.layers.3.self_attn.o_proj.weight") == ("blk.3.attn_output.weight", None)
+    assert gguf_name("model.layers.0.block_sparse_moe.experts.5.w2.weight") == ("blk.0.ffn_down_exps.weight", 5)
+    assert gguf_name("model.layers.0.self_attn.rotary_emb.inv_freq") is None
+    with pytest.raises(ValueError):
+        gguf_name("model.layers.0.self_attn.q_proj.bias")
+
+
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-mixtral"])
+def test_hf_source_matches_gguf(tmp_path, name):
+    cfg0 = preset(name)
+    gp = str(tmp_path / "m.gguf")
+    write_random_gguf(gp, cfg0, "BF16", seed=1)
+    g = GgufSource(gp)
+    cfg_g = g.model_config()
+    hd = tmp_path / "hf"
+    gguf_to_hf(g, cfg_g, str(hd))
+    h = HfSource(str(hd))
+    cfg_h = h.model_config()
+    assert cfg_h.rope_neox and not cfg_g.rope_neox
+    for f in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab", "n_experts",
+              "n_experts_used", "tie_embeddings"):
+        assert getattr(cfg_h, f) == getattr(cfg_g, f), f
+    # Same GGUF names and shapes; bytes identical where no permutation applies.
+    assert set(h.tensors) == set(g.tensors)
+    for n in g.tensors:
+        gi, hi = g.info(n), h.info(n)
+        assert gi.ne == hi.ne, n
+        if gi.gtype == GType.BF16 and "attn_q" not in n and "attn_k" not in n:
+            assert hi.gtype == GType.BF16
+            assert torch.equal(h.rows(n), g.rows(n)), n
+    # Row slices that straddle two experts.
+    if cfg_g.is_moe:
+        n, F = "blk.1.ffn_up_exps.weight", cfg_g.ffn
+        assert torch.equal(h.rows(n, F - 3, F + 5), g.rows(n, F - 3, F + 5))
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, cfg_g.vocab, 19).tolist()
+    lg = forward_logits(load_dense(g, cfg_g), cfg_g, toks)
+    lh = forward_logits(load_dense(h, cfg_h), cfg_h, toks)
+    assert torch.allclose(lg, lh, atol=1e-3 * float(lg.abs().max()), rtol=0), float((lg - lh).abs().max())
+
+
+def test_single_file_and_tied_embeddings(tmp_path):
+    cfg = preset("tiny-llama")
+    H, V = cfg.hidden, cfg.vocab
+    t = {"model.embed_tokens.weight": torch.randn(V, H).bfloat16(), "model.norm.weight": torch.ones(H).bfloat16()}
+    d = tmp_path / "m"
+    d.mkdir()
+    save_file(t, str(d / "model.safetensors"))
+    json.dump({"model_type": "llama", "num_hidden_layers": 0, "hidden_size": H, "num_attention_heads": cfg.n_heads,
+               "intermediate_size": cfg.ffn, "vocab_size": V}, open(d / "config.json", "w"))
+    h = HfSource(str(d / "model.safetensors"))
+    assert h.model_config().tie_embeddings
+    norm = h.rows("output_norm.weight")
+    assert h.info("output_norm.weight").gtype == GType.F32 and norm.dtype == torch.float32
+    assert torch.equal(norm.view(-1), torch.ones(H))
+    json.dump({"model_type": "qwen2", "num_hidden_layers": 0, "hidden_size": H, "num_attention_heads": 8,
+               "intermediate_size": 8, "vocab_size": V}, open(d / "config.json", "w"))
+    with pytest.raises(ValueError):
+        HfSource(str(d))
+
+
+def test_tokenizer_json_maps_to_gguf_keys(tmp_path):
+    from vm_c_b200.server.tokenizer import Tokenizer, _byte_unicode
+    b2u, _ = _byte_unicode()
+    alphabet = [b2u[b] for b in range(256)]
+    merges = ["h e", "l l", "he ll", "hell o", "Ġ w", "o r", "Ġw or", "Ġwor l", "Ġworl d"]
+    tokens = alphabet + [m.replace(" ", "") for m in merges]
+    vocab = {t: i for i, t in enumerate(tokens)}
+    specials = ["<|begin_of_text|>", "<|end_of_text|>"]
+    added = [{"id": len(tokens) + i, "content": s, "special": True} for i, s in enumerate(specials)]
+    llama3_split = ("(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\\r\\n\\p{L}\\p{N}]?\\p{L}+|\\p{N}{1,3}| ?[^\\s\\p{L}\\p{N}]+"
+                    "[\\r\\n]*|\\s*[\\r\\n]+|\\s+(?!\\S)|\\s+")
+    tj = {"model": {"type": "BPE", "vocab": vocab, "merges": [m.split(" ") for m in merges], "byte_fallback": False},
+          "added_tokens": added,
+          "pre_tokenizer": {"type": "Sequence", "pretokenizers": [{"type": "Split", "pattern": {"Regex": llama3_split}},
+                                                                  {"type": "ByteLevel"}]},
+          "post_processor": {"type": "TemplateProcessing", "single": [{"SpecialToken": {"id": "<|begin_of_text|>"}},
+                                                                      {"Sequence": {"id": "A"}}]}}
+    d = tmp_path / "tok"
+    d.mkdir()
+    json.dump(tj, open(d / "tokenizer.json", "w"))
+    json.dump({"bos_token": "<|begin_of_text|>", "eos_token": {"content": "<|end_of_text|>"},
+               "chat_template": "{{ messages[0]['content'] }}"}, open(d / "tokenizer_config.json", "w"))
+    V = len(tokens) + 2
+    save_file({"model.embed_tokens.weight": torch.zeros(V, 8).bfloat16()}, str(d / "model.safetensors"))
+    json.dump({"model_type": "llama", "num_hidden_layers": 0, "hidden_size": 8, "num_attention_heads": 1,
+               "intermediate_size": 8, "vocab_size": V}, open(d / "config.json", "w"))
+    src = HfSource(str(d))
+    assert src.metadata("tokenizer.ggml.pre") == "llama-bpe"
+    tok = Tokenizer.from_gguf(src)
+    direct = Tokenizer(tokens + specials, [], [1] * len(tokens) + [3, 3], merges, "gpt2", "llama-bpe",
+                       len(tokens), [len(tokens) + 1], True, False)
+    for text in ["hello world", "hello<|end_of_text|>", " worldhello  x"]:
+        assert tok.encode(text) == direct.encode(text), text
+        assert tok.decode(tok.encode(text, add_bos=False), skip_special=False) == text
+    ids = tok.encode("hello world")
+    assert ids[0] == len(tokens)  # BOS from the post-processor template
+    assert ids[1:] == [vocab["hello"], vocab["Ġworld"]]
+    assert tok.eos_ids == [len(tokens) + 1]
+    assert tok.chat_template == "{{ messages[0]['content'] }}"

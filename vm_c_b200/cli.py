@@ -21,7 +21,8 @@ from .config import VmCConfig
 
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="vm_c_server", description="OpenAI-compatible LLM server for B200")
-    ap.add_argument("model", help="GGUF checkpoint path, or random:<preset>[:<mix>[:<seed>]]")
+    ap.add_argument("model", help="GGUF checkpoint path, a HuggingFace checkpoint directory (config.json + *.safetensors, "
+                    "llama / mistral / mixtral), or random:<preset>[:<mix>[:<seed>]]")
     ap.add_argument("--tokenizer", default="", help="GGUF file whose vocabulary to use (default: the model's)")
     ap.add_argument("--kv-cache-dtype", default="auto",
                     choices=["auto", "float16", "bfloat16", "fp8_e4m3", "fp8_e5m2", "int8_per_token_head",

@@ -1,7 +1,8 @@
 """User-facing entry point: ``LLM(model, ...)`` builds config, weights, runner and engine on this rank.
 
-``model`` is a GGUF path, or ``random:<preset>[:<mix>[:<seed>]]`` for a seeded random-init model of a
-benchmark architecture generated on the GPU (e.g. ``random:llama3-8b:Q4_K_M``).
+``model`` is a GGUF path, a HuggingFace checkpoint directory (config.json + *.safetensors; BF16 / F16 /
+F32 weights run as bf16 tiles), or ``random:<preset>[:<mix>[:<seed>]]`` for a seeded random-init model
+of a benchmark architecture generated on the GPU (e.g. ``random:llama3-8b:Q4_K_M``).
 """
 from __future__ import annotations
 
@@ -21,6 +22,11 @@ def make_source(model: str, device="cuda"):
         seed = int(parts[3]) if len(parts) > 3 else 0
         cfg = preset(name)
         return GpuRandomSource(cfg, mix, seed, device), cfg
+    import os
+    if os.path.isdir(model) or model.endswith(".safetensors"):
+        from .hf.source import HfSource
+        src = HfSource(model)
+        return src, src.model_config()
     from .gguf.reader import GgufSource
     src = GgufSource(model)
     return src, src.model_config()
