@@ -6,6 +6,7 @@
 
 #include "attention.h"
 #include "comm.h"
+#include "gdn.h"
 #include "gemm_tcgen05.h"
 #include "layers.h"
 #include "moe.h"
@@ -212,6 +213,59 @@ void kv_move(torch::Tensor cache, int64_t Hkv, int64_t D, torch::Tensor src, tor
                static_cast<int>(max_moves), cur_stream());
 }
 
+void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor q_start, torch::Tensor slot, torch::Tensor has_state,
+              int64_t nseq, torch::Tensor conv_state, torch::Tensor y) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && y.scalar_type() == torch::kFloat32 && x.stride(1) == 1 &&
+                  y.stride(1) == 1, "gdn_conv: fp32 row-major x and y");
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.size(0) == x.size(1), "gdn_conv: w [C, K] contiguous");
+  const int64_t C = w.size(0), K = w.size(1);
+  TORCH_CHECK(conv_state.is_contiguous() && conv_state.dim() == 3 && conv_state.size(1) == K - 1 &&
+                  conv_state.size(2) == C, "gdn_conv: conv_state [slots, K-1, C]");
+  vmc::gdn_conv(ptr<float>(x), x.stride(0), ptr<float>(w), static_cast<int>(C), static_cast<int>(K),
+                ptr<int32_t>(q_start), ptr<int32_t>(slot), ptr<int32_t>(has_state), static_cast<int>(nseq),
+                ptr<float>(conv_state), ptr<float>(y), y.stride(0), cur_stream());
+}
+
+void gdn_recurrent(torch::Tensor qkv, torch::Tensor alpha, torch::Tensor beta, torch::Tensor z, torch::Tensor a_neg,
+                   torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state, torch::Tensor slot,
+                   torch::Tensor has_state, torch::Tensor q_start, int64_t nseq, int64_t Hk, double eps,
+                   torch::Tensor out) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(state.is_contiguous() && state.dim() == 4 && state.size(2) == state.size(3) &&
+                  state.scalar_type() == torch::kFloat32, "gdn_recurrent: state [slots, Hv, D, D] fp32");
+  const int64_t Hv = state.size(1), D = state.size(2);
+  TORCH_CHECK(qkv.scalar_type() == torch::kFloat32 && qkv.stride(1) == 1 && qkv.size(1) >= (2 * Hk + Hv) * D,
+              "gdn_recurrent: qkv [T, (2Hk+Hv)D] fp32");
+  TORCH_CHECK(alpha.stride(1) == 1 && beta.stride(1) == 1 && alpha.stride(0) == beta.stride(0) &&
+                  alpha.scalar_type() == torch::kFloat32 && beta.scalar_type() == torch::kFloat32,
+              "gdn_recurrent: alpha/beta fp32 [T, Hv] with one row stride");
+  TORCH_CHECK(z.scalar_type() == torch::kFloat32 && z.stride(1) == 1 && out.scalar_type() == torch::kBFloat16 &&
+                  out.stride(1) == 1, "gdn_recurrent: z fp32, out bf16");
+  vmc::GdnArgs a{};
+  a.qkv = ptr<float>(qkv);
+  a.qkv_stride = qkv.stride(0);
+  a.alpha = ptr<float>(alpha);
+  a.beta = ptr<float>(beta);
+  a.ab_stride = alpha.stride(0);
+  a.z = ptr<float>(z);
+  a.z_stride = z.stride(0);
+  a.a_neg = ptr<float>(a_neg);
+  a.dt_bias = ptr<float>(dt_bias);
+  a.norm_w = ptr<float>(norm_w);
+  a.state = ptr<float>(state);
+  a.slot = ptr<int32_t>(slot);
+  a.has_state = ptr<int32_t>(has_state);
+  a.q_start = ptr<int32_t>(q_start);
+  a.out = static_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_stride = out.stride(0);
+  a.Hk = static_cast<int>(Hk);
+  a.Hv = static_cast<int>(Hv);
+  a.D = static_cast<int>(D);
+  a.eps = static_cast<float>(eps);
+  vmc::gdn_recurrent(a, static_cast<int>(nseq), cur_stream());
+}
+
 void embed(torch::Tensor ids, int64_t T, torch::Tensor table, int gtype, int64_t row_bytes, int64_t H,
            c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> out_bf16) {
   vmc::embed(ptr<int32_t>(ids), static_cast<int>(T), table.data_ptr(), gtype, row_bytes, static_cast<int>(H),
@@ -333,6 +387,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed);
   m.def("add_rmsnorm", &add_rmsnorm);
   m.def("rope_store", &rope_store);
+  m.def("gdn_conv", &gdn_conv);
+  m.def("gdn_recurrent", &gdn_recurrent);
   m.def("swiglu", &swiglu);
   m.def("gather_rows", &gather_rows);
   m.def("f32_to_bf16", &f32_to_bf16);

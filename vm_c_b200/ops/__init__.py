@@ -193,6 +193,18 @@ def rope_store(qkv, T, Hq, Hkv, D, pos, slots, cos_sin, neox, q_out, kv, nsplit=
     _count()
 
 
+def gdn_conv(x, w, q_start, slot, has_state, nseq, conv_state, y):
+    """Causal depthwise conv + SiLU of the gated delta-net mixed q|k|v channels (gdn.cu)."""
+    C().gdn_conv(x, w, q_start, slot, has_state, nseq, conv_state, y)
+    _count()
+
+
+def gdn_recurrent(qkv, alpha, beta, z, a_neg, dt_bias, norm_w, state, slot, has_state, q_start, nseq, Hk, eps, out):
+    """Gated delta-rule recurrence over each sequence's tokens + gated RMSNorm (gdn.cu)."""
+    C().gdn_recurrent(qkv, alpha, beta, z, a_neg, dt_bias, norm_w, state, slot, has_state, q_start, nseq, Hk, eps, out)
+    _count()
+
+
 class TqTables:
     """TurboQuant layout of one model (csrc/host/turboquant.hpp) and its Lloyd-Max tables on the
     device. ``layer`` selects the random rotation of a layer (set per call through ``for_layer``)."""
