@@ -178,6 +178,9 @@ def _g(f, key, default=None):
 def model_config_from_gguf(f) -> ModelConfig:
     """Fill a ModelConfig from an opened GgufFile (vm_c_b200._native.host().GgufFile)."""
     arch = _g(f, "general.architecture", "llama")
+    if arch == "qwen35moe":
+        raise ValueError("GGUF architecture 'qwen35moe' (hybrid gated delta-net) is not supported yet: its "
+                         "linear-attention kernels exist (csrc/kernels/gdn.cu) but the model is not wired")
     if arch not in ("llama", "mixtral"):
         raise ValueError(f"unsupported GGUF architecture {arch!r} (supported: llama, mixtral)")
     a = "llama" if arch in ("llama", "mixtral") and f.has("llama.block_count") else arch
