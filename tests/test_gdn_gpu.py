@@ -6,38 +6,9 @@ import torch
 
 from vm_c_b200 import ops
 
+from ref_qwen35 import ref_conv, ref_gdn
+
 pytestmark = pytest.mark.gpu
-
-
-def ref_conv(x, w, hist):
-    K = w.shape[1]
-    xin = torch.cat([hist, x], 0)
-    y = torch.stack([(w * xin[t:t + K].T).sum(1) for t in range(x.shape[0])])
-    return torch.nn.functional.silu(y), xin[-(K - 1):]
-
-
-def ref_gdn(y, alpha, beta, z, a_neg, dt_bias, norm_w, S, Hk, eps):
-    T = y.shape[0]
-    Hv, D = S.shape[0], S.shape[1]
-    out = torch.empty(T, Hv * D)
-    S = S.clone()
-    for t in range(T):
-        for h in range(Hv):
-            kh = h % Hk
-            q = y[t, kh * D:(kh + 1) * D]
-            k = y[t, (Hk + kh) * D:(Hk + kh + 1) * D]
-            v = y[t, 2 * Hk * D + h * D:2 * Hk * D + (h + 1) * D]
-            q = q / torch.clamp(q.norm(), min=eps) / D ** 0.5
-            k = k / torch.clamp(k.norm(), min=eps)
-            g = torch.exp(a_neg[h] * torch.nn.functional.softplus(alpha[t, h] + dt_bias[h]))
-            b = torch.sigmoid(beta[t, h])
-            S[h] = g * S[h]
-            d = b * (v - S[h].T @ k)
-            S[h] = S[h] + torch.outer(k, d)
-            o = S[h].T @ q
-            zz = z[t, h * D:(h + 1) * D]
-            out[t, h * D:(h + 1) * D] = o * torch.rsqrt(o.pow(2).mean() + eps) * norm_w * torch.nn.functional.silu(zz)
-    return out, S
 
 
 @pytest.mark.parametrize("D,Hk,Hv", [(128, 2, 4), (64, 1, 2)])

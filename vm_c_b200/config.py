@@ -39,6 +39,24 @@ class ModelConfig:
     bos_token_id: int = 1
     eos_token_ids: list[int] = field(default_factory=lambda: [2])
     tie_embeddings: bool = False
+    # Hybrid gated delta-net models (arch "qwen35moe"); zero for llama / mixtral.
+    rope_dims: int = 0               # rotated dims per head (0: head_dim)
+    ssm_conv: int = 0                # causal conv kernel size
+    ssm_state: int = 0               # GDN head dim (key = value)
+    ssm_k_heads: int = 0             # GDN key heads (ssm.group_count)
+    ssm_v_heads: int = 0             # GDN value heads (ssm.time_step_rank)
+    full_attn_interval: int = 0      # every n-th layer is full attention
+    ffn_shexp: int = 0               # shared-expert FFN width
+    nextn_layers: int = 0            # trailing MTP blocks (not run in the main pass)
+
+    @property
+    def is_hybrid(self) -> bool:
+        return self.arch == "qwen35moe"
+
+    def is_recurrent(self, i: int) -> bool:
+        """Layer i is a gated delta-net layer (reference: qwen35moe.cpp:24-29 of load_arch_hparams)."""
+        return (self.is_hybrid and i < self.n_layers - self.nextn_layers
+                and (i + 1) % max(1, self.full_attn_interval) != 0)
 
     @property
     def q_size(self) -> int:
@@ -179,8 +197,7 @@ def model_config_from_gguf(f) -> ModelConfig:
     """Fill a ModelConfig from an opened GgufFile (vm_c_b200._native.host().GgufFile)."""
     arch = _g(f, "general.architecture", "llama")
     if arch == "qwen35moe":
-        raise ValueError("GGUF architecture 'qwen35moe' (hybrid gated delta-net) is not supported yet: its "
-                         "linear-attention kernels exist (csrc/kernels/gdn.cu) but the model is not wired")
+        return _qwen35moe_config(f)
     if arch not in ("llama", "mixtral"):
         raise ValueError(f"unsupported GGUF architecture {arch!r} (supported: llama, mixtral)")
     a = "llama" if arch in ("llama", "mixtral") and f.has("llama.block_count") else arch
@@ -219,6 +236,48 @@ def model_config_from_gguf(f) -> ModelConfig:
     if eot is not None and int(eot) not in m.eos_token_ids:
         m.eos_token_ids.append(int(eot))
     names = {t["name"] for t in f.tensors()}
+    m.tie_embeddings = "output.weight" not in names
+    return m
+
+
+def _qwen35moe_config(f) -> ModelConfig:
+    """Hybrid Qwen3.5-MoE hyper-parameters (reference: src/official/llama/models/qwen35moe.cpp:5-42)."""
+    a = "qwen35moe"
+    m = ModelConfig(arch=a)
+    m.name = _g(f, "general.name", "") or ""
+    m.n_layers = int(_g(f, f"{a}.block_count"))
+    m.hidden = int(_g(f, f"{a}.embedding_length"))
+    m.n_heads = int(_g(f, f"{a}.attention.head_count"))
+    kvh = _g(f, f"{a}.attention.head_count_kv", m.n_heads)
+    m.n_kv_heads = int(kvh[0] if isinstance(kvh, list) else kvh)
+    m.head_dim = int(_g(f, f"{a}.attention.key_length", m.hidden // m.n_heads))
+    m.rms_eps = float(_g(f, f"{a}.attention.layer_norm_rms_epsilon", 1e-6))
+    m.rope_theta = float(_g(f, f"{a}.rope.freq_base", 10000000.0))
+    m.rope_neox = True
+    m.rope_dims = int(_g(f, f"{a}.rope.dimension_count", m.head_dim))
+    m.context_length = int(_g(f, f"{a}.context_length", 4096))
+    m.n_experts = int(_g(f, f"{a}.expert_count", 0) or 0)
+    m.n_experts_used = int(_g(f, f"{a}.expert_used_count", 0) or 0)
+    ff = _g(f, f"{a}.feed_forward_length", 0) or 0
+    m.ffn = int(_g(f, f"{a}.expert_feed_forward_length", 0) or (ff // max(1, m.n_experts_used)))
+    m.ffn_shexp = int(_g(f, f"{a}.expert_shared_feed_forward_length", 0) or ff)
+    m.ssm_conv = int(_g(f, f"{a}.ssm.conv_kernel"))
+    m.ssm_state = int(_g(f, f"{a}.ssm.state_size"))
+    m.ssm_k_heads = int(_g(f, f"{a}.ssm.group_count"))
+    m.ssm_v_heads = int(_g(f, f"{a}.ssm.time_step_rank"))
+    m.full_attn_interval = int(_g(f, f"{a}.full_attention_interval", 4))
+    m.nextn_layers = int(_g(f, f"{a}.nextn_predict_layers", 0) or 0)
+    if m.nextn_layers >= m.n_layers:
+        raise ValueError("nextn_predict_layers must be smaller than block_count")
+    names = {t["name"] for t in f.tensors()}
+    tokens = f.get("tokenizer.ggml.tokens") if f.has("tokenizer.ggml.tokens") else None
+    vocab = _g(f, f"{a}.vocab_size", None)
+    if vocab is None:
+        vocab = len(tokens) if tokens is not None else \
+            [t for t in f.tensors() if t["name"] == "token_embd.weight"][0]["ne"][1]
+    m.vocab = int(vocab)
+    m.bos_token_id = int(_g(f, "tokenizer.ggml.bos_token_id", 1))
+    m.eos_token_ids = [int(_g(f, "tokenizer.ggml.eos_token_id", 2))]
     m.tie_embeddings = "output.weight" not in names
     return m
 

@@ -43,6 +43,13 @@ PRESETS: dict[str, ModelConfig] = {
     "tiny-mixtral": ModelConfig(name="tiny-mixtral", n_layers=2, hidden=256, n_heads=8, n_kv_heads=4, head_dim=32,
                                 ffn=512, vocab=32000, rms_eps=1e-5, rope_theta=10000.0, context_length=2048,
                                 n_experts=4, n_experts_used=2, bos_token_id=1, eos_token_ids=[2]),
+    # small hybrid gated delta-net model (Qwen3.5-MoE architecture): layers 0-2 GDN, layer 3 full
+    # attention with partial RoPE, 4 experts (top-2) plus a shared expert
+    "tiny-qwen35moe": ModelConfig(arch="qwen35moe", name="tiny-qwen35moe", n_layers=4, hidden=256, n_heads=4,
+                                  n_kv_heads=2, head_dim=64, ffn=128, vocab=32000, rms_eps=1e-6,
+                                  rope_theta=10000000.0, rope_neox=True, context_length=2048, n_experts=4,
+                                  n_experts_used=2, bos_token_id=1, eos_token_ids=[2], rope_dims=16, ssm_conv=4,
+                                  ssm_state=64, ssm_k_heads=2, ssm_v_heads=4, full_attn_interval=4, ffn_shexp=256),
     # config 5 draft model
     "draft-16l-2048": ModelConfig(name="draft-16l-2048", n_layers=16, hidden=2048, n_heads=32, n_kv_heads=8,
                                   head_dim=64, ffn=8192, vocab=128256, rms_eps=1e-5, rope_theta=500000.0,
@@ -86,6 +93,48 @@ def _fit(gtype: int, K: int) -> int:
     return gtype if K % be == 0 else int(GType.F16)
 
 
+def _hybrid_plan(cfg: ModelConfig, t) -> list[TensorSpec]:
+    """Tensors of a qwen35moe GGUF (reference: src/official/llama/models/qwen35moe.cpp:62-112)."""
+    H, F, V, L, D = cfg.hidden, cfg.ffn, cfg.vocab, cfg.n_layers, cfg.head_dim
+    Ds, Hk, Hv, E, Fs = cfg.ssm_state, cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.n_experts, cfg.ffn_shexp
+    conv_dim = 2 * Hk * Ds + Hv * Ds
+    f32 = int(GType.F32)
+    specs = [TensorSpec("token_embd.weight", [H, V], t("embd", None, H))]
+    for i in range(L - cfg.nextn_layers):
+        b = f"blk.{i}."
+        specs.append(TensorSpec(b + "attn_norm.weight", [H], f32, const=1.0))
+        specs.append(TensorSpec(b + "post_attention_norm.weight", [H], f32, const=1.0))
+        if cfg.is_recurrent(i):
+            specs += [TensorSpec(b + "attn_qkv.weight", [H, conv_dim], t("attn_qkv", i, H)),
+                      TensorSpec(b + "attn_gate.weight", [H, Hv * Ds], t("attn_gate", i, H)),
+                      TensorSpec(b + "ssm_conv1d.weight", [cfg.ssm_conv, conv_dim], f32, std=0.3),
+                      TensorSpec(b + "ssm_dt.bias", [Hv], f32, std=0.1),
+                      TensorSpec(b + "ssm_a", [Hv], f32, const=-0.5),
+                      TensorSpec(b + "ssm_beta.weight", [H, Hv], f32),
+                      TensorSpec(b + "ssm_alpha.weight", [H, Hv], f32),
+                      TensorSpec(b + "ssm_norm.weight", [Ds], f32, const=1.0),
+                      TensorSpec(b + "ssm_out.weight", [Hv * Ds, H], t("ssm_out", i, Hv * Ds))]
+        else:
+            specs += [TensorSpec(b + "attn_q.weight", [H, 2 * cfg.n_heads * D], t("attn_q", i, H)),
+                      TensorSpec(b + "attn_k.weight", [H, cfg.kv_size], t("attn_k", i, H)),
+                      TensorSpec(b + "attn_v.weight", [H, cfg.kv_size], t("attn_v", i, H)),
+                      TensorSpec(b + "attn_output.weight", [cfg.q_size, H], t("attn_output", i, cfg.q_size)),
+                      TensorSpec(b + "attn_q_norm.weight", [D], f32, const=1.0),
+                      TensorSpec(b + "attn_k_norm.weight", [D], f32, const=1.0)]
+        specs += [TensorSpec(b + "ffn_gate_inp.weight", [H, E], f32),
+                  TensorSpec(b + "ffn_gate_exps.weight", [H, F, E], t("ffn_gate", i, H)),
+                  TensorSpec(b + "ffn_up_exps.weight", [H, F, E], t("ffn_up", i, H)),
+                  TensorSpec(b + "ffn_down_exps.weight", [F, H, E], t("ffn_down", i, F)),
+                  TensorSpec(b + "ffn_gate_inp_shexp.weight", [H], f32),
+                  TensorSpec(b + "ffn_gate_shexp.weight", [H, Fs], t("ffn_gate", i, H)),
+                  TensorSpec(b + "ffn_up_shexp.weight", [H, Fs], t("ffn_up", i, H)),
+                  TensorSpec(b + "ffn_down_shexp.weight", [Fs, H], t("ffn_down", i, Fs))]
+    specs.append(TensorSpec("output_norm.weight", [H], f32, const=1.0))
+    if not cfg.tie_embeddings:
+        specs.append(TensorSpec("output.weight", [H, V], t("output", None, H)))
+    return specs
+
+
 def tensor_plan(cfg: ModelConfig, mix: str) -> list[TensorSpec]:
     H, F, V, L = cfg.hidden, cfg.ffn, cfg.vocab, cfg.n_layers
     q, kv = cfg.q_size, cfg.kv_size
@@ -101,6 +150,8 @@ def tensor_plan(cfg: ModelConfig, mix: str) -> list[TensorSpec]:
                 g = GType.Q6_K
         return _fit(int(g), K)
 
+    if cfg.is_hybrid:
+        return _hybrid_plan(cfg, t)
     specs = [TensorSpec("token_embd.weight", [H, V], t("embd", None, H))]
     for i in range(L):
         specs.append(TensorSpec(blk(i, "attn_norm"), [H], int(GType.F32), const=1.0))
@@ -155,7 +206,7 @@ def synthetic_vocab(V: int) -> tuple[list[str], list[float], list[int]]:
 
 def gguf_metadata(cfg: ModelConfig, mix: str) -> list[tuple[str, int, object, int]]:
     """(key, value type, value, array element type) entries of a llama-architecture GGUF."""
-    a = "llama"
+    a = "qwen35moe" if cfg.is_hybrid else "llama"
     md = [
         ("general.architecture", VType.STRING, a, 0),
         ("general.name", VType.STRING, cfg.name or "random-init", 0),
@@ -179,6 +230,18 @@ def gguf_metadata(cfg: ModelConfig, mix: str) -> list[tuple[str, int, object, in
     if cfg.is_moe:
         md.append((f"{a}.expert_count", VType.UINT32, cfg.n_experts, 0))
         md.append((f"{a}.expert_used_count", VType.UINT32, cfg.n_experts_used, 0))
+    if cfg.is_hybrid:
+        md = [m for m in md if m[0] not in (f"{a}.full_attention_interval", f"{a}.rope.dimension_count")]
+        md += [(f"{a}.expert_feed_forward_length", VType.UINT32, cfg.ffn, 0),
+               (f"{a}.expert_shared_feed_forward_length", VType.UINT32, cfg.ffn_shexp, 0),
+               (f"{a}.rope.dimension_count", VType.UINT32, cfg.rope_dims or cfg.head_dim, 0),
+               (f"{a}.ssm.conv_kernel", VType.UINT32, cfg.ssm_conv, 0),
+               (f"{a}.ssm.inner_size", VType.UINT32, cfg.ssm_v_heads * cfg.ssm_state, 0),
+               (f"{a}.ssm.state_size", VType.UINT32, cfg.ssm_state, 0),
+               (f"{a}.ssm.time_step_rank", VType.UINT32, cfg.ssm_v_heads, 0),
+               (f"{a}.ssm.group_count", VType.UINT32, cfg.ssm_k_heads, 0),
+               (f"{a}.full_attention_interval", VType.UINT32, cfg.full_attn_interval, 0),
+               (f"{a}.nextn_predict_layers", VType.UINT32, cfg.nextn_layers, 0)]
     toks, scores, types = synthetic_vocab(cfg.vocab)
     md += [
         ("tokenizer.ggml.model", VType.STRING, "llama", 0),
