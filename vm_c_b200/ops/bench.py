@@ -4,7 +4,8 @@
 
 Cases: gemm:<name> (decode / prefill projections of the 8B model, see GEMM_CASES), attn:decode,
 attn:prefill (one 2048-token prompt), attn:prefill2 (two 1024-token prompts), norm, rope, swiglu,
-sample, and step:decode (a whole engine decode step; not part of "all"). Each case is captured in a CUDA graph after warm-up and timed with CUDA events around the
+sample, gdn:decode / gdn:prefill2 (gated delta-net conv + recurrence, 64 x 1 and 2 x 1024 tokens), and
+step:decode (a whole engine decode step; not part of "all"). Each case is captured in a CUDA graph after warm-up and timed with CUDA events around the
 graph replay (no host launch overhead, as in the engine's decode graphs), with a 256 MB buffer
 written between repetitions so that every repetition reads its inputs from HBM; the median is reported with the achieved bandwidth / FLOP rate. These are the
 cases the committed ncu summaries were captured on.
@@ -204,6 +205,37 @@ def bench_step(kind: str, reps: int) -> str:
     return f"step:decode  64 requests, context ~{P + 8}  median {sorted(ts)[len(ts) // 2]:.3f} ms  ({len(ts)} steps)"
 
 
+def bench_gdn(kind: str, reps: int, flush: torch.Tensor) -> str:
+    """Gated delta-net layer core (conv + recurrence + gated norm) at 16 key / 32 value heads of dim
+    128, conv kernel 4: `decode` = 64 sequences x 1 token, `prefill2` = two 1024-token prompts."""
+    from . import gdn_conv, gdn_recurrent
+    Hk, Hv, D, K = 16, 32, 128, 4
+    C = (2 * Hk + Hv) * D
+    lens = [1] * 64 if kind == "decode" else [1024, 1024]
+    nseq, T = len(lens), sum(lens)
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(T, C, device=dev, generator=g)
+    w = torch.randn(C, K, device=dev, generator=g) * 0.5
+    ab = torch.randn(T, 2 * Hv, device=dev, generator=g)
+    z = torch.randn(T, Hv * D, device=dev, generator=g)
+    a_neg, dt_bias, norm_w = -torch.ones(Hv, device=dev), torch.zeros(Hv, device=dev), torch.ones(D, device=dev)
+    conv_state = torch.zeros(nseq, K - 1, C, device=dev)
+    state = torch.randn(nseq, Hv, D, D, device=dev, generator=g) * 0.01
+    qs = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
+    slot = torch.arange(nseq, dtype=torch.int32, device=dev)
+    has = torch.ones(nseq, dtype=torch.int32, device=dev)
+    y = torch.empty(T, C, device=dev)
+    out = torch.empty(T, Hv * D, dtype=torch.bfloat16, device=dev)
+
+    def run():
+        gdn_conv(x, w, qs, slot, has, nseq, conv_state, y)
+        gdn_recurrent(y, ab[:, :Hv], ab[:, Hv:], z, a_neg, dt_bias, norm_w, state, slot, has, qs, nseq, Hk, 1e-6, out)
+    t = _time(run, reps, flush)
+    nbytes = state.numel() * 4 * 2 + conv_state.numel() * 4 * 2 + T * (C * 4 * 2 + 2 * Hv * 4 + Hv * D * (4 + 2))
+    return f"gdn:{kind:8s} {t:8.1f} us  {nbytes / t / 1e6:5.2f} TB/s  ({nseq} seqs, {T} tokens)"
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("cases", nargs="*", default=["all"])
@@ -212,7 +244,7 @@ def main(argv=None) -> None:
     cases = a.cases
     if cases == ["all"]:
         cases = [f"gemm:{k}" for k in GEMM_CASES] + ["attn:decode", "attn:prefill", "attn:prefill2", "norm", "rope",
-                                                      "swiglu", "sample"]
+                                                      "swiglu", "sample", "gdn:decode", "gdn:prefill2"]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for c in cases:
         if c.startswith("gemm:"):
@@ -221,6 +253,8 @@ def main(argv=None) -> None:
             line = bench_step(c[5:], min(a.reps, 10))
         elif c.startswith("attn:"):
             line = bench_attn(c[5:], a.reps, flush)
+        elif c.startswith("gdn:"):
+            line = bench_gdn(c[4:], a.reps, flush)
         else:
             line = bench_small(c, a.reps, flush)
         print(line, flush=True)
