@@ -183,7 +183,7 @@ def run_rank(rank: int, world: int, a, cfg: VmCConfig) -> None:
                               cfg.model.eos_token_ids, True)
     else:
         tokenizer = Tokenizer.from_gguf(tok_src)
-    name = cfg.server.served_model_name or os.path.basename(a.model)
+    name = cfg.server.served_model_name or os.path.basename(os.path.normpath(a.model))
     srv = OpenAIServer(engine, tokenizer, name, cfg.server, driver=driver)
     serve(srv, cfg.server.host, cfg.server.port)
 
