@@ -44,6 +44,49 @@ def ref_gdn(y, alpha, beta, z, a_neg, dt_bias, norm_w, S, Hk, eps):
     return out, S
 
 
+def ref_gdn_chunked(y, alpha, beta, z, a_neg, dt_bias, norm_w, S, Hk, eps, chunk):
+    """The same recurrence in chunks of `chunk` tokens, written as matrix products (the form a
+    tensor-core prefill kernel computes). Per chunk, with gamma the cumulative log decay, S0 the
+    entering state, A[t, s] = beta_t e^(gamma_t - gamma_s) k_t.k_s (s < t) and
+    M[t, s] = e^(gamma_t - gamma_s) (s <= t):
+        D   = (I + A)^-1 (beta * (V - e^gamma * K S0))      (the delta rows d_t)
+        O   = e^gamma * Q S0 + (M * Q K^T) D
+        S_C = e^gamma_C S0 + K^T (e^(gamma_C - gamma) * D)
+    """
+    T = y.shape[0]
+    Hv, D = S.shape[0], S.shape[1]
+    out = torch.empty(T, Hv * D)
+    S = S.clone().double()
+    for h in range(Hv):
+        kh = h % Hk
+        Q = y[:, kh * D:(kh + 1) * D].double()
+        K = y[:, (Hk + kh) * D:(Hk + kh + 1) * D].double()
+        V = y[:, 2 * Hk * D + h * D:2 * Hk * D + (h + 1) * D].double()
+        Q = Q / torch.clamp(Q.norm(dim=1, keepdim=True), min=eps) / D ** 0.5
+        K = K / torch.clamp(K.norm(dim=1, keepdim=True), min=eps)
+        lg = (a_neg[h] * Fn.softplus(alpha[:, h] + dt_bias[h])).double()
+        b = torch.sigmoid(beta[:, h]).double()
+        O = torch.empty(T, D, dtype=torch.float64)
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            q, k, v, bb = Q[c0:c1], K[c0:c1], V[c0:c1], b[c0:c1]
+            gam = torch.cumsum(lg[c0:c1], 0)
+            n = c1 - c0
+            diff = gam[:, None] - gam[None, :]
+            tril = torch.tril(torch.ones(n, n, dtype=torch.bool))
+            Mx = torch.where(tril, torch.exp(torch.where(tril, diff, torch.zeros_like(diff))), torch.zeros_like(diff))
+            A = (bb[:, None] * Mx * (k @ k.T)).tril(-1)
+            rhs = bb[:, None] * (v - torch.exp(gam)[:, None] * (k @ S[h]))
+            Dm = torch.linalg.solve_triangular(torch.eye(n, dtype=torch.float64) + A, rhs, upper=False,
+                                               unitriangular=True)
+            O[c0:c1] = torch.exp(gam)[:, None] * (q @ S[h]) + (Mx * (q @ k.T)) @ Dm
+            S[h] = torch.exp(gam[-1]) * S[h] + k.T @ (torch.exp(gam[-1] - gam)[:, None] * Dm)
+        O = O.float()
+        zz = z[:, h * D:(h + 1) * D]
+        out[:, h * D:(h + 1) * D] = O * torch.rsqrt(O.pow(2).mean(1, keepdim=True) + eps) * norm_w * Fn.silu(zz)
+    return out, S.float()
+
+
 def load(src):
     """Every tensor of the GGUF as a dense fp32 matrix [rows, ne0] (1-D tensors as vectors)."""
     h = _native.host()

@@ -52,3 +52,19 @@ def test_serving_refused_with_message(model):
     from vm_c_b200.models.llama import load_weights
     with pytest.raises(ValueError, match="qwen35moe"):
         load_weights(src, cfg, "cpu")
+
+
+@pytest.mark.parametrize("chunk", [1, 16, 64])
+def test_chunked_delta_rule_equals_recurrence(chunk):
+    # The chunked (matrix-product) form of the gated delta rule, the planned prefill algorithm,
+    # equals the token-serial recurrence, including a partial last chunk and a non-zero entering state.
+    torch.manual_seed(1)
+    T, Hk, Hv, D, eps = 100, 2, 4, 32, 1e-6
+    y = torch.randn(T, (2 * Hk + Hv) * D)
+    alpha, beta, z = torch.randn(T, Hv), torch.randn(T, Hv), torch.randn(T, Hv * D)
+    a_neg, dt_bias, norm_w = -torch.exp(torch.randn(Hv) * 0.5), torch.randn(Hv) * 0.1, 1 + 0.1 * torch.randn(D)
+    S0 = torch.randn(Hv, D, D) * 0.1
+    o1, s1 = R.ref_gdn(y, alpha, beta, z, a_neg, dt_bias, norm_w, S0, Hk, eps)
+    o2, s2 = R.ref_gdn_chunked(y, alpha, beta, z, a_neg, dt_bias, norm_w, S0, Hk, eps, chunk)
+    torch.testing.assert_close(o2, o1, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(s2, s1, rtol=1e-4, atol=1e-5)
