@@ -176,6 +176,9 @@ def run_rank(rank: int, world: int, a, cfg: VmCConfig) -> None:
     from .server.http import OpenAIServer, serve
     from .server.tokenizer import Tokenizer
     tok_src = GgufSource(a.tokenizer) if a.tokenizer else (src if hasattr(src, "metadata") else None)
+    if tok_src is not None and not tok_src.metadata("tokenizer.ggml.tokens"):
+        log.warning("%s has no tokenizer vocabulary; using a synthetic one (give --tokenizer)", a.tokenizer or a.model)
+        tok_src = None
     if tok_src is None:
         from .gguf.random_init import synthetic_vocab
         toks, scores, types = synthetic_vocab(cfg.model.vocab)
