@@ -24,11 +24,11 @@ def tiny(tmp_path_factory):
     return str(p)
 
 
-def run_tp(model, backend, tmp_path, n=2, ep=1):
-    out = tmp_path / f"tp_{backend}_ep{ep}.json"
+def run_tp(model, backend, tmp_path, n=2, ep=1, spec=False):
+    out = tmp_path / f"tp_{backend}_ep{ep}_{int(spec)}.json"
     cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29631",
-           os.path.join(HERE, "tp_worker.py"), model, backend, str(out), str(ep)]
+           os.path.join(HERE, "tp_worker.py"), model, backend, str(out), str(ep), "spec" if spec else "plain"]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
@@ -70,5 +70,22 @@ def test_mixtral_expert_parallel_matches_single_gpu(tmp_path, backend):
     llm.shutdown()
     got = run_tp(p, backend, tmp_path, ep=2)
     assert got["err"] == 0
+    agree = sum(a == b for r, g in zip(ref, got["tokens"]) for a, b in zip(r, g))
+    assert agree >= 0.9 * sum(len(r) for r in ref), (ref, got["tokens"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_speculative_sampling_cold_matches_greedy(tiny, tmp_path):
+    # Rejection sampling at TP=2 (gathered vocab shards, rank 0's draws broadcast) with the model as
+    # its own draft and a temperature low enough that p and q are one-hot: greedy tokens of TP=1.
+    from vm_c_b200.llm import LLM
+    llm = LLM(tiny, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256)
+    rng = np.random.default_rng(2)  # the worker's prompts
+    prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
+    ref = [o.output_token_ids for o in llm.generate(prompts, SamplingParams.greedy_params(max_tokens=12,
+                                                                                          ignore_eos=True))]
+    llm.shutdown()
+    got = run_tp(tiny, "nccl", tmp_path, spec=True)
+    assert got["err"] == 0 and got["spec_steps"] > 0
     agree = sum(a == b for r, g in zip(ref, got["tokens"]) for a, b in zip(r, g))
     assert agree >= 0.9 * sum(len(r) for r in ref), (ref, got["tokens"])

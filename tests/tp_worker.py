@@ -16,6 +16,7 @@ from vm_c_b200.parallel.comm import NcclComm, init_distributed  # noqa: E402
 def main():
     model, backend, out = sys.argv[1], sys.argv[2], sys.argv[3]
     ep = int(sys.argv[4]) if len(sys.argv) > 4 else 1
+    spec = len(sys.argv) > 5 and sys.argv[5] == "spec"  # the model drafts for itself, cold sampling
     rank, world, local = init_distributed(timeout_s=60)
     torch.cuda.set_device(local)
     if backend == "fused":
@@ -23,14 +24,18 @@ def main():
         comm = FusedComm()
     else:
         comm = NcclComm()
+    extra = dict(draft_model=model, num_speculative_tokens=3, enable_prefix_caching=False) if spec else {}
     llm = LLM(model, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256, num_gpu_blocks=256,
-              tp_rank=rank, tp_size=world, ep_size=ep, comm=comm, device=f"cuda:{local}")
+              tp_rank=rank, tp_size=world, ep_size=ep, comm=comm, device=f"cuda:{local}", **extra)
     rng = np.random.default_rng(2)
     prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
-    outs = llm.generate(prompts, SamplingParams.greedy_params(max_tokens=12, ignore_eos=True))
+    sp = SamplingParams(temperature=1e-4, top_k=0, top_p=1.0, max_tokens=12, ignore_eos=True, seed=5) if spec \
+        else SamplingParams.greedy_params(max_tokens=12, ignore_eos=True)
+    outs = llm.generate(prompts, sp)
     err = int(comm.device_error()) if hasattr(comm, "device_error") else 0
+    steps = llm.runner.spec.stats.as_dict()["steps"] if spec else 0
     if rank == 0:
-        json.dump({"tokens": [o.output_token_ids for o in outs], "err": err}, open(out, "w"))
+        json.dump({"tokens": [o.output_token_ids for o in outs], "err": err, "spec_steps": steps}, open(out, "w"))
     llm.shutdown()
     if hasattr(comm, "close"):
         comm.close()

@@ -273,7 +273,10 @@ class DraftSpeculator:
 # Decoding", ICML 2023; Chen et al., "Accelerating Large Language Model Decoding with Speculative
 # Sampling", 2023). Greedy rows of the same batch use one-hot distributions, which reduces to the
 # greedy rule. The random stream differs from the non-speculative sampler's, so individual sampled
-# outputs are not reproduced token for token — their distribution is.
+# outputs are not reproduced token for token — their distribution is. Under tensor parallelism the
+# vocab-parallel logit shards are all-gathered (every rank computes the same p and q), and rank 0's
+# draft tokens, acceptance decisions and resampled tokens are broadcast, so every rank writes the
+# same tokens into its cache and issues the same collectives in the next step.
 
 _MAX_CAND = 1024  # candidate cap of the GPU sampler's restricted path
 
@@ -323,11 +326,32 @@ class _RowParams:
         return filtered_probs(logits, f(self.temp), f(self.top_k), f(self.top_p), f(self.min_p))
 
 
+def gather_vocab(model, rows: int) -> torch.Tensor:
+    """Full-vocabulary logits [rows, V] from the vocab-parallel shards of `model` (rank order is
+    vocabulary order); every rank receives the same tensor."""
+    lg = model.ws.logits[:rows]
+    if model.tp == 1:
+        return lg
+    import torch.distributed as dist
+    parts = [torch.empty_like(lg) for _ in range(model.tp)]
+    dist.all_gather(parts, lg.contiguous())
+    return torch.cat(parts, -1)
+
+
+def from_rank0(t: torch.Tensor, tp: int) -> torch.Tensor:
+    """Rank 0's values of `t` on every rank (tensor parallelism: all ranks must take the same draft
+    tokens and acceptance decisions, so their caches and their next collectives stay identical)."""
+    if tp > 1:
+        import torch.distributed as dist
+        t = t.contiguous()
+        dist.broadcast(t, src=0)
+    return t
+
+
 def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int]]:
     """Speculative step with rejection-sampling verification (see the section comment above)."""
     L, k, r = self.RL, self.k, self.runner
-    if self.model.tp > 1:
-        raise RuntimeError("speculative sampling needs unsharded logits (tensor-parallel size 1)")
+    tp = self.model.tp
     h = r.meta_host.numpy()
     R = counts.R
     ids = [int(x) for x in request_ids]
@@ -340,7 +364,7 @@ def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed & 0x7fffffffffffffff)
     rp = _RowParams(params, dev)
-    V = self.model.v_local
+    V = self.model.v_local * tp
 
     def slot(i, p):
         return int(bt[i, p // bs]) * bs + p % bs
@@ -362,8 +386,8 @@ def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int
     self.model.forward(self.kv, self._meta(T1, R, R, 0 if T1 > R else R, int(np.max(np.diff(qsd)))), self.params,
                        self.tok_dev, None)
     for j in range(k):
-        qdist[:, j] = rp.probs(self.model.ws.logits[:R])
-        drafts[:, j] = torch.multinomial(qdist[:, j], 1, generator=gen).squeeze(1)
+        qdist[:, j] = rp.probs(gather_vocab(self.model, R))
+        drafts[:, j] = from_rank0(torch.multinomial(qdist[:, j], 1, generator=gen).squeeze(1), tp)
         if j + 1 < k:
             pj = p0 + j + 1
             dj = drafts[:, j].cpu().numpy()
@@ -379,12 +403,12 @@ def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int
     self._upload(vt, vp, vs, np.arange(R + 1) * n, p0 + n, np.arange(R * n), bt)
     r.model.attn_splits = 1
     r.model.forward(r.kv, self._meta(R * n, R, R * n, 0, n), self.params, r.tok_spec, None)
-    pdist = rp.probs(r.model.ws.logits[:R * n], reps=n).view(R, n, V)
+    pdist = rp.probs(gather_vocab(r.model, R * n), reps=n).view(R, n, V)
     # acceptance of d_{j+1} with probability min(1, p_j(d) / q_j(d))
     pd = torch.gather(pdist[:, :k], 2, drafts[:, :, None]).squeeze(2)
     qd = torch.gather(qdist, 2, drafts[:, :, None]).squeeze(2)
     u = torch.rand(R, k, device=dev, generator=gen)
-    acc = (u * qd < pd).cpu().numpy()
+    acc = from_rank0((u * qd < pd).to(torch.uint8), tp).bool().cpu().numpy()
     a_len = np.array([int(np.argmin(row)) if not row.all() else k for row in acc])
     # the token after the accepted prefix: residual at the first rejection, p_k if all accepted
     rows = torch.arange(R, device=dev)
@@ -394,7 +418,7 @@ def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int
     res = torch.clamp(pj - qj, min=0.0)
     mass = res.sum(-1, keepdim=True)
     res = torch.where(mass > 0, res / mass.clamp_min(1e-30), pj)
-    nxt = torch.multinomial(res, 1, generator=gen).squeeze(1).cpu().numpy()
+    nxt = from_rank0(torch.multinomial(res, 1, generator=gen).squeeze(1), tp).cpu().numpy()
     t2 = time.perf_counter()
     out = []
     for i in range(R):
@@ -414,5 +438,4 @@ def _sampled_step(self, request_ids, counts, params, seed: int) -> list[list[int
 
 
 DraftSpeculator.sampled_step = _sampled_step
-# sampled requests need unsharded logits: tensor-parallel size 1
-DraftSpeculator.supports_sampling = property(lambda self: self.model.tp == 1)
+DraftSpeculator.supports_sampling = True
