@@ -24,6 +24,7 @@ from ..config import VmCConfig
 from ..utils.logging import get_logger
 from ..utils.metrics import EngineMetrics
 from .sampling_params import FinishReason, Request, RequestOutput, SamplingParams
+from ..utils import nvtx
 
 log = get_logger("engine")
 
@@ -213,6 +214,12 @@ class LLMEngine:
 
     def step(self) -> list[RequestOutput]:
         """Run one scheduler step; returns outputs of requests that produced tokens or finished."""
+        if nvtx.ENABLED:
+            with nvtx.nvtx_range(f"engine.step {self.step_id}"):
+                return self._step()
+        return self._step()
+
+    def _step(self) -> list[RequestOutput]:
         self._drain()
         spec = getattr(self.runner, "spec", None)
         plan = self.sched.schedule()

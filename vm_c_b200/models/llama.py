@@ -22,6 +22,7 @@ from dataclasses import dataclass, field
 import torch
 
 from .. import ops
+from ..utils.nvtx import LayerRanges
 from ..config import ModelConfig, rope_inv_freq
 from ..gguf.constants import GType, blk, row_bytes
 
@@ -391,7 +392,9 @@ class LlamaModel:
             tr.probe("inp_embd", ws.resid[:T])
         layers = self.w.layers
         ops.add_rmsnorm(ws.resid, layers[0].attn_norm, T, self.H, cfg.rms_eps, out=ws.h)
+        rng = LayerRanges()
         for li, lw in enumerate(layers):
+            rng.next(li)
             for host, dev in lw.offload:  # CPU-offloaded weights of this layer into the staging buffer
                 dev.copy_(host, non_blocking=True)
             if tr:
@@ -436,6 +439,7 @@ class LlamaModel:
             self._row_parallel_norm(ws.act, lw.w_down, T, nxt)
             if tr:
                 tr.probe(f"l_out-{li}", ws.resid[:T])
+        rng.close()
         ops.gather_rows(ws.h, m.logits_idx, m.S, self.H, ws.hs)
         if tr:
             tr.probe("result_norm", ws.hs[:m.S])

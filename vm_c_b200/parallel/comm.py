@@ -15,6 +15,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from ..utils.nvtx import nvtx_range
 
 
 def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
@@ -39,7 +40,8 @@ class NcclComm:
         self._gather_buf = None
 
     def all_reduce(self, t: torch.Tensor) -> None:
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        with nvtx_range("allreduce"):
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     def barrier(self) -> None:
         dist.barrier(group=self.group)
