@@ -11,6 +11,7 @@
 #include "block_manager.hpp"
 #include "gguf.hpp"
 #include "quants.hpp"
+#include "safetensors.hpp"
 #include "scheduler.hpp"
 #include "tokenizer.hpp"
 #include "turboquant.hpp"
@@ -123,6 +124,34 @@ PYBIND11_MODULE(_host, m) {
         if (!t) throw py::key_error("no tensor " + name);
         auto holder = py::cast(f);
         py::array_t<uint8_t> arr({static_cast<py::ssize_t>(t->nbytes)}, {1}, f->tensor_data(*t), holder);
+        py::detail::array_proxy(arr.ptr())->flags &= ~py::detail::npy_api::NPY_ARRAY_WRITEABLE_;
+        return arr;
+      });
+
+  // ---------------- safetensors ----------------
+  py::class_<SafetensorsFile, std::shared_ptr<SafetensorsFile>>(m, "SafetensorsFile")
+      .def_static("open", &SafetensorsFile::open, py::arg("path"))
+      .def_property_readonly("path", &SafetensorsFile::path)
+      .def("metadata", &SafetensorsFile::metadata)
+      .def("tensors", [](const SafetensorsFile& f) {
+        py::list out;
+        for (auto& t : f.tensors()) {
+          py::dict d;
+          d["name"] = t.name;
+          d["dtype"] = t.dtype;
+          d["shape"] = t.shape;
+          d["begin"] = t.begin;
+          d["end"] = t.end;
+          out.append(d);
+        }
+        return out;
+      })
+      // Zero-copy read-only view of a tensor's bytes (keeps the mapping alive).
+      .def("tensor_bytes", [](std::shared_ptr<SafetensorsFile> f, const std::string& name) {
+        const StTensorInfo* t = f->find(name);
+        if (!t) throw py::key_error("no tensor " + name);
+        auto holder = py::cast(f);
+        py::array_t<uint8_t> arr({static_cast<py::ssize_t>(t->end - t->begin)}, {1}, f->data(*t), holder);
         py::detail::array_proxy(arr.ptr())->flags &= ~py::detail::npy_api::NPY_ARRAY_WRITEABLE_;
         return arr;
       });

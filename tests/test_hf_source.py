@@ -40,6 +40,37 @@ def test_truncated_file_is_rejected(tmp_path):
         SafetensorsFile(str(p))
 
 
+def test_native_header_parser_edge_cases(tmp_path):
+    # Escaped names (\u escapes incl. a surrogate pair, quotes, backslashes), keys the parser must
+    # skip (floats, booleans, null, nested values), metadata with escapes, and space padding.
+    import struct
+    names = ["w\u00e9ight", "emoji_\U0001F600", 'q"uote\\slash']
+    data = [np.arange(6, dtype=np.float32).reshape(2, 3), np.arange(4, dtype=np.int32), np.ones(2, np.float16)]
+    header, blobs, off = {}, [], 0
+    for n, a in zip(names, data):
+        b = a.tobytes()
+        header[n] = {"dtype": {"float32": "F32", "int32": "I32", "float16": "F16"}[str(a.dtype)], "shape": list(a.shape),
+                     "data_offsets": [off, off + len(b)], "extra": {"x": [1.5, True, None, {"y": -2e-3}]}}
+        blobs.append(b)
+        off += len(b)
+    header["__metadata__"] = {"format": "pt", "note": "tab\there \u2603"}
+    h = json.dumps(header, ensure_ascii=True).encode() + b"   "
+    p = tmp_path / "edge.safetensors"
+    p.write_bytes(struct.pack("<Q", len(h)) + h + b"".join(blobs))
+    f = SafetensorsFile(str(p))
+    assert set(f.entries) == set(names)
+    assert f.metadata == {"format": "pt", "note": "tab\there \u2603"}
+    for n, a in zip(names, data):
+        assert np.array(f.raw(n)).tobytes() == a.tobytes()
+    bad = json.dumps({"x": {"dtype": "F32", "shape": [2], "data_offsets": [0, 4]}}).encode()
+    p.write_bytes(struct.pack("<Q", len(bad)) + bad + b"\0" * 8)
+    with pytest.raises(ValueError):  # byte range does not match the shape
+        SafetensorsFile(str(p))
+    p.write_bytes(struct.pack("<Q", 5) + b'{"x":')
+    with pytest.raises(ValueError):  # truncated JSON
+        SafetensorsFile(str(p))
+
+
 def test_name_map():
     assert gguf_name("model.layers.3.self_attn.o_proj.weight") == ("blk.3.attn_output.weight", None)
     assert gguf_name("model.layers.0.block_sparse_moe.experts.5.w2.weight") == ("blk.0.ffn_down_exps.weight", 5)

@@ -20,7 +20,7 @@ EXT_DIR = PKG_DIR / "_ext"
 CSRC = REPO_DIR / "csrc"
 
 HOST_SOURCES = ["host/gguf.cpp", "host/quants.cpp", "host/block_manager.cpp", "host/scheduler.cpp",
-                "host/tokenizer.cpp", "host/turboquant.cpp", "host/bindings.cpp"]
+                "host/tokenizer.cpp", "host/turboquant.cpp", "host/safetensors.cpp", "host/bindings.cpp"]
 
 SM100_FLAGS = ["-gencode=arch=compute_100a,code=sm_100a"]
 

@@ -3,8 +3,10 @@
 Counterpart of the reference's ``SafeTensorsLoader`` (src/model/model_loader.cpp:78-296). The
 format is fixed by its public specification: an 8-byte little-endian header length N, N bytes of
 JSON (``{name: {"dtype", "shape", "data_offsets": [begin, end]}, "__metadata__": {...}}``; the
-offsets are relative to the first byte after the header), then the tensor bytes, row-major. Files
-are opened as read-only memory maps, so a tensor slice costs one copy of the bytes it covers.
+offsets are relative to the first byte after the header), then the tensor bytes, row-major. The
+reader is the native host library's (csrc/host/safetensors.cpp: memory map, header parse, byte
+range checks); tensors come out as zero-copy read-only views of the mapping, so a row slice costs
+one copy of the bytes it covers. The writer (tests, conversions) is plain Python.
 """
 from __future__ import annotations
 
@@ -18,8 +20,6 @@ import numpy as np
 DTYPES = {"F64": (np.float64, 8), "F32": (np.float32, 4), "F16": (np.float16, 2), "BF16": (np.uint16, 2),
           "I64": (np.int64, 8), "I32": (np.int32, 4), "I16": (np.int16, 2), "I8": (np.int8, 1),
           "U8": (np.uint8, 1), "BOOL": (np.bool_, 1), "F8_E4M3": (np.uint8, 1), "F8_E5M2": (np.uint8, 1)}
-
-_MAX_HEADER = 100 << 20
 
 
 @dataclass
@@ -37,39 +37,28 @@ class StEntry:
 
 class SafetensorsFile:
     def __init__(self, path: str):
+        from .. import _native
+        try:
+            self.f = _native.host().SafetensorsFile.open(path)
+        except RuntimeError as e:
+            raise ValueError(str(e)) from e
         self.path = path
-        with open(path, "rb") as f:
-            raw = f.read(8)
-            if len(raw) != 8:
-                raise ValueError(f"{path}: not a safetensors file (shorter than 8 bytes)")
-            (n,) = struct.unpack("<Q", raw)
-            if n > _MAX_HEADER:
-                raise ValueError(f"{path}: header of {n} bytes is implausibly large")
-            header = json.loads(f.read(n).decode("utf-8"))
-        self.metadata = header.pop("__metadata__", None) or {}
-        self.map = np.memmap(path, dtype=np.uint8, mode="r")
-        base = 8 + n
+        self.metadata = dict(self.f.metadata())
         self.entries: dict[str, StEntry] = {}
-        for name, d in header.items():
-            if d["dtype"] not in DTYPES:
-                raise ValueError(f"{path}: tensor {name} has unsupported dtype {d['dtype']}")
-            b, e = d["data_offsets"]
-            ent = StEntry(name, d["dtype"], list(d["shape"]), base + b, base + e)
-            numel = int(np.prod(ent.shape)) if ent.shape else 1
-            if ent.end - ent.begin != numel * ent.itemsize or ent.end > self.map.size:
-                raise ValueError(f"{path}: tensor {name} byte range does not match its shape")
-            self.entries[name] = ent
+        for t in self.f.tensors():
+            if t["dtype"] not in DTYPES:
+                raise ValueError(f"{path}: tensor {t['name']} has unsupported dtype {t['dtype']}")
+            self.entries[t["name"]] = StEntry(t["name"], t["dtype"], list(t["shape"]), int(t["begin"]), int(t["end"]))
 
     def raw(self, name: str) -> np.ndarray:
         """The tensor's bytes as a read-only uint8 view of the mapping."""
-        e = self.entries[name]
-        return self.map[e.begin:e.end]
+        return self.f.tensor_bytes(name)
 
     def rows_bytes(self, name: str, r0: int, r1: int) -> np.ndarray:
         """Rows [r0, r1) of the tensor viewed as [prod(shape[:-1]), shape[-1]] (bytes, a view)."""
         e = self.entries[name]
         rb = (e.shape[-1] if e.shape else 1) * e.itemsize
-        return self.map[e.begin + r0 * rb:e.begin + r1 * rb].reshape(r1 - r0, rb)
+        return self.raw(name)[r0 * rb:r1 * rb].reshape(r1 - r0, rb)
 
 
 def save_file(tensors: dict, path: str, metadata: dict | None = None) -> None:
