@@ -167,8 +167,60 @@ def test_tokenizer_json_maps_to_gguf_keys(tmp_path):
     for text in ["hello world", "hello<|end_of_text|>", " worldhello  x"]:
         assert tok.encode(text) == direct.encode(text), text
         assert tok.decode(tok.encode(text, add_bos=False), skip_special=False) == text
+    tokenizers = pytest.importorskip("tokenizers")
+    lib_json = {"version": "1.0", "truncation": None, "padding": None, "normalizer": None, "post_processor": None,
+                "decoder": None,
+                "added_tokens": [dict(a, single_word=False, lstrip=False, rstrip=False, normalized=False) for a in added],
+                "pre_tokenizer": {"type": "Sequence", "pretokenizers": [
+                    {"type": "Split", "pattern": {"Regex": llama3_split}, "behavior": "Isolated", "invert": False},
+                    {"type": "ByteLevel", "add_prefix_space": False, "trim_offsets": True, "use_regex": False}]},
+                "model": dict(tj["model"], dropout=None, unk_token=None, continuing_subword_prefix=None,
+                              end_of_word_suffix=None, fuse_unk=False, ignore_merges=False)}
+    lib = tokenizers.Tokenizer.from_str(json.dumps(lib_json))
+    for text in ["hello world", " worldhello  x", "hello\n\nworld 123 héllo"]:
+        assert tok.encode(text, add_bos=False) == lib.encode(text, add_special_tokens=False).ids, text
     ids = tok.encode("hello world")
     assert ids[0] == len(tokens)  # BOS from the post-processor template
     assert ids[1:] == [vocab["hello"], vocab["Ġworld"]]
     assert tok.eos_ids == [len(tokens) + 1]
     assert tok.chat_template == "{{ messages[0]['content'] }}"
+
+
+def test_spm_tokenizer_json_matches_the_tokenizers_library(tmp_path):
+    # SentencePiece-style BPE (Llama 2 / Mistral / Mixtral tokenizer.json: byte fallback, "▁" for
+    # spaces, a prepended "▁"): our tokenizer built from the mapped keys encodes like the library.
+    tokenizers = pytest.importorskip("tokenizers")
+    from vm_c_b200.server.tokenizer import Tokenizer
+    base = ["<unk>", "<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)]
+    chars = ["▁"] + list("abcdefghijklmnopqrstuvwxyz") + list(",.!?")
+    merges = ["▁ t", "h e", "▁t he", "l l", "he ll", "hell o", "▁ hello", "o r", "▁ w", "▁w or", "l d",
+              "▁wor ld", "i n", "▁ in", "▁ a"]
+    vocab = {t: i for i, t in enumerate(base + chars)}
+    for m in merges:
+        a, b = m.split(" ")
+        assert a in vocab and b in vocab, m
+        vocab.setdefault(a + b, len(vocab))
+    tj = {"version": "1.0", "truncation": None, "padding": None,
+          "added_tokens": [{"id": i, "content": t, "single_word": False, "lstrip": False, "rstrip": False,
+                            "normalized": False, "special": True} for i, t in enumerate(base[:3])],
+          "normalizer": {"type": "Sequence", "normalizers": [{"type": "Prepend", "prepend": "▁"},
+                                                             {"type": "Replace", "pattern": {"String": " "},
+                                                              "content": "▁"}]},
+          "pre_tokenizer": None, "post_processor": None, "decoder": None,
+          "model": {"type": "BPE", "dropout": None, "unk_token": "<unk>", "continuing_subword_prefix": None,
+                    "end_of_word_suffix": None, "fuse_unk": True, "byte_fallback": True, "ignore_merges": False,
+                    "vocab": vocab, "merges": [m.split(" ") for m in merges]}}
+    d = tmp_path / "spm"
+    d.mkdir()
+    (d / "tokenizer.json").write_text(json.dumps(tj), encoding="utf-8")
+    json.dump({"bos_token": "<s>", "eos_token": "</s>", "add_bos_token": True}, open(d / "tokenizer_config.json", "w"))
+    V = len(vocab)
+    save_file({"model.embed_tokens.weight": torch.zeros(V, 8).bfloat16()}, str(d / "model.safetensors"))
+    json.dump({"model_type": "mistral", "num_hidden_layers": 0, "hidden_size": 8, "num_attention_heads": 1,
+               "intermediate_size": 8, "vocab_size": V}, open(d / "config.json", "w"))
+    ours = Tokenizer.from_gguf(HfSource(str(d)))
+    lib = tokenizers.Tokenizer.from_str(json.dumps(tj))
+    for text in ["the world", "hello world in the", "hello, the world!", "a theworld", "héllo wörld", "x  y"]:
+        want = lib.encode(text, add_special_tokens=False).ids
+        assert ours.encode(text, add_bos=False, parse_special=False) == want, (text, want)
+    assert ours.encode("the")[0] == vocab["<s>"]

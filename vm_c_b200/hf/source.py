@@ -14,7 +14,8 @@ sharding and tiling run on it:
 * BF16 / F16 / F32 matrices are handed over as their raw bytes (the GEMM reads bf16 tiles); 1-D
   tensors (norm weights) are converted to F32, as GGUF stores them;
 * ``metadata`` answers the ``tokenizer.*`` keys from tokenizer.json / tokenizer_config.json for a
-  byte-level BPE tokenizer (Llama 3), so ``Tokenizer.from_gguf`` builds the same tokenizer.
+  byte-level BPE tokenizer (Llama 3) or a SentencePiece-style BPE with byte fallback (Llama 2 /
+  Mistral / Mixtral), so ``Tokenizer.from_gguf`` builds the same tokenizer.
 """
 from __future__ import annotations
 
@@ -194,6 +195,54 @@ def _token_id(tok, vocab: dict) -> Optional[int]:
     return vocab.get(tok) if isinstance(tok, str) else None
 
 
+def _special_ids(d: str, hf_config: dict, vocab: dict) -> tuple[dict, int, int]:
+    tc_path = os.path.join(d, "tokenizer_config.json")
+    tc = json.load(open(tc_path, encoding="utf-8")) if os.path.exists(tc_path) else {}
+    bos = _token_id(tc.get("bos_token"), vocab)
+    eos = _token_id(tc.get("eos_token"), vocab)
+    bos = hf_config.get("bos_token_id", 1) if bos is None else bos
+    cfg_eos = hf_config.get("eos_token_id", 2)
+    eos = (cfg_eos[0] if isinstance(cfg_eos, list) else cfg_eos) if eos is None else eos
+    return tc, int(bos), int(eos)
+
+
+def _spm_metadata(tj, model, vocab, tokens, types, merges, added, n, d, hf_config) -> dict:
+    """SentencePiece-style BPE (byte fallback, "▁" for spaces) as the GGUF "llama" tokenizer: the
+    native SPM merger takes the adjacent pair whose merged token scores highest, so each merged token
+    scores minus its merge rank (the earliest merge wins, as in BPE)."""
+    scores = [0.0] * n
+    for r, m in enumerate(merges):
+        a, _, b = m.partition(" ")
+        i = vocab.get(a + b)
+        if i is not None and scores[i] == 0.0:
+            scores[i] = -float(r + 1)
+    for i, t in enumerate(tokens):
+        if len(t) == 6 and t.startswith("<0x") and t.endswith(">"):
+            types[i] = 6  # byte
+    unk = model.get("unk_token")
+    unk_id = vocab.get(unk, -1) if isinstance(unk, str) else -1
+    if unk_id >= 0:
+        types[unk_id] = 2
+    for a in added:
+        types[int(a["id"])] = 3 if a.get("special") else 4
+    norm = json.dumps(tj.get("normalizer") or {})
+    pre = tj.get("pre_tokenizer") or {}
+    prefix = '"Prepend"' in norm or (pre.get("type") == "Metaspace" and
+                                      pre.get("prepend_scheme", "always") in ("always", "first"))
+    tc, bos, eos = _special_ids(d, hf_config, vocab)
+    md = {"tokenizer.ggml.model": "llama", "tokenizer.ggml.tokens": tokens, "tokenizer.ggml.scores": scores,
+          "tokenizer.ggml.token_type": types, "tokenizer.ggml.bos_token_id": bos,
+          "tokenizer.ggml.eos_token_id": eos, "tokenizer.ggml.add_space_prefix": bool(prefix),
+          "tokenizer.ggml.add_bos_token": bool(tc.get("add_bos_token", True)),
+          "tokenizer.ggml.unknown_token_id": unk_id}
+    ct = tc.get("chat_template")
+    if isinstance(ct, list):
+        ct = next((c.get("template") for c in ct if c.get("name") == "default"), None)
+    if ct:
+        md["tokenizer.chat_template"] = ct
+    return md
+
+
 def _tokenizer_metadata(d: str, hf_config: dict) -> dict:
     """GGUF tokenizer.* keys from tokenizer.json (byte-level BPE) and tokenizer_config.json."""
     p = os.path.join(d, "tokenizer.json")
@@ -201,9 +250,11 @@ def _tokenizer_metadata(d: str, hf_config: dict) -> dict:
         return {}
     tj = json.load(open(p, encoding="utf-8"))
     model = tj.get("model") or {}
-    if model.get("type") != "BPE" or model.get("byte_fallback"):
-        raise ValueError("tokenizer.json: only byte-level BPE tokenizers are supported "
-                         "(give a GGUF file with --tokenizer for others)")
+    if model.get("type") != "BPE":
+        raise ValueError("tokenizer.json: only BPE tokenizers are supported (byte-level, as Llama 3, or "
+                         "SentencePiece-style with byte fallback, as Llama 2 / Mistral); give a GGUF file "
+                         "with --tokenizer for others")
+    spm = bool(model.get("byte_fallback"))
     vocab = dict(model.get("vocab") or {})
     added = tj.get("added_tokens") or []
     for a in added:
@@ -220,6 +271,8 @@ def _tokenizer_metadata(d: str, hf_config: dict) -> dict:
     for a in added:
         types[int(a["id"])] = 3 if a.get("special") else 4  # control / user-defined
     merges = [m if isinstance(m, str) else " ".join(m) for m in (model.get("merges") or [])]
+    if spm:
+        return _spm_metadata(tj, model, vocab, tokens, types, merges, added, n, d, hf_config)
     pre = "gpt2"
     if "(?i:'s|'t|'re|'ve|'m|'ll|'d)" in json.dumps(tj.get("pre_tokenizer") or {}):
         pre = "llama-bpe"
