@@ -224,3 +224,12 @@ def test_spm_tokenizer_json_matches_the_tokenizers_library(tmp_path):
         want = lib.encode(text, add_special_tokens=False).ids
         assert ours.encode(text, add_bos=False, parse_special=False) == want, (text, want)
     assert ours.encode("the")[0] == vocab["<s>"]
+
+
+def test_hf_config_null_fields(tmp_path):
+    from vm_c_b200.config import model_config_from_hf
+    json.dump({"model_type": "mistral", "num_hidden_layers": 2, "hidden_size": 512, "num_attention_heads": 8,
+               "num_key_value_heads": None, "head_dim": None, "intermediate_size": 1024, "vocab_size": 1000,
+               "rope_theta": None, "rope_scaling": None, "sliding_window": None}, open(tmp_path / "config.json", "w"))
+    m = model_config_from_hf(str(tmp_path))
+    assert (m.n_kv_heads, m.head_dim, m.rope_theta, m.rope_scaling) == (8, 64, 10000.0, None) and m.rope_neox

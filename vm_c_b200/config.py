@@ -290,17 +290,17 @@ def model_config_from_hf(model_dir: str) -> ModelConfig:
     m.n_layers = cfg["num_hidden_layers"]
     m.hidden = cfg["hidden_size"]
     m.n_heads = cfg["num_attention_heads"]
-    m.n_kv_heads = cfg.get("num_key_value_heads", m.n_heads)
-    m.head_dim = cfg.get("head_dim", m.hidden // m.n_heads)
+    m.n_kv_heads = cfg.get("num_key_value_heads") or m.n_heads  # a key may be present as null
+    m.head_dim = cfg.get("head_dim") or m.hidden // m.n_heads
     m.ffn = cfg["intermediate_size"]
     m.vocab = cfg["vocab_size"]
-    m.rms_eps = cfg.get("rms_norm_eps", 1e-5)
-    m.rope_theta = cfg.get("rope_theta", 10000.0)
+    m.rms_eps = cfg.get("rms_norm_eps") or 1e-5
+    m.rope_theta = cfg.get("rope_theta") or 10000.0
     m.rope_neox = True  # HF checkpoints keep the rotate-half layout
     m.rope_scaling = cfg.get("rope_scaling")
-    m.context_length = cfg.get("max_position_embeddings", 4096)
-    m.n_experts = cfg.get("num_local_experts", 0)
-    m.n_experts_used = cfg.get("num_experts_per_tok", 0)
+    m.context_length = cfg.get("max_position_embeddings") or 4096
+    m.n_experts = cfg.get("num_local_experts") or 0
+    m.n_experts_used = cfg.get("num_experts_per_tok") or 0
     m.bos_token_id = cfg.get("bos_token_id", 1) or 1
     eos = cfg.get("eos_token_id", 2)
     m.eos_token_ids = list(eos) if isinstance(eos, list) else [eos]
