@@ -233,3 +233,7 @@ def test_hf_config_null_fields(tmp_path):
                "rope_theta": None, "rope_scaling": None, "sliding_window": None}, open(tmp_path / "config.json", "w"))
     m = model_config_from_hf(str(tmp_path))
     assert (m.n_kv_heads, m.head_dim, m.rope_theta, m.rope_scaling) == (8, 64, 10000.0, None) and m.rope_neox
+    cfg = json.load(open(tmp_path / "config.json"))
+    cfg.update(sliding_window=4096, max_position_embeddings=32768)
+    json.dump(cfg, open(tmp_path / "config.json", "w"))
+    assert model_config_from_hf(str(tmp_path)).context_length == 4096  # no window mask: capped at the window

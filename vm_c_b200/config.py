@@ -299,6 +299,11 @@ def model_config_from_hf(model_dir: str) -> ModelConfig:
     m.rope_neox = True  # HF checkpoints keep the rotate-half layout
     m.rope_scaling = cfg.get("rope_scaling")
     m.context_length = cfg.get("max_position_embeddings") or 4096
+    sw = cfg.get("sliding_window")
+    if sw and sw < m.context_length:
+        # The attention kernels have no sliding-window mask; up to the window length full attention
+        # equals windowed attention, so the context is capped there and outputs stay exact.
+        m.context_length = int(sw)
     m.n_experts = cfg.get("num_local_experts") or 0
     m.n_experts_used = cfg.get("num_experts_per_tok") or 0
     m.bos_token_id = cfg.get("bos_token_id", 1) or 1
