@@ -237,3 +237,26 @@ def test_hf_config_null_fields(tmp_path):
     cfg.update(sliding_window=4096, max_position_embeddings=32768)
     json.dump(cfg, open(tmp_path / "config.json", "w"))
     assert model_config_from_hf(str(tmp_path)).context_length == 4096  # no window mask: capped at the window
+
+
+def test_hf_config_hybrid_and_nested(tmp_path):
+    # Qwen3.5-MoE style: nested text_config, layer_types, linear_* dims, shared expert, partial RoPE.
+    from vm_c_b200.config import model_config_from_hf
+    tc = {"num_hidden_layers": 8, "hidden_size": 2048, "num_attention_heads": 16, "num_key_value_heads": 2,
+          "head_dim": 256, "intermediate_size": 5120, "vocab_size": 151936, "rms_norm_eps": 1e-6,
+          "rope_parameters": {"rope_theta": 10000000, "partial_rotary_factor": 0.25}, "num_experts": 256,
+          "num_experts_per_tok": 8, "moe_intermediate_size": 512, "shared_expert_intermediate_size": 512,
+          "layer_types": (["linear_attention"] * 3 + ["full_attention"]) * 2, "linear_conv_kernel_dim": 4,
+          "linear_key_head_dim": 128, "linear_value_head_dim": 128, "linear_num_key_heads": 16,
+          "linear_num_value_heads": 32, "max_position_embeddings": 262144}
+    json.dump({"model_type": "qwen3_5_moe", "text_config": tc, "eos_token_id": [1, 2]}, open(tmp_path / "config.json", "w"))
+    m = model_config_from_hf(str(tmp_path))
+    assert m.is_hybrid and m.full_attn_interval == 4
+    assert [m.is_recurrent(i) for i in range(8)] == [True, True, True, False] * 2
+    assert (m.ssm_conv, m.ssm_state, m.ssm_k_heads, m.ssm_v_heads) == (4, 128, 16, 32)
+    assert (m.n_experts, m.n_experts_used, m.ffn, m.ffn_shexp, m.rope_dims) == (256, 8, 512, 512, 64)
+    assert m.rope_theta == 10000000 and m.eos_token_ids == [1, 2]
+    tc["layer_types"] = ["linear_attention", "full_attention", "linear_attention", "linear_attention"]
+    json.dump({"text_config": tc}, open(tmp_path / "config.json", "w"))
+    with pytest.raises(ValueError):
+        model_config_from_hf(str(tmp_path))

@@ -282,34 +282,71 @@ def _qwen35moe_config(f) -> ModelConfig:
     return m
 
 
+def _hybrid_schedule(tc: dict, n_layers: int) -> int:
+    """full_attention_interval of a config's layer schedule (0: no linear-attention layers)."""
+    types = tc.get("layer_types")
+    if types:
+        if "linear_attention" not in types:
+            return 0
+        full = [i for i, t in enumerate(types) if t == "full_attention"]
+        iv = full[0] + 1 if full else 0
+        if not iv or any(types[i] != ("full_attention" if (i + 1) % iv == 0 else "linear_attention")
+                         for i in range(len(types))):
+            raise ValueError("layer_types: only a periodic schedule (every n-th layer full attention) is supported")
+        return iv
+    return int(tc["full_attention_interval"]) if tc.get("full_attention_interval") else 0
+
+
 def model_config_from_hf(model_dir: str) -> ModelConfig:
-    """ModelConfig from a HuggingFace config.json (reference: src/core/config.cpp:27)."""
+    """ModelConfig from a HuggingFace config.json (reference: src/core/config.cpp:27-200, including the
+    nested text_config, the expert-count spellings, the shared expert and the gated delta-net
+    dimensions of hybrid models). Keys present with a null value count as absent."""
     cfg = json.loads((Path(model_dir) / "config.json").read_text())
+    tc = cfg["text_config"] if isinstance(cfg.get("text_config"), dict) else cfg
     m = ModelConfig()
     m.arch = "llama"
-    m.n_layers = cfg["num_hidden_layers"]
-    m.hidden = cfg["hidden_size"]
-    m.n_heads = cfg["num_attention_heads"]
-    m.n_kv_heads = cfg.get("num_key_value_heads") or m.n_heads  # a key may be present as null
-    m.head_dim = cfg.get("head_dim") or m.hidden // m.n_heads
-    m.ffn = cfg["intermediate_size"]
-    m.vocab = cfg["vocab_size"]
-    m.rms_eps = cfg.get("rms_norm_eps") or 1e-5
-    m.rope_theta = cfg.get("rope_theta") or 10000.0
+    m.n_layers = tc["num_hidden_layers"]
+    m.hidden = tc["hidden_size"]
+    m.n_heads = tc["num_attention_heads"]
+    m.n_kv_heads = tc.get("num_key_value_heads") or m.n_heads
+    m.head_dim = tc.get("head_dim") or m.hidden // m.n_heads
+    m.ffn = tc["intermediate_size"]
+    m.vocab = tc.get("vocab_size") or cfg["vocab_size"]
+    m.rms_eps = tc.get("rms_norm_eps") or 1e-5
+    rp = tc.get("rope_parameters") if isinstance(tc.get("rope_parameters"), dict) else {}
+    m.rope_theta = tc.get("rope_theta") or rp.get("rope_theta") or 10000.0
     m.rope_neox = True  # HF checkpoints keep the rotate-half layout
-    m.rope_scaling = cfg.get("rope_scaling")
-    m.context_length = cfg.get("max_position_embeddings") or 4096
-    sw = cfg.get("sliding_window")
+    m.rope_scaling = tc.get("rope_scaling")
+    prf = tc.get("partial_rotary_factor") or rp.get("partial_rotary_factor")
+    if prf:
+        m.rope_dims = int(m.head_dim * float(prf))
+    m.context_length = tc.get("max_position_embeddings") or 4096
+    sw = tc.get("sliding_window")
     if sw and sw < m.context_length:
         # The attention kernels have no sliding-window mask; up to the window length full attention
         # equals windowed attention, so the context is capped there and outputs stay exact.
         m.context_length = int(sw)
-    m.n_experts = cfg.get("num_local_experts") or 0
-    m.n_experts_used = cfg.get("num_experts_per_tok") or 0
-    m.bos_token_id = cfg.get("bos_token_id", 1) or 1
-    eos = cfg.get("eos_token_id", 2)
+    m.n_experts = tc.get("n_routed_experts") or tc.get("num_local_experts") or tc.get("num_experts") or 0
+    m.n_experts_used = tc.get("num_experts_per_tok") or 0
+    if m.n_experts and tc.get("moe_intermediate_size"):
+        m.ffn = int(tc["moe_intermediate_size"])
+    m.ffn_shexp = int(tc.get("shared_expert_intermediate_size") or 0)
+    iv = _hybrid_schedule(tc, m.n_layers)
+    if iv:
+        m.arch = "qwen35moe"
+        m.full_attn_interval = iv
+        m.ssm_conv = int(tc.get("linear_conv_kernel_dim") or 4)
+        kd, vd = tc.get("linear_key_head_dim"), tc.get("linear_value_head_dim")
+        if kd and vd and kd != vd:
+            raise ValueError("gated delta-net layers need equal key and value head dims")
+        m.ssm_state = int(kd or vd or 0)
+        m.ssm_k_heads = int(tc.get("linear_num_key_heads") or 0)
+        m.ssm_v_heads = int(tc.get("linear_num_value_heads") or 0)
+        m.nextn_layers = 0  # MTP blocks live outside num_hidden_layers in HF checkpoints
+    m.bos_token_id = cfg.get("bos_token_id", tc.get("bos_token_id", 1)) or 1
+    eos = cfg.get("eos_token_id", tc.get("eos_token_id", 2))
     m.eos_token_ids = list(eos) if isinstance(eos, list) else [eos]
-    m.tie_embeddings = bool(cfg.get("tie_word_embeddings", False))
+    m.tie_embeddings = bool(cfg.get("tie_word_embeddings", tc.get("tie_word_embeddings", False)))
     return m
 
 
