@@ -68,3 +68,20 @@ def test_chunked_delta_rule_equals_recurrence(chunk):
     o2, s2 = R.ref_gdn_chunked(y, alpha, beta, z, a_neg, dt_bias, norm_w, S0, Hk, eps, chunk)
     torch.testing.assert_close(o2, o1, rtol=1e-4, atol=1e-4)
     torch.testing.assert_close(s2, s1, rtol=1e-4, atol=1e-5)
+
+
+def test_tensor_plan_matches_checkpoint(model):
+    from vm_c_b200.models.hybrid import check_hybrid_tensors, hybrid_tensor_plan
+    src, cfg = model
+    plan = hybrid_tensor_plan(cfg)
+    assert set(plan) == set(src.tensors)
+    check_hybrid_tensors(src, cfg)
+
+    class Missing:
+        def has(self, n):
+            return n != "blk.1.ssm_a" and src.has(n)
+
+        def info(self, n):
+            return src.info(n)
+    with pytest.raises(ValueError, match="blk.1.ssm_a"):
+        check_hybrid_tensors(Missing(), cfg)

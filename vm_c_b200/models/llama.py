@@ -116,6 +116,8 @@ def _tile_raw(raw: torch.Tensor, gtype: int, N: int, K: int) -> ops.TiledWeight:
 def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1, ep_size: int = 1) -> ModelWeights:
     """Load (and shard) the weights of a llama-architecture model from a tensor source."""
     if cfg.is_hybrid:
+        from .hybrid import check_hybrid_tensors
+        check_hybrid_tensors(src, cfg)
         raise ValueError("GGUF architecture 'qwen35moe' (hybrid gated delta-net) cannot be served yet: its "
                          "linear-attention kernels exist (csrc/kernels/gdn.cu) but the model is not wired")
     check_tp(cfg, tp_size)
