@@ -260,3 +260,20 @@ def test_hf_config_hybrid_and_nested(tmp_path):
     json.dump({"text_config": tc}, open(tmp_path / "config.json", "w"))
     with pytest.raises(ValueError):
         model_config_from_hf(str(tmp_path))
+
+
+def test_f16_and_f32_weights(tmp_path):
+    # F16 matrices are handed over as raw bytes (GGUF F16 rows), F32 matrices as float32 rows.
+    H, V = 32, 64
+    emb = torch.randn(V, H).half()
+    out = torch.randn(V, H)
+    save_file({"model.embed_tokens.weight": emb, "lm_head.weight": out, "model.norm.weight": torch.ones(H).half()},
+              str(tmp_path / "model.safetensors"))
+    json.dump({"model_type": "llama", "num_hidden_layers": 0, "hidden_size": H, "num_attention_heads": 4,
+               "intermediate_size": 64, "vocab_size": V}, open(tmp_path / "config.json", "w"))
+    h = HfSource(str(tmp_path))
+    assert h.info("token_embd.weight").gtype == GType.F16 and h.info("output.weight").gtype == GType.F32
+    r = h.rows("token_embd.weight", 3, 7)
+    assert r.dtype == torch.uint8 and torch.equal(r.view(torch.float16), emb[3:7])
+    assert torch.equal(h.rows("output.weight", 5, 9), out[5:9])
+    assert torch.equal(h.rows("output_norm.weight").view(-1), torch.ones(H))
