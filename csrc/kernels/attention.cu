@@ -352,8 +352,9 @@ __device__ __forceinline__ void decode_merge_store(const AttnParams& p, uint8_t*
         }
         *reinterpret_cast<uint32_t*>(p.out + orow * D + d) = pack_bf16x2(a0 * inv, a1 * inv);
       }
-    } else {
-      // Partial: normalised O and log2-sum-exp of this split.
+    } else if (qs + t < total_tokens) {
+      // Partial: normalised O and log2-sum-exp of this split. Rows past the partial buffers'
+      // total_tokens rows (a q_start beyond the launch's token count) are not written.
       const float inv = L > 0.f ? 1.f / L : 0.f;
       float* po = p.part_o + (static_cast<int64_t>(split) * total_tokens * p.Hq + orow) * D;
       for (int d = d0; d < d0 + PER; ++d) {

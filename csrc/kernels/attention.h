@@ -43,3 +43,6 @@ void kv_move(void* cache, int L, int64_t layer_elems, int Hkv, int D, const int3
 int attn_decode_ctas_per_sm(int D);
 
 }  // namespace vmc
+
+// The allocation-free C entry point of split-KV decode attention (attention_noalloc.cu).
+#include "attention_noalloc.h"

@@ -27,9 +27,14 @@
 //    kernels may overlap (different streams with no ordering between them, or several host
 //    threads) race on the scratch and corrupt each other's results. Serialise them, e.g. issue
 //    them on one stream.
+//  * Query layout: request r owns rows r * q_len .. r * q_len + q_len - 1, i.e. q_start must hold
+//    exactly 0, q_len, 2 * q_len, ... (the scratch is sized from num_reqs * q_len rows). The decode
+//    kernel skips partial rows past that count, so a larger q_start cannot write outside the
+//    scratch, but its rows are then missing from the output.
 //  * The first call on each device does the set-up: with that device current it asks the runtime
 //    for the address of the scratch array (cudaGetSymbolAddress) and caches it. Make that first
-//    call on a device outside any stream capture.
+//    call on a device outside any stream capture. The cached address belongs to the device's
+//    primary context: do not keep using the entry point across cudaDeviceReset().
 //  * Errors are returned, never thrown: 0 on success, a negative kNoAllocErr* code otherwise, with
 //    a message written to the caller's buffer (errbuf, errbuf_len; may be null).
 #include <cuda_runtime.h>
@@ -40,6 +45,7 @@
 #include <mutex>
 
 #include "attention.h"
+#include "attention_noalloc.h"
 
 namespace {
 
@@ -47,11 +53,11 @@ constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB of fp32
 constexpr int kNoAllocMaxDevices = 64;
 
 enum : int {
-  kNoAllocOk = 0,
-  kNoAllocErrArgs = -1,
-  kNoAllocErrTooLarge = -2,
-  kNoAllocErrSetup = -3,
-  kNoAllocErrLaunch = -4,
+  kNoAllocOk = VMC_NOALLOC_OK,
+  kNoAllocErrArgs = VMC_NOALLOC_ERR_ARGS,
+  kNoAllocErrTooLarge = VMC_NOALLOC_ERR_TOO_LARGE,
+  kNoAllocErrSetup = VMC_NOALLOC_ERR_SETUP,
+  kNoAllocErrLaunch = VMC_NOALLOC_ERR_LAUNCH,
 };
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];

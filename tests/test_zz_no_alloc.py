@@ -25,7 +25,7 @@ def _lib():
     return fn
 
 
-def _setup(ctx_lens, Hq, Hkv, D, nblocks=400, seed=3):
+def _setup(ctx_lens, Hq, Hkv, D, q_len=1, nblocks=400, seed=3):
     g = torch.Generator(device="cuda").manual_seed(seed)
     kv = (torch.randn(nblocks, 2, Hkv, 16, D, generator=g, device="cuda") * 0.5).bfloat16()
     R = len(ctx_lens)
@@ -37,12 +37,13 @@ def _setup(ctx_lens, Hq, Hkv, D, nblocks=400, seed=3):
         nb = (c + 15) // 16
         bt[r, :nb] = perm[o:o + nb].int()
         o += nb
-    q = torch.randn(R, Hq, D, generator=g, device="cuda").bfloat16()
-    qs = torch.arange(R + 1, dtype=torch.int32, device="cuda")
+    q = torch.randn(R * q_len, Hq, D, generator=g, device="cuda").bfloat16()
+    qs = torch.arange(0, R * q_len + 1, q_len, dtype=torch.int32, device="cuda")
     return kv, bt.cuda(), q, qs, torch.tensor(ctx_lens, dtype=torch.int32, device="cuda")
 
 
-def _ref(kv, bt, q, ctx, Hq, Hkv, D):
+def _ref(kv, bt, q, ctx, Hq, Hkv, D, q_len=1):
+    """fp32 causal attention: token j (of q_len) of request r sees the first ctx - q_len + 1 + j keys."""
     G = Hq // Hkv
     out = torch.zeros_like(q, dtype=torch.float32)
     for r in range(ctx.numel()):
@@ -51,16 +52,19 @@ def _ref(kv, bt, q, ctx, Hq, Hkv, D):
         blocks = bt[r, :nb].long()
         K = kv[blocks, 0].permute(1, 0, 2, 3).reshape(Hkv, nb * 16, D)[:, :c].float()
         V = kv[blocks, 1].permute(1, 0, 2, 3).reshape(Hkv, nb * 16, D)[:, :c].float()
-        for h in range(Hq):
-            s = q[r, h].float() @ K[h // G].T / math.sqrt(D)
-            out[r, h] = torch.softmax(s, -1) @ V[h // G]
+        for j in range(q_len):
+            row = r * q_len + j
+            n = c - q_len + 1 + j
+            for h in range(Hq):
+                s = q[row, h].float() @ K[h // G, :n].T / math.sqrt(D)
+                out[row, h] = torch.softmax(s, -1) @ V[h // G, :n]
     return out
 
 
-def _call(fn, kv, bt, q, qs, cl, Hq, Hkv, D, splits, out):
+def _call(fn, kv, bt, q, qs, cl, Hq, Hkv, D, splits, out, q_len=1):
     err = ctypes.create_string_buffer(256)
     rc = fn(q.data_ptr(), kv.data_ptr(), qs.data_ptr(), cl.data_ptr(), bt.data_ptr(), bt.shape[1],
-            q.shape[0], 1, Hq, Hkv, D, 1.0 / math.sqrt(D), splits, out.data_ptr(),
+            q.shape[0] // q_len, q_len, Hq, Hkv, D, 1.0 / math.sqrt(D), splits, out.data_ptr(),
             torch.cuda.current_stream().cuda_stream, err, len(err))
     return rc, err.value.decode()
 
@@ -70,19 +74,24 @@ def fn(cuda_ext):
     return _lib()
 
 
-def test_noalloc_matches_regular_entry_point(fn):
-    Hq, Hkv, D, S = 32, 8, 128, 4
+@pytest.mark.parametrize("q_len,D,splits", [(1, 128, 4), (1, 64, 1), (2, 128, 8), (2, 64, 8), (1, 128, 8)])
+def test_noalloc_matches_regular_entry_point(fn, q_len, D, splits):
+    # GQA 4 (q_len 1 or 2 rows per KV group fit the 16-row decode tile); one context of 3 tokens,
+    # shorter than `splits` pages, leaves most of its split ranges empty (the -inf LSE path).
+    Hq, Hkv = 32, 8
     ctx = [700, 1500, 3, 64, 257]
-    kv, bt, q, qs, cl = _setup(ctx, Hq, Hkv, D)
+    kv, bt, q, qs, cl = _setup(ctx, Hq, Hkv, D, q_len=q_len)
     R = len(ctx)
+    T = R * q_len
     want = torch.empty_like(q)
-    po = torch.empty(S, R, Hq, D, device="cuda")
-    pl = torch.empty(S, R, Hq, device="cuda")
-    ops.paged_attention(q, kv, qs, cl, bt, R, 0, 1, R, Hq, Hkv, D, 1 / math.sqrt(D), True, want, S, po, pl)
-    ref = _ref(kv, bt, q, cl, Hq, Hkv, D)
+    po = torch.empty(splits, T, Hq, D, device="cuda")
+    pl = torch.empty(splits, T, Hq, device="cuda")
+    ops.paged_attention(q, kv, qs, cl, bt, R, 0, q_len, T, Hq, Hkv, D, 1 / math.sqrt(D), True, want, splits,
+                        po if splits > 1 else None, pl if splits > 1 else None)
+    ref = _ref(kv, bt, q, cl, Hq, Hkv, D, q_len)
     for _ in range(2):  # two calls in a row reuse the same static scratch
         got = torch.full_like(q, float("nan"))
-        rc, msg = _call(fn, kv, bt, q, qs, cl, Hq, Hkv, D, S, got)
+        rc, msg = _call(fn, kv, bt, q, qs, cl, Hq, Hkv, D, splits, got, q_len)
         assert rc == 0, msg
         torch.cuda.synchronize()
         assert torch.isfinite(got.float()).all()

@@ -25,16 +25,6 @@ HOST_SOURCES = ["host/gguf.cpp", "host/quants.cpp", "host/block_manager.cpp", "h
 SM100_FLAGS = ["-gencode=arch=compute_100a,code=sm_100a"]
 
 
-def _cutlass_include() -> list[str]:
-    """CuTe/CUTLASS headers vendored in site-packages (used only for `cute/arch` definitions)."""
-    import site
-    for sp in site.getsitepackages():
-        p = Path(sp) / "flashinfer" / "data" / "cutlass" / "include"
-        if p.is_dir():
-            return [str(p)]
-    return []
-
-
 def cuda_sources() -> list[str]:
     kdir = CSRC / "kernels"
     return sorted(str(p) for p in kdir.glob("*.cu")) + sorted(str(p) for p in kdir.glob("*.cpp"))
