@@ -31,4 +31,9 @@ cmake -S "${HERE}" -B "${OUT}/build" -G Ninja -DCMAKE_BUILD_TYPE=Release \
   -DCMAKE_CUDA_ARCHITECTURES=100 -DVMC_REF_SRC="${SCRATCH}" -DVMC_JSON_INCLUDE="${JSON_DIR}"
 cmake --build "${OUT}/build" --target vmc_ref_bench -j "${JOBS}"
 cp "${OUT}/build/vmc_ref_bench" "${OUT}/vmc_ref_bench"
-echo "built ${OUT}/vmc_ref_bench"
+# CPU-only stack (vendored libllama + ggml-cpu): the config-1 oracle; runs without a GPU driver.
+cmake -S "${HERE}" -B "${OUT}/build_cpu" -G Ninja -DCMAKE_BUILD_TYPE=Release -DVMC_REF_CUDA=OFF \
+  -DVMC_REF_SRC="${SCRATCH}" -DVMC_JSON_INCLUDE="${JSON_DIR}"
+cmake --build "${OUT}/build_cpu" --target vmc_ref_bench -j "${JOBS}"
+cp "${OUT}/build_cpu/vmc_ref_bench" "${OUT}/vmc_ref_cpu"
+echo "built ${OUT}/vmc_ref_bench and ${OUT}/vmc_ref_cpu"

@@ -30,12 +30,16 @@
 #include <thread>
 #include <vector>
 
+#ifndef VMC_REF_CPU_ONLY
 #include <cuda_runtime.h>
+#endif
 
 #include "ggml.h"
 #include "gguf.h"
 #include "llama.h"
+#ifndef VMC_REF_CPU_ONLY
 #include "vm_c/cuda/kernels_sampler.h"
+#endif
 
 namespace {
 
@@ -72,11 +76,18 @@ Args parse(int argc, char** argv) {
   return a;
 }
 
+#ifndef VMC_REF_CPU_ONLY
 #define CK(x)                                                                                   \
   do {                                                                                          \
     cudaError_t e_ = (x);                                                                       \
     if (e_ != cudaSuccess) throw std::runtime_error(std::string(#x) + ": " + cudaGetErrorString(e_)); \
   } while (0)
+#else
+// CPU-only build: no CUDA runtime; the GPU branches below are compiled out.
+#define CK(x) (void)0
+typedef void* cudaStream_t;
+typedef void* cudaEvent_t;
+#endif
 
 // ------------------------------------------------------------------------------------------------
 // gen
@@ -242,6 +253,9 @@ struct Server {
     h_ids.resize(n_seq);
     h_lp.resize(n_seq);
     if (cpu) return;
+#ifdef VMC_REF_CPU_ONLY
+    throw std::runtime_error("this build has no CUDA backend: pass --cpu");
+#else
     CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     CK(cudaMalloc(&d_logits, static_cast<size_t>(n_seq) * V * sizeof(float)));
     CK(cudaMalloc(&d_ids, n_seq * 4));
@@ -258,6 +272,7 @@ struct Server {
     CK(cudaMemcpy(d_topk, tk.data(), n_seq * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(d_topp, tp.data(), n_seq * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(d_minp, mp.data(), n_seq * 4, cudaMemcpyHostToDevice));
+#endif
   }
 
   // Greedy token of each logits row (batch indices `rows`).
@@ -270,6 +285,7 @@ struct Server {
       }
       return;
     }
+#ifndef VMC_REF_CPU_ONLY
     for (int i = 0; i < ns; ++i) {  // engine.cpp copy_llama_logits_rows
       const float* l = llama_get_logits_ith(ctx, rows[i]);
       CK(cudaMemcpyAsync(d_logits + static_cast<size_t>(i) * V, l, static_cast<size_t>(V) * 4, cudaMemcpyDefault, st));
@@ -279,6 +295,7 @@ struct Server {
     CK(cudaMemcpyAsync(h_ids.data(), d_ids, ns * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(h_lp.data(), d_lp, ns * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+#endif
   }
 
   // One complete serving run of `prompts`; returns the finished requests.
@@ -377,7 +394,7 @@ int bench(const Args& a) {
   llama_model_params mp = llama_model_default_params();
   mp.n_gpu_layers = a.cpu ? 0 : -1;
   mp.split_mode = LLAMA_SPLIT_MODE_NONE;
-  mp.main_gpu = 0;
+  mp.main_gpu = a.cpu ? -1 : 0;
   mp.use_mmap = false;
   llama_model* model = llama_model_load_from_file(a.model.c_str(), mp);
   if (!model) throw std::runtime_error("llama_model_load_from_file failed");
@@ -406,13 +423,15 @@ int bench(const Args& a) {
     llama_memory_clear(mem, true);
     s.run(prompts, now_ms());
   }
-  if (!a.cpu) CK(cudaDeviceSynchronize());
+#ifndef VMC_REF_CPU_ONLY
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   if (!a.cpu) {
+    CK(cudaDeviceSynchronize());
     CK(cudaEventCreate(&e0));
     CK(cudaEventCreate(&e1));
     CK(cudaEventRecord(e0, s.st));
   }
+#endif
   const double w0 = now_ms();
   std::vector<double> ttft, itl;
   std::vector<Req> last;
@@ -426,6 +445,7 @@ int bench(const Args& a) {
     }
   }
   double ms = now_ms() - w0;
+#ifndef VMC_REF_CPU_ONLY
   if (!a.cpu) {
     CK(cudaDeviceSynchronize());
     CK(cudaEventRecord(e1, s.st));
@@ -434,6 +454,7 @@ int bench(const Args& a) {
     CK(cudaEventElapsedTime(&dev_ms, e0, e1));
     ms = dev_ms;
   }
+#endif
   const double toks = static_cast<double>(a.runs) * n_req * a.gen;
   printf("{\"ms_total\": %.3f, \"runs\": %d, \"ms_per_run\": %.3f, \"tok_per_s\": %.2f, \"p50_ttft_ms\": %.3f, "
          "\"p50_itl_ms\": %.4f, \"n_req\": %d, \"prompt_len\": %d, \"gen_len\": %d, \"vocab\": %d}\n",
