@@ -28,10 +28,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "output tok/s (box, device-timed, max over ranks) @TP1/2/4/8; p50 TTFT/ITL"
 MODEL = "Llama-3-8B (random-init, Q4_K_M GGUF)"
-REFERENCE_UNAVAILABLE = (
-    "reference is a C++ server with no Python package (no setup.py/pyproject.toml: pip install fails) and its "
-    "CMake build fetches spdlog/json/httplib from GitHub (no network) and includes missing headers "
-    "(vm_c/model/tensor_schema.hpp)")
+REF_EXE = os.path.join(ROOT, "baseline", "_ref", "vmc_ref_bench")
+REFERENCE_TP_UNAVAILABLE = (
+    "the reference's multi-GPU path is its full engine (TPRuntime + NcclComm, src/distributed/), which does not "
+    "build as shipped: src/model/gguf_model_loader.cpp:6,11 include vm_c/model/tensor_schema.hpp and "
+    "vm_c/vmc_engine/ggml_weight.hpp, which do not exist (TensorSchema, ShardContext, TpShardMode and "
+    "compute_quant_alloc_bytes are defined nowhere); its single-GPU forward (vendored libllama + ggml-cuda) is "
+    "what the N=1 reference arm runs")
 
 
 def parse():
@@ -101,8 +104,67 @@ class ClockSampler:
 
 
 def reference_arm(args):
-    print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE, "metric": METRIC,
-                      "n_gpus": args.gpus}))
+    """The reference through its own forward-pass API: its vendored libllama + ggml-cuda, built offline from
+    the reference tree by baseline/build_ref.sh into baseline/_ref, driven by baseline/ref_bench.cpp (decode-
+    first continuous batching of the same workload, the reference engine's GPU sampler). Nothing of this
+    repository's engine, models or kernels is loaded in this process or the driver."""
+    import numpy as np
+    base = {"impl": "reference", "metric": METRIC, "n_gpus": args.gpus}
+    if args.gpus > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({**base, "unavailable": REFERENCE_TP_UNAVAILABLE}), flush=True)
+        return
+    if not os.path.exists(REF_EXE):
+        print(json.dumps({**base, "unavailable": "reference arm not built (run baseline/build_ref.sh)"}), flush=True)
+        return
+    R, P, G = args.num_reqs, args.prompt_len, args.gen_len
+    tmp = tempfile.mkdtemp(prefix="vmc_ref_")
+    gguf = os.path.join(tmp, "model.gguf")
+    preset, mix = (args.model.split(":") + ["", "", ""])[1:3]
+    def failed(what, r):
+        tail = " | ".join((r.stderr or "").strip().splitlines()[-3:])
+        print(json.dumps({**base, "unavailable": f"reference {what} failed (rc {r.returncode}): {tail}"}), flush=True)
+
+    r = subprocess.run([REF_EXE, "gen", "--preset", preset or "llama3-8b", "--mix", mix or "Q4_K_M", "--seed", "0",
+                        "--out", gguf], capture_output=True, text=True)
+    if r.returncode != 0:
+        return failed("checkpoint generation", r)
+    rng = np.random.default_rng(1_000)
+    prompts = rng.integers(0, 128256 if (preset or "llama3-8b") == "llama3-8b" else 32000, (R, P)).astype(np.int32)
+    pfile = os.path.join(tmp, "prompts.bin")
+    with open(pfile, "wb") as f:
+        f.write(np.asarray([R, P], np.int32).tobytes())
+        f.write(prompts.tobytes())
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    t0 = time.perf_counter()
+    out = subprocess.run([REF_EXE, "bench", "--model", gguf, "--prompts", pfile, "--gen", str(G), "--batch",
+                          str(args.max_num_batched_tokens), "--runs", str(args.steps), "--warmup", str(args.warmup)],
+                         capture_output=True, text=True)
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    if out.returncode != 0:
+        os.unlink(gguf)
+        return failed("serving run", out)
+    r = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith("{")][-1])
+    os.unlink(gguf)
+    value = r["tok_per_s"]
+    line = {**base, "value": value, "unit": "output tokens/s", "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms_per_run"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 KV, Q4_K_M weights (ggml-cuda kernels)",
+            "data": "synthetic: random-init Q4_K_M GGUF written by the reference's own ggml quantisers; "
+                    "uniform-random prompt token ids (seeded)",
+            "config": {"model": MODEL, "global_batch": R, "seq_len": P, "gen_len": G, "parallelism": "tp1",
+                       "kv_cache": "bf16 (libllama cache)", "max_num_batched_tokens": args.max_num_batched_tokens,
+                       "path": "reference libllama llama_decode + ggml-cuda, reference GPU sampler",
+                       "l2": "inputs larger than L2 (4.9 GB weights + KV streamed every step)",
+                       "step": "one full serving run of global_batch requests"},
+            "p50_ttft_ms": r["p50_ttft_ms"], "p50_itl_ms": r["p50_itl_ms"],
+            "e2e": {"value": round(args.steps * R * G / r["ms_wall_total"] * 1e3, 2),
+                    "unit": "output tokens/s (host wall clock of the timed runs)",
+                    "h2d_bytes_per_step": r["h2d_bytes_per_run"], "d2h_bytes_per_step": r["d2h_bytes_per_run"]},
+            "gpu_launches": None, "clocks": clk, "process_wall_s": round(wall, 1)}
+    print(json.dumps(line), flush=True)
 
 
 def main():

@@ -186,6 +186,155 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
   }
 }
 
+// ---- reduce-scatter + residual + RMSNorm + all-gather ------------------------------------------
+//
+// Memory-model protocol (PTX scopes): every producer of remote data (a source GEMM CTA storing its
+// partial tile into the owner's receive buffer, or an owner CTA pushing its normalised rows into a
+// peer's h) finishes its stores, synchronises its threads (bar.sync), and one thread issues a
+// system-scope acq_rel fence followed by a relaxed system-scope add on the consumer's arrival
+// counter: a release pattern, so a consumer that reads the counter with a system-scope acquire load
+// observes every store made before the barrier. Counters only grow; the expected value of the next
+// call lives in the consumer's private `state` and advances by the number of arrivals per call.
+// Waits are bounded and record kErrCommWait.
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_add_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *p >= target (wrap-safe comparison), system-scope acquire.
+__device__ __forceinline__ bool wait_count_sys(const uint32_t* p, uint32_t target, uint32_t* err) {
+  for (uint32_t i = 0;; ++i) {
+    if (static_cast<int32_t>(ld_acquire_sys(p) - target) >= 0) return true;
+    if (i > kSpinLimit) {
+      atomicCAS(err, 0u, static_cast<uint32_t>(kErrCommWait));
+      return false;
+    }
+    if (i > 32) __nanosleep(100);
+  }
+}
+
+struct RsArgs {
+  const __nv_bfloat16* recv;  // this rank's receive buffer of the site: [slots][rpr][H]
+  uint32_t* rs_count;         // this rank's reduce-scatter arrival counter of the site
+  uint32_t* ag_count[kMaxRanks];  // every rank's all-gather arrival counter of the site
+  __nv_bfloat16* h[kMaxRanks];    // every rank's h buffer [max_tokens][H]
+  uint32_t* state;            // this site's bookkeeping: [0] rs target, [1] ag target, [2] CTAs done
+  float* resid;
+  const float* w;
+  float eps;
+  int T, H, rpr, slots, rank;
+  uint32_t rs_inc;
+  uint32_t* err;
+};
+
+constexpr int kRsThreads = 256;
+constexpr int kRsMaxVec = 4;  // 8-element vectors per thread (H <= 256 * 8 * 4 = 8192)
+
+template <int NR>
+__global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsArgs a) {
+  __shared__ float red[32];
+  __shared__ int ok;
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x, G = gridDim.x;
+  if (threadIdx.x == 0) ok = wait_count_sys(a.rs_count, a.state[0] + a.rs_inc, a.err) ? 1 : 0;
+  __syncthreads();
+  const int H = a.H, nvec = H / 8;
+  if (ok) {
+    for (int lr = b; lr < a.rpr; lr += G) {
+      const int m = a.rank * a.rpr + lr;
+      if (m >= a.T) break;
+      const size_t row = static_cast<size_t>(m) * H;
+      float v[kRsMaxVec][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kRsMaxVec; ++j) {
+        const int vi = threadIdx.x + j * kRsThreads;
+        if (vi >= nvec) continue;
+        const float4 r0 = *reinterpret_cast<const float4*>(a.resid + row + 8 * vi);
+        const float4 r1 = *reinterpret_cast<const float4*>(a.resid + row + 8 * vi + 4);
+        float acc[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        // partial slots in (source rank, split) order: the same sum on every owner
+        int sl = 0;
+        for (; sl + 4 <= a.slots; sl += 4) {
+          uint4 p[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            p[u] = __ldcg(reinterpret_cast<const uint4*>(a.recv + (static_cast<size_t>(sl + u) * a.rpr + lr) * H) + vi);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t q[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc[2 * e] += bf16_lo(q[e]);
+              acc[2 * e + 1] += bf16_hi(q[e]);
+            }
+          }
+        }
+        for (; sl < a.slots; ++sl) {
+          const uint4 p = __ldcg(reinterpret_cast<const uint4*>(a.recv + (static_cast<size_t>(sl) * a.rpr + lr) * H) + vi);
+          const uint32_t q[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[2 * e] += bf16_lo(q[e]);
+            acc[2 * e + 1] += bf16_hi(q[e]);
+          }
+        }
+        *reinterpret_cast<float4*>(a.resid + row + 8 * vi) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(a.resid + row + 8 * vi + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          v[j][e] = acc[e];
+          ss += acc[e] * acc[e];
+        }
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        float t = threadIdx.x < kRsThreads / 32 ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+      }
+      __syncthreads();
+      const float inv = rsqrtf(red[0] / H + a.eps);
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < kRsMaxVec; ++j) {
+        const int vi = threadIdx.x + j * kRsThreads;
+        if (vi >= nvec) continue;
+        const float4 w0 = *reinterpret_cast<const float4*>(a.w + 8 * vi);
+        const float4 w1 = *reinterpret_cast<const float4*>(a.w + 8 * vi + 4);
+        uint4 o;
+        o.x = pack_bf16x2(v[j][0] * inv * w0.x, v[j][1] * inv * w0.y);
+        o.y = pack_bf16x2(v[j][2] * inv * w0.z, v[j][3] * inv * w0.w);
+        o.z = pack_bf16x2(v[j][4] * inv * w1.x, v[j][5] * inv * w1.y);
+        o.w = pack_bf16x2(v[j][6] * inv * w1.z, v[j][7] * inv * w1.w);
+#pragma unroll
+        for (int q = 0; q < NR; ++q) {  // own rank first is not required: the order is irrelevant
+          const int dst = (a.rank + q) % NR;
+          *reinterpret_cast<uint4*>(a.h[dst] + row + 8 * vi) = o;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+#pragma unroll
+    for (int q = 0; q < NR; ++q) red_add_sys(a.ag_count[q], 1u);
+    if (b == 0) wait_count_sys(a.ag_count[a.rank], a.state[1] + static_cast<uint32_t>(NR * G), a.err);
+    // The last CTA to finish advances the targets of the next call at this site (every CTA has read
+    // them by then).
+    if (atomicAdd(a.state + 2, 1u) == static_cast<uint32_t>(G - 1)) {
+      a.state[0] += a.rs_inc;
+      a.state[1] += static_cast<uint32_t>(NR * G);
+      a.state[2] = 0;
+      __threadfence();
+    }
+  }
+}
+
 }  // namespace
 
 void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
@@ -202,6 +351,40 @@ void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
     case 6: launch_k(ar_add_rmsnorm_kernel<6>, dim3(grid), dim3(kArThreads), 0, st, a); break;
     case 7: launch_k(ar_add_rmsnorm_kernel<7>, dim3(grid), dim3(kArThreads), 0, st, a); break;
     default: launch_k(ar_add_rmsnorm_kernel<8>, dim3(grid), dim3(kArThreads), 0, st, a); break;
+  }
+}
+
+void rs_norm_ag(const TpComm& c, int site, int T, int H, int splits, int rs_inc, float* resid, const float* w,
+                float eps, cudaStream_t st) {
+  VMC_CHECK(c.nranks >= 1 && c.nranks <= kMaxRanks && (site == 0 || site == 1), "rs_norm_ag: bad ranks / site");
+  VMC_CHECK(H % 8 == 0 && H <= kRsThreads * 8 * kRsMaxVec, "rs_norm_ag: hidden size unsupported");
+  const int rpr = tp_rows_per_rank(T, c.nranks);
+  VMC_CHECK(static_cast<int64_t>(c.nranks) * splits * rpr <= c.recv_rows, "rs_norm_ag: receive buffer too small");
+  RsArgs a{};
+  a.recv = static_cast<const __nv_bfloat16*>(c.recv[site][c.rank]);
+  a.rs_count = c.rs_count[site][c.rank];
+  for (int q = 0; q < kMaxRanks; ++q) {
+    a.ag_count[q] = q < c.nranks ? c.ag_count[site][q] : nullptr;
+    a.h[q] = q < c.nranks ? static_cast<__nv_bfloat16*>(c.h[q]) : nullptr;
+  }
+  a.state = c.state + 4 * site;
+  a.resid = resid;
+  a.w = w;
+  a.eps = eps;
+  a.T = T;
+  a.H = H;
+  a.rpr = rpr;
+  a.slots = c.nranks * splits;
+  a.rank = c.rank;
+  a.rs_inc = static_cast<uint32_t>(rs_inc);
+  a.err = c.err;
+  const int grid = tp_norm_ctas(rpr, c.max_ctas);
+  switch (c.nranks) {
+    case 1: launch_k(rs_norm_ag_kernel<1>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    case 2: launch_k(rs_norm_ag_kernel<2>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    case 4: launch_k(rs_norm_ag_kernel<4>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    case 8: launch_k(rs_norm_ag_kernel<8>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    default: throw std::runtime_error("rs_norm_ag: 1, 2, 4 or 8 ranks");
   }
 }
 

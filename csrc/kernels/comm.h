@@ -23,6 +23,43 @@ struct ArArgs {
 // One-shot all-reduce of the partials + residual add + RMSNorm (see comm.cu).
 void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st);
 
+// Tensor-parallel communication state of one rank for the reduce-scatter / all-gather design
+// (rs_norm_ag below and the scatter epilogue of the row-parallel GEMM, gemm_tcgen05.h).
+//
+// Rows of a step's token batch are owned round the ranks in contiguous shards of rpr = ceil(T / N)
+// rows (rank o owns rows [o * rpr, (o + 1) * rpr)). Each rank's symmetric region (CUDA IPC, mapped
+// on every peer) holds:
+//   recv[site]  bf16 [N * splits][rpr][H]: the partial sums of this rank's rows, one slot per
+//               (source rank, K split), written by the sources' GEMM epilogues;
+//   h           bf16 [max_tokens][H]: the normalised activations of every row, written by the
+//               owners (the all-gather) and read by the next column-parallel GEMM;
+//   counters    uint32 rs[site], ag[site]: monotonic arrival counters (peers add to them).
+// `state` is this rank's private bookkeeping (the counter targets of the next call per site).
+struct TpComm {
+  int nranks = 1, rank = 0;
+  void* recv[2][8] = {};          // [site][rank]: each rank's receive buffer of this site
+  int64_t recv_rows = 0;          // rows of one receive buffer
+  void* h[8] = {};                // each rank's h buffer
+  uint32_t* rs_count[2][8] = {};  // [site][rank]
+  uint32_t* ag_count[2][8] = {};  // [site][rank]
+  uint32_t* state = nullptr;      // [2 sites][4] (rs target, ag target, CTAs done, spare)
+  uint32_t* err = nullptr;
+  int max_ctas = 148;
+};
+
+// Rows per rank of a T-token step.
+inline int tp_rows_per_rank(int T, int nranks) { return (T + nranks - 1) / nranks; }
+// CTAs of rs_norm_ag for rpr rows per rank (the same on every rank).
+inline int tp_norm_ctas(int rpr, int max_ctas) { return rpr < 1 ? 1 : (rpr < max_ctas ? rpr : max_ctas); }
+
+// Owner side of one row-parallel site: waits until every source rank's GEMM has delivered its
+// partial rows (rs_inc arrivals: sources x their GEMM's CTAs), sums the N * splits partials of each
+// owned row in a fixed order, adds the residual (fp32, updated in place for the owned rows only),
+// applies RMSNorm with weight w, and writes the bf16 row into every rank's h (all-gather by push).
+// CTA 0 returns only after every rank's rows have arrived here, so the next kernel may read all of h.
+void rs_norm_ag(const TpComm& c, int site, int T, int H, int splits, int rs_inc, float* resid, const float* w,
+                float eps, cudaStream_t st);
+
 // Symmetric allocations through CUDA IPC (handle_out: 64-byte cudaIpcMemHandle_t).
 uint64_t sym_alloc(size_t bytes, void* handle_out);
 uint64_t sym_open(const void* handle);

@@ -244,7 +244,47 @@ struct GemmArgs {
   const int32_t* grp_count;
   const int32_t* grp_offset;
   int64_t grp_w_stride;  // bytes
+  // Scatter mode (kGemmOutScatterBF16: the reduce-scatter of a tensor-parallel row-parallel GEMM):
+  // output row m belongs to rank o = m / scat_rpr and is stored (bf16) as row m - o * scat_rpr of
+  // slot (scat_rank * splits + split) of that rank's receive buffer scat[o] (row stride ldo, slots
+  // scat_rpr rows apart). When a CTA has stored all its units it releases them (barrier over the
+  // epilogue warps, system-scope fence) and adds 1 to every rank's arrival counter scat_count[o].
+  void* scat[8];
+  uint32_t* scat_count[8];
+  int scat_rpr, scat_rank, scat_nranks;
 };
+
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Reduce-scatter epilogue of 16 consecutive rows m_base .. m_base + 15 (column n) of a unit.
+__device__ __forceinline__ void scatter_rows(const GemmArgs& a, int split, int n, int m_base, int m_end,
+                                             const uint32_t (&v)[16]) {
+  const int rpr = a.scat_rpr;
+  int o = m_base / rpr;
+  int lr = m_base - o * rpr;
+  const size_t slot = static_cast<size_t>(a.scat_rank * a.splits + split) * rpr;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (m_base + j < m_end) {
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.scat[o]) + (slot + lr) * a.ldo + n;
+      *dst = __float2bfloat16(__uint_as_float(v[j]));
+    }
+    if (++lr == rpr) {
+      lr = 0;
+      ++o;
+    }
+  }
+}
+
+// After a CTA's last unit: make its peer stores visible, then count one arrival at every rank.
+__device__ __forceinline__ void scatter_release(const GemmArgs& a, int warp, int first_epi_warp, int lane) {
+  epi_bar_sync();
+  if (warp == first_epi_warp && lane == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int q = 0; q < a.scat_nranks; ++q)
+      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.scat_count[q]) : "memory");
+  }
+}
 
 // Per-role timestamps of CTA 0 and per-phase cycle totals for pipeline diagnostics; compiled in only
 // with -DVMC_GEMM_TRACE=1 (the default build has no timing code in the hot loops).
@@ -568,6 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
             }
           }
+        } else if (args.out_mode == kGemmOutScatterBF16) {
+          const int n = w.nt * 128 + n_local;
+          if (n < args.N) scatter_rows(args, w.split, n, m_base, m_end, v);
         } else {
           const int n = w.nt * 128 + n_local;
           if (n < args.N) {
@@ -590,6 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_ph ^= 1; }
     }
+    if (args.out_mode == kGemmOutScatterBF16) scatter_release(args, warp, kFirstEpiWarp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -986,6 +1030,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
                 reinterpret_cast<__nv_bfloat16*>(args.out)[static_cast<size_t>(m) * args.ldo + f] = __float2bfloat16(y);
             }
           }
+        } else if (args.out_mode == kGemmOutScatterBF16) {
+          const int nn = w.nt * 128 + n_local;
+          if (nn < args.N) scatter_rows(args, w.split, nn, m_base, m_end, v);
         } else {
           const int nn = w.nt * 128 + n_local;
           if (nn < args.N) {
@@ -1014,6 +1061,7 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       phase_add(args, 14, ph_ld);
       phase_add(args, 15, ph_out);
     }
+    if (args.out_mode == kGemmOutScatterBF16) scatter_release(args, warp, kDFirstEpi, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -1053,7 +1101,7 @@ int num_sms() {
 }
 
 template <int WF, int BN>
-void launch(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+int launch(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   constexpr GemmSmemPlan P = make_plan(WF, BN);
   static_assert(P.total() <= 227 * 1024, "shared memory plan too large");
   static bool configured = false;
@@ -1063,10 +1111,11 @@ void launch(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   }
   const int grid = a.units < num_sms() ? a.units : num_sms();
   launch_k(gemm_kernel<WF, BN>, dim3(grid), dim3(kThreads), P.total(), st, map, a);
+  return grid;
 }
 
 template <int WF, int BN>
-void launch_qd(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+int launch_qd(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   constexpr GemmDPlan P = make_dplan(WF, BN);
   static_assert(P.total() <= 227 * 1024, "shared memory plan too large");
   // More than half the SM's shared memory: no second CTA (and no second 512-column TMEM
@@ -1079,34 +1128,35 @@ void launch_qd(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   }
   const int grid = a.units < num_sms() ? a.units : num_sms();
   launch_k(gemm_qd_kernel<WF, BN>, dim3(grid), dim3(kDThreads), P.total(), st, map, a);
+  return grid;
 }
 
 // Quantized weights with decode-width token tiles take the TMEM-A kernel; bf16 weights and wide
 // (prefill) tiles the shared-memory kernel.
 template <int WF, int BN>
-void launch_any(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
-  if constexpr (WF != kWfBF16 && BN <= 64) launch_qd<WF, BN>(map, a, st);
-  else launch<WF, BN>(map, a, st);
+int launch_any(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+  if constexpr (WF != kWfBF16 && BN <= 64) return launch_qd<WF, BN>(map, a, st);
+  else return launch<WF, BN>(map, a, st);
 }
 
 template <int WF>
-void dispatch_bn(int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+int dispatch_bn(int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   switch (bn) {
-    case 16: launch_any<WF, 16>(map, a, st); break;
-    case 32: launch_any<WF, 32>(map, a, st); break;
-    case 64: launch_any<WF, 64>(map, a, st); break;
-    case 128: launch_any<WF, 128>(map, a, st); break;
-    case 256: launch_any<WF, 256>(map, a, st); break;
+    case 16: return launch_any<WF, 16>(map, a, st);
+    case 32: return launch_any<WF, 32>(map, a, st);
+    case 64: return launch_any<WF, 64>(map, a, st);
+    case 128: return launch_any<WF, 128>(map, a, st);
+    case 256: return launch_any<WF, 256>(map, a, st);
     default: throw std::runtime_error("gemm: unsupported BN");
   }
 }
 
-void dispatch_wf(int wf, int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+int dispatch_wf(int wf, int bn, const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
   switch (wf) {
-    case kWfBF16: dispatch_bn<kWfBF16>(bn, map, a, st); break;
-    case kWfQ4K: dispatch_bn<kWfQ4K>(bn, map, a, st); break;
-    case kWfQ6K: dispatch_bn<kWfQ6K>(bn, map, a, st); break;
-    case kWfQ8_0: dispatch_bn<kWfQ8_0>(bn, map, a, st); break;
+    case kWfBF16: return dispatch_bn<kWfBF16>(bn, map, a, st);
+    case kWfQ4K: return dispatch_bn<kWfQ4K>(bn, map, a, st);
+    case kWfQ6K: return dispatch_bn<kWfQ6K>(bn, map, a, st);
+    case kWfQ8_0: return dispatch_bn<kWfQ8_0>(bn, map, a, st);
     default: throw std::runtime_error("gemm: unknown weight format");
   }
 }
@@ -1137,17 +1187,14 @@ int gemm_pick_bn(int M) {
   return 256;
 }
 
-void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
-                  int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride) {
-  VMC_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
-  if (bn <= 0) bn = gemm_pick_bn(M);
+namespace {
+GemmArgs dense_args(int wf, const void* w_tiled, int N, int K, int M, void* out, int ldo, int out_mode, int& splits,
+                    int bn, uint32_t* err, int64_t split_stride) {
   const int chunk = wf_chunk(wf);
   const int KC = (K + chunk - 1) / chunk;
   if (splits < 1) splits = 1;
   if (splits > KC) splits = KC;
-  VMC_CHECK(splits == 1 || out_mode == kGemmOutF32Add || out_mode == kGemmOutF32Split,
-            "gemm: split-K needs an fp32 accumulate / per-split output mode");
-  GemmArgs a;
+  GemmArgs a = {};
   a.w = static_cast<const uint8_t*>(w_tiled);
   a.N = N;
   a.K = K;
@@ -1167,12 +1214,43 @@ void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int 
   a.trace = g_gemm_trace;
   a.bn = bn;
   a.groups = 0;
-  a.grp_count = nullptr;
-  a.grp_offset = nullptr;
-  a.grp_w_stride = 0;
+  return a;
+}
+}  // namespace
+
+int gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
+                 int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride) {
+  VMC_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
+  VMC_CHECK(out_mode != kGemmOutScatterBF16, "gemm: the scatter output mode goes through gemm_tcgen05_scatter");
+  if (bn <= 0) bn = gemm_pick_bn(M);
+  GemmArgs a = dense_args(wf, w_tiled, N, K, M, out, ldo, out_mode, splits, bn, err, split_stride);
+  VMC_CHECK(splits == 1 || out_mode == kGemmOutF32Add || out_mode == kGemmOutF32Split,
+            "gemm: split-K needs an fp32 accumulate / per-split output mode");
   CUtensorMap map;
   make_act_tensor_map(&map, x, M, K, ldx, bn);
-  dispatch_wf(wf, bn, map, a, st);
+  return dispatch_wf(wf, bn, map, a, st);
+}
+
+int gemm_tcgen05_scatter(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, int splits,
+                         void* const* recv, uint32_t* const* counters, int nranks, int rank, int64_t recv_rows,
+                         uint32_t* err, cudaStream_t st, int* splits_used) {
+  VMC_CHECK(M > 0 && N > 0 && K > 0, "gemm_scatter: empty problem");
+  VMC_CHECK(nranks >= 1 && nranks <= 8 && rank >= 0 && rank < nranks, "gemm_scatter: bad ranks");
+  const int bn = gemm_pick_bn(M);
+  GemmArgs a = dense_args(wf, w_tiled, N, K, M, nullptr, N, kGemmOutScatterBF16, splits, bn, err, 0);
+  const int rpr = (M + nranks - 1) / nranks;
+  VMC_CHECK(static_cast<int64_t>(nranks) * splits * rpr <= recv_rows, "gemm_scatter: receive buffer too small");
+  for (int q = 0; q < 8; ++q) {
+    a.scat[q] = q < nranks ? recv[q] : nullptr;
+    a.scat_count[q] = q < nranks ? counters[q] : nullptr;
+  }
+  a.scat_rpr = rpr;
+  a.scat_rank = rank;
+  a.scat_nranks = nranks;
+  if (splits_used) *splits_used = splits;
+  CUtensorMap map;
+  make_act_tensor_map(&map, x, M, K, ldx, bn);
+  return dispatch_wf(wf, bn, map, a, st);
 }
 
 void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, int N, int K, const void* x,
@@ -1184,7 +1262,7 @@ void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, i
             "gemm_grouped: bf16, fp32 or SwiGLU output");
   if (bn <= 0) bn = gemm_pick_bn(max_rows);
   const int chunk = wf_chunk(wf);
-  GemmArgs a;
+  GemmArgs a = {};
   a.w = static_cast<const uint8_t*>(w_tiled);
   a.N = N;
   a.K = K;

@@ -12,13 +12,23 @@ enum GemmOut : int {
   kGemmOutF32Add = 2,  // out[m, n] += acc (fp32 red.add; required for split-K; output pre-zeroed)
   kGemmOutSwiGLU = 3,  // rows interleave gate/up: out[m, f] = silu(acc[2f]) * acc[2f+1] (bf16)
   kGemmOutF32Split = 4,  // out[split][m, n] = partial over this split's K range (fp32, no atomics)
+  kGemmOutScatterBF16 = 5,  // tensor-parallel reduce-scatter: rows stored into their owner rank's buffer
 };
 
 // out = x[M, K] (bf16, row stride ldx) @ W[N, K]^T with W in a tiled format (weight_formats.cuh).
 // splits > 1 partitions K across CTAs (out_mode must be kGemmOutF32Add). bn = 0 picks the token
 // tile from M. `err` receives a DeviceError code if a bounded wait expires.
-void gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
-                  int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride = 0);
+// Returns the number of CTAs launched.
+int gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, void* out, int ldo,
+                 int out_mode, int splits, int bn, uint32_t* err, cudaStream_t st, int64_t split_stride = 0);
+// Row-parallel GEMM of a tensor-parallel layer with the reduce-scatter in its epilogue: row m of the
+// bf16 product goes to rank o = m / ceil(M / nranks) (row m - o * rpr of slot rank * splits + split of
+// recv[o], row stride N), and every CTA, after its last unit, adds 1 to counters[q] of every rank q
+// (release at system scope). recv / counters are the peers' IPC-mapped addresses. Returns the CTA
+// count (the arrivals each owner gets from this rank); *splits_used receives the effective K splits.
+int gemm_tcgen05_scatter(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, int splits,
+                         void* const* recv, uint32_t* const* counters, int nranks, int rank, int64_t recv_rows,
+                         uint32_t* err, cudaStream_t st, int* splits_used);
 // Grouped GEMM (MoE experts): for every group g with rows [offsets[g], offsets[g] + counts[g]) of
 // x (device arrays, at most max_rows rows per group), out[rows] = x[rows] @ W_g^T where W_g starts
 // w_group_stride bytes after W_{g-1}. One launch for all groups; no host synchronisation on the

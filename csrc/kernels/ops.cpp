@@ -6,6 +6,7 @@
 
 #include "attention.h"
 #include "comm.h"
+#include "forward.h"
 #include "gdn.h"
 #include "gemm_tcgen05.h"
 #include "layers.h"
@@ -359,6 +360,149 @@ torch::Tensor wrap_ptr(int64_t p, std::vector<int64_t> sizes, int dtype, int dev
   return torch::from_blob(reinterpret_cast<void*>(p), sizes, opts);
 }
 
+// ---- native step forward (forward.h) ----------------------------------------------------------
+// Layers arrive as flat int lists: [attn_norm, ffn_norm, n_qkv, (wf, ptr, N, K) x 3, col x 3,
+// wo (4), gate_up (4), down (4)]; pointers are device addresses of tensors the Python model owns.
+vmc::LinearDesc lin_at(const std::vector<int64_t>& v, size_t o) {
+  vmc::LinearDesc d;
+  d.wf = static_cast<int>(v[o]);
+  d.w = reinterpret_cast<const void*>(v[o + 1]);
+  d.N = static_cast<int>(v[o + 2]);
+  d.K = static_cast<int>(v[o + 3]);
+  return d;
+}
+template <typename T>
+T* dptr(const py::dict& d, const char* k) {
+  return d.contains(k) ? reinterpret_cast<T*>(d[k].cast<int64_t>()) : nullptr;
+}
+
+std::shared_ptr<vmc::Forward> make_forward(py::dict cfg, std::vector<std::vector<int64_t>> layers, py::dict bufs) {
+  vmc::ForwardConfig c;
+  c.L = cfg["L"].cast<int>();
+  c.H = cfg["H"].cast<int>();
+  c.Hq = cfg["Hq"].cast<int>();
+  c.Hkv = cfg["Hkv"].cast<int>();
+  c.D = cfg["D"].cast<int>();
+  c.F = cfg["F"].cast<int>();
+  c.V_local = cfg["V_local"].cast<int>();
+  c.max_tokens = cfg["max_tokens"].cast<int>();
+  c.max_samples = cfg["max_samples"].cast<int>();
+  c.max_blocks = cfg["max_blocks"].cast<int>();
+  c.eps = cfg["eps"].cast<float>();
+  c.scale = cfg["scale"].cast<float>();
+  c.neox = cfg["neox"].cast<bool>();
+  c.embd = dptr<const void>(cfg, "embd");
+  c.embd_type = cfg["embd_type"].cast<int>();
+  c.embd_row_bytes = cfg["embd_row_bytes"].cast<int64_t>();
+  c.out_norm = dptr<const float>(cfg, "out_norm");
+  c.lm_head = lin_at(cfg["lm_head"].cast<std::vector<int64_t>>(), 0);
+  c.cos_sin = dptr<const float>(cfg, "cos_sin");
+  c.num_sms = cfg["num_sms"].cast<int>();
+  std::vector<vmc::LayerDesc> ls;
+  for (const auto& v : layers) {
+    TORCH_CHECK(v.size() == 30, "make_forward: layer descriptors have 30 entries");
+    vmc::LayerDesc d;
+    d.attn_norm = reinterpret_cast<const float*>(v[0]);
+    d.ffn_norm = reinterpret_cast<const float*>(v[1]);
+    d.n_qkv = static_cast<int>(v[2]);
+    for (int i = 0; i < 3; ++i) {
+      d.qkv[i] = lin_at(v, 3 + 4 * i);
+      d.qkv_col[i] = static_cast<int>(v[15 + i]);
+    }
+    d.wo = lin_at(v, 18);
+    d.gate_up = lin_at(v, 22);
+    d.down = lin_at(v, 26);
+    ls.push_back(d);
+  }
+  vmc::ForwardBuffers b;
+  b.resid = dptr<float>(bufs, "resid");
+  b.h = dptr<void>(bufs, "h");
+  b.qkv_bf16 = dptr<void>(bufs, "qkv_bf16");
+  b.split_ws = dptr<float>(bufs, "split_ws");
+  b.split_ws_elems = bufs["split_ws_elems"].cast<int64_t>();
+  b.q = dptr<void>(bufs, "q");
+  b.attn = dptr<void>(bufs, "attn");
+  b.o16 = dptr<void>(bufs, "o16");
+  b.act = dptr<void>(bufs, "act");
+  b.hs = dptr<void>(bufs, "hs");
+  b.logits = dptr<float>(bufs, "logits");
+  b.part_o = dptr<float>(bufs, "part_o");
+  b.part_lse = dptr<float>(bufs, "part_lse");
+  b.attn_max_splits = bufs["attn_max_splits"].cast<int>();
+  b.ids = dptr<const int32_t>(bufs, "ids");
+  b.pos = dptr<const int32_t>(bufs, "pos");
+  b.slots = dptr<const int32_t>(bufs, "slots");
+  b.q_start = dptr<const int32_t>(bufs, "q_start");
+  b.ctx_len = dptr<const int32_t>(bufs, "ctx_len");
+  b.block_tables = dptr<const int32_t>(bufs, "block_tables");
+  b.logits_idx = dptr<const int32_t>(bufs, "logits_idx");
+  b.params = dptr<const void>(bufs, "params");
+  b.out_tok = dptr<int32_t>(bufs, "out_tok");
+  b.out_lp = dptr<float>(bufs, "out_lp");
+  b.kv = dptr<void>(bufs, "kv");
+  b.kv_layer_bytes = bufs["kv_layer_bytes"].cast<int64_t>();
+  b.err = dptr<uint32_t>(bufs, "err");
+  if (bufs.contains("tq_meta")) {
+    const auto meta = bufs["tq_meta"].cast<std::vector<int64_t>>();
+    TORCH_CHECK(meta.size() == 10, "make_forward: tq_meta must have 10 entries");
+    b.tq = true;
+    b.tq_tab.slot = static_cast<int>(meta[0]);
+    b.tq_tab.mse_bytes = static_cast<int>(meta[1]);
+    b.tq_tab.key_packed = static_cast<int>(meta[2]);
+    b.tq_tab.val_bytes = static_cast<int>(meta[3]);
+    b.tq_tab.key_bits = static_cast<int>(meta[4]);
+    b.tq_tab.value_bits = static_cast<int>(meta[5]);
+    b.tq_tab.norm_correction = static_cast<int>(meta[6]);
+    b.tq_tab.key_fp8 = static_cast<int>(meta[7]);
+    b.tq_tab.rot_seed = static_cast<uint32_t>(meta[8]);
+    b.tq_tab.centroids = dptr<const float>(bufs, "tq_centroids");
+    b.tq_tab.midpoints = dptr<const float>(bufs, "tq_midpoints");
+  }
+  return std::make_shared<vmc::Forward>(c, std::move(ls), b);
+}
+
+// TpComm from Python: peer address lists of the symmetric region.
+vmc::TpComm make_tp_comm(py::dict d) {
+  vmc::TpComm c;
+  c.nranks = d["nranks"].cast<int>();
+  c.rank = d["rank"].cast<int>();
+  TORCH_CHECK(c.nranks >= 1 && c.nranks <= 8, "tp comm: 1..8 ranks");
+  c.recv_rows = d["recv_rows"].cast<int64_t>();
+  c.max_ctas = d["max_ctas"].cast<int>();
+  const auto recv0 = d["recv0"].cast<std::vector<int64_t>>(), recv1 = d["recv1"].cast<std::vector<int64_t>>();
+  const auto h = d["h"].cast<std::vector<int64_t>>();
+  const auto rs0 = d["rs0"].cast<std::vector<int64_t>>(), rs1 = d["rs1"].cast<std::vector<int64_t>>();
+  const auto ag0 = d["ag0"].cast<std::vector<int64_t>>(), ag1 = d["ag1"].cast<std::vector<int64_t>>();
+  for (int q = 0; q < c.nranks; ++q) {
+    c.recv[0][q] = reinterpret_cast<void*>(recv0.at(q));
+    c.recv[1][q] = reinterpret_cast<void*>(recv1.at(q));
+    c.h[q] = reinterpret_cast<void*>(h.at(q));
+    c.rs_count[0][q] = reinterpret_cast<uint32_t*>(rs0.at(q));
+    c.rs_count[1][q] = reinterpret_cast<uint32_t*>(rs1.at(q));
+    c.ag_count[0][q] = reinterpret_cast<uint32_t*>(ag0.at(q));
+    c.ag_count[1][q] = reinterpret_cast<uint32_t*>(ag1.at(q));
+  }
+  c.state = reinterpret_cast<uint32_t*>(d["state"].cast<int64_t>());
+  c.err = reinterpret_cast<uint32_t*>(d["err"].cast<int64_t>());
+  return c;
+}
+
+// One reduce-scatter + norm + all-gather site driven from Python (tests and the comm benchmark):
+// x [M, K] bf16 times the tiled weight, partial rows scattered, then rs_norm_ag.
+int64_t tp_row_parallel(py::dict comm, int site, int wf, torch::Tensor w, int64_t N, int64_t K, torch::Tensor x,
+                        int64_t M, int64_t splits, torch::Tensor resid, torch::Tensor norm_w, double eps,
+                        torch::Tensor err) {
+  const vmc::TpComm c = make_tp_comm(comm);
+  int used = static_cast<int>(splits);
+  const int grid = vmc::gemm_tcgen05_scatter(wf, w.data_ptr(), static_cast<int>(N), static_cast<int>(K), x.data_ptr(),
+                                             static_cast<int>(M), static_cast<int>(x.stride(0)), static_cast<int>(splits),
+                                             c.recv[site], c.rs_count[site], c.nranks, c.rank, c.recv_rows,
+                                             ptr<uint32_t>(err), cur_stream(), &used);
+  vmc::rs_norm_ag(c, site, static_cast<int>(M), static_cast<int>(N), used, grid * c.nranks, ptr<float>(resid),
+                  ptr<float>(norm_w), static_cast<float>(eps), cur_stream());
+  return used;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -401,6 +545,32 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sym_close", [](int64_t p) { vmc::sym_close(static_cast<uint64_t>(p)); });
   m.def("sym_free", [](int64_t p) { vmc::sym_free(static_cast<uint64_t>(p)); });
   m.def("wrap_ptr", &wrap_ptr);
+  py::class_<vmc::Forward, std::shared_ptr<vmc::Forward>>(m, "Forward")
+      .def("run",
+           [](vmc::Forward& f, int T, int R, int S, int nd, int max_qlen, int decode_qlen, int attn_splits,
+              bool do_sample) {
+             vmc::StepDims d;
+             d.T = T;
+             d.R = R;
+             d.S = S;
+             d.nd = nd;
+             d.max_qlen = max_qlen;
+             d.decode_qlen = decode_qlen;
+             d.attn_splits = attn_splits;
+             d.sample = do_sample;
+             return f.run(d, cur_stream());
+           })
+      .def("set_comm", [](vmc::Forward& f, py::dict d) { f.set_comm(make_tp_comm(d)); })
+      .def("splits_for", [](vmc::Forward& f, int wf, int N, int K, int M) {
+        vmc::LinearDesc w;
+        w.wf = wf;
+        w.N = N;
+        w.K = K;
+        return f.splits_for(w, M);
+      });
+  m.def("make_forward", &make_forward);
+  m.def("tp_row_parallel", &tp_row_parallel);
+  m.def("gemm_pick_splits", [](int wf, int N, int K, int M, int sms) { return vmc::gemm_pick_splits(wf, N, K, M, sms); });
   m.attr("OUT_BF16") = static_cast<int>(vmc::kGemmOutBF16);
   m.attr("OUT_F32") = static_cast<int>(vmc::kGemmOutF32);
   m.attr("OUT_F32_ADD") = static_cast<int>(vmc::kGemmOutF32Add);

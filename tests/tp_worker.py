@@ -12,6 +12,31 @@ from vm_c_b200.core.sampling_params import SamplingParams  # noqa: E402
 from vm_c_b200.llm import LLM  # noqa: E402
 from vm_c_b200.parallel.comm import NcclComm, init_distributed  # noqa: E402
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from ref_llama import forward_logits, load_dense  # noqa: E402
+
+
+def oracle_report(model, prompts, outs, rows):
+    """Teacher-forced fp32 oracle along the engine's own greedy trajectories: the largest logit error
+    relative to each row's largest oracle logit, and argmax disagreements outside near-ties."""
+    from vm_c_b200.llm import make_source
+    src, cfg = make_source(model, "cpu")
+    W = load_dense(src, cfg)
+    got = {}
+    for ids, lg in rows:
+        for k, i in enumerate(ids):
+            got.setdefault(i, []).append(lg[k])
+    worst, flips = 0.0, 0
+    for idx, (p, o) in enumerate(zip(prompts, outs)):
+        ref = forward_logits(W, cfg, p + o.output_token_ids[:-1])[len(p) - 1:]
+        mine = torch.stack(got[sorted(got)[idx]])
+        scale = ref.abs().max(-1).values
+        worst = max(worst, float(((mine - ref).abs().max(-1).values / scale).max()))
+        top2 = torch.topk(ref, 2, -1).values
+        decided = (top2[:, 0] - top2[:, 1]) > 0.05 * scale
+        flips += int(((mine.argmax(-1) != ref.argmax(-1)) & decided).sum())
+    return {"max_rel_logit_err": worst, "argmax_flips": flips}
+
 
 def main():
     model, backend, out = sys.argv[1], sys.argv[2], sys.argv[3]
@@ -31,11 +56,16 @@ def main():
     prompts = [rng.integers(0, llm.cfg.model.vocab, n).tolist() for n in (5, 40, 17, 100)]
     sp = SamplingParams(temperature=1e-4, top_k=0, top_p=1.0, max_tokens=12, ignore_eos=True, seed=5) if spec \
         else SamplingParams.greedy_params(max_tokens=12, ignore_eos=True)
+    rows = []
+    if not spec:
+        llm.engine.logits_hook = lambda ids, lg: rows.append((ids, lg))
     outs = llm.generate(prompts, sp)
     err = int(comm.device_error()) if hasattr(comm, "device_error") else 0
+    report = oracle_report(model, prompts, outs, rows) if (rows and rank == 0) else {}
     steps = llm.runner.spec.stats.as_dict()["steps"] if spec else 0
     if rank == 0:
-        json.dump({"tokens": [o.output_token_ids for o in outs], "err": err, "spec_steps": steps}, open(out, "w"))
+        json.dump({"tokens": [o.output_token_ids for o in outs], "err": err, "spec_steps": steps, **report},
+                  open(out, "w"))
     llm.shutdown()
     if hasattr(comm, "close"):
         comm.close()

@@ -101,6 +101,9 @@ class LLMEngine:
         self.metrics = EngineMetrics()
         self.step_id = 0
         self.on_step: Optional[Callable] = None   # hook(plan, counts, dt)
+        # hook(request ids, logits [S, vocab] on the host): full-vocabulary logits of every sampled row of
+        # a non-speculative step (tests compare them with an fp32 oracle); None costs nothing.
+        self.logits_hook: Optional[Callable] = None
 
     # -------------------------------------------------------------------------------------------
     # request intake (thread-safe: the server's HTTP threads call these)
@@ -258,6 +261,8 @@ class LLMEngine:
         else:
             params = self._sample_params(plan, counts.S, counts.R_pad)
             toks, lps = self.runner.execute(self.meta, counts, params, pen)
+            if self.logits_hook is not None:
+                self.logits_hook([int(i) for i in sample_ids], self.runner.full_logits(counts.S))
             if spec is not None:  # keep the draft's cache in step with the target's
                 spec.set_batch([e.id for e in plan.entries])
                 spec.shadow(counts)

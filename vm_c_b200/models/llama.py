@@ -17,6 +17,7 @@ row-parallel, embedding replicated; the lm_head is vocab-parallel here (the refe
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -300,6 +301,13 @@ class LlamaModel:
         self.fused = self.tp > 1 and comm is not None and hasattr(comm, "allreduce_add_rmsnorm")
         if self.fused:
             comm.setup(max_tokens, self.H)
+            # The gathered activations live in the symmetric region: owners push their rows there.
+            self.ws.h = comm.h
+        # Native step forward (csrc/kernels/forward.cpp): the whole kernel program of a step issued
+        # from C++. VMC_NATIVE=0 keeps every step on the Python path below.
+        self.use_native = os.environ.get("VMC_NATIVE", "1") != "0"
+        self._nat = None
+        self._nat_key = None
         self.moe_runner = None
         self.tq = None  # TurboQuant tables when the KV cache is compressed (set by the runner)
         self.tracer = None  # utils.trace.HiddenTracer when VMC_LOG_HIDDEN / VMC_LOG_LOGITS is set
@@ -383,9 +391,71 @@ class LlamaModel:
         else:
             ops.gemm(ws.h, w, ws.act[:M], M, ops.OUT_SWIGLU, 1)
 
+    # -- native step forward ----------------------------------------------------------------------
+    def native_ok(self, m: StepMeta) -> bool:
+        """Steps the C++ forward handles: dense layers, no tracing, no CPU-offloaded weights, no
+        token-tree masks; one rank, or tensor parallel over the fused peer-memory backend."""
+        return (self.use_native and self.tracer is None and self.moe_runner is None and m.tree_mask is None
+                and not any(lw.offload for lw in self.w.layers) and (self.tp == 1 or self.fused))
+
+    @staticmethod
+    def _lin(w: ops.TiledWeight) -> list[int]:
+        return [w.wf, w.data.data_ptr(), w.N, w.K]
+
+    def _native(self, kv_cache: torch.Tensor, m: StepMeta, params: torch.Tensor, out_tok: torch.Tensor,
+                out_lp: torch.Tensor | None):
+        key = (kv_cache.data_ptr(), m.input_ids.data_ptr(), m.block_tables.data_ptr(), params.data_ptr(),
+               out_tok.data_ptr(), 0 if out_lp is None else out_lp.data_ptr())
+        if self._nat is not None and self._nat_key == key:
+            return self._nat
+        w, ws, cfg = self.w, self.ws, self.cfg
+        zero = [0, 0, 0, 0]
+        layers = []
+        for lw in w.layers:
+            q = [self._lin(x) for x in lw.wqkv] + [zero] * (3 - len(lw.wqkv))
+            cols = list(lw.qkv_split) + [0] * (3 - len(lw.qkv_split))
+            layers.append([lw.attn_norm.data_ptr(), lw.ffn_norm.data_ptr(), len(lw.wqkv)] + q[0] + q[1] + q[2] + cols
+                          + self._lin(lw.wo) + self._lin(lw.w_gate_up) + self._lin(lw.w_down))
+        c = dict(L=len(w.layers), H=self.H, Hq=self.hq, Hkv=self.hkv, D=self.D, F=max(self.f_local, 1),
+                 V_local=self.v_local, max_tokens=self.max_tokens, max_samples=self.max_samples,
+                 max_blocks=int(m.block_tables.shape[-1]), eps=float(cfg.rms_eps), scale=float(self.scale),
+                 neox=bool(cfg.rope_neox), embd=w.embd.data_ptr(), embd_type=int(w.embd_type),
+                 embd_row_bytes=int(w.embd_row_bytes), out_norm=w.output_norm.data_ptr(), lm_head=self._lin(w.lm_head),
+                 cos_sin=self.cos_sin.data_ptr(), num_sms=ops.NUM_SMS)
+        b = dict(resid=ws.resid.data_ptr(), h=ws.h.data_ptr(), qkv_bf16=self.qkv_bf16.data_ptr(),
+                 split_ws=self.split_ws.data_ptr(), split_ws_elems=self.split_ws.numel(), q=ws.q.data_ptr(),
+                 attn=ws.attn.data_ptr(), o16=self.o16.data_ptr(), act=ws.act.data_ptr(), hs=ws.hs.data_ptr(),
+                 logits=ws.logits.data_ptr(), attn_max_splits=1, ids=m.input_ids.data_ptr(),
+                 pos=m.positions.data_ptr(), slots=m.slot_mapping.data_ptr(), q_start=m.q_start.data_ptr(),
+                 ctx_len=m.ctx_len.data_ptr(), block_tables=m.block_tables.data_ptr(),
+                 logits_idx=m.logits_idx.data_ptr(), params=params.data_ptr(), out_tok=out_tok.data_ptr(),
+                 kv=kv_cache.data_ptr(), kv_layer_bytes=kv_cache.stride(0) * kv_cache.element_size(),
+                 err=ops._err_word(self.dev).data_ptr())
+        if out_lp is not None:
+            b["out_lp"] = out_lp.data_ptr()
+        if ws.part_o is not None:
+            b.update(part_o=ws.part_o.data_ptr(), part_lse=ws.part_lse.data_ptr(), attn_max_splits=ws.part_o.shape[0])
+        if self.tq is not None:
+            b.update(tq_meta=self.tq.meta(), tq_centroids=self.tq.centroids.data_ptr(),
+                     tq_midpoints=self.tq.midpoints.data_ptr())
+        nat = ops.C().make_forward(c, layers, b)
+        if self.fused:
+            nat.set_comm(self.comm.tp_desc())
+        self._nat, self._nat_key = nat, key
+        return nat
+
     def forward(self, kv_cache: torch.Tensor, m: StepMeta, params: torch.Tensor, out_tok: torch.Tensor,
                 out_lp: torch.Tensor | None = None, pre_sample=None) -> None:
         """One step: writes sampled token ids for the m.S sample rows into out_tok."""
+        if self.native_ok(m):
+            nat = self._native(kv_cache, m, params, out_tok, out_lp)
+            local_sample = pre_sample is None and self.tp == 1
+            ops._count(nat.run(m.T, m.R, m.S, m.num_decode, m.max_qlen, m.decode_qlen, self.attn_splits, local_sample))
+            if not local_sample and m.S > 0:
+                if pre_sample is not None:
+                    pre_sample(self)
+                self._sample(m.S, params, out_tok, out_lp)
+            return
         cfg, ws = self.cfg, self.ws
         T = m.T
         tr = self.tracer

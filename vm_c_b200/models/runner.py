@@ -248,6 +248,13 @@ class GpuModelRunner(ModelRunner):
         self.done.synchronize()
         return self.tok_host[:S].numpy(), self.lp_host[:S].numpy()
 
+    def full_logits(self, S: int):
+        """Host copy of the last step's full-vocabulary logits of its S sampled rows (after any
+        penalties): the gathered vocabulary shards under tensor parallelism."""
+        if self.tp_size > 1:
+            return self.comm._full[:S].float().cpu()
+        return self.model.ws.logits[:S].float().cpu()
+
     # -- CUDA graphs -------------------------------------------------------------------------------
     def _fake_decode_meta(self, B: int) -> None:
         """Metadata for a batch of B padding decode rows (no KV writes, empty contexts)."""

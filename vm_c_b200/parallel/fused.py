@@ -1,12 +1,18 @@
 """Fused peer-memory tensor-parallel communication (the product path; NCCL is the baseline).
 
 Every rank allocates one symmetric region (cudaMalloc + CUDA IPC handle, exchanged through the
-process group) holding two fp32 partial buffers [max_tokens, hidden] (the two all-reduce sites of
-a layer alternate between them) and a flag array. The row-parallel O / down GEMMs write their
-partial sums straight into this rank's buffer; ``ar_add_rmsnorm`` then reads every rank's partial
-over NVLink, adds the residual and applies the next RMSNorm in one kernel (csrc/kernels/comm.cu).
+process group) and maps every peer's. It holds:
+
+* for the reduce-scatter / all-gather design used by the native step forward (csrc/kernels/forward.cpp):
+  two bf16 receive buffers (one per row-parallel site) into which the row-parallel O / down GEMMs of
+  all ranks store the partial rows that this rank owns (the GEMM epilogue writes over NVLink), the
+  bf16 activations ``h`` that every owner fills with its normalised rows (all-gather by push) and that
+  the next column-parallel GEMM reads locally, and four monotonic arrival counters;
+* for the one-shot all-reduce of the Python step path: two fp32 partial buffers and a flag array
+  (``ar_add_rmsnorm`` reads every rank's partial over NVLink, adds the residual and applies RMSNorm).
+
 No NCCL call sits on the per-layer path; NCCL is used only to exchange the IPC handles at start-up
-and to gather the vocab-parallel logits before sampling.
+and, for now, to gather the vocab-parallel logits before sampling.
 """
 from __future__ import annotations
 
@@ -42,10 +48,26 @@ class FusedComm(NcclComm):
             return
         C = ops.C()
         self.max_tokens, self.hidden = max_tokens, hidden
+        nr = self.world
         self.buf_elems = max_tokens * hidden
-        flag_bytes = _FLAG_SLOTS * _MAX_RANKS * 4
-        data_bytes = 2 * self.buf_elems * 4
-        total = data_bytes + flag_bytes
+        # Receive rows: K-split partials only occur for steps of at most 256 tokens (one token tile),
+        # with at most 8 splits; unsplit steps need one slot of ceil(T / nr) rows per source.
+        rpr256 = (256 + nr - 1) // nr
+        self.recv_rows = max(8 * nr * rpr256, nr * ((max_tokens + nr - 1) // nr))
+        a = 256
+        rnd = lambda x: (x + a - 1) // a * a  # noqa: E731
+        off = 0
+        self.off_partial = [off, off + rnd(self.buf_elems * 4)]
+        off += 2 * rnd(self.buf_elems * 4)
+        self.off_recv = [off, off + rnd(self.recv_rows * hidden * 2)]
+        off += 2 * rnd(self.recv_rows * hidden * 2)
+        self.off_h = off
+        off += rnd(max_tokens * hidden * 2)
+        self.off_count = off          # rs0, rs1, ag0, ag1 (uint32, 64 bytes apart)
+        off += 256
+        self.off_flags = off
+        off += rnd(_FLAG_SLOTS * _MAX_RANKS * 4)
+        total = off
         self.local_ptr, handle = C.sym_alloc(total)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=self.group)
@@ -58,16 +80,27 @@ class FusedComm(NcclComm):
                 p = C.sym_open(h)
                 self._opened.append(p)
                 self.peer_ptrs.append(p)
-        self.flag_ptrs = [p + data_bytes for p in self.peer_ptrs]
+        self.flag_ptrs = [p + self.off_flags for p in self.peer_ptrs]
         dev = self.dev.index
-        f32 = 6  # c10::ScalarType::Float
-        self.partials = [C.wrap_ptr(self.local_ptr + s * self.buf_elems * 4, [max_tokens, hidden], f32, dev)
+        f32, bf16 = 6, 15  # c10::ScalarType::Float, BFloat16
+        self.partials = [C.wrap_ptr(self.local_ptr + self.off_partial[s], [max_tokens, hidden], f32, dev)
                          for s in range(2)]
+        self.h = C.wrap_ptr(self.local_ptr + self.off_h, [max_tokens, hidden], bf16, dev)
         self.epochs = torch.zeros(_FLAG_SLOTS, dtype=torch.int32, device=self.dev)
         self.err = torch.zeros(4, dtype=torch.int32, device=self.dev)
+        self.state = torch.zeros(8, dtype=torch.int32, device=self.dev)
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
         self._ready = True
+
+    def tp_desc(self) -> dict:
+        """Peer addresses of the reduce-scatter / all-gather buffers (TpComm, csrc/kernels/comm.h)."""
+        P = self.peer_ptrs
+        cnt = [[p + self.off_count + 64 * k for p in P] for k in range(4)]
+        return {"nranks": self.world, "rank": self.rank, "recv_rows": self.recv_rows, "max_ctas": self.max_ctas,
+                "recv0": [p + self.off_recv[0] for p in P], "recv1": [p + self.off_recv[1] for p in P],
+                "h": [p + self.off_h for p in P], "rs0": cnt[0], "rs1": cnt[1], "ag0": cnt[2], "ag1": cnt[3],
+                "state": self.state.data_ptr(), "err": self.err.data_ptr()}
 
     def partial(self, site: int) -> torch.Tensor:
         """This rank's fp32 partial buffer for all-reduce site `site` (0 or 1)."""
@@ -75,10 +108,20 @@ class FusedComm(NcclComm):
 
     def allreduce_add_rmsnorm(self, site: int, T: int, resid: torch.Tensor, w: torch.Tensor, eps: float,
                               out: torch.Tensor, nsplit: int = 1, split_stride: int = 0) -> None:
-        off = (site & 1) * self.buf_elems * 4
+        off = self.off_partial[site & 1]
         ops.C().ar_add_rmsnorm([p + off for p in self.peer_ptrs], self.flag_ptrs, self.epochs, self.rank, T,
                                self.hidden, nsplit, split_stride, resid, w, eps, out, self.err, self.max_ctas)
         ops._count()
+
+    def row_parallel_rs(self, site: int, x: torch.Tensor, w, M: int, resid: torch.Tensor, norm_w: torch.Tensor,
+                        eps: float, splits: int = 1) -> int:
+        """One row-parallel site through the reduce-scatter design: x[:M] @ w^T with the partial rows
+        scattered to their owners in the GEMM epilogue, then residual + RMSNorm on the owned rows and
+        the all-gather into every rank's ``self.h``. Returns the K splits used."""
+        used = ops.C().tp_row_parallel(self.tp_desc(), site & 1, w.wf, w.data, w.N, w.K, x, M, splits, resid, norm_w,
+                                      eps, self.err)
+        ops._count(2)
+        return used
 
     def device_error(self) -> int:
         return int(self.err.max().item())
