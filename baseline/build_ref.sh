@@ -3,7 +3,8 @@
 # the rest of the tree). Steps: copy the read-only reference tree to a scratch directory, run the
 # reference's own build-time patch step (scripts/apply_ggml_vm_c.sh, idempotent), then configure and
 # build its vendored ggml (CUDA + CPU backends) and libllama with the reference's ggml options plus the
-# driver in this directory. Offline: the only third-party header libllama needs (nlohmann/json, for
+# driver in this directory. Architecture: sm_100 SASS only ("100-real"; the reference's own GPU query
+# picks "100", which adds compute_100 PTX that a B200 never JIT-compiles since the SASS matches). Offline: the only third-party header libllama needs (nlohmann/json, for
 # its jinja engine) is taken from a copy bundled with an installed Python package.
 #
 #   baseline/build_ref.sh [REFERENCE_TREE] [JOBS]
@@ -28,7 +29,7 @@ PY
 )"
 test -n "${JSON_DIR}" || { echo "nlohmann/json.hpp not found" >&2; exit 1; }
 cmake -S "${HERE}" -B "${OUT}/build" -G Ninja -DCMAKE_BUILD_TYPE=Release \
-  -DCMAKE_CUDA_ARCHITECTURES=100 -DVMC_REF_SRC="${SCRATCH}" -DVMC_JSON_INCLUDE="${JSON_DIR}"
+  -DCMAKE_CUDA_ARCHITECTURES=100-real -DVMC_REF_SRC="${SCRATCH}" -DVMC_JSON_INCLUDE="${JSON_DIR}"
 cmake --build "${OUT}/build" --target vmc_ref_bench -j "${JOBS}"
 cp "${OUT}/build/vmc_ref_bench" "${OUT}/vmc_ref_bench"
 # CPU-only stack (vendored libllama + ggml-cpu): the config-1 oracle; runs without a GPU driver.

@@ -248,6 +248,10 @@ struct Server {
   int32_t* d_topk = nullptr;
   std::vector<int32_t> h_ids;
   std::vector<float> h_lp;
+  // Host <-> device traffic of the serving loop (per run): the batch's token ids, positions and
+  // sequence ids go to the device; libllama returns every output row's logits to host memory, and
+  // the engine sends the sampled rows back up to its sampler and reads the sampled ids and logprobs.
+  double h2d = 0, d2h = 0;
 
   void init() {
     h_ids.resize(n_seq);
@@ -366,6 +370,8 @@ struct Server {
       const int rc = llama_decode(ctx, batch);
       if (rc != 0) throw std::runtime_error("llama_decode failed: rc=" + std::to_string(rc));
       sample(sample_row);
+      h2d += 12.0 * batch.n_tokens + (cpu ? 0.0 : 4.0 * V * sample_row.size());
+      d2h += 4.0 * V * sample_row.size() + 8.0 * sample_row.size();
       const double t = now_ms() - t0;
       for (size_t i = 0; i < sample_req.size(); ++i) {
         Req& q = reqs[sample_req[i]];
@@ -445,6 +451,7 @@ int bench(const Args& a) {
     }
   }
   double ms = now_ms() - w0;
+  const double wall_ms = ms;
 #ifndef VMC_REF_CPU_ONLY
   if (!a.cpu) {
     CK(cudaDeviceSynchronize());
@@ -456,9 +463,11 @@ int bench(const Args& a) {
   }
 #endif
   const double toks = static_cast<double>(a.runs) * n_req * a.gen;
-  printf("{\"ms_total\": %.3f, \"runs\": %d, \"ms_per_run\": %.3f, \"tok_per_s\": %.2f, \"p50_ttft_ms\": %.3f, "
-         "\"p50_itl_ms\": %.4f, \"n_req\": %d, \"prompt_len\": %d, \"gen_len\": %d, \"vocab\": %d}\n",
-         ms, a.runs, ms / a.runs, toks / (ms / 1e3), p50(ttft), p50(itl), n_req, plen, a.gen, V);
+  printf("{\"ms_total\": %.3f, \"ms_wall_total\": %.3f, \"runs\": %d, \"ms_per_run\": %.3f, \"tok_per_s\": %.2f, "
+         "\"p50_ttft_ms\": %.3f, \"p50_itl_ms\": %.4f, \"n_req\": %d, \"prompt_len\": %d, \"gen_len\": %d, "
+         "\"vocab\": %d, \"h2d_bytes_per_run\": %.0f, \"d2h_bytes_per_run\": %.0f}\n",
+         ms, wall_ms, a.runs, ms / a.runs, toks / (ms / 1e3), p50(ttft), p50(itl), n_req, plen, a.gen, V,
+         s.h2d / std::max(1, a.runs + a.warmup), s.d2h / std::max(1, a.runs + a.warmup));
   fflush(stdout);
   if (!a.dump.empty()) {
     FILE* f = fopen(a.dump.c_str(), "w");

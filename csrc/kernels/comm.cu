@@ -201,15 +201,17 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 __device__ __forceinline__ void red_add_sys(uint32_t* p, uint32_t v) {
   asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Bounded wait until *p >= target (wrap-safe comparison), system-scope acquire.
+// Bounded wait until *p >= target (wrap-safe comparison), system-scope acquire. The bound is time
+// (about 2 s of SM clock), not an iteration count, so sleeping between polls cannot stretch it.
 __device__ __forceinline__ bool wait_count_sys(const uint32_t* p, uint32_t target, uint32_t* err) {
+  const long long t0 = clock64();
   for (uint32_t i = 0;; ++i) {
     if (static_cast<int32_t>(ld_acquire_sys(p) - target) >= 0) return true;
-    if (i > kSpinLimit) {
+    if (clock64() - t0 > (4ll << 30)) {
       atomicCAS(err, 0u, static_cast<uint32_t>(kErrCommWait));
       return false;
     }
-    if (i > 32) __nanosleep(100);
+    if (i > 32) __nanosleep(64);
   }
 }
 

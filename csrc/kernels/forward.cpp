@@ -97,6 +97,11 @@ void Forward::set_comm(const TpComm& comm) {
   has_comm_ = comm.nranks > 1;
 }
 
+void Forward::set_sampler(const TpSample& s) {
+  tps_ = s;
+  has_tps_ = s.nranks > 1;
+}
+
 int Forward::splits_for(const LinearDesc& w, int M) const {
   int s = gemm_pick_splits(w.wf, w.N, w.K, M, c_.num_sms);
   while (s > 1 && static_cast<int64_t>(s) * M > c_.max_tokens) --s;
@@ -252,9 +257,14 @@ int Forward::run(const StepDims& d, cudaStream_t st) {
     gemm(b_.hs, c_.H, c_.lm_head, b_.logits, c_.V_local, d.S, kGemmOutF32, 1, 0, st);
     n += 2;
     if (d.sample) {
-      sample(b_.logits, d.S, c_.V_local, c_.V_local, static_cast<const SampleParams*>(b_.params), b_.out_tok, b_.out_lp,
-             st);
-      n += 1;
+      const SampleParams* sp = static_cast<const SampleParams*>(b_.params);
+      if (has_tps_) {
+        tp_sample(tps_, b_.logits, d.S, c_.V_local, c_.V_local, sp, b_.out_tok, b_.out_lp, st);
+        n += 2;
+      } else {
+        sample(b_.logits, d.S, c_.V_local, c_.V_local, sp, b_.out_tok, b_.out_lp, st);
+        n += 1;
+      }
     }
   }
   return n;

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "comm.h"
+#include "sampling.h"
 #include "turboquant_types.h"
 
 namespace vmc {
@@ -102,6 +103,8 @@ class Forward {
   Forward(const ForwardConfig& cfg, std::vector<LayerDesc> layers, const ForwardBuffers& bufs);
   // Tensor-parallel communication (peer-memory reduce-scatter + all-gather); absent for one rank.
   void set_comm(const TpComm& comm);
+  // Vocabulary-parallel sampling over the ranks' lm_head shards (sampling.h); absent for one rank.
+  void set_sampler(const TpSample& s);
   // Issues one step on `st`; returns the number of kernels launched.
   int run(const StepDims& d, cudaStream_t st);
   // K-split count the step uses for weight w at M tokens (the consumer kernels sum exactly this many).
@@ -123,6 +126,8 @@ class Forward {
   int qkv_n_ = 0;
   bool has_comm_ = false;
   TpComm comm_{};
+  bool has_tps_ = false;
+  TpSample tps_{};
 };
 
 // Split-K policy shared with the Python wrappers (ops.pick_splits / ops.effective_splits): the

@@ -487,6 +487,29 @@ vmc::TpComm make_tp_comm(py::dict d) {
   return c;
 }
 
+vmc::TpSample make_tp_sample(py::dict d) {
+  vmc::TpSample t;
+  t.nranks = d["nranks"].cast<int>();
+  t.rank = d["rank"].cast<int>();
+  t.max_rows = d["max_rows"].cast<int>();
+  const auto xs = d["xbuf"].cast<std::vector<int64_t>>(), cs = d["xcount"].cast<std::vector<int64_t>>();
+  for (int q = 0; q < t.nranks; ++q) {
+    t.xbuf[q] = reinterpret_cast<void*>(xs.at(q));
+    t.count[q] = reinterpret_cast<uint32_t*>(cs.at(q));
+  }
+  t.state = reinterpret_cast<uint32_t*>(d["xstate"].cast<int64_t>());
+  t.err = reinterpret_cast<uint32_t*>(d["err"].cast<int64_t>());
+  return t;
+}
+
+void tp_sample(py::dict d, torch::Tensor logits, int64_t S, int64_t V_local, torch::Tensor params, torch::Tensor out_tok,
+               c10::optional<torch::Tensor> out_lp) {
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "tp_sample: fp32 logits");
+  vmc::tp_sample(make_tp_sample(d), ptr<float>(logits), static_cast<int>(S), static_cast<int>(V_local),
+                 logits.stride(0), reinterpret_cast<const vmc::SampleParams*>(params.data_ptr()), ptr<int32_t>(out_tok),
+                 opt_ptr<float>(out_lp), cur_stream());
+}
+
 // One reduce-scatter + norm + all-gather site driven from Python (tests and the comm benchmark):
 // x [M, K] bf16 times the tiled weight, partial rows scattered, then rs_norm_ag.
 int64_t tp_row_parallel(py::dict comm, int site, int wf, torch::Tensor w, int64_t N, int64_t K, torch::Tensor x,
@@ -560,7 +583,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              d.sample = do_sample;
              return f.run(d, cur_stream());
            })
-      .def("set_comm", [](vmc::Forward& f, py::dict d) { f.set_comm(make_tp_comm(d)); })
+      .def("set_comm", [](vmc::Forward& f, py::dict d) {
+        f.set_comm(make_tp_comm(d));
+        f.set_sampler(make_tp_sample(d));
+      })
       .def("splits_for", [](vmc::Forward& f, int wf, int N, int K, int M) {
         vmc::LinearDesc w;
         w.wf = wf;
@@ -570,6 +596,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       });
   m.def("make_forward", &make_forward);
   m.def("tp_row_parallel", &tp_row_parallel);
+  m.def("tp_sample", &tp_sample);
+  m.def("tp_sample_row_bytes", &vmc::tp_sample_row_bytes);
   m.def("gemm_pick_splits", [](int wf, int N, int K, int M, int sms) { return vmc::gemm_pick_splits(wf, N, K, M, sms); });
   m.attr("OUT_BF16") = static_cast<int>(vmc::kGemmOutBF16);
   m.attr("OUT_F32") = static_cast<int>(vmc::kGemmOutF32);

@@ -24,6 +24,43 @@ def gen(seed):
     return torch.Generator().manual_seed(seed)
 
 
+def sampler_check(comm, rank, world, dev):
+    """Vocabulary-parallel sampling (tp_sample) against the single-GPU sampler on the whole row: the
+    same tokens for greedy, unrestricted and top-k / top-p / min-p rows, and the same log-probs."""
+    from types import SimpleNamespace
+    from vm_c_b200.core.engine import SAMPLE_DTYPE
+    V, S = 128256, 48
+    V_local = V // world
+    g = gen(11)
+    full = (torch.randn(S, V, generator=g) * 3).to(dev)
+    rec = np.zeros(S, dtype=SAMPLE_DTYPE)
+    for r in range(S):
+        kind = r % 4
+        rec[r]["temperature"] = 0.0 if kind == 0 else 0.7 + 0.1 * (r % 3)
+        rec[r]["top_k"] = [0, 0, 40, 0][kind]
+        rec[r]["top_p"] = [1.0, 1.0, 0.95, 0.9][kind]
+        rec[r]["min_p"] = [0.0, 0.0, 0.0, 0.05][kind]
+        rec[r]["repetition_penalty"] = 1.0
+        rec[r]["step"] = r
+        rec[r]["seed"] = 1234 + 17 * r
+    params = torch.from_numpy(rec.view(np.uint8).copy()).to(dev)
+    tok_ref = torch.zeros(S, dtype=torch.int32, device=dev)
+    lp_ref = torch.zeros(S, dtype=torch.float32, device=dev)
+    ops.sample(full, S, V, params, tok_ref, lp_ref)
+    model = SimpleNamespace(ws=SimpleNamespace(logits=full[:, rank * V_local:(rank + 1) * V_local].contiguous()),
+                            v_local=V_local)
+    mism = 0
+    lp_err = 0.0
+    for _ in range(3):   # repeated calls advance the exchange counters
+        tok = torch.zeros(S, dtype=torch.int32, device=dev)
+        lp = torch.zeros(S, dtype=torch.float32, device=dev)
+        comm.sample_vocab_parallel(model, S, params, tok, lp)
+        torch.cuda.synchronize(dev)
+        mism += int((tok != tok_ref).sum())
+        lp_err = max(lp_err, float((lp - lp_ref).abs().max()))
+    return {"sampler_mismatch": mism, "sampler_lp_err": lp_err}
+
+
 def main():
     out, bursts, per_burst = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
     rank, world, local = init_distributed(timeout_s=120)
@@ -32,7 +69,7 @@ def main():
     from vm_c_b200.parallel.fused import FusedComm
     comm = FusedComm()
     H, K, T_MAX, eps = 1024, 256, 2048, 1e-5
-    comm.setup(T_MAX, H)
+    comm.setup(T_MAX, H, 64)
     W = [torch.randint(-1, 2, (H, K), generator=gen(7 + r)).float() for r in range(world)]
     Wd = [w.to(dev) for w in W]
     tw = ops.tile_weight(Wd[rank], int(GType.F32), H, K)
@@ -74,6 +111,7 @@ def main():
         dist.all_reduce(mine)
         if hi > lo:
             stats["max_vs_nccl"] = max(stats["max_vs_nccl"], float((resid[lo:hi] - (r0 + mine)[lo:hi]).abs().max()))
+    stats.update(sampler_check(comm, rank, world, dev))
     stats["err"] = comm.device_error()
     stats["world"] = world
     if rank == 0:

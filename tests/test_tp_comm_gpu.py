@@ -1,6 +1,7 @@
 """The fused reduce-scatter / all-gather of the row-parallel sites (scatter-epilogue GEMM +
 rs_norm_ag) on 2, 4 and 8 GPUs: exact sums over bursts of back-to-back calls, normalised rows
-gathered on every rank, and agreement with NCCL's all-reduce on the same partials (tests/comm_worker.py)."""
+gathered on every rank, and agreement with NCCL's all-reduce on the same partials; plus vocabulary-parallel
+sampling against the single-GPU sampler on the whole rows (tests/comm_worker.py)."""
 import json
 import os
 import subprocess
@@ -29,3 +30,5 @@ def test_reduce_scatter_all_gather_exact(tmp_path, n):
     assert s["max_resid_err"] == 0.0          # integer partials: exact
     assert s["max_vs_nccl"] == 0.0
     assert s["max_h_rel_err"] < 1e-2          # bf16 output rounding
+    assert s["sampler_mismatch"] == 0         # vocabulary-parallel sampling = whole-row sampling
+    assert s["sampler_lp_err"] < 1e-3

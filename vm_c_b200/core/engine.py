@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import hashlib
 import itertools
+import os
 import threading
 import time
 from collections import deque
@@ -104,6 +105,11 @@ class LLMEngine:
         # hook(request ids, logits [S, vocab] on the host): full-vocabulary logits of every sampled row of
         # a non-speculative step (tests compare them with an fp32 oracle); None costs nothing.
         self.logits_hook: Optional[Callable] = None
+        # Launch step n+1 before emitting step n's outputs (runners with launch / wait, no speculation;
+        # VMC_PIPELINE=0 turns it off).
+        self._inflight = None
+        self.pipelined = (hasattr(runner, "launch") and getattr(runner, "spec_k", 0) == 0
+                          and os.environ.get("VMC_PIPELINE", "1") != "0")
 
     # -------------------------------------------------------------------------------------------
     # request intake (thread-safe: the server's HTTP threads call these)
@@ -152,6 +158,8 @@ class LLMEngine:
                 self._finish(self.requests[iid], FinishReason.ABORTED)
 
     def has_unfinished(self) -> bool:
+        if self._inflight is not None:
+            return True
         with self._lock:
             if self._pending:
                 return True
@@ -223,6 +231,11 @@ class LLMEngine:
         return self._step()
 
     def _step(self) -> list[RequestOutput]:
+        # Pipelined steps: the previous step's kernels may still be running. Its tokens are applied
+        # to the scheduler first (C++, cheap), the next step is scheduled and launched, and only then
+        # are the previous step's outputs emitted (callbacks, finish bookkeeping, metrics), so that
+        # host work overlaps the GPU instead of sitting between two steps.
+        done = self._complete_inflight()
         self._drain()
         spec = getattr(self.runner, "spec", None)
         plan = self.sched.schedule()
@@ -231,7 +244,7 @@ class LLMEngine:
             if spec is not None:
                 spec.forget(int(iid))
         if len(plan) == 0:
-            return []
+            return self._emit(done) if done else []
         t0 = time.perf_counter()
         pen = self._penalties(plan, plan.num_sample)
         all_decode = plan.num_decode == len(plan)
@@ -248,6 +261,12 @@ class LLMEngine:
         counts = self._counts()
         if not pad:
             counts.R_pad = 0
+        if self.pipelined and not speculate:
+            params = self._sample_params(plan, counts.S, counts.R_pad)
+            handle = self.runner.launch(self.meta, counts, params, pen)
+            self._inflight = (plan, counts, sample_ids, handle, t0)
+            return self._emit(done) if done else []
+        outs = self._emit(done) if done else []
         lp_by_id = {}
         if speculate and all_greedy:
             new = spec.step(sample_ids, counts)
@@ -269,8 +288,24 @@ class LLMEngine:
             events = self.sched.update(plan, toks[:counts.S])
             for k, iid in enumerate(sample_ids):
                 lp_by_id[int(iid)] = float(lps[k]) if lps is not None else 0.0
+        return outs + self._emit(self._apply(events, lp_by_id, plan, counts, t0))
+
+    def _complete_inflight(self):
+        """Wait for the launched step and apply its tokens (scheduler and per-request token lists)."""
+        f = self._inflight
+        if f is None:
+            return None
+        self._inflight = None
+        plan, counts, sample_ids, handle, t0 = f
+        toks, lps = self.runner.wait(handle)
+        if self.logits_hook is not None:
+            self.logits_hook([int(i) for i in sample_ids], self.runner.full_logits(counts.S))
+        events = self.sched.update(plan, toks[:counts.S])
+        lp_by_id = {int(iid): float(lps[k]) for k, iid in enumerate(sample_ids)}
+        return self._apply(events, lp_by_id, plan, counts, t0)
+
+    def _apply(self, events, lp_by_id, plan, counts, t0):
         now = time.perf_counter()
-        outs = []
         for iid, new_toks, finished, reason in events:
             req = self.requests.get(int(iid))
             if req is None:
@@ -278,12 +313,22 @@ class LLMEngine:
             req.output_token_ids.extend(new_toks)
             req.output_logprobs.extend([lp_by_id.get(int(iid), 0.0)] * len(new_toks))
             req.token_times.extend([now] * len(new_toks))
+        return events, plan, counts, t0, now
+
+    def _emit(self, done) -> list[RequestOutput]:
+        """Callbacks, finish bookkeeping and metrics of a completed step."""
+        events, plan, counts, t0, now = done
+        outs = []
+        for iid, new_toks, finished, reason in events:
+            req = self.requests.get(int(iid))
+            if req is None:
+                continue
             if finished:
                 self._finish(req, FinishReason(reason), new_toks)
             elif req.stream_callback:
                 req.stream_callback(req, new_toks, False)
             outs.append(req.to_output() if (finished or req.stream_callback is None) else None)
-        dt = time.perf_counter() - t0
+        dt = now - t0
         self.metrics.record_step(counts.T, counts.S, counts.num_decode, dt, plan.num_cached_tokens)
         self.step_id += 1
         if self.on_step:
@@ -308,6 +353,7 @@ class LLMEngine:
     def fail_all(self, reason: FinishReason = FinishReason.ERROR) -> int:
         """Finish every queued and running request with `reason` (after a rank or device failure).
         Returns how many requests were failed."""
+        self._inflight = None
         self._drain()
         reqs = list(self.requests.values())
         for req in reqs:

@@ -300,7 +300,7 @@ class LlamaModel:
             self.ws.part_lse = torch.empty(attn_splits, max_samples, self.hq, dtype=torch.float32, device=dev)
         self.fused = self.tp > 1 and comm is not None and hasattr(comm, "allreduce_add_rmsnorm")
         if self.fused:
-            comm.setup(max_tokens, self.H)
+            comm.setup(max_tokens, self.H, max_samples)
             # The gathered activations live in the symmetric region: owners push their rows there.
             self.ws.h = comm.h
         # Native step forward (csrc/kernels/forward.cpp): the whole kernel program of a step issued
@@ -449,7 +449,7 @@ class LlamaModel:
         """One step: writes sampled token ids for the m.S sample rows into out_tok."""
         if self.native_ok(m):
             nat = self._native(kv_cache, m, params, out_tok, out_lp)
-            local_sample = pre_sample is None and self.tp == 1
+            local_sample = pre_sample is None and (self.tp == 1 or self.fused)
             ops._count(nat.run(m.T, m.R, m.S, m.num_decode, m.max_qlen, m.decode_qlen, self.attn_splits, local_sample))
             if not local_sample and m.S > 0:
                 if pre_sample is not None:

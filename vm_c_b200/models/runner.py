@@ -215,12 +215,28 @@ class GpuModelRunner(ModelRunner):
         self.params_dev[:nb].copy_(self.params_host[:nb], non_blocking=True)
 
     def execute(self, meta, counts: StepCounts, params: np.ndarray, penalties=None):
+        return self.wait(self.launch(meta, counts, params, penalties))
+
+    def wait(self, S: int):
+        """Block until the launched step's sampled ids are on the host."""
+        self.done.synchronize()
+        return self.tok_host[:S].numpy().copy(), self.lp_host[:S].numpy().copy()
+
+    def launch(self, meta, counts: StepCounts, params: np.ndarray, penalties=None) -> int:
+        """Issue one step (uploads, kernels, read-back of the sampled ids) without waiting for it."""
         if counts.R_pad > 0 and penalties is None and counts.R_pad not in self.graphs:
             self._capture(counts.R_pad)   # before the upload: capture uses the device buffers
         self._upload(meta, params)
         pen = None
         if penalties is not None:
-            rows, toks, cnts = (torch.from_numpy(a).to(self.dev, non_blocking=True) for a in penalties)
+            if self.tp_size > 1:
+                # the lm_head is vocabulary-parallel: this rank's logits hold tokens [v0, v1) only
+                v0, v1 = self.model.w.vocab_begin, self.model.w.vocab_end
+                rows_np, toks_np, cnts_np = penalties
+                keep = (toks_np >= v0) & (toks_np < v1)
+                penalties = (rows_np[keep], (toks_np[keep] - v0).astype(np.int32), cnts_np[keep])
+            rows, toks, cnts = (torch.from_numpy(np.ascontiguousarray(a)).to(self.dev, non_blocking=True)
+                                for a in penalties)
             n = rows.numel()
 
             def pen(model):  # applied to the logits before sampling
@@ -245,14 +261,13 @@ class GpuModelRunner(ModelRunner):
         self.h2d_bytes += meta.numel() * 4 + params.nbytes
         self.d2h_bytes += S * 8
         self.done.record()
-        self.done.synchronize()
-        return self.tok_host[:S].numpy(), self.lp_host[:S].numpy()
+        return S
 
     def full_logits(self, S: int):
         """Host copy of the last step's full-vocabulary logits of its S sampled rows (after any
         penalties): the gathered vocabulary shards under tensor parallelism."""
         if self.tp_size > 1:
-            return self.comm._full[:S].float().cpu()
+            return self.comm.gather_logits(self.model, S).float().cpu()
         return self.model.ws.logits[:S].float().cpu()
 
     # -- CUDA graphs -------------------------------------------------------------------------------

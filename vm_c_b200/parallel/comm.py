@@ -46,6 +46,10 @@ class NcclComm:
     def barrier(self) -> None:
         dist.barrier(group=self.group)
 
+    def gather_logits(self, model, S: int) -> torch.Tensor:
+        """Full-vocabulary logits of the last step's S rows (after sample_vocab_parallel)."""
+        return self._full[:S]
+
     def sample_vocab_parallel(self, model, S: int, params: torch.Tensor, out_tok: torch.Tensor, out_lp) -> None:
         """Gather the vocab-parallel logits of the S sampled rows, then sample identically on every rank."""
         ws = model.ws

@@ -42,12 +42,13 @@ class FusedComm(NcclComm):
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self._ready = False
 
-    def setup(self, max_tokens: int, hidden: int) -> None:
+    def setup(self, max_tokens: int, hidden: int, max_samples: int = 0) -> None:
         """Allocate and map the symmetric region (collective: every rank must call it)."""
         if self._ready:
             return
         C = ops.C()
         self.max_tokens, self.hidden = max_tokens, hidden
+        self.max_samples = max_samples or max_tokens
         nr = self.world
         self.buf_elems = max_tokens * hidden
         # Receive rows: K-split partials only occur for steps of at most 256 tokens (one token tile),
@@ -63,8 +64,11 @@ class FusedComm(NcclComm):
         off += 2 * rnd(self.recv_rows * hidden * 2)
         self.off_h = off
         off += rnd(max_tokens * hidden * 2)
-        self.off_count = off          # rs0, rs1, ag0, ag1 (uint32, 64 bytes apart)
-        off += 256
+        self.off_count = off          # rs0, rs1, ag0, ag1, sampler (uint32, 64 bytes apart)
+        off += 320
+        off = rnd(off)
+        self.off_xbuf = off           # vocabulary-parallel sampler exchange [nr][max_samples][row bytes]
+        off += rnd(nr * self.max_samples * C.tp_sample_row_bytes())
         self.off_flags = off
         off += rnd(_FLAG_SLOTS * _MAX_RANKS * 4)
         total = off
@@ -89,6 +93,7 @@ class FusedComm(NcclComm):
         self.epochs = torch.zeros(_FLAG_SLOTS, dtype=torch.int32, device=self.dev)
         self.err = torch.zeros(4, dtype=torch.int32, device=self.dev)
         self.state = torch.zeros(8, dtype=torch.int32, device=self.dev)
+        self.xstate = torch.zeros(2, dtype=torch.int32, device=self.dev)
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
         self._ready = True
@@ -100,7 +105,22 @@ class FusedComm(NcclComm):
         return {"nranks": self.world, "rank": self.rank, "recv_rows": self.recv_rows, "max_ctas": self.max_ctas,
                 "recv0": [p + self.off_recv[0] for p in P], "recv1": [p + self.off_recv[1] for p in P],
                 "h": [p + self.off_h for p in P], "rs0": cnt[0], "rs1": cnt[1], "ag0": cnt[2], "ag1": cnt[3],
-                "state": self.state.data_ptr(), "err": self.err.data_ptr()}
+                "state": self.state.data_ptr(), "err": self.err.data_ptr(),
+                "xbuf": [p + self.off_xbuf for p in P], "xcount": [p + self.off_count + 256 for p in P],
+                "xstate": self.xstate.data_ptr(), "max_rows": self.max_samples}
+
+    def sample_vocab_parallel(self, model, S: int, params: torch.Tensor, out_tok: torch.Tensor, out_lp) -> None:
+        """Sample the S rows from this rank's vocabulary shard of the logits: a local reduction and a
+        candidate exchange through peer memory (no logits all-gather)."""
+        ops.C().tp_sample(self.tp_desc(), model.ws.logits, S, model.v_local, params, out_tok, out_lp)
+        ops._count(2)
+
+    def gather_logits(self, model, S: int) -> torch.Tensor:
+        """Full-vocabulary logits of the last step's S rows (diagnostics and tests; NCCL, not captured)."""
+        shard = model.ws.logits[:S].contiguous()
+        parts = [torch.empty_like(shard) for _ in range(self.world)]
+        dist.all_gather(parts, shard, group=self.group)
+        return torch.cat(parts, dim=1)
 
     def partial(self, site: int) -> torch.Tensor:
         """This rank's fp32 partial buffer for all-reduce site `site` (0 or 1)."""
