@@ -24,6 +24,9 @@
 // Every wait is bounded; on expiry the CTA records an error code and unwinds (TMEM is freed).
 #include <cuda.h>
 
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "gemm_tcgen05.h"
 #include "weight_formats.cuh"
@@ -252,6 +255,15 @@ struct GemmArgs {
   void* scat[8];
   uint32_t* scat_count[8];
   int scat_rpr, scat_rank, scat_nranks;
+  // Stream-K (decode kernel, one token tile, no K split): CTA b of G takes chunks
+  // [b * W / G, (b + 1) * W / G) of the W = n_tiles * KC sequence (weight tile, 256-K chunk), cut
+  // into segments at tile borders. A tile split across CTAs is finished by the CTA holding its chunk 0
+  // (its last segment): the later CTAs store their fp32 partial accumulators into their slot of sk_ws
+  // ([G][BN][128]) and count on sk_cnt[tile]; the finisher waits for the count, adds the partials in
+  // CTA order and runs the normal epilogue, then resets the count.
+  int sk;
+  float* sk_ws;
+  uint32_t* sk_cnt;
 };
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -375,6 +387,55 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u, int tile_bytes
   const int n = r.c1 - r.c0;
   r.rot = n > 0 ? u % n : 0;
   return r;
+}
+
+// Work enumeration of the decode kernel: round-robin units, or one stream-K chunk range per CTA.
+struct UnitIter {
+  int u, step;
+  long long x, e;
+};
+__device__ __forceinline__ UnitIter iter_begin(const GemmArgs& a, int first, int step) {
+  UnitIter it;
+  it.u = first;
+  it.step = step;
+  it.x = it.e = 0;
+  if (a.sk) {
+    const long long W = static_cast<long long>(a.n_tiles) * a.KC;
+    it.x = static_cast<long long>(blockIdx.x) * W / gridDim.x;
+    it.e = static_cast<long long>(blockIdx.x + 1) * W / gridDim.x;
+  }
+  return it;
+}
+__device__ __forceinline__ bool iter_next(const GemmArgs& a, UnitIter& it, Unit& w, int tile_bytes) {
+  if constexpr ((VMC_GEMM_SKIP & 16) != 0) return false;
+  if (a.sk) {
+    if (it.x >= it.e) return false;
+    const int nt = static_cast<int>(it.x / a.KC);
+    const int c0 = static_cast<int>(it.x - static_cast<long long>(nt) * a.KC);
+    const int c1 = static_cast<int>(min(static_cast<long long>(a.KC), c0 + (it.e - it.x)));
+    w.nt = nt;
+    w.mt = 0;
+    w.split = 0;
+    w.c0 = c0;
+    w.c1 = c1;
+    w.row0 = 0;
+    w.rows = min(a.bn, a.M);
+    w.wtile = static_cast<size_t>(nt) * a.KC * tile_bytes;
+    w.rot = 0;
+    it.x += c1 - c0;
+    return true;
+  }
+  while (it.u < a.units) {
+    w = unit_of(a, it.u, tile_bytes);
+    it.u += it.step;
+    if (w.rows > 0) return true;
+  }
+  return false;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 template <int WF, int BN>
@@ -826,9 +887,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       const uint64_t pol = l2_policy_evict_first();
       int st = 0;
       uint32_t ph = 0;
-      for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
-        if (w.rows <= 0) continue;
+      UnitIter it = iter_begin(args, first, step);
+      Unit w;
+      while (!*abort_flag && iter_next(args, it, w, wf_tile_bytes(WF))) {
         const uint8_t* wbase = args.w + w.wtile;
         for (int i = 0; i < w.nchunks(); ++i) {
           const int c = w.chunk(i);
@@ -850,9 +911,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       pdl_wait();
       int st = 0;
       uint32_t ph = 0;
-      for (int u = first; u < args.units && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
-        if (w.rows <= 0) continue;
+      UnitIter it = iter_begin(args, first, step);
+      Unit w;
+      while (!*abort_flag && iter_next(args, it, w, wf_tile_bytes(WF))) {
         for (int i = 0; i < w.nchunks(); ++i) {
           const int c = w.chunk(i);
           if (!mbar_wait(&b_empty[st], ph ^ 1, args.err, kErrGemmWait)) { *abort_flag = 1; break; }
@@ -879,9 +940,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       PhaseClock pc;
       long long ph_acc = 0, ph_a = 0, ph_b = 0, ph_mma = 0;
       pc.start();
-      for (int u = first; u < args.units && ok && !*abort_flag; u += step) {
-        const Unit w = unit_of(args, u, wf_tile_bytes(WF));
-        if (w.rows <= 0) continue;
+      UnitIter it = iter_begin(args, first, step);
+      Unit w;
+      while (ok && !*abort_flag && iter_next(args, it, w, wf_tile_bytes(WF))) {
         const int buf = ui & 1;
         if (!mbar_wait(&acc_empty[buf], ((ui >> 1) & 1) ^ 1, args.err, kErrGemmWait)) { ok = false; break; }
         ph_acc += pc.lap();
@@ -933,9 +994,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
     PhaseClock pc;
     long long ph_raw = 0, ph_dq = 0, ph_slot = 0, ph_st = 0, ph_rest = 0;
     pc.start();
-    for (int u = first; u < args.units && !*abort_flag; u += step) {
-      const Unit w = unit_of(args, u, wf_tile_bytes(WF));
-        if (w.rows <= 0) continue;
+    UnitIter it = iter_begin(args, first, step);
+    Unit w;
+    while (!*abort_flag && iter_next(args, it, w, wf_tile_bytes(WF))) {
       bool ok = true;
       for (int i = 0; i < w.nchunks(); ++i, ++g) {
         ph_rest += pc.lap();
@@ -993,14 +1054,37 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
     PhaseClock pc;
     long long ph_ew = 0, ph_ld = 0, ph_out = 0;
     pc.start();
-    for (int u = first; u < args.units && !*abort_flag; u += step) {
-      const Unit w = unit_of(args, u, wf_tile_bytes(WF));
-        if (w.rows <= 0) continue;
+    UnitIter it = iter_begin(args, first, step);
+    Unit w;
+    while (!*abort_flag && iter_next(args, it, w, wf_tile_bytes(WF))) {
       const int buf = ui & 1;
       const uint32_t acc_ph = (ui >> 1) & 1;
       const bool ok = mbar_wait(&acc_full[2 * buf], acc_ph, args.err, kErrGemmWait) &&
                       mbar_wait(&acc_full[2 * buf + 1], acc_ph, args.err, kErrGemmWait);
       if (!ok) { *abort_flag = 1; break; }
+      // Stream-K: a segment after chunk 0 of its tile stores a partial; the segment holding chunk 0
+      // of a split tile first waits for the later CTAs' partials.
+      const bool sk_part = args.sk && w.c0 > 0;
+      const bool sk_head = args.sk && w.c0 == 0 && w.c1 < args.KC;
+      int n_contrib = 0;
+      if (sk_head) {
+        const long long W = static_cast<long long>(args.n_tiles) * args.KC, G = gridDim.x;
+        const long long xlast = static_cast<long long>(w.nt + 1) * args.KC - 1;
+        n_contrib = static_cast<int>(((xlast + 1) * G + W - 1) / W - 1) - static_cast<int>(blockIdx.x);
+        int good = 1;
+        if (lane == 0) {
+          const long long t0 = clock64();
+          while (static_cast<int>(ld_acquire_gpu(args.sk_cnt + w.nt)) < n_contrib) {
+            if (clock64() - t0 > (4ll << 30)) {
+              atomicCAS(args.err, 0u, static_cast<uint32_t>(kErrGemmWait));
+              good = 0;
+              break;
+            }
+          }
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) { *abort_flag = 1; break; }
+      }
       ph_ew += pc.lap();
       tc_fence_after();
       const uint32_t d = tmem + static_cast<uint32_t>(2 * buf) * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
@@ -1015,6 +1099,18 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
         ph_ld += pc.lap();
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(t[j]));
+        if (sk_part) {
+          float* slot = args.sk_ws + static_cast<size_t>(blockIdx.x) * (BN * 128);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) slot[(cb + j) * 128 + n_local] = __uint_as_float(v[j]);
+          continue;
+        }
+        for (int c = 1; c <= n_contrib; ++c) {
+          const float* slot = args.sk_ws + static_cast<size_t>(blockIdx.x + c) * (BN * 128);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            v[j] = __float_as_uint(__uint_as_float(v[j]) + __ldcg(slot + (cb + j) * 128 + n_local));
+        }
         const int m_base = w.row0 + cb;
         const int m_end = w.row0 + w.rows;
         if (args.out_mode == kGemmOutSwiGLU) {
@@ -1054,6 +1150,17 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       ++ui;
+      if (sk_part || sk_head) {
+        epi_bar_sync();  // all four epilogue warps have stored (partial) or read (finisher) the slots
+        if (warp == kDFirstEpi && lane == 0) {
+          if (sk_part) {
+            __threadfence();
+            atomicAdd(args.sk_cnt + w.nt, 1u);
+          } else {
+            args.sk_cnt[w.nt] = 0;  // every contributor has counted: ready for the next launch
+          }
+        }
+      }
       ph_out += pc.lap();
     }
     if (lane == 0) {
@@ -1188,6 +1295,55 @@ int gemm_pick_bn(int M) {
 }
 
 namespace {
+// Stream-K workspace of the current device: partial slots for every CTA at the widest decode tile
+// and one arrival counter per weight tile (zeroed once; finishers reset their counters).
+constexpr int kSkMaxTiles = 1 << 14;
+struct SkWorkspace {
+  float* ws = nullptr;
+  uint32_t* cnt = nullptr;
+};
+SkWorkspace g_sk[64];
+
+bool streamk_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VMC_STREAMK");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  return on;
+}
+
+SkWorkspace& sk_workspace() {
+  int dev = 0;
+  VMC_CUDA_CHECK(cudaGetDevice(&dev));
+  SkWorkspace& w = g_sk[dev];
+  if (!w.ws) {
+    VMC_CUDA_CHECK(cudaMalloc(&w.ws, static_cast<size_t>(num_sms()) * 64 * 128 * sizeof(float)));
+    VMC_CUDA_CHECK(cudaMalloc(&w.cnt, kSkMaxTiles * sizeof(uint32_t)));
+    VMC_CUDA_CHECK(cudaMemset(w.cnt, 0, kSkMaxTiles * sizeof(uint32_t)));
+  }
+  return w;
+}
+
+// Decode-width quantized GEMMs with one token tile and no K split take the stream-K schedule.
+bool use_streamk(int wf, int bn, int m_tiles, int splits, int n_tiles) {
+  return streamk_enabled() && wf != kWfBF16 && bn <= 64 && m_tiles == 1 && splits == 1 && n_tiles <= kSkMaxTiles;
+}
+
+void apply_streamk(GemmArgs& a, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  VMC_CUDA_CHECK(cudaStreamIsCapturing(st, &cs));
+  int dev = 0;
+  VMC_CUDA_CHECK(cudaGetDevice(&dev));
+  VMC_CHECK(g_sk[dev].ws != nullptr || cs == cudaStreamCaptureStatusNone,
+            "gemm: the stream-K workspace must be allocated (gemm_prepare) before stream capture");
+  SkWorkspace& ws = sk_workspace();
+  a.sk = 1;
+  a.sk_ws = ws.ws;
+  a.sk_cnt = ws.cnt;
+  const long long W = static_cast<long long>(a.n_tiles) * a.KC;
+  a.units = static_cast<int>(W < num_sms() ? W : num_sms());  // grid size: one CTA per SM at most
+}
+
 GemmArgs dense_args(int wf, const void* w_tiled, int N, int K, int M, void* out, int ldo, int out_mode, int& splits,
                     int bn, uint32_t* err, int64_t split_stride) {
   const int chunk = wf_chunk(wf);
@@ -1226,6 +1382,7 @@ int gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M
   GemmArgs a = dense_args(wf, w_tiled, N, K, M, out, ldo, out_mode, splits, bn, err, split_stride);
   VMC_CHECK(splits == 1 || out_mode == kGemmOutF32Add || out_mode == kGemmOutF32Split,
             "gemm: split-K needs an fp32 accumulate / per-split output mode");
+  if (use_streamk(wf, bn, a.m_tiles, splits, a.n_tiles)) apply_streamk(a, st);
   CUtensorMap map;
   make_act_tensor_map(&map, x, M, K, ldx, bn);
   return dispatch_wf(wf, bn, map, a, st);
@@ -1248,6 +1405,7 @@ int gemm_tcgen05_scatter(int wf, const void* w_tiled, int N, int K, const void* 
   a.scat_rank = rank;
   a.scat_nranks = nranks;
   if (splits_used) *splits_used = splits;
+  if (use_streamk(wf, bn, a.m_tiles, splits, a.n_tiles)) apply_streamk(a, st);
   CUtensorMap map;
   make_act_tensor_map(&map, x, M, K, ldx, bn);
   return dispatch_wf(wf, bn, map, a, st);
@@ -1289,6 +1447,9 @@ void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, i
   dispatch_wf(wf, bn, map, a, st);
 }
 
+
+void gemm_prepare() { (void)sk_workspace(); }
+bool gemm_streamk() { return streamk_enabled(); }
 
 int gemm_smem_bytes(int wf, int bn) {
   return (wf != kWfBF16 && bn <= 64) ? make_dplan(wf, bn).total() : make_plan(wf, bn).total();

@@ -38,6 +38,10 @@ void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, i
                           const int32_t* counts, const int32_t* offsets, int max_rows, int bn, uint32_t* err,
                           cudaStream_t st);
 int gemm_pick_bn(int M);
+// Allocates this device's stream-K workspace (call once per device before any stream capture).
+void gemm_prepare();
+// Whether decode-width quantized GEMMs use the stream-K schedule (VMC_STREAMK=0 turns it off).
+bool gemm_streamk();
 // Diagnostics: when set, CTA 0 of every GEMM writes per-role clock64 stamps into buf[512].
 void gemm_set_trace(unsigned long long* buf);
 int gemm_smem_bytes(int wf, int bn);

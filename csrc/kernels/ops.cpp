@@ -539,6 +539,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     vmc::gemm_set_trace(t.has_value() && t->defined() ? reinterpret_cast<unsigned long long*>(t->data_ptr()) : nullptr);
   });
   m.def("gemm_pick_bn", &vmc::gemm_pick_bn);
+  m.def("gemm_prepare", &vmc::gemm_prepare);
   m.def("tiled_weight_bytes", &vmc::tiled_weight_bytes);
   m.def("repack_weight", &repack_weight);
   m.def("untile_bf16", &untile_bf16);

@@ -130,3 +130,38 @@ def test_gemm_many_units_persistent(host, cuda_ext):
     torch.cuda.synchronize()
     ref = _ref(x, host, GType.Q4_K, raw, N, K)
     assert (out.float() - ref).abs().max().item() <= 0.02 * ref.abs().max().item() + 1e-3
+
+
+@pytest.mark.parametrize("gtype,N,K,M", [(GType.Q4_K, 1024, 14336, 64), (GType.Q6_K, 512, 4096, 7),
+                                         (GType.Q8_0, 4096, 512, 33), (GType.Q4_K, 6144, 4096, 1)])
+def test_gemm_stream_k_decode_shapes(host, cuda_ext, gtype, N, K, M):
+    # Decode-width quantized GEMMs run the stream-K schedule: tiles are cut across CTAs (heads,
+    # middles and tails), the finisher adds the later CTAs' partials. Repeated launches check that the
+    # per-tile arrival counters are reset by their finishers.
+    tw, raw = _make(host, gtype, N, K, seed=N + M)
+    ref = None
+    for rep in range(3):
+        x = (torch.randn(M, K, device="cuda", generator=torch.Generator(device="cuda").manual_seed(rep)) * 0.5
+             ).bfloat16()
+        out = torch.empty(M, N, dtype=torch.float32, device="cuda")
+        ops.gemm(x, tw, out, M, ops.OUT_F32, 1)
+        torch.cuda.synchronize()
+        ref = _ref(x, host, gtype, raw, N, K)
+        err = (out - ref).abs().max().item()
+        assert ops.device_error() == 0
+        assert err <= 0.01 * ref.abs().max().item() + 1e-3, (rep, err)
+
+
+def test_gemm_stream_k_swiglu(host, cuda_ext):
+    N, K, M = 2 * 2816, 4096, 24   # interleaved gate / up rows
+    tw, raw = _make(host, GType.Q4_K, N, K, seed=5)
+    tw.interleaved_swiglu = True
+    x = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    out = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, tw, out, M, ops.OUT_SWIGLU, 1)
+    torch.cuda.synchronize()
+    y = _ref(x, host, GType.Q4_K, raw, N, K)
+    g, u = y[:, 0::2], y[:, 1::2]
+    ref = torch.nn.functional.silu(g) * u
+    assert ops.device_error() == 0
+    assert (out.float() - ref).abs().max().item() <= 0.02 * ref.abs().max().item() + 1e-3

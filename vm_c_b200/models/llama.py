@@ -298,6 +298,7 @@ class LlamaModel:
         if attn_splits > 1:
             self.ws.part_o = torch.empty(attn_splits, max_samples, self.hq, self.D, dtype=torch.float32, device=dev)
             self.ws.part_lse = torch.empty(attn_splits, max_samples, self.hq, dtype=torch.float32, device=dev)
+        ops.C().gemm_prepare()  # per-device GEMM workspace, before any CUDA-graph capture
         self.fused = self.tp > 1 and comm is not None and hasattr(comm, "allreduce_add_rmsnorm")
         if self.fused:
             comm.setup(max_tokens, self.H, max_samples)

@@ -7,6 +7,7 @@ extension is missing the first call raises ImportError.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -18,6 +19,9 @@ from ..gguf.constants import GType
 WF_BF16, WF_Q4K, WF_Q6K, WF_Q8_0 = 0, 1, 2, 3
 OUT_BF16, OUT_F32, OUT_F32_ADD, OUT_SWIGLU, OUT_F32_SPLIT = 0, 1, 2, 3, 4
 NUM_SMS = 148
+# Decode-width quantized GEMMs run a stream-K schedule (csrc/kernels/gemm_tcgen05.cu); VMC_STREAMK=0
+# returns them to split-K. Read by the C++ side from the same variable.
+STREAMK = os.environ.get("VMC_STREAMK", "1") != "0"
 
 _WF_FOR_GTYPE = {GType.Q4_K: WF_Q4K, GType.Q6_K: WF_Q6K, GType.Q8_0: WF_Q8_0,
                  GType.F32: WF_BF16, GType.F16: WF_BF16, GType.BF16: WF_BF16}
@@ -88,6 +92,8 @@ def pick_splits(w: TiledWeight, M: int, bn: int = 0, sms: int = NUM_SMS, max_spl
     m_tiles = (M + bn - 1) // bn
     if m_tiles > 1 or w.chunks < 2:
         return 1
+    if STREAMK and w.wf != WF_BF16 and bn <= 64:
+        return 1  # decode-width quantized GEMMs are balanced by the stream-K schedule instead
     base = (w.N + 127) // 128
     wbytes = w.nbytes
 
