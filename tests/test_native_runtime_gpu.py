@@ -1,0 +1,57 @@
+"""The PyTorch-free runtime (csrc/runtime/vmc_run.cpp): the native scheduler, native step forward
+and decode CUDA graphs driven from C++ must produce the Python engine's greedy tokens exactly on the
+same checkpoint, prompts and scheduler settings, and the executable must not map libtorch or
+libpython."""
+import json
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+from vm_c_b200.core.sampling_params import SamplingParams
+from vm_c_b200.gguf.random_init import preset, write_random_gguf
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+EXE = os.path.join(ROOT, "vm_c_b200", "_ext", "runtime", "vmc_run")
+
+
+@pytest.fixture(scope="module")
+def exe():
+    if not os.path.exists(EXE):
+        from vm_c_b200._build import build_runtime
+        build_runtime()
+    return EXE
+
+
+def test_runtime_links_no_torch(exe):
+    out = subprocess.run(["ldd", exe], capture_output=True, text=True).stdout
+    assert "torch" not in out and "python" not in out, out
+
+
+@pytest.mark.parametrize("mix", ["Q8_0", "Q4_K_M"])
+def test_runtime_matches_python_engine(exe, tmp_path, mix):
+    cfg = preset("tiny-llama")
+    if mix == "Q4_K_M":
+        cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.n_layers = 1024, 8, 4, 128, 2816, 2
+    path = str(tmp_path / "m.gguf")
+    write_random_gguf(path, cfg, mix, seed=3)
+    rng = np.random.default_rng(9)
+    prompts = rng.integers(0, cfg.vocab, (6, 40)).astype(np.int32)
+    pf = tmp_path / "p.bin"
+    pf.write_bytes(struct.pack("<ii", *prompts.shape) + prompts.tobytes())
+    dump = tmp_path / "t.json"
+    r = subprocess.run([exe, path, "--prompts", str(pf), "--gen", "12", "--max-num-seqs", "8",
+                        "--max-num-batched-tokens", "128", "--max-model-len", "256", "--num-blocks", "256",
+                        "--dump-tokens", str(dump)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["device_error"] == 0
+    native = json.load(open(dump))
+    from vm_c_b200.llm import LLM
+    llm = LLM(path, max_model_len=256, max_num_seqs=8, max_num_batched_tokens=128, num_gpu_blocks=256)
+    outs = llm.generate(prompts.tolist(), SamplingParams.greedy_params(max_tokens=12, ignore_eos=True))
+    llm.shutdown()
+    assert native == [o.output_token_ids for o in outs]

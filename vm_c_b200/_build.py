@@ -4,6 +4,10 @@ Two extensions:
   * ``_host``  — C++17 host runtime (GGUF, quant codecs, block manager, scheduler). No CUDA.
   * ``_cuda``  — sm_100a kernels (tcgen05 / TMA GEMMs, attention, norms, sampling, comm) and their
                  launchers. Compiled only for ``sm_100a``; nothing else is generated.
+and one executable:
+  * ``vmc_run`` — the serving loop without Python or PyTorch (csrc/runtime/vmc_run.cpp): the same
+                 kernels, native forward, scheduler and GGUF reader, linked against the CUDA runtime
+                 and driver only.
 
 The shared objects land in ``vm_c_b200/_ext/<name>/`` so that they travel with a copy of the
 repository; :mod:`vm_c_b200._native` imports them from there without invoking the compiler.
@@ -62,9 +66,52 @@ def build_cuda(verbose: bool = False):
                 is_python_module=True)
 
 
+RUNTIME_HOST = ["host/gguf.cpp", "host/quants.cpp", "host/block_manager.cpp", "host/scheduler.cpp"]
+RUNTIME_EXCLUDE = {"ops.cpp"}   # the PyTorch bindings
+
+
+def build_runtime(verbose: bool = False) -> Path:
+    """Compile and link vm_c_b200/_ext/runtime/vmc_run (objects are rebuilt when their source or a
+    header in csrc/ is newer)."""
+    import concurrent.futures
+    import shutil
+    import subprocess
+    out = EXT_DIR / "runtime"
+    obj = out / "obj"
+    obj.mkdir(parents=True, exist_ok=True)
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    kdir = CSRC / "kernels"
+    srcs = [p for p in sorted(kdir.glob("*.cu")) + sorted(kdir.glob("*.cpp")) if p.name not in RUNTIME_EXCLUDE]
+    srcs += [CSRC / s for s in RUNTIME_HOST] + [CSRC / "runtime" / "vmc_run.cpp"]
+    headers = max(p.stat().st_mtime for p in CSRC.rglob("*") if p.suffix in (".h", ".hpp", ".cuh"))
+    flags = SM100_FLAGS + ["-O3", "-std=c++17", "--expt-relaxed-constexpr", "-lineinfo", "-DNDEBUG",
+                           f"-I{kdir}", f"-I{CSRC / 'host'}", "-Xcompiler", "-fPIC"]
+
+    def compile_one(src: Path) -> Path:
+        o = obj / (src.parent.name + "_" + src.name + ".o")
+        if not o.exists() or o.stat().st_mtime < max(src.stat().st_mtime, headers):
+            cmd = [nvcc] + flags + ["-x", "cu" if src.suffix == ".cu" else "c++", "-c", str(src), "-o", str(o)]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed on {src}:\n{r.stderr[-4000:]}")
+            if verbose:
+                print("compiled", src.name)
+        return o
+
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(16, os.cpu_count() or 4))) as ex:
+        objs = list(ex.map(compile_one, srcs))
+    exe = out / "vmc_run"
+    r = subprocess.run([nvcc] + SM100_FLAGS + [str(o) for o in objs] + ["-o", str(exe), "-lcuda", "-lpthread"],
+                       capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link of vmc_run failed:\n{r.stderr[-4000:]}")
+    return exe
+
+
 def build_all(verbose: bool = False) -> None:
     build_host(verbose)
     build_cuda(verbose)
+    build_runtime(verbose)
 
 
 if __name__ == "__main__":
@@ -74,3 +121,5 @@ if __name__ == "__main__":
         build_host(v)
     if what in ("cuda", "all"):
         build_cuda(v)
+    if what in ("runtime", "all"):
+        build_runtime(v)
