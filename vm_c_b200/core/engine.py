@@ -290,6 +290,15 @@ class LLMEngine:
                 lp_by_id[int(iid)] = float(lps[k]) if lps is not None else 0.0
         return outs + self._emit(self._apply(events, lp_by_id, plan, counts, t0))
 
+    def quiesce(self) -> list[RequestOutput]:
+        """Finish the launched step (if any) and wait for the device, so that nothing of this rank is
+        left in flight (a rank leaving a tensor-parallel job between steps calls this first)."""
+        done = self._complete_inflight()
+        outs = self._emit(done) if done else []
+        if hasattr(self.runner, "synchronize"):
+            self.runner.synchronize()
+        return outs
+
     def _complete_inflight(self):
         """Wait for the launched step and apply its tokens (scheduler and per-request token lists)."""
         f = self._inflight

@@ -217,6 +217,9 @@ class GpuModelRunner(ModelRunner):
     def execute(self, meta, counts: StepCounts, params: np.ndarray, penalties=None):
         return self.wait(self.launch(meta, counts, params, penalties))
 
+    def synchronize(self) -> None:
+        torch.cuda.synchronize(self.dev)
+
     def wait(self, S: int):
         """Block until the launched step's sampled ids are on the host."""
         self.done.synchronize()

@@ -49,7 +49,11 @@ class StepDriver:
     # every rank, before each control collective ------------------------------------------------
     def _pre_collective(self) -> None:
         if self.faults is not None:
-            self.faults.fire(self.rank, self.engine.step_id)
+            step = self.engine.step_id
+            if self.faults.due(self.rank, step) is not None:
+                # an injected departure happens between steps: no kernel of this rank in flight
+                self.engine.quiesce()
+            self.faults.fire(self.rank, step)
         if self.health is not None:
             self.health.check()
 
