@@ -166,7 +166,10 @@ int gen(const Args& a) {
   std::vector<uint8_t> meta(gguf_get_meta_size(g));
   gguf_get_meta_data(g, meta.data());
   fwrite(meta.data(), 1, meta.size(), f);
-  const size_t data0 = gguf_get_data_offset(g);
+  // The data section starts right after the metadata block (gguf_get_meta_size includes the padding
+  // to the alignment); gguf_get_data_offset is only set for a context read from a file.
+  const size_t align = gguf_get_alignment(g);
+  const size_t data0 = (meta.size() + align - 1) / align * align;
   const int nthr = std::max(1u, std::thread::hardware_concurrency());
   for (size_t ti = 0; ti < specs.size(); ++ti) {
     const TSpec& t = specs[ti];
