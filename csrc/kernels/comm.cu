@@ -217,6 +217,7 @@ __device__ __forceinline__ bool wait_count_sys(const uint32_t* p, uint32_t targe
 
 struct RsArgs {
   const __nv_bfloat16* recv;  // this rank's receive buffer of the site: [slots][rpr][H]
+                              // (expert-parallel combine: [rpr][k][H], the k expert outputs per row)
   uint32_t* rs_count;         // this rank's reduce-scatter arrival counter of the site
   uint32_t* ag_count[kMaxRanks];  // every rank's all-gather arrival counter of the site
   __nv_bfloat16* h[kMaxRanks];    // every rank's h buffer [max_tokens][H]
@@ -227,12 +228,18 @@ struct RsArgs {
   int T, H, rpr, slots, rank;
   uint32_t rs_inc;
   uint32_t* err;
+  int gather;                 // 0: write this rank's rows of h only (no all-gather)
+  const float* topk_w;        // expert-parallel combine: router weights [rpr][slots]
+  uint32_t* reset;            // expert-parallel combine: counters to zero once the rows are read
+  int reset_n;
 };
 
 constexpr int kRsThreads = 256;
 constexpr int kRsMaxVec = 4;  // 8-element vectors per thread (H <= 256 * 8 * 4 = 8192)
 
-template <int NR>
+// MOE = false: sum of the slots (source rank, K split) of each owned row. MOE = true: the router-
+// weighted sum of the k expert outputs returned for each owned row (expert-parallel combine).
+template <int NR, bool MOE>
 __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsArgs a) {
   __shared__ float red[32];
   __shared__ int ok;
@@ -256,8 +263,20 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsArgs a) {
         const float4 r0 = *reinterpret_cast<const float4*>(a.resid + row + 8 * vi);
         const float4 r1 = *reinterpret_cast<const float4*>(a.resid + row + 8 * vi + 4);
         float acc[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        if constexpr (MOE) {
+          for (int sl = 0; sl < a.slots; ++sl) {  // expert outputs in top-k order
+            const float wt = a.topk_w[static_cast<size_t>(lr) * a.slots + sl];
+            const uint4 p = __ldcg(reinterpret_cast<const uint4*>(a.recv + (static_cast<size_t>(lr) * a.slots + sl) * H) + vi);
+            const uint32_t q[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc[2 * e] += wt * bf16_lo(q[e]);
+              acc[2 * e + 1] += wt * bf16_hi(q[e]);
+            }
+          }
+        }
         // partial slots in (source rank, split) order: the same sum on every owner
-        int sl = 0;
+        int sl = MOE ? a.slots : 0;
         for (; sl + 4 <= a.slots; sl += 4) {
           uint4 p[4];
 #pragma unroll
@@ -312,26 +331,33 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsArgs a) {
         o.y = pack_bf16x2(v[j][2] * inv * w0.z, v[j][3] * inv * w0.w);
         o.z = pack_bf16x2(v[j][4] * inv * w1.x, v[j][5] * inv * w1.y);
         o.w = pack_bf16x2(v[j][6] * inv * w1.z, v[j][7] * inv * w1.w);
+        if (a.gather) {
 #pragma unroll
-        for (int q = 0; q < NR; ++q) {  // own rank first is not required: the order is irrelevant
-          const int dst = (a.rank + q) % NR;
-          *reinterpret_cast<uint4*>(a.h[dst] + row + 8 * vi) = o;
+          for (int q = 0; q < NR; ++q) {  // own rank first is not required: the order is irrelevant
+            const int dst = (a.rank + q) % NR;
+            *reinterpret_cast<uint4*>(a.h[dst] + row + 8 * vi) = o;
+          }
+        } else {
+          *reinterpret_cast<uint4*>(a.h[a.rank] + row + 8 * vi) = o;
         }
       }
     }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    fence_acq_rel_sys();
+    if (a.gather) {
+      fence_acq_rel_sys();
 #pragma unroll
-    for (int q = 0; q < NR; ++q) red_add_sys(a.ag_count[q], 1u);
-    if (b == 0) wait_count_sys(a.ag_count[a.rank], a.state[1] + static_cast<uint32_t>(NR * G), a.err);
+      for (int q = 0; q < NR; ++q) red_add_sys(a.ag_count[q], 1u);
+      if (b == 0) wait_count_sys(a.ag_count[a.rank], a.state[1] + static_cast<uint32_t>(NR * G), a.err);
+    }
     // The last CTA to finish advances the targets of the next call at this site (every CTA has read
-    // them by then).
+    // them by then) and clears the expert row counters this combine consumed.
     if (atomicAdd(a.state + 2, 1u) == static_cast<uint32_t>(G - 1)) {
       a.state[0] += a.rs_inc;
-      a.state[1] += static_cast<uint32_t>(NR * G);
+      if (a.gather) a.state[1] += static_cast<uint32_t>(NR * G);
       a.state[2] = 0;
+      for (int i = 0; i < a.reset_n; ++i) a.reset[i] = 0;
       __threadfence();
     }
   }
@@ -356,17 +382,24 @@ void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
   }
 }
 
-void rs_norm_ag(const TpComm& c, int site, int T, int H, int splits, int rs_inc, float* resid, const float* w,
-                float eps, cudaStream_t st) {
-  VMC_CHECK(c.nranks >= 1 && c.nranks <= kMaxRanks && (site == 0 || site == 1), "rs_norm_ag: bad ranks / site");
+namespace {
+template <bool MOE>
+void launch_rs(const RsArgs& a, int nranks, int grid, cudaStream_t st) {
+  switch (nranks) {
+    case 1: launch_k(rs_norm_ag_kernel<1, MOE>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    case 2: launch_k(rs_norm_ag_kernel<2, MOE>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    case 4: launch_k(rs_norm_ag_kernel<4, MOE>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    case 8: launch_k(rs_norm_ag_kernel<8, MOE>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
+    default: throw std::runtime_error("rs_norm_ag: 1, 2, 4 or 8 ranks");
+  }
+}
+
+RsArgs rs_common(const TpComm& c, int site, int T, int H, float* resid, const float* w, float eps, int gather) {
+  VMC_CHECK(c.nranks >= 1 && c.nranks <= kMaxRanks && site >= 0 && site < 4, "rs_norm_ag: bad ranks / site");
   VMC_CHECK(H % 8 == 0 && H <= kRsThreads * 8 * kRsMaxVec, "rs_norm_ag: hidden size unsupported");
-  const int rpr = tp_rows_per_rank(T, c.nranks);
-  VMC_CHECK(static_cast<int64_t>(c.nranks) * splits * rpr <= c.recv_rows, "rs_norm_ag: receive buffer too small");
   RsArgs a{};
-  a.recv = static_cast<const __nv_bfloat16*>(c.recv[site][c.rank]);
-  a.rs_count = c.rs_count[site][c.rank];
   for (int q = 0; q < kMaxRanks; ++q) {
-    a.ag_count[q] = q < c.nranks ? c.ag_count[site][q] : nullptr;
+    a.ag_count[q] = q < c.nranks ? c.ag_count[site & 1][q] : nullptr;
     a.h[q] = q < c.nranks ? static_cast<__nv_bfloat16*>(c.h[q]) : nullptr;
   }
   a.state = c.state + 4 * site;
@@ -375,19 +408,37 @@ void rs_norm_ag(const TpComm& c, int site, int T, int H, int splits, int rs_inc,
   a.eps = eps;
   a.T = T;
   a.H = H;
-  a.rpr = rpr;
-  a.slots = c.nranks * splits;
+  a.rpr = tp_rows_per_rank(T, c.nranks);
   a.rank = c.rank;
-  a.rs_inc = static_cast<uint32_t>(rs_inc);
   a.err = c.err;
-  const int grid = tp_norm_ctas(rpr, c.max_ctas);
-  switch (c.nranks) {
-    case 1: launch_k(rs_norm_ag_kernel<1>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
-    case 2: launch_k(rs_norm_ag_kernel<2>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
-    case 4: launch_k(rs_norm_ag_kernel<4>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
-    case 8: launch_k(rs_norm_ag_kernel<8>, dim3(grid), dim3(kRsThreads), 0, st, a); break;
-    default: throw std::runtime_error("rs_norm_ag: 1, 2, 4 or 8 ranks");
-  }
+  a.gather = gather;
+  return a;
+}
+}  // namespace
+
+void rs_norm_ag(const TpComm& c, int site, int T, int H, int splits, int rs_inc, float* resid, const float* w,
+                float eps, cudaStream_t st, int gather) {
+  RsArgs a = rs_common(c, site, T, H, resid, w, eps, gather);
+  VMC_CHECK(static_cast<int64_t>(c.nranks) * splits * a.rpr <= c.recv_rows, "rs_norm_ag: receive buffer too small");
+  a.recv = static_cast<const __nv_bfloat16*>(c.recv[site & 1][c.rank]);
+  a.rs_count = c.rs_count[site & 1][c.rank];
+  a.slots = c.nranks * splits;
+  a.rs_inc = static_cast<uint32_t>(rs_inc);
+  launch_rs<false>(a, c.nranks, tp_norm_ctas(a.rpr, c.max_ctas), st);
+}
+
+void moe_combine_norm_ag(const TpComm& c, const void* comb, uint32_t* comb_count, int comb_inc, const float* topk_w,
+                         int k, uint32_t* reset, int reset_n, int T, int H, float* resid, const float* w, float eps,
+                         cudaStream_t st) {
+  RsArgs a = rs_common(c, 2, T, H, resid, w, eps, 1);
+  a.recv = static_cast<const __nv_bfloat16*>(comb);
+  a.rs_count = comb_count;
+  a.slots = k;
+  a.rs_inc = static_cast<uint32_t>(comb_inc);
+  a.topk_w = topk_w;
+  a.reset = reset;
+  a.reset_n = reset_n;
+  launch_rs<true>(a, c.nranks, tp_norm_ctas(a.rpr, c.max_ctas), st);
 }
 
 // ---- symmetric memory through CUDA IPC ----------------------------------------------------------

@@ -42,7 +42,8 @@ struct TpComm {
   void* h[8] = {};                // each rank's h buffer
   uint32_t* rs_count[2][8] = {};  // [site][rank]
   uint32_t* ag_count[2][8] = {};  // [site][rank]
-  uint32_t* state = nullptr;      // [2 sites][4] (rs target, ag target, CTAs done, spare)
+  uint32_t* state = nullptr;      // [3 sites][4] (rs target, ag target, CTAs done, spare); site 2 is
+                                  // the expert-parallel combine
   uint32_t* err = nullptr;
   int max_ctas = 148;
 };
@@ -57,8 +58,18 @@ inline int tp_norm_ctas(int rpr, int max_ctas) { return rpr < 1 ? 1 : (rpr < max
 // owned row in a fixed order, adds the residual (fp32, updated in place for the owned rows only),
 // applies RMSNorm with weight w, and writes the bf16 row into every rank's h (all-gather by push).
 // CTA 0 returns only after every rank's rows have arrived here, so the next kernel may read all of h.
+// gather = 0 writes the normalised rows into this rank's h only (the consumer needs only its own
+// rows, e.g. the router of an expert-parallel MoE layer); no all-gather, no wait.
 void rs_norm_ag(const TpComm& c, int site, int T, int H, int splits, int rs_inc, float* resid, const float* w,
-                float eps, cudaStream_t st);
+                float eps, cudaStream_t st, int gather = 1);
+
+// Owner side of an expert-parallel MoE layer's combine: waits for comb_inc arrivals (every expert
+// rank's down GEMM CTAs), forms for each owned row the router-weighted sum of its k expert outputs
+// (comb: this rank's [rpr][k][H] bf16 rows, topk_w [rpr][k]), adds the residual, applies RMSNorm and
+// all-gathers like rs_norm_ag; then zeroes `reset` (this rank's expert row counters of the layer).
+void moe_combine_norm_ag(const TpComm& c, const void* comb, uint32_t* comb_count, int comb_inc, const float* topk_w,
+                         int k, uint32_t* reset, int reset_n, int T, int H, float* resid, const float* w, float eps,
+                         cudaStream_t st);
 
 // Symmetric allocations through CUDA IPC (handle_out: 64-byte cudaIpcMemHandle_t).
 uint64_t sym_alloc(size_t bytes, void* handle_out);

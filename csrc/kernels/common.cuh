@@ -289,6 +289,33 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();
 
+// ----------------------------------------------------------------------------------------------
+// Cross-GPU signalling through peer memory (PTX memory model, system scope). A producer finishes its
+// stores to peer memory, synchronises the threads that made them, and one thread issues
+// sys_fence() then sys_count() on the consumer's counter; the consumer polls with sys_load() (an
+// acquire), so it observes every store made before the producer's barrier. Counters only grow.
+__device__ __forceinline__ void sys_fence() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void sys_count(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t sys_load(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait (about 2 s of SM clock) until *p >= target, wrap-safe; records `code` on expiry.
+__device__ __forceinline__ bool sys_wait(const uint32_t* p, uint32_t target, uint32_t* err, uint32_t code) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (static_cast<int32_t>(sys_load(p) - target) >= 0) return true;
+    if (clock64() - t0 > (4ll << 30)) {
+      if (err) atomicCAS(err, 0u, code);
+      return false;
+    }
+    if (i > 32) __nanosleep(64);
+  }
+}
+
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg = {};

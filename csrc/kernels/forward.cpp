@@ -61,7 +61,6 @@ int gemm_pick_splits(int wf, int N, int K, int M, int num_sms, int max_splits) {
   const int m_tiles = (M + bn - 1) / bn;
   const int chunks = chunks_of(wf, K);
   if (m_tiles > 1 || chunks < 2) return 1;
-  if (gemm_streamk() && wf != 0 && bn <= 64) return 1;  // balanced by the stream-K schedule instead
   const int base = (N + 127) / 128;
   const double wbytes = static_cast<double>(tiled_bytes_host(wf, N, K));
   auto cost = [&](int s) {

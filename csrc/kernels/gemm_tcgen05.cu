@@ -255,6 +255,12 @@ struct GemmArgs {
   void* scat[8];
   uint32_t* scat_count[8];
   int scat_rpr, scat_rank, scat_nranks;
+  // Row-scatter mode (kGemmOutRowScatterBF16, the combine of an expert-parallel MoE layer): output
+  // row m goes to the rank, row and top-k slot packed in row_ret[m] ((rank << 24) | (row << 3) | j):
+  // row (row * row_k + j) of that rank's buffer scat[rank] (row stride ldo); release / arrival as in
+  // scatter mode. Rows whose return word is negative are skipped.
+  const int32_t* row_ret;
+  int row_k;
   // Stream-K (decode kernel, one token tile, no K split): CTA b of G takes chunks
   // [b * W / G, (b + 1) * W / G) of the W = n_tiles * KC sequence (weight tile, 256-K chunk), cut
   // into segments at tile borders. A tile split across CTAs is finished by the CTA holding its chunk 0
@@ -284,6 +290,24 @@ __device__ __forceinline__ void scatter_rows(const GemmArgs& a, int split, int n
     if (++lr == rpr) {
       lr = 0;
       ++o;
+    }
+  }
+}
+
+// Expert-parallel combine epilogue: each row goes back to the rank and slot its token came from.
+__device__ __forceinline__ void row_scatter_rows(const GemmArgs& a, int n, int m_base, int m_end,
+                                                 const uint32_t (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m_base + j;
+    if (m < m_end) {
+      const int32_t ret = a.row_ret[m];
+      if (ret >= 0) {
+        const int src = ret >> 24, row = (ret >> 3) & 0x1fffff, slot = ret & 7;
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.scat[src]) +
+                             (static_cast<size_t>(row) * a.row_k + slot) * a.ldo + n;
+        *dst = __float2bfloat16(__uint_as_float(v[j]));
+      }
     }
   }
 }
@@ -672,6 +696,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         } else if (args.out_mode == kGemmOutScatterBF16) {
           const int n = w.nt * 128 + n_local;
           if (n < args.N) scatter_rows(args, w.split, n, m_base, m_end, v);
+        } else if (args.out_mode == kGemmOutRowScatterBF16) {
+          const int n = w.nt * 128 + n_local;
+          if (n < args.N) row_scatter_rows(args, n, m_base, m_end, v);
         } else {
           const int n = w.nt * 128 + n_local;
           if (n < args.N) {
@@ -694,7 +721,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_ph ^= 1; }
     }
-    if (args.out_mode == kGemmOutScatterBF16) scatter_release(args, warp, kFirstEpiWarp, lane);
+    if (args.out_mode == kGemmOutScatterBF16 || args.out_mode == kGemmOutRowScatterBF16)
+      scatter_release(args, warp, kFirstEpiWarp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -1129,6 +1157,9 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
         } else if (args.out_mode == kGemmOutScatterBF16) {
           const int nn = w.nt * 128 + n_local;
           if (nn < args.N) scatter_rows(args, w.split, nn, m_base, m_end, v);
+        } else if (args.out_mode == kGemmOutRowScatterBF16) {
+          const int nn = w.nt * 128 + n_local;
+          if (nn < args.N) row_scatter_rows(args, nn, m_base, m_end, v);
         } else {
           const int nn = w.nt * 128 + n_local;
           if (nn < args.N) {
@@ -1168,7 +1199,8 @@ __global__ void __launch_bounds__(kDThreads, 1) gemm_qd_kernel(const __grid_cons
       phase_add(args, 14, ph_ld);
       phase_add(args, 15, ph_out);
     }
-    if (args.out_mode == kGemmOutScatterBF16) scatter_release(args, warp, kDFirstEpi, lane);
+    if (args.out_mode == kGemmOutScatterBF16 || args.out_mode == kGemmOutRowScatterBF16)
+      scatter_release(args, warp, kDFirstEpi, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -1450,6 +1482,47 @@ void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, i
 
 void gemm_prepare() { (void)sk_workspace(); }
 bool gemm_streamk() { return streamk_enabled(); }
+
+int gemm_tcgen05_grouped_rowscatter(int wf, const void* w_tiled, int64_t w_group_stride, int N, int K, const void* x,
+                                    int rows_total, int ldx, int groups, const int32_t* counts, const int32_t* offsets,
+                                    int max_rows, int bn, const int32_t* row_ret, int row_k, void* const* dst,
+                                    uint32_t* const* counters, int nranks, uint32_t* err, cudaStream_t st) {
+  VMC_CHECK(rows_total > 0 && N > 0 && K > 0 && groups > 0 && max_rows > 0, "gemm_rowscatter: empty problem");
+  VMC_CHECK(nranks >= 1 && nranks <= 8 && row_k >= 1 && row_k <= 8, "gemm_rowscatter: bad ranks / k");
+  if (bn <= 0) bn = gemm_pick_bn(max_rows);
+  const int chunk = wf_chunk(wf);
+  GemmArgs a = {};
+  a.w = static_cast<const uint8_t*>(w_tiled);
+  a.N = N;
+  a.K = K;
+  a.M = rows_total;
+  a.KC = (K + chunk - 1) / chunk;
+  a.chunks_per_split = a.KC;
+  a.splits = 1;
+  a.n_tiles = (N + 127) / 128;
+  a.m_tiles = (max_rows + bn - 1) / bn;
+  a.units = groups * a.n_tiles * a.m_tiles;
+  a.out = nullptr;
+  a.ldo = N;
+  a.out_mode = kGemmOutRowScatterBF16;
+  a.err = err;
+  a.trace = g_gemm_trace;
+  a.bn = bn;
+  a.groups = groups;
+  a.grp_count = counts;
+  a.grp_offset = offsets;
+  a.grp_w_stride = w_group_stride;
+  for (int q = 0; q < 8; ++q) {
+    a.scat[q] = q < nranks ? dst[q] : nullptr;
+    a.scat_count[q] = q < nranks ? counters[q] : nullptr;
+  }
+  a.scat_nranks = nranks;
+  a.row_ret = row_ret;
+  a.row_k = row_k;
+  CUtensorMap map;
+  make_act_tensor_map(&map, x, rows_total, K, ldx, bn);
+  return dispatch_wf(wf, bn, map, a, st);
+}
 
 int gemm_smem_bytes(int wf, int bn) {
   return (wf != kWfBF16 && bn <= 64) ? make_dplan(wf, bn).total() : make_plan(wf, bn).total();

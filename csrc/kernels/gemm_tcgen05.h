@@ -13,6 +13,7 @@ enum GemmOut : int {
   kGemmOutSwiGLU = 3,  // rows interleave gate/up: out[m, f] = silu(acc[2f]) * acc[2f+1] (bf16)
   kGemmOutF32Split = 4,  // out[split][m, n] = partial over this split's K range (fp32, no atomics)
   kGemmOutScatterBF16 = 5,  // tensor-parallel reduce-scatter: rows stored into their owner rank's buffer
+  kGemmOutRowScatterBF16 = 6,  // expert-parallel combine: each row returned to its token's rank and slot
 };
 
 // out = x[M, K] (bf16, row stride ldx) @ W[N, K]^T with W in a tiled format (weight_formats.cuh).
@@ -37,6 +38,14 @@ void gemm_tcgen05_grouped(int wf, const void* w_tiled, int64_t w_group_stride, i
                           int rows_total, int ldx, void* out, int ldo, int out_mode, int groups,
                           const int32_t* counts, const int32_t* offsets, int max_rows, int bn, uint32_t* err,
                           cudaStream_t st);
+// Grouped GEMM (local experts) whose output rows go back over NVLink to the rank / row / top-k slot
+// packed in row_ret[m] ((rank << 24) | (row << 3) | j; negative = skip): row (row * row_k + j) of
+// dst[rank] (bf16, stride N). Every CTA then releases its stores and adds 1 to counters[q] of every
+// rank. Returns the CTA count.
+int gemm_tcgen05_grouped_rowscatter(int wf, const void* w_tiled, int64_t w_group_stride, int N, int K, const void* x,
+                                    int rows_total, int ldx, int groups, const int32_t* counts, const int32_t* offsets,
+                                    int max_rows, int bn, const int32_t* row_ret, int row_k, void* const* dst,
+                                    uint32_t* const* counters, int nranks, uint32_t* err, cudaStream_t st);
 int gemm_pick_bn(int M);
 // Allocates this device's stream-K workspace (call once per device before any stream capture).
 void gemm_prepare();

@@ -19,8 +19,8 @@ from ..gguf.constants import GType
 WF_BF16, WF_Q4K, WF_Q6K, WF_Q8_0 = 0, 1, 2, 3
 OUT_BF16, OUT_F32, OUT_F32_ADD, OUT_SWIGLU, OUT_F32_SPLIT = 0, 1, 2, 3, 4
 NUM_SMS = 148
-# Decode-width quantized GEMMs run a stream-K schedule (csrc/kernels/gemm_tcgen05.cu); VMC_STREAMK=0
-# returns them to split-K. Read by the C++ side from the same variable.
+# Decode-width quantized GEMMs that the split policy leaves unsplit run a stream-K schedule
+# (csrc/kernels/gemm_tcgen05.cu); VMC_STREAMK=0 turns it off (read by the C++ side).
 STREAMK = os.environ.get("VMC_STREAMK", "1") != "0"
 
 _WF_FOR_GTYPE = {GType.Q4_K: WF_Q4K, GType.Q6_K: WF_Q6K, GType.Q8_0: WF_Q8_0,
@@ -92,8 +92,6 @@ def pick_splits(w: TiledWeight, M: int, bn: int = 0, sms: int = NUM_SMS, max_spl
     m_tiles = (M + bn - 1) // bn
     if m_tiles > 1 or w.chunks < 2:
         return 1
-    if STREAMK and w.wf != WF_BF16 and bn <= 64:
-        return 1  # decode-width quantized GEMMs are balanced by the stream-K schedule instead
     base = (w.N + 127) // 128
     wbytes = w.nbytes
 
