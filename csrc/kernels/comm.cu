@@ -399,7 +399,7 @@ RsArgs rs_common(const TpComm& c, int site, int T, int H, float* resid, const fl
   VMC_CHECK(H % 8 == 0 && H <= kRsThreads * 8 * kRsMaxVec, "rs_norm_ag: hidden size unsupported");
   RsArgs a{};
   for (int q = 0; q < kMaxRanks; ++q) {
-    a.ag_count[q] = q < c.nranks ? c.ag_count[site & 1][q] : nullptr;
+    a.ag_count[q] = q < c.nranks ? c.ag_count[site][q] : nullptr;
     a.h[q] = q < c.nranks ? static_cast<__nv_bfloat16*>(c.h[q]) : nullptr;
   }
   a.state = c.state + 4 * site;

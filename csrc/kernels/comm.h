@@ -41,7 +41,7 @@ struct TpComm {
   int64_t recv_rows = 0;          // rows of one receive buffer
   void* h[8] = {};                // each rank's h buffer
   uint32_t* rs_count[2][8] = {};  // [site][rank]
-  uint32_t* ag_count[2][8] = {};  // [site][rank]
+  uint32_t* ag_count[3][8] = {};  // [site][rank]; site 2: the expert-parallel combine
   uint32_t* state = nullptr;      // [3 sites][4] (rs target, ag target, CTAs done, spare); site 2 is
                                   // the expert-parallel combine
   uint32_t* err = nullptr;

@@ -17,6 +17,7 @@
 #include "attention.h"
 #include "gemm_tcgen05.h"
 #include "layers.h"
+#include "moe.h"
 #include "sampling.h"
 #include "turboquant_ops.h"
 
@@ -88,13 +89,107 @@ Forward::Forward(const ForwardConfig& cfg, std::vector<LayerDesc> layers, const 
   qkv_n_ = (c_.Hq + 2 * c_.Hkv) * c_.D;
   for (const LayerDesc& l : layers_) {
     check(l.n_qkv >= 1 && l.n_qkv <= 3, "qkv parts");
-    check(l.wo.w && l.gate_up.w && l.down.w, "dense layers only (MoE layers take the Python path)");
+    check(l.wo.w && (l.moe ? (l.m.router.w && l.m.gate_up.w && l.m.down.w) : (l.gate_up.w && l.down.w)),
+          "layer weights");
   }
 }
 
 void Forward::set_comm(const TpComm& comm) {
   comm_ = comm;
   has_comm_ = comm.nranks > 1;
+}
+
+void Forward::set_moe(const MoeBuffers& m) {
+  moe_ = m;
+  has_moe_ = true;
+}
+
+// One MoE FFN (after the attention site): writes the next layer's normalised input into h.
+int Forward::moe_layer(const LayerDesc& lw, int l, const float* next_norm, int T, cudaStream_t st) {
+  check(has_moe_, "MoE layer without MoE buffers");
+  const MoeDesc& md = lw.m;
+  const MoeBuffers& mb = moe_;
+  int n = 0;
+  if (!mb.ep) {
+    check(!has_comm_, "expert-sliced MoE layers under tensor parallelism take the Python path");
+    const int R = T * mb.k;
+    gemm(b_.h, c_.H, md.router, mb.logits, mb.E, T, kGemmOutF32, 1, 0, st);
+    MoeRouteArgs ra;
+    ra.logits = mb.logits;
+    ra.ld_logits = mb.E;
+    ra.T = T;
+    ra.E = mb.E;
+    ra.k = mb.k;
+    ra.norm_topk = mb.norm_topk;
+    ra.e0 = md.e0;
+    ra.e_local = md.e_local;
+    ra.topk_id = mb.topk_id;
+    ra.topk_w = mb.topk_w;
+    ra.counts = mb.counts;
+    ra.offsets = mb.offsets;
+    ra.sorted_src = mb.sorted_src;
+    ra.slot_row = mb.slot_row;
+    ra.total_rows = mb.total;
+    moe_route(ra, st);
+    gather_rows(b_.h, mb.sorted_src, R, c_.H, mb.xs, st);
+    const int bn = gemm_pick_bn(std::max(1, (R + md.e_local - 1) / md.e_local));
+    gemm_tcgen05_grouped(md.gate_up.wf, md.gate_up.w, md.gate_up_stride, md.gate_up.N, md.gate_up.K, mb.xs, R, c_.H,
+                         mb.act, md.f_local, kGemmOutSwiGLU, md.e_local, mb.counts, mb.offsets, T, bn, b_.err, st);
+    gemm_tcgen05_grouped(md.down.wf, md.down.w, md.down_stride, md.down.N, md.down.K, mb.act, R, md.f_local, mb.y,
+                         c_.H, kGemmOutF32, md.e_local, mb.counts, mb.offsets, T, bn, b_.err, st);
+    moe_combine(mb.y, c_.H, mb.slot_row, mb.topk_w, T, mb.k, c_.H, mb.out, c_.H, st);
+    add_rmsnorm(b_.resid, mb.out, true, 1, 0, next_norm, T, c_.H, c_.eps, b_.h, st);
+    return n + 8;
+  }
+  // expert-parallel: route own rows, dispatch, experts, return, combine + norm + all-gather
+  const TpComm& c = comm_;
+  const int rpr = tp_rows_per_rank(T, c.nranks);
+  const int row0 = c.rank * rpr;
+  const int rows = std::max(0, std::min(rpr, T - row0));
+  if (rows > 0) {
+    gemm(static_cast<const uint16_t*>(b_.h) + static_cast<int64_t>(row0) * c_.H, c_.H, md.router, mb.ep_logits, mb.E,
+         rows, kGemmOutF32, 1, 0, st);
+    ++n;
+  }
+  const int par = l & 1;
+  MoeDispatchArgs da{};
+  da.logits = mb.ep_logits;
+  da.ld_logits = mb.E;
+  da.x = static_cast<const uint16_t*>(b_.h) + static_cast<int64_t>(row0) * c_.H;
+  da.rows = rows;
+  da.rpr = rpr;
+  da.H = c_.H;
+  da.E = mb.E;
+  da.k = mb.k;
+  da.norm_topk = mb.norm_topk;
+  da.e_local = md.e_local;
+  da.cap = mb.cap;
+  da.rank = c.rank;
+  da.nranks = c.nranks;
+  for (int q = 0; q < c.nranks; ++q) {
+    da.recv_x[q] = mb.recv_x[q];
+    da.recv_ret[q] = mb.recv_ret[q];
+    da.cnt[q] = mb.cnt[par][q];
+    da.arrive[q] = mb.disp_arrive[q];
+  }
+  da.topk_w = mb.ep_topk_w;
+  da.state = mb.disp_state;
+  da.err = c.err;
+  moe_dispatch(da, st);
+  const int rows_cap = md.e_local * mb.cap;
+  const int max_rows = std::min(mb.cap, T);
+  const int bn = gemm_pick_bn(std::max(1, (T * mb.k + mb.E - 1) / mb.E));
+  const int32_t* counts = reinterpret_cast<const int32_t*>(mb.cnt[par][c.rank]);
+  gemm_tcgen05_grouped(md.gate_up.wf, md.gate_up.w, md.gate_up_stride, md.gate_up.N, md.gate_up.K,
+                       mb.recv_x[c.rank], rows_cap, c_.H, mb.ep_act, md.f_local, kGemmOutSwiGLU, md.e_local, counts,
+                       mb.ep_offsets, max_rows, bn, b_.err, st);
+  const int grid = gemm_tcgen05_grouped_rowscatter(md.down.wf, md.down.w, md.down_stride, md.down.N, md.down.K,
+                                                   mb.ep_act, rows_cap, md.f_local, md.e_local, counts,
+                                                   mb.ep_offsets, max_rows, bn, mb.recv_ret[c.rank], mb.k, mb.comb,
+                                                   mb.comb_arrive, c.nranks, b_.err, st);
+  moe_combine_norm_ag(c, mb.comb[c.rank], mb.comb_arrive[c.rank], grid * c.nranks, mb.ep_topk_w, mb.k,
+                      mb.cnt[par][c.rank], md.e_local, T, c_.H, b_.resid, next_norm, c_.eps, st);
+  return n + 4;
 }
 
 void Forward::set_sampler(const TpSample& s) {
@@ -199,16 +294,17 @@ int Forward::attention(int l, const StepDims& d, cudaStream_t st) {
   return n;
 }
 
-// Row-parallel GEMM (x @ w^T), then residual add + RMSNorm(norm_w) into h.
+// Row-parallel GEMM (x @ w^T), then residual add + RMSNorm(norm_w) into h (all rows; with
+// gather = 0 under tensor parallelism, this rank's rows only).
 int Forward::row_parallel(int site, const void* x, int ldx, const LinearDesc& w, const float* norm_w, int M,
-                          cudaStream_t st) {
+                          cudaStream_t st, int gather) {
   const int s = splits_for(w, M);
   if (has_comm_) {
     const TpComm& c = comm_;
     int used = s;
     const int grid = gemm_tcgen05_scatter(w.wf, w.w, w.N, w.K, x, M, ldx, s, c.recv[site], c.rs_count[site],
                                           c.nranks, c.rank, c.recv_rows, b_.err, st, &used);
-    rs_norm_ag(c, site, M, c_.H, used, grid * c.nranks, b_.resid, norm_w, c_.eps, st);
+    rs_norm_ag(c, site, M, c_.H, used, grid * c.nranks, b_.resid, norm_w, c_.eps, st, gather);
     return 2;
   }
   if (s > 1) {
@@ -247,9 +343,15 @@ int Forward::run(const StepDims& d, cudaStream_t st) {
     const LayerDesc& lw = layers_[l];
     n += qkv(lw, l, d, st);
     n += attention(l, d, st);
+    const float* nxt = l + 1 < c_.L ? layers_[l + 1].attn_norm : c_.out_norm;
+    if (lw.moe) {
+      // an expert-parallel layer routes only this rank's rows: no all-gather after the attention
+      n += row_parallel(0, b_.attn, c_.Hq * c_.D, lw.wo, lw.ffn_norm, d.T, st, moe_.ep ? 0 : 1);
+      n += moe_layer(lw, l, nxt, d.T, st);
+      continue;
+    }
     n += row_parallel(0, b_.attn, c_.Hq * c_.D, lw.wo, lw.ffn_norm, d.T, st);
     n += gate_up(lw, d.T, st);
-    const float* nxt = l + 1 < c_.L ? layers_[l + 1].attn_norm : c_.out_norm;
     n += row_parallel(1, b_.act, c_.F, lw.down, nxt, d.T, st);
   }
   if (d.S > 0) {

@@ -27,6 +27,16 @@ struct LinearDesc {
   int N = 0, K = 0;
 };
 
+// Mixture-of-experts FFN of a layer (Mixtral): the router and this rank's experts, stacked.
+struct MoeDesc {
+  LinearDesc router;         // [E, H]
+  LinearDesc gate_up;        // one expert [2 F_local, H], gate / up rows interleaved
+  int64_t gate_up_stride = 0;  // bytes between experts
+  LinearDesc down;           // one expert [H, F_local]
+  int64_t down_stride = 0;
+  int e0 = 0, e_local = 0, f_local = 0;
+};
+
 struct LayerDesc {
   const float* attn_norm = nullptr;
   const float* ffn_norm = nullptr;
@@ -34,6 +44,43 @@ struct LayerDesc {
   LinearDesc qkv[3];
   int qkv_col[3] = {0, 0, 0};  // first output column of each part
   LinearDesc wo, gate_up, down;  // gate_up rows interleave gate / up (fused SwiGLU)
+  bool moe = false;
+  MoeDesc m;
+};
+
+// MoE model settings and buffers. Expert-sliced layout (the reference's, single rank): router,
+// routing, gather, grouped GEMMs and combine on this rank. Expert-parallel (ep = tp > 1): each rank
+// routes its own token rows and the rows travel to the experts' ranks and back through peer memory
+// (moe_dispatch, the grouped GEMMs, the row-scatter down GEMM and moe_combine_norm_ag).
+struct MoeBuffers {
+  int E = 0, k = 0, norm_topk = 1;
+  bool ep = false;
+  // expert-sliced path
+  float* logits = nullptr;     // [max_tokens, E]
+  int32_t* topk_id = nullptr;
+  float* topk_w = nullptr;
+  int32_t* counts = nullptr;
+  int32_t* offsets = nullptr;
+  int32_t* sorted_src = nullptr;
+  int32_t* slot_row = nullptr;
+  int32_t* total = nullptr;
+  void* xs = nullptr;          // bf16 [max_tokens * k, H]
+  void* act = nullptr;         // bf16 [max_tokens * k, F_local]
+  float* y = nullptr;          // fp32 [max_tokens * k, H]
+  float* out = nullptr;        // fp32 [max_tokens, H]
+  // expert-parallel path
+  int cap = 0;                 // rows per expert in the receive buffers
+  void* recv_x[8] = {};        // every rank's [e_local][cap][H] bf16
+  int32_t* recv_ret[8] = {};   // every rank's [e_local][cap]
+  uint32_t* cnt[2][8] = {};    // [layer parity][rank]: per-expert row counters [e_local]
+  void* comb[8] = {};          // every rank's [rpr_max][k][H] bf16
+  uint32_t* disp_arrive[8] = {};
+  uint32_t* comb_arrive[8] = {};
+  uint32_t* disp_state = nullptr;  // this rank: 2 words
+  float* ep_logits = nullptr;  // this rank: [rpr_max, E]
+  float* ep_topk_w = nullptr;  // this rank: [rpr_max, k]
+  void* ep_act = nullptr;      // this rank: [e_local * cap, F_local] bf16
+  int32_t* ep_offsets = nullptr;  // this rank: [e_local] = e * cap
 };
 
 struct ForwardConfig {
@@ -105,6 +152,8 @@ class Forward {
   void set_comm(const TpComm& comm);
   // Vocabulary-parallel sampling over the ranks' lm_head shards (sampling.h); absent for one rank.
   void set_sampler(const TpSample& s);
+  // Buffers of the MoE layers (required when any layer is MoE).
+  void set_moe(const MoeBuffers& m);
   // Issues one step on `st`; returns the number of kernels launched.
   int run(const StepDims& d, cudaStream_t st);
   // K-split count the step uses for weight w at M tokens (the consumer kernels sum exactly this many).
@@ -116,8 +165,9 @@ class Forward {
   int qkv(const LayerDesc& lw, int l, const StepDims& d, cudaStream_t st);
   int attention(int l, const StepDims& d, cudaStream_t st);
   int row_parallel(int site, const void* x, int ldx, const LinearDesc& w, const float* norm_w, int M,
-                   cudaStream_t st);
+                   cudaStream_t st, int gather = 1);
   int gate_up(const LayerDesc& lw, int M, cudaStream_t st);
+  int moe_layer(const LayerDesc& lw, int l, const float* next_norm, int T, cudaStream_t st);
   TqDev tq_for(int l) const;
 
   ForwardConfig c_;
@@ -128,6 +178,8 @@ class Forward {
   TpComm comm_{};
   bool has_tps_ = false;
   TpSample tps_{};
+  bool has_moe_ = false;
+  MoeBuffers moe_{};
 };
 
 // Split-K policy shared with the Python wrappers (ops.pick_splits / ops.effective_splits): the

@@ -153,4 +153,82 @@ void moe_combine(const float* y, int ldy, const int32_t* slot_row, const float* 
   launch_k(moe_combine_kernel, dim3(T), dim3(256), 0, st, y, ldy, slot_row, topk_w, T, k, H, out, ldo);
 }
 
+
+// ---- expert-parallel dispatch ------------------------------------------------------------------
+
+namespace {
+
+__global__ void __launch_bounds__(256) moe_dispatch_kernel(MoeDispatchArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row < a.rows) {
+    const float lg = lane < a.E ? a.logits[static_cast<size_t>(row) * a.ld_logits + lane] : -INFINITY;
+    const float mx = warp_max(lg);
+    const float ex = lane < a.E ? __expf(lg - mx) : 0.f;
+    const float sum = warp_sum(ex);
+    uint32_t taken = 0;
+    int isel[kMaxTopK];
+    float wsel[kMaxTopK];
+    float wsum = 0.f;
+    for (int j = 0; j < a.k; ++j) {
+      // warp argmax over the untaken experts, ties to the lower id (as moe_route)
+      float v = (lane < a.E && !((taken >> lane) & 1u)) ? lg : -INFINITY;
+      int id = lane < a.E && !((taken >> lane) & 1u) ? lane : 0x7fffffff;
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, id, o);
+        if (v2 > v || (v2 == v && i2 < id)) {
+          v = v2;
+          id = i2;
+        }
+      }
+      isel[j] = id;
+      wsel[j] = __shfl_sync(0xffffffffu, ex, id) / sum;
+      wsum += wsel[j];
+      taken |= 1u << id;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) + static_cast<size_t>(row) * a.H);
+    for (int j = 0; j < a.k; ++j) {
+      const int e = isel[j];
+      const int o = e / a.e_local, le = e - o * a.e_local;
+      uint32_t slot = 0;
+      if (lane == 0) slot = atomicAdd_system(a.cnt[o] + le, 1u);
+      slot = __shfl_sync(0xffffffffu, slot, 0);
+      if (slot < static_cast<uint32_t>(a.cap)) {
+        const size_t dst_row = static_cast<size_t>(le) * a.cap + slot;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.recv_x[o]) + dst_row * a.H);
+        for (int i = lane; i < a.H / 8; i += 32) dst[i] = src[i];
+        if (lane == 0) a.recv_ret[o][dst_row] = (a.rank << 24) | (row << 3) | j;
+      } else if (lane == 0) {
+        atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
+      }
+      if (lane == 0) a.topk_w[static_cast<size_t>(row) * a.k + j] = a.norm_topk ? wsel[j] / wsum : wsel[j];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    sys_fence();
+    for (int q = 0; q < a.nranks; ++q) sys_count(a.arrive[q], 1u);
+    const uint32_t G = gridDim.x;
+    if (blockIdx.x == 0) sys_wait(a.arrive[a.rank], a.state[0] + a.nranks * G, a.err, kErrCommWait);
+    if (atomicAdd(a.state + 1, 1u) == G - 1) {
+      a.state[0] += a.nranks * G;
+      a.state[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace
+
+void moe_dispatch(const MoeDispatchArgs& a, cudaStream_t st) {
+  VMC_CHECK(a.E >= 1 && a.E <= 32, "moe_dispatch: at most 32 experts (one lane each)");
+  VMC_CHECK(a.k >= 1 && a.k <= kMaxTopK && a.k <= a.E, "moe_dispatch: bad top-k");
+  VMC_CHECK(a.H % 8 == 0 && a.nranks >= 1 && a.nranks <= 8 && a.e_local >= 1, "moe_dispatch: bad shape");
+  VMC_CHECK(a.rpr < (1 << 21), "moe_dispatch: too many rows per rank for the return word");
+  launch_k(moe_dispatch_kernel, dim3(moe_dispatch_ctas(a.rpr)), dim3(256), 0, st, a);
+}
+
 }  // namespace vmc

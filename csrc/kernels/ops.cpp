@@ -400,7 +400,7 @@ std::shared_ptr<vmc::Forward> make_forward(py::dict cfg, std::vector<std::vector
   c.num_sms = cfg["num_sms"].cast<int>();
   std::vector<vmc::LayerDesc> ls;
   for (const auto& v : layers) {
-    TORCH_CHECK(v.size() == 30, "make_forward: layer descriptors have 30 entries");
+    TORCH_CHECK(v.size() == 30 || v.size() == 48, "make_forward: layer descriptors have 30 (dense) or 48 (MoE) entries");
     vmc::LayerDesc d;
     d.attn_norm = reinterpret_cast<const float*>(v[0]);
     d.ffn_norm = reinterpret_cast<const float*>(v[1]);
@@ -412,6 +412,17 @@ std::shared_ptr<vmc::Forward> make_forward(py::dict cfg, std::vector<std::vector
     d.wo = lin_at(v, 18);
     d.gate_up = lin_at(v, 22);
     d.down = lin_at(v, 26);
+    if (v.size() == 48) {  // [30] = 1, router (4), gate_up (4), stride, down (4), stride, e0, e_local, f_local
+      d.moe = v[30] != 0;
+      d.m.router = lin_at(v, 31);
+      d.m.gate_up = lin_at(v, 35);
+      d.m.gate_up_stride = v[39];
+      d.m.down = lin_at(v, 40);
+      d.m.down_stride = v[44];
+      d.m.e0 = static_cast<int>(v[45]);
+      d.m.e_local = static_cast<int>(v[46]);
+      d.m.f_local = static_cast<int>(v[47]);
+    }
     ls.push_back(d);
   }
   vmc::ForwardBuffers b;
@@ -473,6 +484,7 @@ vmc::TpComm make_tp_comm(py::dict d) {
   const auto h = d["h"].cast<std::vector<int64_t>>();
   const auto rs0 = d["rs0"].cast<std::vector<int64_t>>(), rs1 = d["rs1"].cast<std::vector<int64_t>>();
   const auto ag0 = d["ag0"].cast<std::vector<int64_t>>(), ag1 = d["ag1"].cast<std::vector<int64_t>>();
+  const auto ag2 = d.contains("ag2") ? d["ag2"].cast<std::vector<int64_t>>() : ag1;
   for (int q = 0; q < c.nranks; ++q) {
     c.recv[0][q] = reinterpret_cast<void*>(recv0.at(q));
     c.recv[1][q] = reinterpret_cast<void*>(recv1.at(q));
@@ -481,10 +493,53 @@ vmc::TpComm make_tp_comm(py::dict d) {
     c.rs_count[1][q] = reinterpret_cast<uint32_t*>(rs1.at(q));
     c.ag_count[0][q] = reinterpret_cast<uint32_t*>(ag0.at(q));
     c.ag_count[1][q] = reinterpret_cast<uint32_t*>(ag1.at(q));
+    c.ag_count[2][q] = reinterpret_cast<uint32_t*>(ag2.at(q));
   }
   c.state = reinterpret_cast<uint32_t*>(d["state"].cast<int64_t>());
   c.err = reinterpret_cast<uint32_t*>(d["err"].cast<int64_t>());
   return c;
+}
+
+vmc::MoeBuffers make_moe(py::dict d) {
+  vmc::MoeBuffers m;
+  m.E = d["E"].cast<int>();
+  m.k = d["k"].cast<int>();
+  m.norm_topk = d["norm_topk"].cast<int>();
+  m.ep = d["ep"].cast<bool>();
+  m.logits = dptr<float>(d, "logits");
+  m.topk_id = dptr<int32_t>(d, "topk_id");
+  m.topk_w = dptr<float>(d, "topk_w");
+  m.counts = dptr<int32_t>(d, "counts");
+  m.offsets = dptr<int32_t>(d, "offsets");
+  m.sorted_src = dptr<int32_t>(d, "sorted_src");
+  m.slot_row = dptr<int32_t>(d, "slot_row");
+  m.total = dptr<int32_t>(d, "total");
+  m.xs = dptr<void>(d, "xs");
+  m.act = dptr<void>(d, "act");
+  m.y = dptr<float>(d, "y");
+  m.out = dptr<float>(d, "out");
+  if (m.ep) {
+    m.cap = d["cap"].cast<int>();
+    const auto rx = d["recv_x"].cast<std::vector<int64_t>>(), rr = d["recv_ret"].cast<std::vector<int64_t>>();
+    const auto c0 = d["cnt0"].cast<std::vector<int64_t>>(), c1 = d["cnt1"].cast<std::vector<int64_t>>();
+    const auto cb = d["comb"].cast<std::vector<int64_t>>(), da = d["disp_arrive"].cast<std::vector<int64_t>>();
+    const auto ca = d["comb_arrive"].cast<std::vector<int64_t>>();
+    for (size_t q = 0; q < rx.size() && q < 8; ++q) {
+      m.recv_x[q] = reinterpret_cast<void*>(rx[q]);
+      m.recv_ret[q] = reinterpret_cast<int32_t*>(rr[q]);
+      m.cnt[0][q] = reinterpret_cast<uint32_t*>(c0[q]);
+      m.cnt[1][q] = reinterpret_cast<uint32_t*>(c1[q]);
+      m.comb[q] = reinterpret_cast<void*>(cb[q]);
+      m.disp_arrive[q] = reinterpret_cast<uint32_t*>(da[q]);
+      m.comb_arrive[q] = reinterpret_cast<uint32_t*>(ca[q]);
+    }
+    m.disp_state = dptr<uint32_t>(d, "disp_state");
+    m.ep_logits = dptr<float>(d, "ep_logits");
+    m.ep_topk_w = dptr<float>(d, "ep_topk_w");
+    m.ep_act = dptr<void>(d, "ep_act");
+    m.ep_offsets = dptr<int32_t>(d, "ep_offsets");
+  }
+  return m;
 }
 
 vmc::TpSample make_tp_sample(py::dict d) {
@@ -588,6 +643,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         f.set_comm(make_tp_comm(d));
         f.set_sampler(make_tp_sample(d));
       })
+      .def("set_moe", [](vmc::Forward& f, py::dict d) { f.set_moe(make_moe(d)); })
       .def("splits_for", [](vmc::Forward& f, int wf, int N, int K, int M) {
         vmc::LinearDesc w;
         w.wf = wf;

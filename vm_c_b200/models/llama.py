@@ -310,11 +310,16 @@ class LlamaModel:
         self._nat = None
         self._nat_key = None
         self.moe_runner = None
+        self.ep = 1
         self.tq = None  # TurboQuant tables when the KV cache is compressed (set by the runner)
         self.tracer = None  # utils.trace.HiddenTracer when VMC_LOG_HIDDEN / VMC_LOG_LOGITS is set
         if cfg.is_moe:
             from .moe import MoERunner
             self.moe_runner = MoERunner(self, max_tokens)
+            moe0 = next(lw.moe for lw in w.layers if lw.moe is not None)
+            self.ep = cfg.n_experts // moe0.e_local if moe0.e_local < cfg.n_experts else 1
+            if self.ep > 1 and self.fused and self.use_native:
+                comm.setup_moe(cfg.n_experts, cfg.n_experts_used, moe0.e_local, moe0.f_local, self.H)
 
     # -- split-K policy ----------------------------------------------------------------------------
     def _splits(self, w: ops.TiledWeight, M: int) -> int:
@@ -396,8 +401,11 @@ class LlamaModel:
     def native_ok(self, m: StepMeta) -> bool:
         """Steps the C++ forward handles: dense layers, no tracing, no CPU-offloaded weights, no
         token-tree masks; one rank, or tensor parallel over the fused peer-memory backend."""
-        return (self.use_native and self.tracer is None and self.moe_runner is None and m.tree_mask is None
-                and not any(lw.offload for lw in self.w.layers) and (self.tp == 1 or self.fused))
+        if not (self.use_native and self.tracer is None and m.tree_mask is None
+                and not any(lw.offload for lw in self.w.layers) and (self.tp == 1 or self.fused)):
+            return False
+        # MoE layers: one rank (expert-sliced), or expert parallelism over the fused backend
+        return self.moe_runner is None or self.tp == 1 or self.ep > 1
 
     @staticmethod
     def _lin(w: ops.TiledWeight) -> list[int]:
@@ -415,8 +423,14 @@ class LlamaModel:
         for lw in w.layers:
             q = [self._lin(x) for x in lw.wqkv] + [zero] * (3 - len(lw.wqkv))
             cols = list(lw.qkv_split) + [0] * (3 - len(lw.qkv_split))
-            layers.append([lw.attn_norm.data_ptr(), lw.ffn_norm.data_ptr(), len(lw.wqkv)] + q[0] + q[1] + q[2] + cols
-                          + self._lin(lw.wo) + self._lin(lw.w_gate_up) + self._lin(lw.w_down))
+            ffn = (self._lin(lw.w_gate_up) + self._lin(lw.w_down)) if lw.moe is None else zero + zero
+            d = [lw.attn_norm.data_ptr(), lw.ffn_norm.data_ptr(), len(lw.wqkv)] + q[0] + q[1] + q[2] + cols \
+                + self._lin(lw.wo) + ffn
+            if lw.moe is not None:
+                mo = lw.moe
+                d += [1] + self._lin(mo.router) + self._lin(mo.gate_up) + [mo.gate_up_stride] + self._lin(mo.down) \
+                    + [mo.down_stride, mo.e0, mo.e_local, mo.f_local]
+            layers.append(d)
         c = dict(L=len(w.layers), H=self.H, Hq=self.hq, Hkv=self.hkv, D=self.D, F=max(self.f_local, 1),
                  V_local=self.v_local, max_tokens=self.max_tokens, max_samples=self.max_samples,
                  max_blocks=int(m.block_tables.shape[-1]), eps=float(cfg.rms_eps), scale=float(self.scale),
@@ -442,6 +456,11 @@ class LlamaModel:
         nat = ops.C().make_forward(c, layers, b)
         if self.fused:
             nat.set_comm(self.comm.tp_desc())
+        if self.moe_runner is not None:
+            if self.ep > 1:
+                nat.set_moe(self.comm.moe_desc())
+            else:
+                nat.set_moe(self.moe_runner.native_desc())
         self._nat, self._nat_key = nat, key
         return nat
 

@@ -132,6 +132,15 @@ class MoERunner:
         self.y = torch.zeros(R, self.H, **f32)
         self.out = torch.zeros(max_tokens, self.H, **f32)
 
+    def native_desc(self) -> dict:
+        """MoeBuffers (csrc/kernels/forward.h) of the expert-sliced path of the native forward."""
+        t = lambda x: x.data_ptr()  # noqa: E731
+        return {"E": self.E, "k": self.k, "norm_topk": int(self.norm_topk), "ep": False,
+                "logits": t(self.logits), "topk_id": t(self.topk_id), "topk_w": t(self.topk_w),
+                "counts": t(self.counts), "offsets": t(self.offsets), "sorted_src": t(self.sorted_src),
+                "slot_row": t(self.slot_row), "total": t(self.total), "xs": t(self.xs), "act": t(self.act),
+                "y": t(self.y), "out": t(self.out)}
+
     def forward(self, moe: MoEWeights, h: torch.Tensor, T: int, out: torch.Tensor | None = None):
         """Weighted sum of this rank's expert outputs for tokens h[:T] into out[:T] (fp32)."""
         if out is None:

@@ -64,8 +64,10 @@ class FusedComm(NcclComm):
         off += 2 * rnd(self.recv_rows * hidden * 2)
         self.off_h = off
         off += rnd(max_tokens * hidden * 2)
-        self.off_count = off          # rs0, rs1, ag0, ag1, sampler (uint32, 64 bytes apart)
-        off += 320
+        # uint32 counters, 64 bytes apart: rs0, rs1, ag0, ag1, sampler, ag2 (MoE combine), MoE dispatch,
+        # MoE combine arrivals
+        self.off_count = off
+        off += 512
         off = rnd(off)
         self.off_xbuf = off           # vocabulary-parallel sampler exchange [nr][max_samples][row bytes]
         off += rnd(nr * self.max_samples * C.tp_sample_row_bytes())
@@ -92,7 +94,7 @@ class FusedComm(NcclComm):
         self.h = C.wrap_ptr(self.local_ptr + self.off_h, [max_tokens, hidden], bf16, dev)
         self.epochs = torch.zeros(_FLAG_SLOTS, dtype=torch.int32, device=self.dev)
         self.err = torch.zeros(4, dtype=torch.int32, device=self.dev)
-        self.state = torch.zeros(8, dtype=torch.int32, device=self.dev)
+        self.state = torch.zeros(12, dtype=torch.int32, device=self.dev)   # 3 sites x 4 words
         self.xstate = torch.zeros(2, dtype=torch.int32, device=self.dev)
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=self.group)
@@ -105,9 +107,67 @@ class FusedComm(NcclComm):
         return {"nranks": self.world, "rank": self.rank, "recv_rows": self.recv_rows, "max_ctas": self.max_ctas,
                 "recv0": [p + self.off_recv[0] for p in P], "recv1": [p + self.off_recv[1] for p in P],
                 "h": [p + self.off_h for p in P], "rs0": cnt[0], "rs1": cnt[1], "ag0": cnt[2], "ag1": cnt[3],
+                "ag2": [p + self.off_count + 320 for p in P],
                 "state": self.state.data_ptr(), "err": self.err.data_ptr(),
                 "xbuf": [p + self.off_xbuf for p in P], "xcount": [p + self.off_count + 256 for p in P],
                 "xstate": self.xstate.data_ptr(), "max_rows": self.max_samples}
+
+    def setup_moe(self, E: int, k: int, e_local: int, f_local: int, hidden: int) -> None:
+        """Expert-parallel buffers (collective): a second symmetric region with every rank's expert
+        input rows, their return words, the per-expert row counters (two layer parities) and the rows
+        that come back to their token's owner; plus this rank's routing and expert activations."""
+        if getattr(self, "_moe_ready", False):
+            return
+        C = ops.C()
+        nr, T = self.world, self.max_tokens
+        cap = T                       # a token selects an expert at most once
+        rpr = (T + nr - 1) // nr
+        rnd = lambda x: (x + 255) // 256 * 256  # noqa: E731
+        off = 0
+        o_x = off
+        off += rnd(e_local * cap * hidden * 2)
+        o_ret = off
+        off += rnd(e_local * cap * 4)
+        o_cnt = [off, off + rnd(e_local * 4)]
+        off += 2 * rnd(e_local * 4)
+        o_comb = off
+        off += rnd(rpr * k * hidden * 2)
+        total = off
+        self.moe_local, handle = C.sym_alloc(total)
+        handles = [None] * nr
+        dist.all_gather_object(handles, handle, group=self.group)
+        peers = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                peers.append(self.moe_local)
+            else:
+                p = C.sym_open(h)
+                self._opened.append(p)
+                peers.append(p)
+        dev = self.dev
+        self.moe_peers = peers
+        self._moe_off = dict(x=o_x, ret=o_ret, cnt=o_cnt, comb=o_comb)
+        self.moe_dims = dict(E=E, k=k, e_local=e_local, f_local=f_local, cap=cap, rpr=rpr)
+        self.disp_state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.ep_logits = torch.zeros(rpr, E, dtype=torch.float32, device=dev)
+        self.ep_topk_w = torch.zeros(rpr, k, dtype=torch.float32, device=dev)
+        self.ep_act = torch.zeros(e_local * cap, f_local, dtype=torch.bfloat16, device=dev)
+        self.ep_offsets = torch.arange(0, e_local * cap, cap, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+        self._moe_ready = True
+
+    def moe_desc(self) -> dict:
+        """MoeBuffers (csrc/kernels/forward.h) of the expert-parallel path."""
+        P, o, md = self.moe_peers, self._moe_off, self.moe_dims
+        cnt = [p + self.off_count for p in self.peer_ptrs]
+        return {"E": md["E"], "k": md["k"], "norm_topk": 1, "ep": True, "cap": md["cap"],
+                "recv_x": [p + o["x"] for p in P], "recv_ret": [p + o["ret"] for p in P],
+                "cnt0": [p + o["cnt"][0] for p in P], "cnt1": [p + o["cnt"][1] for p in P],
+                "comb": [p + o["comb"] for p in P], "disp_arrive": [c + 384 for c in cnt],
+                "comb_arrive": [c + 448 for c in cnt], "disp_state": self.disp_state.data_ptr(),
+                "ep_logits": self.ep_logits.data_ptr(), "ep_topk_w": self.ep_topk_w.data_ptr(),
+                "ep_act": self.ep_act.data_ptr(), "ep_offsets": self.ep_offsets.data_ptr()}
 
     def sample_vocab_parallel(self, model, S: int, params: torch.Tensor, out_tok: torch.Tensor, out_lp) -> None:
         """Sample the S rows from this rank's vocabulary shard of the logits: a local reduction and a
