@@ -51,7 +51,26 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--comm", default=os.environ.get("VMC_COMM", "fused"), choices=["nccl", "fused"])
     ap.add_argument("--e2e-steps", type=int, default=1)
-    return ap.parse_args()
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+                    help="BASELINE.json config: 2 Llama-3-8B Q4_K_M (default, the headline), 3 Llama-3-70B Q8_0 with "
+                         "TurboQuant KV, 4 Mixtral-8x7B Q4_K expert-parallel, 5 speculative decoding (draft model, tree)")
+    ap.add_argument("--kv-cache-dtype", default="")
+    ap.add_argument("--moe-mode", default="a2a", choices=["a2a", "allreduce"],
+                    help="config 4: expert-parallel all-to-all over peer memory, or the partial-sum all-reduce")
+    ap.add_argument("--spec-tree", default="2,2,1", help="config 5: token-tree branching per depth")
+    ap.add_argument("--self-draft", action="store_true", help="config 5: the target drafts for itself (upper bound)")
+    a = ap.parse_args()
+    cfgs = {3: ("random:llama3-70b:Q8_0:0", 128, 2048, 512), 4: ("random:mixtral-8x7b:Q4_K:0", 256, 512, 256),
+            5: ("random:llama3-8b:BF16:0", 32, 512, 256)}
+    if a.config in cfgs:
+        m, R, P, G = cfgs[a.config]
+        a.model = m if a.model == "random:llama3-8b:Q4_K_M:0" else a.model
+        a.num_reqs, a.prompt_len, a.gen_len = R, P, G
+    if a.config == 3 and not a.kv_cache_dtype:
+        a.kv_cache_dtype = "turboquant_4bit_nc"
+    if a.config == 4 and a.moe_mode == "allreduce":
+        a.comm = "nccl"
+    return a
 
 
 class ClockSampler:
@@ -193,10 +212,18 @@ def main():
             comm = NcclComm()
     R, P, G = args.num_reqs, args.prompt_len, args.gen_len
     max_len = P + G + 16
+    extra = {}
+    if args.kv_cache_dtype:
+        extra["kv_cache_dtype"] = args.kv_cache_dtype
+    if args.config == 4:
+        extra["ep_size"] = world
+    if args.config == 5:
+        extra.update(draft_model=args.model if args.self_draft else "random:draft-16l-2048:Q8_0:0",
+                     spec_tree=args.spec_tree, num_speculative_tokens=5)
     llm = LLM(args.model, max_model_len=max(2048, max_len), max_num_seqs=R,
-              max_num_batched_tokens=args.max_num_batched_tokens, num_gpu_blocks=R * ((max_len + 15) // 16) + 64,
+              max_num_batched_tokens=args.max_num_batched_tokens, num_gpu_blocks=R * ((max_len + 15) // 16 + 4) + 64,
               enable_prefix_caching=True, use_cuda_graphs=not args.no_graphs, tp_rank=rank, tp_size=world, comm=comm,
-              device=f"cuda:{local}")
+              device=f"cuda:{local}", **extra)
     eng = llm.engine
     V = llm.cfg.model.vocab
     sp = SamplingParams.greedy_params(max_tokens=G, ignore_eos=True)
@@ -260,22 +287,39 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e = args.e2e_steps * R * G / float(te.item())
     err = ops.device_error(f"cuda:{local}")
+    extra_keys = {}
+    if args.config != 2:
+        extra_keys["bench_config"] = args.config
+    if args.kv_cache_dtype:
+        # KV cache bytes per token of the whole model (all ranks)
+        extra_keys["kv_bytes_per_token"] = int(llm.runner.kv_bytes_per_token) * world
+    if args.config == 4:
+        extra_keys["moe_mode"] = args.moe_mode
+    spec = getattr(llm.runner, "spec", None)
+    if spec is not None:
+        st = spec.stats.as_dict()
+        extra_keys["spec"] = {"tree": args.spec_tree, "self_draft": args.self_draft, **st,
+                              "accepted_tok_per_s": round(value, 2)}
     if rank == 0:
+        model_name = {3: "Llama-3-70B (random-init, Q8_0 GGUF)", 4: "Mixtral-8x7B (random-init, Q4_K GGUF)",
+                      5: "Llama-3-8B (random-init, BF16 GGUF) + 16-layer draft (Q8_0)"}.get(args.config, MODEL)
+        par = f"ep{world}+tp{world}" if args.config == 4 else f"tp{world}"
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init Q4_K_M weights generated on device in GGUF block format; "
                     "uniform-random prompt token ids (seeded, fresh per run)",
-            "config": {"model": MODEL, "global_batch": R, "seq_len": P, "gen_len": G, "parallelism": f"tp{world}",
-                       "kv_cache": "paged bf16, block 16", "max_num_batched_tokens": args.max_num_batched_tokens,
+            "config": {"model": model_name, "global_batch": R, "seq_len": P, "gen_len": G, "parallelism": par,
+                       "kv_cache": args.kv_cache_dtype or "paged bf16, block 16",
+                       "max_num_batched_tokens": args.max_num_batched_tokens,
                        "comm": args.comm if world > 1 else "none",
                        "l2": "inputs larger than L2 (4.9 GB weights + KV streamed every step)",
                        "step": "one full serving run of global_batch requests"},
             "p50_ttft_ms": round(summ["p50_ttft_ms"], 2), "p50_itl_ms": round(summ["p50_itl_ms"], 3),
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s (LLM.generate, wall clock)",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": launches, "clocks": clk, "device_error": err,
+            "gpu_launches": launches, "clocks": clk, "device_error": err, **extra_keys,
         }
         print(json.dumps(line), flush=True)
     llm.shutdown()

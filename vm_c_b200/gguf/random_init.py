@@ -43,6 +43,10 @@ PRESETS: dict[str, ModelConfig] = {
     "tiny-mixtral": ModelConfig(name="tiny-mixtral", n_layers=2, hidden=256, n_heads=8, n_kv_heads=4, head_dim=32,
                                 ffn=512, vocab=32000, rms_eps=1e-5, rope_theta=10000.0, context_length=2048,
                                 n_experts=4, n_experts_used=2, bos_token_id=1, eos_token_ids=[2]),
+    # small Mixtral-architecture model with 8 experts (expert parallelism up to 8 ranks)
+    "tiny-mixtral8": ModelConfig(name="tiny-mixtral8", n_layers=2, hidden=256, n_heads=8, n_kv_heads=8, head_dim=32,
+                                 ffn=512, vocab=32000, rms_eps=1e-5, rope_theta=10000.0, context_length=2048,
+                                 n_experts=8, n_experts_used=2, bos_token_id=1, eos_token_ids=[2]),
     # small hybrid gated delta-net model (Qwen3.5-MoE architecture): layers 0-2 GDN, layer 3 full
     # attention with partial RoPE, 4 experts (top-2) plus a shared expert
     "tiny-qwen35moe": ModelConfig(arch="qwen35moe", name="tiny-qwen35moe", n_layers=4, hidden=256, n_heads=4,
