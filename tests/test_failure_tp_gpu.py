@@ -23,11 +23,18 @@ def test_rank_leaves_between_steps(tmp_path):
     model = str(tmp_path / "tiny.gguf")
     write_random_gguf(model, preset("tiny-llama"), "Q8_0", seed=0)
     out = str(tmp_path / "res")
-    cmd = ["timeout", "-k", "10", "180", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29651",
-           os.path.join(HERE, "failure_tp_worker.py"), model, out]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", VMC_FAULT="exit:1:6")
-    subprocess.run(cmd, capture_output=True, text=True, env=env)  # rank 1's exit fails the launcher
+    # The two ranks are plain child processes with the rendezvous variables set here: under
+    # torch.distributed.run the departing rank's exit would make the launcher stop the survivor too.
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, NCCL_NVLS_ENABLE="0", VMC_FAULT="exit:1:6", RANK=str(r), LOCAL_RANK=str(r),
+                   WORLD_SIZE="2", LOCAL_WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT="29651")
+        procs.append(subprocess.Popen(["timeout", "-k", "10", "180", sys.executable,
+                                       os.path.join(HERE, "failure_tp_worker.py"), model, out], env=env,
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    logs = [p.communicate()[0] for p in procs]
+    assert procs[1].returncode == 3, logs[1][-2000:]   # the injected departure's exit status
+    assert os.path.exists(out + ".0"), logs[0][-3000:]
     r0 = json.load(open(out + ".0"))
     assert not os.path.exists(out + ".1")   # the departed rank wrote nothing
     assert r0["error"] == "RankFailure" and r0["failed_rank"] == 1, r0

@@ -111,12 +111,22 @@ def _moe_out(src, cfg, layer, h, tp_rank, tp_size, ep_size):
     return out.clone()
 
 
-@pytest.mark.parametrize("tp,ep", [(2, 1), (2, 2), (4, 4)])
-def test_expert_placements_sum_to_full(cuda_ext, tiny_moe, tp, ep):
-    src = GgufSource(tiny_moe)
+@pytest.fixture(scope="module")
+def tiny_moe8(tmp_path_factory):
+    p = tmp_path_factory.mktemp("moe8") / "tiny-mixtral8-q8.gguf"
+    write_random_gguf(str(p), preset("tiny-mixtral8"), "Q8_0", seed=0)
+    return str(p)
+
+
+@pytest.mark.parametrize("model,tp,ep,T", [("tiny_moe", 2, 1, 23), ("tiny_moe", 2, 2, 23), ("tiny_moe", 4, 4, 23),
+                                           ("tiny_moe8", 2, 2, 23), ("tiny_moe8", 2, 2, 162),
+                                           ("tiny_moe8", 4, 4, 8), ("tiny_moe8", 8, 8, 162)])
+def test_expert_placements_sum_to_full(cuda_ext, request, model, tp, ep, T):
+    # Every placement's per-rank partial outputs sum to the single-rank output (the all-reduce of
+    # the expert-parallel NCCL path), for 4 and 8 experts and decode- and prefill-sized batches.
+    src = GgufSource(request.getfixturevalue(model))
     cfg = src.model_config()
     torch.manual_seed(2)
-    T = 23
     h = (torch.randn(T, cfg.hidden, device="cuda")).bfloat16()
     full = _moe_out(src, cfg, 1, h, 0, 1, 1)
     parts = sum(_moe_out(src, cfg, 1, h, r, tp, ep) for r in range(tp))
