@@ -770,6 +770,10 @@ void paged_attention(const AttnLaunch& a, cudaStream_t st) {
   VMC_CHECK(!(a.decode && a.tree_mask), "attention: tree masks need the prefill path");
   VMC_CHECK(!a.tree_mask || (a.tree_span >= 1 && a.tree_span <= 64), "attention: tree span must be 1..64");
   if (a.num_reqs <= 0) return;
+  if (attn_prefill_tc_eligible(a)) {
+    attn_prefill_tc(a, st);
+    return;
+  }
   if (a.decode) {
     VMC_CHECK(a.max_qlen * p.G <= 16, "attention: decode path needs q_len * group <= 16");
     VMC_CHECK(p.splits == 1 || (a.part_o && a.part_lse), "attention: split-KV needs partial buffers");

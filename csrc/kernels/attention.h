@@ -28,9 +28,18 @@ struct AttnLaunch {
   const TqDev* tq = nullptr; // TurboQuant cache of this layer instead of bf16 pages (kv unused)
   const uint64_t* tree_mask = nullptr;  // [T] tree-verification masks (prefill path only), or null
   int tree_span = 0;         // bit 0 of a mask is the key at position ctx - tree_span
+  int64_t num_blocks = 0;    // blocks of the bf16 page array (0: unknown; the tcgen05 prefill path needs it)
+  uint32_t* err = nullptr;   // device error word for expired bounded waits (tcgen05 prefill path)
 };
 
 void paged_attention(const AttnLaunch& a, cudaStream_t st);
+
+// Prefill chunks of bf16 caches with head dim 128 and causal masks run on the tcgen05 kernel
+// (attention_tc.cu); everything else on the mma.sync kernels. VMC_ATTN_TC=0 (or
+// attn_prefill_tc_enable(0)) keeps prefill on mma.sync.
+bool attn_prefill_tc_eligible(const AttnLaunch& a);
+void attn_prefill_tc(const AttnLaunch& a, cudaStream_t st);
+void attn_prefill_tc_enable(int on);
 
 // Move KV rows inside a bf16 paged cache [L, num_blocks, 2, Hkv, 16, D] (all layers, K and V, all
 // KV heads): request r moves cnt[r] rows, src[r * max_moves + i] -> dst[r * max_moves + i] (slot

@@ -263,6 +263,8 @@ int Forward::attention(int l, const StepDims& d, cudaStream_t st) {
   a.scale = c_.scale;
   a.out = b_.attn;
   a.tq = b_.tq ? &t : nullptr;
+  a.err = b_.err;
+  if (!b_.tq) a.num_blocks = b_.kv_layer_bytes / (static_cast<int64_t>(2) * c_.Hkv * 16 * c_.D * 2);
   const int G = c_.Hq / c_.Hkv;
   if (d.nd > 0) {
     const bool dec_ok = d.decode_qlen * G <= 16;

@@ -171,7 +171,7 @@ void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, t
                      int64_t splits, c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_lse,
                      torch::Tensor out, c10::optional<torch::Tensor> tq_cache, std::vector<int64_t> tq_meta,
                      c10::optional<torch::Tensor> tq_centroids, c10::optional<torch::Tensor> tq_midpoints,
-                     c10::optional<torch::Tensor> tree_mask, int64_t tree_span) {
+                     c10::optional<torch::Tensor> tree_mask, int64_t tree_span, c10::optional<torch::Tensor> err) {
   vmc::TqDev tq;
   const bool use_tq = tq_cache.has_value() && tq_cache->defined();
   if (use_tq) tq = make_tq(*tq_cache, tq_meta, *tq_centroids, *tq_midpoints);
@@ -196,6 +196,8 @@ void paged_attention(torch::Tensor q, torch::Tensor kv, torch::Tensor q_start, t
   a.part_lse = opt_ptr<float>(part_lse);
   a.out = out.data_ptr();
   a.tq = use_tq ? &tq : nullptr;
+  if (!use_tq && kv.dim() == 5 && kv.scalar_type() == torch::kBFloat16) a.num_blocks = kv.size(0);
+  if (err.has_value() && err->defined()) a.err = ptr<uint32_t>(*err);
   if (tree_mask.has_value() && tree_mask->defined()) {
     TORCH_CHECK(tree_mask->scalar_type() == torch::kInt64 && tree_mask->numel() >= total_tokens,
                 "paged_attention: tree_mask must be int64 [T]");
@@ -604,7 +606,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("total_tokens"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("decode"),
         py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("out"), py::arg("tq_cache") = py::none(),
         py::arg("tq_meta") = std::vector<int64_t>{}, py::arg("tq_centroids") = py::none(),
-        py::arg("tq_midpoints") = py::none(), py::arg("tree_mask") = py::none(), py::arg("tree_span") = 0);
+        py::arg("tq_midpoints") = py::none(), py::arg("tree_mask") = py::none(), py::arg("tree_span") = 0,
+        py::arg("err") = py::none());
+  m.def("attention_tc", [](bool on) { vmc::attn_prefill_tc_enable(on ? 1 : 0); },
+        "route bf16 head-dim-128 prefill attention to the tcgen05 kernel (true) or the mma.sync kernel");
   m.def("kv_move", &kv_move);
   m.def("rope_store_tq", &rope_store_tq);
   m.def("embed", &embed);

@@ -84,6 +84,28 @@ def test_prefill_chunks(cuda_ext, D, Hq, Hkv):
     assert (out.float() - ref).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (64, 8), (8, 8), (4, 1)])
+@pytest.mark.parametrize("tc", [True, False])
+def test_prefill_head128_paths(cuda_ext, Hq, Hkv, tc):
+    # Head dim 128, bf16 pages: the tcgen05 kernel (tc=True, 128 packed rows x 128-key tiles) and the
+    # mma.sync kernel, on fresh prompts, chunks continuing a cached prefix (context > q_len), ragged
+    # row and key counts, and a 2048-token context.
+    D = 128
+    ctx = [1024, 2048, 300, 129, 17, 640]
+    ql = [1024, 700, 77, 129, 17, 1]
+    kv, bt, q, qs, cl, T = _setup(ctx, ql, Hq, Hkv, D, nblocks=400)
+    out = torch.full_like(q, float("nan"))
+    ops.C().attention_tc(tc)
+    try:
+        ops.paged_attention(q, kv, qs, cl, bt, len(ctx), 0, max(ql), T, Hq, Hkv, D, 1 / math.sqrt(D), False, out)
+        torch.cuda.synchronize()
+    finally:
+        ops.C().attention_tc(True)
+    assert ops.device_error() == 0
+    ref = _ref(kv, bt, q, qs, cl, Hq, Hkv, D)
+    assert (out.float() - ref).abs().max().item() < 2e-2
+
+
 def test_mixed_offsets(cuda_ext):
     # decodes first (req_offset 0), then prefill requests launched with req_offset = num_decode
     D, Hq, Hkv = 128, 32, 8

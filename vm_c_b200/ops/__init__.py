@@ -270,12 +270,12 @@ def paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset,
     if tq is None:
         C().paged_attention(q, kv, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens, Hq,
                             Hkv, D, scale, decode, splits, part_o, part_lse, out, tree_mask=tree_mask,
-                            tree_span=tree_span)
+                            tree_span=tree_span, err=_err_word(q.device))
     else:
         cache, tab = tq
         C().paged_attention(q, cache, q_start, ctx_len, block_tables, num_reqs, req_offset, max_qlen, total_tokens,
                             Hq, Hkv, D, scale, decode, splits, part_o, part_lse, out, cache, tab.meta(),
-                            tab.centroids, tab.midpoints, tree_mask, tree_span)
+                            tab.centroids, tab.midpoints, tree_mask, tree_span, _err_word(q.device))
     _count(2 if (decode and splits > 1) else 1)
 
 

@@ -9,9 +9,10 @@ W [4096, 14336 / N] Q4_K on each rank) as the engine runs it:
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m vm_c_b200.parallel.bench_comm
 
 Each case captures 20 calls in a CUDA graph, replays it once untimed and once between CUDA events;
-the time per call is the maximum over ranks. Roofline of the fused site: the slower of the GEMM's
-FLOPs at the measured bf16 peak and the bytes that must leave each GPU over NVLink (the reduce-scatter
-and the all-gather each send (N - 1) / N x T x 4096 x 2 bytes) at the measured 770 GB/s per direction.
+the time per call is the maximum over ranks. Roofline of the fused site: the slowest of the GEMM's
+FLOPs at the measured bf16 peak, its Q4_K weight bytes (4.5 bits per weight) at the measured HBM
+bandwidth, and the bytes that must leave each GPU over NVLink (the reduce-scatter and the all-gather
+each send (N - 1) / N x T x 4096 x 2 bytes) at the measured 770 GB/s per direction.
 """
 from __future__ import annotations
 
@@ -30,12 +31,15 @@ H, F = 4096, 14336
 NVLINK_GBS = 770.0
 
 
-def _peak_tflops() -> float:
+def _peaks() -> tuple[float, float]:
+    """(bf16 TFLOP/s, HBM GB/s) measured on this pool (MEASURED_PEAKS.json at the repository root),
+    else the pool's earlier measurement."""
     p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
     try:
-        return float(json.load(open(p))["bf16_tflops"])
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"])
     except (OSError, KeyError, ValueError):
-        return 1590.0
+        return 1590.0, 6650.0
 
 
 def _time(fn, n: int = 20) -> float:
@@ -81,7 +85,7 @@ def main() -> None:
     norm_w = torch.ones(H, device=dev)
     out16 = torch.empty(T_MAX, H, dtype=torch.bfloat16, device=dev)
     o32 = torch.zeros(T_MAX, H, device=dev)
-    peak = _peak_tflops()
+    peak, hbm = _peaks()
     lines = []
     for T in (64, 256, 2048):
         s = ops.pick_splits(w, T)
@@ -100,11 +104,12 @@ def main() -> None:
         tf, tn, tg = _time(fused), _time(nccl), _time(gemm)
         flop = 2.0 * T * H * K
         t_compute = flop / (peak * 1e12) * 1e6
+        t_hbm = H * K * 4.5 / 8 / (hbm * 1e9) * 1e6
         t_link = 2 * (world - 1) / world * T * H * 2 / (NVLINK_GBS * 1e9) * 1e6
-        target = max(t_compute, t_link)
-        lines.append(f"T={T:5d} ranks={world} K_local={K:5d}  fused {tf:8.2f} us  nccl+norm {tn:8.2f} us  "
-                     f"gemm alone {tg:8.2f} us  roofline {target:7.2f} us (compute {t_compute:.2f}, NVLink "
-                     f"{t_link:.2f})  fused/roofline {target / tf:.2f}")
+        target = max(t_compute, t_hbm, t_link)
+        lines.append(f"T={T:5d} ranks={world} K_local={K:5d} splits={s}  fused {tf:8.2f} us  nccl+norm {tn:8.2f} us  "
+                     f"gemm alone (1 split) {tg:8.2f} us  roofline {target:7.2f} us (compute {t_compute:.2f}, HBM "
+                     f"{t_hbm:.2f}, NVLink {t_link:.2f})  fused/roofline {target / tf:.2f}")
     err = comm.device_error()
     if rank == 0:
         for ln in lines:
