@@ -18,8 +18,9 @@
 //              operand (V pages are key-major with D contiguous). S_{j+1} is issued before P_j is
 //              waited on, so the tensor pipe computes the next scores while softmax runs.
 //   warps 2-5  softmax, one packed row per thread (TMEM lane = row): causal mask against the row's
-//              absolute position, online softmax in base 2, P_j (bf16) into TMEM, the rescale of
-//              the O accumulator when a row maximum grew (after PV_{j-1} completed), and the final
+//              absolute position, online softmax in base 2 with a lazy base (moved only when a
+//              row's maximum grows by more than 2^8, then O is rescaled in TMEM after PV_{j-1}
+//              completed), P_j (bf16) into TMEM once PV_{j-2} released its buffer, and the final
 //              O / l epilogue to global memory.
 //
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O [256,384), P0 [384,448), P1 [448,512).
@@ -46,7 +47,8 @@ constexpr uint32_t kTile = 2 * kHalf;                 // 128 rows x 128 bf16
 constexpr uint32_t kSmemData = kTile + kStages * 2 * kTile;
 constexpr uint32_t kSmem = kSmemData + 1024 + 256;   // + alignment slack + barriers
 constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kColP0 = 384, kColP1 = 448;
-// Error word on an expired wait: kErrAttnWait | (n << 8), n = 1..6 naming the wait.
+constexpr float kRescaleLog2 = 8.f;                   // lazy-rescale threshold (factor 256)
+// Error word on an expired wait: kErrAttnWait | (n << 8), n = 1..8 naming the wait.
 __device__ __forceinline__ uint32_t tc_err(uint32_t n) { return static_cast<uint32_t>(kErrAttnWait) | (n << 8); }
 
 struct TcParams {
@@ -115,7 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_empty = bars + kStages;      // [kStages]
   uint64_t* s_full = bars + 2 * kStages;    // [2]
   uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_done = p_full + 2;
+  uint64_t* p_free = p_full + 2;            // [2] PV of the buffer's last P completed
+  uint64_t* o_done = p_free + 2;
   uint64_t* q_full = o_done + 1;
   uint64_t* mma_fin = q_full + 1;           // every MMA of the CTA completed (before TMEM is freed)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_fin + 1);
@@ -128,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 128);
+      mbar_init(&p_free[b], 1);
     }
     mbar_init(o_done, 1);
     mbar_init(q_full, 128);
@@ -203,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_bf16_ts(tmem + kColO, pa + 8 * ks, sdesc_mn_sw128(va + ks * 16 * 128, kHalf), idesc_pv,
                        (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&kv_empty[s]);
+        umma_commit(&p_free[j & 1]);
         umma_commit(o_done);
       }
       umma_commit(mma_fin);
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     mbar_arrive(q_full);
     const int qpos = valid ? ctx - qlen + t : -1;
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // m: the exponent base of this row's P values (log2 domain)
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       ok = warp_all(mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err, tc_err(5)));
@@ -247,9 +252,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         sv[i] = __float_as_uint(x);
         mx = fmaxf(mx, x);
       }
-      const float m_new = fmaxf(m, mx);
+      // Lazy rescale: the base moves only when the tile's maximum exceeds it by more than
+      // kRescaleLog2, so P stays <= 2^kRescaleLog2 (exact enough in bf16, no overflow in the fp32
+      // O and l) and most tiles skip the O round trip and the wait for the previous PV.
+      const bool move = mx > m + kRescaleLog2;   // m = -inf: the row's first visible key
+      const float m_new = move ? mx : m;
       const float base = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m - base);  // 0 on the first visible tile (m = -inf)
+      const float alpha = move ? exp2f(m - base) : 1.f;  // 0 when the base is first set
       float sum = 0.f;
       uint32_t pk[kKeys / 2];
 #pragma unroll
@@ -261,15 +270,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l = l * alpha + sum;
       m = m_new;
+      if (j >= 2) {  // P buffer j & 1 is free once PV_{j-2} completed
+        ok = warp_all(mbar_wait(&p_free[j & 1], ((j >> 1) - 1) & 1, p.err, tc_err(7)));
+        if (!ok) break;
+        tc_fence_after();
+      }
       const uint32_t pcol = tmem + lane_addr + ((j & 1) ? kColP1 : kColP0);
 #pragma unroll
       for (int c = 0; c < kKeys / 32; ++c) tmem_st16(pcol + 16 * c, pk + 16 * c);
-      if (j > 0) {
-        // O holds the sum through tile j-1 once PV_{j-1} completed; rescale it to the new maximum.
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // O holds the sum through tile j-1 once PV_{j-1} completed; rescale it to the new base.
+        // (PV_{j-2} completed above, so phase j-1 is the oldest incomplete phase of o_done.)
         ok = warp_all(mbar_wait(o_done, (j - 1) & 1, p.err, tc_err(6)));
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < kD / 16; ++c) {
             uint32_t ov[16];
@@ -285,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
     }
-    if (ok) ok = warp_all(mbar_wait(o_done, (ntiles - 1) & 1, p.err, tc_err(6)));
+    if (ok) ok = warp_all(mbar_wait(mma_fin, 0, p.err, tc_err(8)));
     if (ok) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;

@@ -33,7 +33,8 @@ def run_tp(model, backend, tmp_path, n=2, ep=1, spec=False):
            os.path.join(HERE, "tp_worker.py"), model, backend, str(out), str(ep), "spec" if spec else "plain"]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
-    assert r.returncode == 0, r.stderr[-3000:]
+    i = r.stderr.find("Traceback")   # the first worker's traceback, not the launcher's summary
+    assert r.returncode == 0, r.stderr[max(i, 0):max(i, 0) + 4000]
     return json.load(open(out))
 
 

@@ -46,8 +46,19 @@ def family(name: str) -> str:
 
 
 def short(name: str) -> str:
+    """Kernel name without return type, namespaces and argument list (template arguments kept)."""
     name = re.sub(r"^void ", "", name)
-    name = name.split("(")[0]
+    name = name.replace("(anonymous namespace)::", "").replace("vmc::", "")
+    depth, cut = 0, len(name)
+    for i, ch in enumerate(name):   # the first '(' outside template brackets starts the arguments
+        if ch == "<":
+            depth += 1
+        elif ch == ">":
+            depth -= 1
+        elif ch == "(" and depth == 0:
+            cut = i
+            break
+    name = name[:cut]
     return name if len(name) < 90 else name[:87] + "..."
 
 
@@ -94,6 +105,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
     ap.add_argument("--json", default="")
+    ap.add_argument("--host-profile", action="store_true",
+                    help="also run the timed decode steps under cProfile and print the top host functions")
     a = ap.parse_args()
 
     from ..core.sampling_params import SamplingParams
@@ -138,6 +151,24 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dec_us = float(t.item())
+    host_lines = []
+    if a.host_profile:
+        import cProfile
+        import io
+        import pstats
+        import time
+        pr = cProfile.Profile()
+        t0 = time.perf_counter()
+        pr.enable()
+        for _ in range(a.steps):
+            eng.step()
+        pr.disable()
+        torch.cuda.synchronize()
+        host_ms = (time.perf_counter() - t0) * 1e3 / a.steps
+        buf = io.StringIO()
+        pstats.Stats(pr, stream=buf).sort_stats("cumulative").print_stats(25)
+        host_lines = [f"== host profile of {a.steps} decode steps: {host_ms:.2f} ms per step (wall, under cProfile)"]
+        host_lines += buf.getvalue().splitlines()
     # 2) decode steps under the profiler
     from torch.profiler import ProfilerActivity, profile
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
@@ -166,6 +197,7 @@ def main() -> None:
         lines = [f"step profile: {a.model}, {R} requests x {P}-token prompts, tp{world}, comm {a.comm if world > 1 else 'none'}"]
         lines += report(f"decode step ({R} tokens)", dec, dec_us)
         lines += report("first prefill step of a fresh batch (2048 tokens)", pre, None)
+        lines += host_lines
         print("\n".join(lines), flush=True)
         if a.json:
             json.dump({"decode_us": dec_us, "decode": dec, "prefill": pre, "tp": world}, open(a.json, "w"))
