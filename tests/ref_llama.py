@@ -36,9 +36,17 @@ def load_dense(src, cfg):
     return W
 
 
-def moe_ffn(L, cfg, h):
-    """Mixtral FFN: softmax router, top-k, renormalised weights, weighted sum of SwiGLU experts."""
-    probs = torch.softmax(h @ L["ffn_gate_inp"].T, -1)
+def moe_ffn(L, cfg, h, margins=None):
+    """Mixtral FFN: softmax router, top-k, renormalised weights, weighted sum of SwiGLU experts.
+    With `margins` (a list), appends per token the gap between the k-th and (k+1)-th router logit
+    relative to the largest router logit magnitude: how close the expert choice is to a tie."""
+    logits = h @ L["ffn_gate_inp"].T
+    if margins is not None:
+        top = torch.topk(logits, min(cfg.n_experts_used + 1, cfg.n_experts), -1).values
+        gap = top[:, cfg.n_experts_used - 1] - top[:, -1] if cfg.n_experts > cfg.n_experts_used else \
+            torch.full_like(top[:, 0], float("inf"))
+        margins.append(gap / logits.abs().max(-1).values.clamp_min(1e-30))
+    probs = torch.softmax(logits, -1)
     w, idx = torch.topk(probs, cfg.n_experts_used, -1)
     w = w / w.sum(-1, keepdim=True)
     out = torch.zeros_like(h)
@@ -65,8 +73,8 @@ def rope(x, pos, inv, neox):
     return out
 
 
-def forward_logits(W, cfg, tokens: list[int]) -> torch.Tensor:
-    """Logits for every position of `tokens` (fp32)."""
+def forward_logits(W, cfg, tokens: list[int], margins=None) -> torch.Tensor:
+    """Logits for every position of `tokens` (fp32). `margins`: see moe_ffn (one entry per layer)."""
     T = len(tokens)
     D, Hq, Hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
     x = W["embd"][torch.tensor(tokens)]
@@ -91,7 +99,7 @@ def forward_logits(W, cfg, tokens: list[int]) -> torch.Tensor:
         x = x + a @ L["attn_output"].T
         h = rms(x, L["ffn_norm"])
         if cfg.is_moe:
-            x = x + moe_ffn(L, cfg, h)
+            x = x + moe_ffn(L, cfg, h, margins)
         else:
             x = x + (torch.nn.functional.silu(h @ L["ffn_gate"].T) * (h @ L["ffn_up"].T)) @ L["ffn_down"].T
     return rms(x, W["norm"]) @ W["out"].T

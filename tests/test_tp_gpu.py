@@ -21,8 +21,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 @pytest.fixture(scope="module")
 def tiny(tmp_path_factory):
+    # tiny Llama with an FFN width whose 1/8 slice is whole Q8_0 blocks (768 / 8 = 96 = 3 x 32), so
+    # that every rank of TP 8 holds block-aligned, 16-byte-strided down-projection columns
     p = tmp_path_factory.mktemp("tp") / "tiny.gguf"
-    write_random_gguf(str(p), preset("tiny-llama"), "Q8_0", seed=0)
+    cfg = preset("tiny-llama")
+    cfg.ffn = 768
+    write_random_gguf(str(p), cfg, "Q8_0", seed=0)
     return str(p)
 
 

@@ -16,9 +16,15 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 from ref_llama import forward_logits, load_dense  # noqa: E402
 
 
+ROUTER_TIE = 0.02   # relative gap between the k-th and (k+1)-th router logit that bf16 can flip
+
+
 def oracle_report(model, prompts, outs, rows):
     """Teacher-forced fp32 oracle along the engine's own greedy trajectories: the largest logit error
-    relative to each row's largest oracle logit, and argmax disagreements outside near-ties."""
+    relative to each row's largest oracle logit, and argmax disagreements outside near-ties.
+    MoE models: a position whose expert choice is a near-tie in the oracle's router at any layer
+    (gap below ROUTER_TIE) may legitimately pick the other expert in bf16, which changes that
+    position's logits by tens of percent; such rows are counted, not compared."""
     from vm_c_b200.llm import make_source
     src, cfg = make_source(model, "cpu")
     W = load_dense(src, cfg)
@@ -26,16 +32,24 @@ def oracle_report(model, prompts, outs, rows):
     for ids, lg in rows:
         for k, i in enumerate(ids):
             got.setdefault(i, []).append(lg[k])
-    worst, flips = 0.0, 0
+    worst, flips, tied = 0.0, 0, 0
     for idx, (p, o) in enumerate(zip(prompts, outs)):
-        ref = forward_logits(W, cfg, p + o.output_token_ids[:-1])[len(p) - 1:]
-        mine = torch.stack(got[sorted(got)[idx]])
+        margins = []
+        ref = forward_logits(W, cfg, p + o.output_token_ids[:-1], margins)[len(p) - 1:]
+        keep = torch.ones(ref.shape[0], dtype=torch.bool)
+        if margins:
+            keep = torch.stack(margins).min(0).values[len(p) - 1:] >= ROUTER_TIE
+            tied += int((~keep).sum())
+        mine = torch.stack(got[sorted(got)[idx]])[keep]
+        ref = ref[keep]
+        if ref.shape[0] == 0:
+            continue
         scale = ref.abs().max(-1).values
         worst = max(worst, float(((mine - ref).abs().max(-1).values / scale).max()))
         top2 = torch.topk(ref, 2, -1).values
         decided = (top2[:, 0] - top2[:, 1]) > 0.05 * scale
         flips += int(((mine.argmax(-1) != ref.argmax(-1)) & decided).sum())
-    return {"max_rel_logit_err": worst, "argmax_flips": flips}
+    return {"max_rel_logit_err": worst, "argmax_flips": flips, "router_tie_rows": tied}
 
 
 def main():

@@ -79,6 +79,10 @@ def check_tp(cfg: ModelConfig, tp: int) -> None:
         raise ValueError(f"tp {tp} not a multiple of n_kv_heads {cfg.n_kv_heads}")
     if cfg.ffn % tp:
         raise ValueError(f"ffn {cfg.ffn} not divisible by tp {tp}")
+    if tp > 1 and (cfg.ffn // tp) % 8:
+        # the down projection reads bf16 activation rows of ffn / tp columns through TMA
+        raise ValueError(f"ffn {cfg.ffn} / tp {tp} = {cfg.ffn // tp} columns per rank: not a multiple of 8 "
+                         f"(16-byte activation rows)")
 
 
 def _to_dev(t: torch.Tensor, device) -> torch.Tensor:

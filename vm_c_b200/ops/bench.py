@@ -184,9 +184,8 @@ def bench_step(kind: str, reps: int) -> str:
     eng = llm.engine
     rng = np.random.default_rng(0)
     sp = SamplingParams.greedy_params(max_tokens=64, ignore_eos=True)
-    for _ in range(R):
-        eng.add_request(rng.integers(0, llm.cfg.model.vocab, P).tolist(), sp)
-    while eng.sched.num_waiting or any(len(r.output_token_ids) < 2 for r in eng.requests.values()):
+    reqs = [eng.add_request(rng.integers(0, llm.cfg.model.vocab, P).tolist(), sp) for _ in range(R)]
+    while any(len(r.output_token_ids) < 2 for r in reqs):   # requests join the scheduler at a step
         eng.step()
     for _ in range(3):
         eng.step()

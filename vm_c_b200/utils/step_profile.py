@@ -14,7 +14,9 @@ tokens) through the engine, and on every rank:
 Rank 0 prints each phase's kernels grouped by family (GEMM, attention, reduce-scatter + norm +
 all-gather, sampling, NCCL, other) with the microseconds per step and the launches per step, max
 over ranks. Kernel durations under the profiler are serialised records; read them as shares of the
-step, not as a bench number. The reference has no equivalent (its per-op timing is ggml's
+step, not as a bench number. With programmatic dependent launch a kernel starts before its
+predecessor ends and its record includes that wait: run with VMC_PDL=0 for per-kernel durations
+(the CUDA-event step time is then the time without PDL). The reference has no equivalent (its per-op timing is ggml's
 GGML_SCHED debug output); this is the breakdown behind the decode-latency analysis.
 """
 from __future__ import annotations
@@ -130,12 +132,12 @@ def main() -> None:
     sp = SamplingParams.greedy_params(max_tokens=a.steps * 3 + 16, ignore_eos=True)
 
     def add_batch():
-        for _ in range(R):
-            eng.add_request(rng.integers(0, llm.cfg.model.vocab, P).tolist(), sp)
+        return [eng.add_request(rng.integers(0, llm.cfg.model.vocab, P).tolist(), sp) for _ in range(R)]
 
-    # warm-up: serve a first batch until every request decodes
-    add_batch()
-    while eng.sched.num_waiting or any(len(r.output_token_ids) < 2 for r in eng.requests.values()):
+    # warm-up: serve a first batch until every request decodes (requests join the scheduler at the
+    # next step, so the loop follows the returned request objects)
+    reqs = add_batch()
+    while any(len(r.output_token_ids) < 2 for r in reqs):
         eng.step()
     for _ in range(3):
         eng.step()
