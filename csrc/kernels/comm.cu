@@ -18,6 +18,9 @@
 // identically on all ranks because every rank launches the same sequence of calls with the same
 // grid. The partial buffers alternate between two sites, and a rank rewrites a site only after its
 // next all-reduce has seen every peer start that next all-reduce, so no reader can still be reading.
+#include <cstdlib>
+#include <cstring>
+
 #include "comm.h"
 #include "common.cuh"
 
@@ -232,6 +235,7 @@ struct RsArgs {
   const float* topk_w;        // expert-parallel combine: router weights [rpr][slots]
   uint32_t* reset;            // expert-parallel combine: counters to zero once the rows are read
   int reset_n;
+  int two_level;              // 1: the all-gather is signalled once per rank (last CTA), else per CTA
 };
 
 constexpr int kRsThreads = 256;
@@ -345,21 +349,37 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsArgs a) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    // Every CTA makes its all-gather stores complete at system scope and counts itself on this
+    // site's CTA counter (GPU-scope acq_rel). The CTA that completes the grid advances the targets of
+    // the next call (every CTA has read them by then), clears the expert row counters this combine
+    // consumed, and signals the all-gather once at every rank: its system-scope fence orders all the
+    // grid's stores, acquired through the CTA counter, before that one arrival. CTA 0 returns only
+    // after every rank's signal has arrived here.
+    const uint32_t ag_inc = static_cast<uint32_t>(a.two_level ? NR : NR * G);
+    const uint32_t ag_target = a.state[1] + ag_inc;  // read before this CTA counts itself
     if (a.gather) {
       fence_acq_rel_sys();
+      if (!a.two_level) {
 #pragma unroll
-      for (int q = 0; q < NR; ++q) red_add_sys(a.ag_count[q], 1u);
-      if (b == 0) wait_count_sys(a.ag_count[a.rank], a.state[1] + static_cast<uint32_t>(NR * G), a.err);
+        for (int q = 0; q < NR; ++q) red_add_sys(a.ag_count[q], 1u);
+      }
     }
-    // The last CTA to finish advances the targets of the next call at this site (every CTA has read
-    // them by then) and clears the expert row counters this combine consumed.
-    if (atomicAdd(a.state + 2, 1u) == static_cast<uint32_t>(G - 1)) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.state + 2) : "memory");
+    if (old == static_cast<uint32_t>(G - 1)) {
       a.state[0] += a.rs_inc;
-      if (a.gather) a.state[1] += static_cast<uint32_t>(NR * G);
+      if (a.gather) a.state[1] += ag_inc;
       a.state[2] = 0;
       for (int i = 0; i < a.reset_n; ++i) a.reset[i] = 0;
-      __threadfence();
+      if (a.gather && a.two_level) {
+        fence_acq_rel_sys();
+#pragma unroll
+        for (int q = 0; q < NR; ++q) red_add_sys(a.ag_count[q], 1u);
+      } else {
+        __threadfence();
+      }
     }
+    if (a.gather && b == 0) wait_count_sys(a.ag_count[a.rank], ag_target, a.err);
   }
 }
 
@@ -380,6 +400,14 @@ void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
     case 7: launch_k(ar_add_rmsnorm_kernel<7>, dim3(grid), dim3(kArThreads), 0, st, a); break;
     default: launch_k(ar_add_rmsnorm_kernel<8>, dim3(grid), dim3(kArThreads), 0, st, a); break;
   }
+}
+
+bool tp_two_level() {
+  static const bool on = [] {
+    const char* e = std::getenv("VMC_TP_TWO_LEVEL");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  return on;
 }
 
 namespace {
@@ -412,6 +440,7 @@ RsArgs rs_common(const TpComm& c, int site, int T, int H, float* resid, const fl
   a.rank = c.rank;
   a.err = c.err;
   a.gather = gather;
+  a.two_level = tp_two_level() ? 1 : 0;
   return a;
 }
 }  // namespace

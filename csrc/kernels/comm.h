@@ -42,8 +42,9 @@ struct TpComm {
   void* h[8] = {};                // each rank's h buffer
   uint32_t* rs_count[2][8] = {};  // [site][rank]
   uint32_t* ag_count[3][8] = {};  // [site][rank]; site 2: the expert-parallel combine
-  uint32_t* state = nullptr;      // [3 sites][4] (rs target, ag target, CTAs done, spare); site 2 is
-                                  // the expert-parallel combine
+  uint32_t* state = nullptr;      // [3 sites][4] (rs target, ag target, CTAs done, the source-side CTA
+                                  // counter of the site's scatter GEMM); site 2 is the expert-parallel
+                                  // combine
   uint32_t* err = nullptr;
   int max_ctas = 148;
 };
@@ -53,8 +54,18 @@ inline int tp_rows_per_rank(int T, int nranks) { return (T + nranks - 1) / nrank
 // CTAs of rs_norm_ag for rpr rows per rank (the same on every rank).
 inline int tp_norm_ctas(int rpr, int max_ctas) { return rpr < 1 ? 1 : (rpr < max_ctas ? rpr : max_ctas); }
 
+// Two-level arrival counting (default; VMC_TP_TWO_LEVEL=0 turns it off): the CTAs of a signalling
+// kernel count themselves in their own GPU's memory and the last one signals each rank once, instead
+// of every CTA signalling every rank.
+bool tp_two_level();
+// The scatter GEMM's CTA counter of a site (gemm_tcgen05_scatter local_count), or null when every CTA
+// signals; tp_scatter_arrivals: the arrivals per call an owner then receives from all sources.
+inline uint32_t* tp_scatter_local(const TpComm& c, int site) { return tp_two_level() ? c.state + 4 * site + 3 : nullptr; }
+inline int tp_scatter_arrivals(const TpComm& c, int grid) { return tp_two_level() ? c.nranks : grid * c.nranks; }
+
 // Owner side of one row-parallel site: waits until every source rank's GEMM has delivered its
-// partial rows (rs_inc arrivals: sources x their GEMM's CTAs), sums the N * splits partials of each
+// partial rows (rs_inc arrivals: one per source rank when the GEMMs count through
+// tp_scatter_local, else sources x their GEMM's CTAs), sums the N * splits partials of each
 // owned row in a fixed order, adds the residual (fp32, updated in place for the owned rows only),
 // applies RMSNorm with weight w, and writes the bf16 row into every rank's h (all-gather by push).
 // CTA 0 returns only after every rank's rows have arrived here, so the next kernel may read all of h.

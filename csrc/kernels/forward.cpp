@@ -186,8 +186,8 @@ int Forward::moe_layer(const LayerDesc& lw, int l, const float* next_norm, int T
   const int grid = gemm_tcgen05_grouped_rowscatter(md.down.wf, md.down.w, md.down_stride, md.down.N, md.down.K,
                                                    mb.ep_act, rows_cap, md.f_local, md.e_local, counts,
                                                    mb.ep_offsets, max_rows, bn, mb.recv_ret[c.rank], mb.k, mb.comb,
-                                                   mb.comb_arrive, c.nranks, b_.err, st);
-  moe_combine_norm_ag(c, mb.comb[c.rank], mb.comb_arrive[c.rank], grid * c.nranks, mb.ep_topk_w, mb.k,
+                                                   mb.comb_arrive, c.nranks, b_.err, st, tp_scatter_local(c, 2));
+  moe_combine_norm_ag(c, mb.comb[c.rank], mb.comb_arrive[c.rank], tp_scatter_arrivals(c, grid), mb.ep_topk_w, mb.k,
                       mb.cnt[par][c.rank], md.e_local, T, c_.H, b_.resid, next_norm, c_.eps, st);
   return n + 4;
 }
@@ -305,8 +305,8 @@ int Forward::row_parallel(int site, const void* x, int ldx, const LinearDesc& w,
     const TpComm& c = comm_;
     int used = s;
     const int grid = gemm_tcgen05_scatter(w.wf, w.w, w.N, w.K, x, M, ldx, s, c.recv[site], c.rs_count[site],
-                                          c.nranks, c.rank, c.recv_rows, b_.err, st, &used);
-    rs_norm_ag(c, site, M, c_.H, used, grid * c.nranks, b_.resid, norm_w, c_.eps, st, gather);
+                                          c.nranks, c.rank, c.recv_rows, b_.err, st, &used, tp_scatter_local(c, site));
+    rs_norm_ag(c, site, M, c_.H, used, tp_scatter_arrivals(c, grid), b_.resid, norm_w, c_.eps, st, gather);
     return 2;
   }
   if (s > 1) {

@@ -251,9 +251,13 @@ struct GemmArgs {
   // output row m belongs to rank o = m / scat_rpr and is stored (bf16) as row m - o * scat_rpr of
   // slot (scat_rank * splits + split) of that rank's receive buffer scat[o] (row stride ldo, slots
   // scat_rpr rows apart). When a CTA has stored all its units it releases them (barrier over the
-  // epilogue warps, system-scope fence) and adds 1 to every rank's arrival counter scat_count[o].
+  // epilogue warps, system-scope fence) and counts itself on scat_local, a counter in this GPU's
+  // memory; the last of the grid's CTAs then adds 1 to every rank's arrival counter scat_count[o]
+  // (one arrival per source rank and call: a peer's counter takes N remote atomics, not N x grid).
+  // Without scat_local every CTA adds to every rank's counter.
   void* scat[8];
   uint32_t* scat_count[8];
+  uint32_t* scat_local;
   int scat_rpr, scat_rank, scat_nranks;
   // Row-scatter mode (kGemmOutRowScatterBF16, the combine of an expert-parallel MoE layer): output
   // row m goes to the rank, row and top-k slot packed in row_ret[m] ((rank << 24) | (row << 3) | j):
@@ -312,13 +316,27 @@ __device__ __forceinline__ void row_scatter_rows(const GemmArgs& a, int n, int m
   }
 }
 
-// After a CTA's last unit: make its peer stores visible, then count one arrival at every rank.
+// After a CTA's last unit: make its peer stores visible (system-scope fence), then count the arrival.
+// Hierarchical (scat_local set): each CTA adds itself to the local counter with a GPU-scope acq_rel
+// atomic; the CTA that completes the grid resets it, and its system-scope fence orders every CTA's
+// stores (acquired through the local counter) before its one arrival at each rank.
 __device__ __forceinline__ void scatter_release(const GemmArgs& a, int warp, int first_epi_warp, int lane) {
   epi_bar_sync();
   if (warp == first_epi_warp && lane == 0) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-    for (int q = 0; q < a.scat_nranks; ++q)
-      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.scat_count[q]) : "memory");
+    bool signal = true;
+    if (a.scat_local != nullptr) {
+      uint32_t old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.scat_local) : "memory");
+      signal = old == gridDim.x - 1;
+      if (signal) {
+        asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(a.scat_local) : "memory");
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+      }
+    }
+    if (signal)
+      for (int q = 0; q < a.scat_nranks; ++q)
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.scat_count[q]) : "memory");
   }
 }
 
@@ -1422,7 +1440,7 @@ int gemm_tcgen05(int wf, const void* w_tiled, int N, int K, const void* x, int M
 
 int gemm_tcgen05_scatter(int wf, const void* w_tiled, int N, int K, const void* x, int M, int ldx, int splits,
                          void* const* recv, uint32_t* const* counters, int nranks, int rank, int64_t recv_rows,
-                         uint32_t* err, cudaStream_t st, int* splits_used) {
+                         uint32_t* err, cudaStream_t st, int* splits_used, uint32_t* local_count) {
   VMC_CHECK(M > 0 && N > 0 && K > 0, "gemm_scatter: empty problem");
   VMC_CHECK(nranks >= 1 && nranks <= 8 && rank >= 0 && rank < nranks, "gemm_scatter: bad ranks");
   const int bn = gemm_pick_bn(M);
@@ -1436,6 +1454,7 @@ int gemm_tcgen05_scatter(int wf, const void* w_tiled, int N, int K, const void* 
   a.scat_rpr = rpr;
   a.scat_rank = rank;
   a.scat_nranks = nranks;
+  a.scat_local = local_count;
   if (splits_used) *splits_used = splits;
   if (use_streamk(wf, bn, a.m_tiles, splits, a.n_tiles)) apply_streamk(a, st);
   CUtensorMap map;
@@ -1486,7 +1505,8 @@ bool gemm_streamk() { return streamk_enabled(); }
 int gemm_tcgen05_grouped_rowscatter(int wf, const void* w_tiled, int64_t w_group_stride, int N, int K, const void* x,
                                     int rows_total, int ldx, int groups, const int32_t* counts, const int32_t* offsets,
                                     int max_rows, int bn, const int32_t* row_ret, int row_k, void* const* dst,
-                                    uint32_t* const* counters, int nranks, uint32_t* err, cudaStream_t st) {
+                                    uint32_t* const* counters, int nranks, uint32_t* err, cudaStream_t st,
+                                    uint32_t* local_count) {
   VMC_CHECK(rows_total > 0 && N > 0 && K > 0 && groups > 0 && max_rows > 0, "gemm_rowscatter: empty problem");
   VMC_CHECK(nranks >= 1 && nranks <= 8 && row_k >= 1 && row_k <= 8, "gemm_rowscatter: bad ranks / k");
   if (bn <= 0) bn = gemm_pick_bn(max_rows);
@@ -1517,6 +1537,7 @@ int gemm_tcgen05_grouped_rowscatter(int wf, const void* w_tiled, int64_t w_group
     a.scat_count[q] = q < nranks ? counters[q] : nullptr;
   }
   a.scat_nranks = nranks;
+  a.scat_local = local_count;
   a.row_ret = row_ret;
   a.row_k = row_k;
   CUtensorMap map;

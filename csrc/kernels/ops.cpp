@@ -574,11 +574,12 @@ int64_t tp_row_parallel(py::dict comm, int site, int wf, torch::Tensor w, int64_
                         torch::Tensor err) {
   const vmc::TpComm c = make_tp_comm(comm);
   int used = static_cast<int>(splits);
-  const int grid = vmc::gemm_tcgen05_scatter(wf, w.data_ptr(), static_cast<int>(N), static_cast<int>(K), x.data_ptr(),
-                                             static_cast<int>(M), static_cast<int>(x.stride(0)), static_cast<int>(splits),
-                                             c.recv[site], c.rs_count[site], c.nranks, c.rank, c.recv_rows,
-                                             ptr<uint32_t>(err), cur_stream(), &used);
-  vmc::rs_norm_ag(c, site, static_cast<int>(M), static_cast<int>(N), used, grid * c.nranks, ptr<float>(resid),
+  const int grid = vmc::gemm_tcgen05_scatter(
+      wf, w.data_ptr(), static_cast<int>(N), static_cast<int>(K), x.data_ptr(), static_cast<int>(M),
+      static_cast<int>(x.stride(0)), static_cast<int>(splits), c.recv[site], c.rs_count[site], c.nranks, c.rank,
+      c.recv_rows, ptr<uint32_t>(err), cur_stream(), &used, vmc::tp_scatter_local(c, site));
+  vmc::rs_norm_ag(c, site, static_cast<int>(M), static_cast<int>(N), used, vmc::tp_scatter_arrivals(c, grid),
+                  ptr<float>(resid),
                   ptr<float>(norm_w), static_cast<float>(eps), cur_stream());
   return used;
 }
