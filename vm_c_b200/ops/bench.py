@@ -37,6 +37,11 @@ GEMM_CASES = {
     "pre_down": (GType.Q4_K, 4096, 14336, 2048, OUT_F32_SPLIT),
     "pre_down6": (GType.Q6_K, 4096, 14336, 2048, OUT_F32_SPLIT),
     "pre_bf16": (GType.BF16, 8192, 4096, 2048, OUT_BF16),
+    # per-rank shapes of the 8B model at tensor parallel 8 (decode, 64 tokens)
+    "tp8_qkv": (GType.Q4_K, 768, 4096, 64, OUT_F32_SPLIT),
+    "tp8_o": (GType.Q4_K, 4096, 512, 64, OUT_F32_SPLIT),
+    "tp8_gu": (GType.Q4_K, 3584, 4096, 64, OUT_F32_SPLIT),
+    "tp8_down": (GType.Q4_K, 4096, 1792, 64, OUT_F32_SPLIT),
 }
 
 
@@ -66,7 +71,7 @@ def _time(fn, reps: int, flush: torch.Tensor) -> float:
     return sorted(ts)[len(ts) // 2]
 
 
-def bench_gemm(name: str, reps: int, flush: torch.Tensor) -> str:
+def bench_gemm(name: str, reps: int, flush: torch.Tensor, splits: int = 0) -> str:
     gt, N, K, M, mode = GEMM_CASES[name]
     g = torch.Generator(device="cuda").manual_seed(0)
     x32 = torch.randn(N, K, device="cuda", generator=g) * 0.02
@@ -75,7 +80,7 @@ def bench_gemm(name: str, reps: int, flush: torch.Tensor) -> str:
     w = tile_weight(raw, int(gt), N, K)
     del raw
     x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    s = effective_splits(w, pick_splits(w, M)) if mode == OUT_F32_SPLIT else 1
+    s = effective_splits(w, splits or pick_splits(w, M)) if mode == OUT_F32_SPLIT else 1
     if mode == OUT_SWIGLU:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
     elif mode == OUT_BF16:
@@ -105,18 +110,21 @@ def _paged_setup(ctx, qlen, Hq=32, Hkv=8, D=128, seed=0):
     return kv, bt.cuda(), q, qs, torch.tensor(ctx, dtype=torch.int32, device="cuda"), T
 
 
-def bench_attn(kind: str, reps: int, flush: torch.Tensor) -> str:
+def bench_attn(kind: str, reps: int, flush: torch.Tensor, splits: int = 0) -> str:
     Hq, Hkv, D = 32, 8, 128
     if kind == "decode":
         ctx, ql = [1280] * 64, [1] * 64
+    elif kind == "decode_tp8":  # one rank of tensor parallel 8: 4 query heads, 1 KV head
+        Hq, Hkv = 4, 1
+        ctx, ql = [1040] * 64, [1] * 64
     elif kind == "prefill2":  # two 1024-token prompts: the 2048-token chunked-prefill step of serving
         ctx, ql = [1024, 1024], [1024, 1024]
     else:
         ctx, ql = [2048], [2048]
     kv, bt, q, qs, cl, T = _paged_setup(ctx, ql, Hq, Hkv, D)
     out = torch.empty_like(q)
-    dec = kind == "decode"
-    s = decode_splits(len(ctx) * Hkv, decode_slots(D)) if dec else 1
+    dec = kind.startswith("decode")
+    s = (splits or decode_splits(len(ctx) * Hkv, decode_slots(D))) if dec else 1
     po = torch.empty(s, T, Hq, D, device="cuda") if s > 1 else None
     pl = torch.empty(s, T, Hq, device="cuda") if s > 1 else None
     t = _time(lambda: paged_attention(q, kv, qs, cl, bt, len(ctx), 0, max(ql), T, Hq, Hkv, D, 1 / math.sqrt(D), dec,
@@ -239,19 +247,21 @@ def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("cases", nargs="*", default=["all"])
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--splits", type=int, default=0,
+                    help="force the split count: K splits of gemm cases with split-K output, KV splits of decode attention")
     a = ap.parse_args(argv)
     cases = a.cases
     if cases == ["all"]:
-        cases = [f"gemm:{k}" for k in GEMM_CASES] + ["attn:decode", "attn:prefill", "attn:prefill2", "norm", "rope",
+        cases = [f"gemm:{k}" for k in GEMM_CASES if not k.startswith("tp8_")] + ["attn:decode", "attn:prefill", "attn:prefill2", "norm", "rope",
                                                       "swiglu", "sample", "gdn:decode", "gdn:prefill2"]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for c in cases:
         if c.startswith("gemm:"):
-            line = bench_gemm(c[5:], a.reps, flush)
+            line = bench_gemm(c[5:], a.reps, flush, a.splits)
         elif c.startswith("step:"):
             line = bench_step(c[5:], min(a.reps, 10))
         elif c.startswith("attn:"):
-            line = bench_attn(c[5:], a.reps, flush)
+            line = bench_attn(c[5:], a.reps, flush, a.splits)
         elif c.startswith("gdn:"):
             line = bench_gdn(c[4:], a.reps, flush)
         else:
