@@ -405,7 +405,7 @@ void ar_add_rmsnorm(const ArArgs& a, int max_ctas, cudaStream_t st) {
 bool tp_two_level() {
   static const bool on = [] {
     const char* e = std::getenv("VMC_TP_TWO_LEVEL");
-    return !(e && std::strcmp(e, "0") == 0);
+    return e && std::strcmp(e, "1") == 0;
   }();
   return on;
 }

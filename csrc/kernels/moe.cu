@@ -209,21 +209,15 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(MoeDispatchArgs a) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    // Each CTA releases its peer stores at system scope and counts itself locally (GPU-scope acq_rel);
-    // the CTA that completes the grid advances the next call's target and signals every rank once.
-    // CTA 0 returns when every rank's dispatch has arrived here.
-    const uint32_t G = gridDim.x;
-    const uint32_t target = a.state[0] + static_cast<uint32_t>(a.nranks);  // read before counting itself
     sys_fence();
-    uint32_t old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.state + 1) : "memory");
-    if (old == G - 1) {
-      a.state[0] += static_cast<uint32_t>(a.nranks);
+    for (int q = 0; q < a.nranks; ++q) sys_count(a.arrive[q], 1u);
+    const uint32_t G = gridDim.x;
+    if (blockIdx.x == 0) sys_wait(a.arrive[a.rank], a.state[0] + a.nranks * G, a.err, kErrCommWait);
+    if (atomicAdd(a.state + 1, 1u) == G - 1) {
+      a.state[0] += a.nranks * G;
       a.state[1] = 0;
-      sys_fence();
-      for (int q = 0; q < a.nranks; ++q) sys_count(a.arrive[q], 1u);
+      __threadfence();
     }
-    if (blockIdx.x == 0) sys_wait(a.arrive[a.rank], target, a.err, kErrCommWait);
   }
 }
 

@@ -33,9 +33,8 @@ void moe_combine(const float* y, int ldy, const int32_t* slot_row, const float* 
 // on e's owner rank (o = e / e_local) with an atomic add on that rank's per-expert row counter, stores
 // the bf16 row there (row slot of expert e % e_local in recv_x[o], `cap` rows per expert) together with
 // a return word (rank << 24) | (row << 3) | j, and keeps the weight in topk_w[row * k + j]. Every CTA
-// then releases its stores; the last CTA of the grid counts one arrival at every rank (one per source
-// rank and call); CTA 0 returns once all ranks' dispatches have arrived here, so the expert GEMMs that
-// follow may read their rows and counts.
+// then releases its stores and counts one arrival at every rank; CTA 0 returns once all ranks'
+// dispatches have arrived here, so the expert GEMMs that follow may read their rows and counts.
 struct MoeDispatchArgs {
   const float* logits;   // this rank's rows [rows][ld_logits]
   int ld_logits;
@@ -46,7 +45,7 @@ struct MoeDispatchArgs {
   uint32_t* cnt[8];      // every rank's per-expert row counters [e_local] (this layer's parity)
   float* topk_w;         // this rank: [rpr][k]
   uint32_t* arrive[8];   // every rank's dispatch arrival counter
-  uint32_t* state;       // this rank: [0] arrival target, [1] CTAs of the current call counted
+  uint32_t* state;       // this rank: [0] arrival target, [1] CTAs done
   uint32_t* err;
 };
 void moe_dispatch(const MoeDispatchArgs& a, cudaStream_t st);
