@@ -73,6 +73,9 @@ def parse():
     return a
 
 
+WEIGHTS = {2: "Q4_K_M", 3: "Q8_0", 4: "Q4_K", 5: "BF16 (target) and Q8_0 (draft)"}
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
@@ -300,6 +303,7 @@ def main():
         st = spec.stats.as_dict()
         extra_keys["spec"] = {"tree": args.spec_tree, "self_draft": args.self_draft, **st,
                               "accepted_tok_per_s": round(value, 2)}
+    wgb = llm.runner.weights.bytes_total / 1e9
     if rank == 0:
         model_name = {3: "Llama-3-70B (random-init, Q8_0 GGUF)", 4: "Mixtral-8x7B (random-init, Q4_K GGUF)",
                       5: "Llama-3-8B (random-init, BF16 GGUF) + 16-layer draft (Q8_0)"}.get(args.config, MODEL)
@@ -308,13 +312,13 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: random-init Q4_K_M weights generated on device in GGUF block format; "
-                    "uniform-random prompt token ids (seeded, fresh per run)",
+            "data": f"synthetic: random-init {WEIGHTS.get(args.config, 'Q4_K_M')} weights generated on device in GGUF "
+                    "block format; uniform-random prompt token ids (seeded, fresh per run)",
             "config": {"model": model_name, "global_batch": R, "seq_len": P, "gen_len": G, "parallelism": par,
                        "kv_cache": args.kv_cache_dtype or "paged bf16, block 16",
                        "max_num_batched_tokens": args.max_num_batched_tokens,
                        "comm": args.comm if world > 1 else "none",
-                       "l2": "inputs larger than L2 (4.9 GB weights + KV streamed every step)",
+                       "l2": f"inputs larger than L2 ({wgb:.1f} GB of weights per rank + KV streamed every step)",
                        "step": "one full serving run of global_batch requests"},
             "p50_ttft_ms": round(summ["p50_ttft_ms"], 2), "p50_itl_ms": round(summ["p50_itl_ms"], 3),
             "e2e": {"value": round(e2e, 2), "unit": "output tokens/s (LLM.generate, wall clock)",

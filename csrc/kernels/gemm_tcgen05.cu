@@ -115,11 +115,6 @@ __device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) 
                              *reinterpret_cast<__nv_bfloat162*>(&c));
   return *reinterpret_cast<uint32_t*>(&r);
 }
-__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
-  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t bf2_splat(float f) { return pack_bf16x2(f, f); }
 // Single-instruction forms for the dequant inner loops. Measured on B200: the bit operations and
 // the packed bf16 ops each issue at 2 warp-instructions per cycle per SM, and the generic
 // __nv_bfloat162 helpers above cost the integer pipe extra instructions on this toolchain.

@@ -28,7 +28,6 @@ constexpr int kMaxExperts = 64;
 constexpr int kMaxTopK = 8;
 
 __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(MoeRouteArgs a) {
-  __shared__ int s_count[kMaxExperts];
   __shared__ int s_warp[kRouteThreads / 32];
   pdl_trigger();
   pdl_wait();
@@ -93,7 +92,6 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(MoeRouteArgs a
       __syncthreads();
     }
     if (tid == 0) {
-      s_count[el] = run;
       a.counts[el] = run;
       a.offsets[el] = base;
     }

@@ -376,7 +376,7 @@ int decode_splits(int ctas, int slots, int max_splits = 16) {
   const int sms = slots >= 148 ? slots / std::max(1, slots / 148) : slots;
   ctas = std::max(1, ctas);
   if (ctas >= sms) return 1;
-  return std::max(1, std::min(max_splits, (2 * sms + ctas - 1) / ctas));
+  return std::max(1, std::min(max_splits, sms / ctas));
 }
 
 double now_ms() {
