@@ -4,10 +4,13 @@ Two extensions:
   * ``_host``  — C++17 host runtime (GGUF, quant codecs, block manager, scheduler). No CUDA.
   * ``_cuda``  — sm_100a kernels (tcgen05 / TMA GEMMs, attention, norms, sampling, comm) and their
                  launchers. Compiled only for ``sm_100a``; nothing else is generated.
-and one executable:
+and two executables:
   * ``vmc_run`` — the serving loop without Python or PyTorch (csrc/runtime/vmc_run.cpp): the same
                  kernels, native forward, scheduler and GGUF reader, linked against the CUDA runtime
-                 and driver only.
+                 and driver only;
+  * ``vmc_tsan_stress`` — the host library (scheduler, block manager, quant codecs, BPE core) built
+                 with ThreadSanitizer around a multi-threaded stress driver (csrc/host/tsan_stress.cpp;
+                 run by tests/test_tsan_host.py, not part of build()).
 
 The shared objects land in ``vm_c_b200/_ext/<name>/`` so that they travel with a copy of the
 repository; :mod:`vm_c_b200._native` imports them from there without invoking the compiler.
@@ -108,6 +111,33 @@ def build_runtime(verbose: bool = False) -> Path:
     return exe
 
 
+TSAN_HOST = ["host/scheduler.cpp", "host/block_manager.cpp", "host/quants.cpp", "host/tokenizer.cpp",
+             "host/tsan_stress.cpp"]
+
+
+def build_tsan(verbose: bool = False) -> Path:
+    """Compile vm_c_b200/_ext/tsan/vmc_tsan_stress with -fsanitize=thread (rebuilt when a host source
+    or header is newer than the executable)."""
+    import shutil
+    import subprocess
+    out = EXT_DIR / "tsan"
+    out.mkdir(parents=True, exist_ok=True)
+    exe = out / "vmc_tsan_stress"
+    srcs = [CSRC / s for s in TSAN_HOST]
+    newest = max(p.stat().st_mtime for p in srcs + list((CSRC / "host").glob("*.hpp")))
+    if exe.exists() and exe.stat().st_mtime >= newest:
+        return exe
+    cxx = shutil.which("g++") or "c++"
+    cmd = [cxx, "-std=c++17", "-O1", "-g", "-fsanitize=thread", "-pthread", f"-I{CSRC / 'host'}"] + \
+        [str(p) for p in srcs] + ["-o", str(exe)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ThreadSanitizer build failed:\n{r.stderr[-4000:]}")
+    if verbose:
+        print("built", exe)
+    return exe
+
+
 def build_all(verbose: bool = False) -> None:
     build_host(verbose)
     build_cuda(verbose)
@@ -123,3 +153,5 @@ if __name__ == "__main__":
         build_cuda(v)
     if what in ("runtime", "all"):
         build_runtime(v)
+    if what == "tsan":
+        build_tsan(v)
