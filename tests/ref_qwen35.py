@@ -133,8 +133,10 @@ def new_state(cfg):
     return {"pos": 0, "layers": st}
 
 
-def forward(W, cfg, tokens, state):
-    """Logits [T, V] of `tokens` continuing from `state` (updated in place)."""
+def forward(W, cfg, tokens, state, margins=None):
+    """Logits [T, V] of `tokens` continuing from `state` (updated in place). With `margins` (a list),
+    appends per layer and token the gap between the k-th and (k+1)-th router logit relative to the
+    largest router logit magnitude (how close the expert choice is to a tie)."""
     T, eps, D = len(tokens), cfg.rms_eps, cfg.head_dim
     pos = torch.arange(state["pos"], state["pos"] + T)
     h = W["token_embd.weight"][torch.tensor(tokens)]
@@ -174,7 +176,11 @@ def forward(W, cfg, tokens, state):
             a = o.reshape(T, Hq * D) @ W[b + "attn_output.weight"].T
         h = h + a
         x2 = _rms(h, W[b + "post_attention_norm.weight"], eps)
-        probs = torch.softmax(x2 @ W[b + "ffn_gate_inp.weight"].T, -1)
+        rl = x2 @ W[b + "ffn_gate_inp.weight"].T
+        if margins is not None:
+            top = torch.topk(rl, cfg.n_experts_used + 1, -1).values
+            margins.append((top[:, -2] - top[:, -1]) / rl.abs().max(-1).values.clamp_min(1e-30))
+        probs = torch.softmax(rl, -1)
         wts, idx = torch.topk(probs, cfg.n_experts_used, -1)
         wts = wts / wts.sum(-1, keepdim=True)
         E, F, H = cfg.n_experts, cfg.ffn, cfg.hidden

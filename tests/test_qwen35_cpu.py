@@ -47,11 +47,13 @@ def test_oracle_state_carry(model):
     assert torch.isfinite(full).all() and float(full.std()) > 0
 
 
-def test_serving_refused_with_message(model):
+def test_tensor_parallel_refused_with_message(model):
+    # The family is served on one GPU; a tensor-parallel load is refused after the tensor check,
+    # before anything is moved to a device.
     src, cfg = model
     from vm_c_b200.models.llama import load_weights
     with pytest.raises(ValueError, match="qwen35moe"):
-        load_weights(src, cfg, "cpu")
+        load_weights(src, cfg, "cpu", 0, 2)
 
 
 @pytest.mark.parametrize("chunk", [1, 16, 64])

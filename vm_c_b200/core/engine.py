@@ -79,7 +79,9 @@ class LLMEngine:
         sc.decode_reserved_tokens = s.decode_reserved_tokens
         sc.num_lookahead_tokens = getattr(runner, "num_lookahead_tokens", 0)
         self.block_size = cfg.cache.block_size
-        self.bm = self.h.BlockManager(runner.num_kv_blocks, self.block_size, cfg.cache.enable_prefix_caching)
+        # Hybrid (recurrent-state) models cannot resume from cached KV blocks: no prefix caching there.
+        self.bm = self.h.BlockManager(runner.num_kv_blocks, self.block_size,
+                                      cfg.cache.enable_prefix_caching and not cfg.model.is_hybrid)
         self.sched = self.h.Scheduler(sc, self.bm)
         max_blocks = (cfg.model.max_model_len + sc.num_lookahead_tokens + self.block_size - 1) // self.block_size + 1
         max_tok = max(s.max_num_batched_tokens, s.max_num_seqs, runner.max_graph_batch())

@@ -50,7 +50,7 @@ PRESETS: dict[str, ModelConfig] = {
     # small hybrid gated delta-net model (Qwen3.5-MoE architecture): layers 0-2 GDN, layer 3 full
     # attention with partial RoPE, 4 experts (top-2) plus a shared expert
     "tiny-qwen35moe": ModelConfig(arch="qwen35moe", name="tiny-qwen35moe", n_layers=4, hidden=256, n_heads=4,
-                                  n_kv_heads=2, head_dim=64, ffn=128, vocab=32000, rms_eps=1e-6,
+                                  n_kv_heads=2, head_dim=64, ffn=256, vocab=32000, rms_eps=1e-6,
                                   rope_theta=10000000.0, rope_neox=True, context_length=2048, n_experts=4,
                                   n_experts_used=2, bos_token_id=1, eos_token_ids=[2], rope_dims=16, ssm_conv=4,
                                   ssm_state=64, ssm_k_heads=2, ssm_v_heads=4, full_attn_interval=4, ffn_shexp=256),

@@ -121,10 +121,8 @@ def _tile_raw(raw: torch.Tensor, gtype: int, N: int, K: int) -> ops.TiledWeight:
 def load_weights(src, cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1, ep_size: int = 1) -> ModelWeights:
     """Load (and shard) the weights of a llama-architecture model from a tensor source."""
     if cfg.is_hybrid:
-        from .hybrid import check_hybrid_tensors
-        check_hybrid_tensors(src, cfg)
-        raise ValueError("GGUF architecture 'qwen35moe' (hybrid gated delta-net) cannot be served yet: its "
-                         "linear-attention kernels exist (csrc/kernels/gdn.cu) but the model is not wired")
+        from .qwen35 import load_hybrid_weights
+        return load_hybrid_weights(src, cfg, device, tp_rank, tp_size)
     check_tp(cfg, tp_size)
     dev = torch.device(device)
     D = cfg.head_dim
@@ -239,6 +237,7 @@ class StepMeta:
     decode_qlen: int = 1
     tree_mask: torch.Tensor | None = None  # int64 [T]: token-tree masks (prefill path)
     tree_span: int = 0                     # bit 0 of a mask = key at position ctx - tree_span
+    seq_slot: torch.Tensor | None = None   # int32 [R]: the scheduler's sequence slot of each request
 
 
 @dataclass

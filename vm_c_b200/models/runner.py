@@ -27,13 +27,16 @@ log = get_logger("runner")
 GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256]
 
 
-def kv_bytes_per_block(cfg: VmCConfig, hkv_local: int, dtype_bytes: int = 2) -> int:
+def kv_bytes_per_block(cfg: VmCConfig, hkv_local: int, dtype_bytes: int = 2, n_layers: int = 0) -> int:
+    """KV bytes of one block over the layers that keep a KV cache (all layers unless n_layers is given:
+    the full-attention layers of a hybrid model)."""
     m = cfg.model
+    L = n_layers or m.n_layers
     if is_turboquant(cfg.cache.kv_cache_dtype):
         from .. import _native
         slot = _native.host().tq_layout(cfg.cache.kv_cache_dtype, m.head_dim)["slot_aligned"]
-        return m.n_layers * cfg.cache.block_size * hkv_local * slot
-    return m.n_layers * 2 * hkv_local * cfg.cache.block_size * m.head_dim * dtype_bytes
+        return L * cfg.cache.block_size * hkv_local * slot
+    return L * 2 * hkv_local * cfg.cache.block_size * m.head_dim * dtype_bytes
 
 
 def is_turboquant(kv_cache_dtype: str) -> bool:
@@ -88,9 +91,22 @@ class GpuModelRunner(ModelRunner):
         if self.tracer is not None and use_graphs:
             log.warning("VMC_LOG_HIDDEN / VMC_LOG_LOGITS set: decode steps run eagerly (no CUDA graphs)")
             use_graphs = False
+        if m.is_hybrid:
+            # Qwen3.5-MoE: one GPU, eager steps, bf16 KV, no speculation or offload (models/qwen35.py)
+            if sp.method:
+                raise ValueError("speculative decoding is not implemented for GGUF architecture 'qwen35moe'")
+            if is_turboquant(cfg.cache.kv_cache_dtype):
+                raise ValueError("TurboQuant KV caches are not implemented for GGUF architecture 'qwen35moe'")
+            if cfg.cache.cpu_offload_gb > 0:
+                raise ValueError("CPU weight offload is not implemented for GGUF architecture 'qwen35moe'")
+            use_graphs = False
         self.use_graphs = use_graphs
-        self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len + self.spec_k, comm=comm,
-                                attn_splits=16)
+        if m.is_hybrid:
+            from .qwen35 import HybridModel
+            self.model = HybridModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len, max_seqs)
+        else:
+            self.model = LlamaModel(self.weights, self.max_tokens, self.max_samples, m.max_model_len + self.spec_k,
+                                    comm=comm, attn_splits=16)
         self.comm = comm
         sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
         self._decode_slots = sms * max(1, ops.C().attn_decode_ctas_per_sm(self.model.D))
@@ -102,7 +118,8 @@ class GpuModelRunner(ModelRunner):
             self.tq = ops.TqTables(cfg.cache.kv_cache_dtype, m.head_dim, self.dev, rot_seed=cfg.cache.tq_rotation_seed)
         self.model.tq = self.tq
         self.model.tracer = self.tracer
-        per_block = kv_bytes_per_block(cfg, self.model.hkv)
+        n_kv_layers = getattr(self.model, "n_kv_layers", m.n_layers)
+        per_block = kv_bytes_per_block(cfg, self.model.hkv, n_layers=n_kv_layers)
         max_blocks_per_seq = (m.max_model_len + cfg.cache.block_size - 1) // cfg.cache.block_size + 1
         want = cfg.cache.num_gpu_blocks
         if want <= 0:
@@ -114,7 +131,7 @@ class GpuModelRunner(ModelRunner):
             want = min(want, 2 * s.max_num_seqs * max_blocks_per_seq + 1)
         self.num_kv_blocks = int(want)
         if self.tq is None:
-            self.kv = torch.zeros(m.n_layers, self.num_kv_blocks, 2, self.model.hkv, cfg.cache.block_size,
+            self.kv = torch.zeros(n_kv_layers, self.num_kv_blocks, 2, self.model.hkv, cfg.cache.block_size,
                                   m.head_dim, dtype=torch.bfloat16, device=self.dev)
         else:
             self.kv = torch.zeros(m.n_layers, self.num_kv_blocks, cfg.cache.block_size, self.model.hkv,
@@ -168,6 +185,7 @@ class GpuModelRunner(ModelRunner):
         self.v_qs = md[L.off_q_start:L.off_q_start + L.max_reqs + 1]
         self.v_ctx = md[L.off_ctx_len:L.off_ctx_len + L.max_reqs]
         self.v_lidx = md[L.off_logits_idx:L.off_logits_idx + L.max_reqs]
+        self.v_sslot = md[L.off_seq_slot:L.off_seq_slot + L.max_reqs]
         self.v_bt = md[L.off_block_tables:L.off_block_tables + L.max_reqs * L.max_blocks_per_seq].view(
             L.max_reqs, L.max_blocks_per_seq)
 
@@ -198,7 +216,7 @@ class GpuModelRunner(ModelRunner):
 
     def _meta(self, T, R, S, nd, max_qlen) -> StepMeta:
         return StepMeta(self.v_ids, self.v_pos, self.v_slots, self.v_qs, self.v_ctx, self.v_bt, self.v_lidx,
-                        T=T, R=R, S=S, num_decode=nd, max_qlen=max_qlen)
+                        T=T, R=R, S=S, num_decode=nd, max_qlen=max_qlen, seq_slot=self.v_sslot)
 
     def _attn_splits(self, nd: int) -> int:
         return ops.decode_splits(nd * self.model.hkv, self._decode_slots)
