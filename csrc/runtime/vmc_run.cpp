@@ -114,6 +114,7 @@ struct DevBuf {
 
 struct Hyper {
   int L, H, Hq, Hkv, D, F, V;
+  int E = 0, K = 0;  // experts per layer and experts used per token (0: dense FFN)
   float eps, theta;
   bool neox = false;
   int ctx;
@@ -137,7 +138,9 @@ Hyper read_hyper(const vmc::GgufFile& f) {
   h.eps = static_cast<float>(f.get_float("llama.attention.layer_norm_rms_epsilon", 1e-5));
   h.theta = static_cast<float>(f.get_float("llama.rope.freq_base", 10000.0));
   h.ctx = static_cast<int>(f.get_int("llama.context_length", 4096));
-  if (f.get_int("llama.expert_count", 0) > 0) throw std::runtime_error("vmc_run: MoE models take the Python engine");
+  h.E = static_cast<int>(f.get_int("llama.expert_count", 0));
+  h.K = static_cast<int>(f.get_int("llama.expert_used_count", h.E > 0 ? 2 : 0));
+  if (h.E > 32) throw std::runtime_error("vmc_run: at most 32 experts per layer");
   const vmc::GTensorInfo* emb = f.find_tensor("token_embd.weight");
   if (!emb) throw std::runtime_error("token_embd.weight missing");
   h.V = static_cast<int>(f.get_int("llama.vocab_size", emb->ne[1]));
@@ -236,6 +239,27 @@ class Loader {
     out.d.K = K;
     return out;
   }
+  // Gate / up rows [F, K] interleaved (row 2f = gate f, row 2f + 1 = up f) for the fused SwiGLU
+  // epilogue; raw blocks when both share a type, else dequantised rows tiled as bf16.
+  Tiled tile_gate_up(GType tg, const std::vector<uint8_t>& g, GType tu, const std::vector<uint8_t>& u, int F, int K) {
+    if (tg == tu) {
+      const size_t rb = vmc::gtype_row_bytes(tg, K);
+      std::vector<uint8_t> inter(2 * rb * F);
+      for (int r = 0; r < F; ++r) {
+        memcpy(inter.data() + (2 * r) * rb, g.data() + r * rb, rb);
+        memcpy(inter.data() + (2 * r + 1) * rb, u.data() + r * rb, rb);
+      }
+      return tile(tg, inter, 2 * F, K);
+    }
+    const auto gf = as_f32(tg, g, static_cast<int64_t>(F) * K), uf = as_f32(tu, u, static_cast<int64_t>(F) * K);
+    std::vector<float> inter(2 * static_cast<size_t>(F) * K);
+    for (int r = 0; r < F; ++r) {
+      memcpy(&inter[(2 * static_cast<size_t>(r)) * K], &gf[static_cast<size_t>(r) * K], K * 4);
+      memcpy(&inter[(2 * static_cast<size_t>(r) + 1) * K], &uf[static_cast<size_t>(r) * K], K * 4);
+    }
+    std::vector<uint8_t> raw(reinterpret_cast<uint8_t*>(inter.data()), reinterpret_cast<uint8_t*>(inter.data() + inter.size()));
+    return tile(GType::F32, raw, 2 * F, K);
+  }
   Tiled tile_tensor(const std::string& n) {
     const auto& t = info(n);
     return tile(t.type, rows(n, 0, t.ne[1]), static_cast<int>(t.ne[1]), static_cast<int>(t.ne[0]));
@@ -274,6 +298,53 @@ struct Model {
   vmc::LinearDesc lm_head;
   DevBuf cos_sin;
 };
+
+// One Mixtral layer's experts (all of them on this GPU, the expert-sliced layout of one rank): the
+// router [E, H] as bf16 tiles, then every expert's interleaved gate/up and its down projection tiled
+// and packed back to back (one grouped GEMM per projection reads expert e at e * stride).
+void load_moe(Loader& ld, Model& m, int i, vmc::LayerDesc& d) {
+  const Hyper& h = m.h;
+  const int E = h.E, F = h.F, H = h.H;
+  d.moe = true;
+  vmc::MoeDesc& md = d.m;
+  const auto& tr = ld.info(blk(i, "ffn_gate_inp"));
+  const auto rf = ld.as_f32(tr.type, ld.rows(blk(i, "ffn_gate_inp"), 0, E), static_cast<int64_t>(E) * H);
+  const std::vector<uint8_t> rraw(reinterpret_cast<const uint8_t*>(rf.data()),
+                                  reinterpret_cast<const uint8_t*>(rf.data() + rf.size()));
+  m.tiles.push_back(ld.tile(GType::F32, rraw, E, H));
+  md.router = m.tiles.back().d;
+  const auto& tg = ld.info(blk(i, "ffn_gate_exps"));
+  const auto& tu = ld.info(blk(i, "ffn_up_exps"));
+  const auto& td = ld.info(blk(i, "ffn_down_exps"));
+  Tiled gu_all, dn_all;
+  for (int e = 0; e < E; ++e) {
+    const int64_t f0 = static_cast<int64_t>(e) * F, h0 = static_cast<int64_t>(e) * H;
+    Tiled gu = ld.tile_gate_up(tg.type, ld.rows(blk(i, "ffn_gate_exps"), f0, f0 + F), tu.type,
+                               ld.rows(blk(i, "ffn_up_exps"), f0, f0 + F), F, H);
+    Tiled dn = ld.tile(td.type, ld.rows(blk(i, "ffn_down_exps"), h0, h0 + H), H, F);
+    if (e == 0) {
+      gu_all.buf = DevBuf(gu.buf.n * E, false);
+      gu_all.d = gu.d;
+      gu_all.d.w = gu_all.buf.p;
+      dn_all.buf = DevBuf(dn.buf.n * E, false);
+      dn_all.d = dn.d;
+      dn_all.d.w = dn_all.buf.p;
+    }
+    if (gu.d.wf != gu_all.d.wf || gu.buf.n * E != gu_all.buf.n || dn.d.wf != dn_all.d.wf || dn.buf.n * E != dn_all.buf.n)
+      throw std::runtime_error("vmc_run: the experts of layer " + std::to_string(i) + " differ in weight type");
+    CK(cudaMemcpy(gu_all.buf.as<uint8_t>() + gu.buf.n * e, gu.buf.p, gu.buf.n, cudaMemcpyDeviceToDevice));
+    CK(cudaMemcpy(dn_all.buf.as<uint8_t>() + dn.buf.n * e, dn.buf.p, dn.buf.n, cudaMemcpyDeviceToDevice));
+  }
+  md.gate_up = gu_all.d;
+  md.gate_up_stride = static_cast<int64_t>(gu_all.buf.n / E);
+  md.down = dn_all.d;
+  md.down_stride = static_cast<int64_t>(dn_all.buf.n / E);
+  md.e0 = 0;
+  md.e_local = E;
+  md.f_local = F;
+  m.tiles.push_back(std::move(gu_all));
+  m.tiles.push_back(std::move(dn_all));
+}
 
 Model load(const std::string& path, int max_pos, cudaStream_t st) {
   auto f = vmc::GgufFile::open(path);
@@ -315,31 +386,17 @@ Model load(const std::string& path, int max_pos, cudaStream_t st) {
     }
     m.tiles.push_back(ld.tile_tensor(blk(i, "attn_output")));
     d.wo = m.tiles.back().d;
-    // gate / up with rows interleaved (row 2f = gate f, row 2f + 1 = up f) for the fused SwiGLU
-    const auto& tg = ld.info(blk(i, "ffn_gate"));
-    const auto& tu = ld.info(blk(i, "ffn_up"));
-    const auto g = ld.rows(blk(i, "ffn_gate"), 0, h.F), u = ld.rows(blk(i, "ffn_up"), 0, h.F);
-    if (tg.type == tu.type) {
-      const size_t rb = vmc::gtype_row_bytes(tg.type, H);
-      std::vector<uint8_t> inter(2 * rb * h.F);
-      for (int r = 0; r < h.F; ++r) {
-        memcpy(inter.data() + (2 * r) * rb, g.data() + r * rb, rb);
-        memcpy(inter.data() + (2 * r + 1) * rb, u.data() + r * rb, rb);
-      }
-      m.tiles.push_back(ld.tile(tg.type, inter, 2 * h.F, H));
+    if (h.E > 0) {
+      load_moe(ld, m, i, d);
     } else {
-      const auto gf = ld.as_f32(tg.type, g, static_cast<int64_t>(h.F) * H), uf = ld.as_f32(tu.type, u, static_cast<int64_t>(h.F) * H);
-      std::vector<float> inter(2 * static_cast<size_t>(h.F) * H);
-      for (int r = 0; r < h.F; ++r) {
-        memcpy(&inter[(2 * static_cast<size_t>(r)) * H], &gf[static_cast<size_t>(r) * H], H * 4);
-        memcpy(&inter[(2 * static_cast<size_t>(r) + 1) * H], &uf[static_cast<size_t>(r) * H], H * 4);
-      }
-      std::vector<uint8_t> raw(reinterpret_cast<uint8_t*>(inter.data()), reinterpret_cast<uint8_t*>(inter.data() + inter.size()));
-      m.tiles.push_back(ld.tile(GType::F32, raw, 2 * h.F, H));
+      const auto& tg = ld.info(blk(i, "ffn_gate"));
+      const auto& tu = ld.info(blk(i, "ffn_up"));
+      m.tiles.push_back(ld.tile_gate_up(tg.type, ld.rows(blk(i, "ffn_gate"), 0, h.F), tu.type,
+                                        ld.rows(blk(i, "ffn_up"), 0, h.F), h.F, H));
+      d.gate_up = m.tiles.back().d;
+      m.tiles.push_back(ld.tile_tensor(blk(i, "ffn_down")));
+      d.down = m.tiles.back().d;
     }
-    d.gate_up = m.tiles.back().d;
-    m.tiles.push_back(ld.tile_tensor(blk(i, "ffn_down")));
-    d.down = m.tiles.back().d;
     m.norms.push_back(ld.norm(blk(i, "attn_norm")));
     d.attn_norm = m.norms.back().as<float>();
     m.norms.push_back(ld.norm(blk(i, "ffn_norm")));
@@ -401,6 +458,10 @@ struct Engine {
   // buffers
   DevBuf resid, h, qkv_bf16, split_ws, q, attn, o16, act, hs, logits, part_o, part_lse, kv, meta_dev, params_dev,
       tok_dev, lp_dev, err;
+  // MoE (expert-sliced, all experts on this GPU): router logits, routing tables, gathered rows, expert
+  // activations and outputs, combined output
+  DevBuf moe_logits, moe_topk_id, moe_topk_w, moe_counts, moe_offsets, moe_sorted, moe_slot_row, moe_total, moe_xs,
+      moe_act, moe_y, moe_out;
   int32_t* meta_host = nullptr;
   vmc::SampleParams* params_host = nullptr;
   int32_t* tok_host = nullptr;
@@ -501,6 +562,39 @@ struct Engine {
     b.kv_layer_bytes = kv_layer;
     b.err = err.as<uint32_t>();
     fwd = std::make_unique<vmc::Forward>(c, m.layers, b);
+    if (hp.E > 0) {
+      const size_t R = static_cast<size_t>(T) * hp.K;
+      moe_logits = DevBuf(static_cast<size_t>(T) * hp.E * 4);
+      moe_topk_id = DevBuf(R * 4);
+      moe_topk_w = DevBuf(R * 4);
+      moe_counts = DevBuf(static_cast<size_t>(hp.E) * 4);
+      moe_offsets = DevBuf(static_cast<size_t>(hp.E) * 4);
+      moe_sorted = DevBuf(R * 4);
+      moe_slot_row = DevBuf(R * 4);
+      moe_total = DevBuf(4);
+      moe_xs = DevBuf(R * H * 2);
+      moe_act = DevBuf(R * hp.F * 2);
+      moe_y = DevBuf(R * H * 4);
+      moe_out = DevBuf(static_cast<size_t>(T) * H * 4);
+      vmc::MoeBuffers mb;
+      mb.E = hp.E;
+      mb.k = hp.K;
+      mb.norm_topk = 1;  // Mixtral renormalises the selected weights
+      mb.ep = false;
+      mb.logits = moe_logits.as<float>();
+      mb.topk_id = moe_topk_id.as<int32_t>();
+      mb.topk_w = moe_topk_w.as<float>();
+      mb.counts = moe_counts.as<int32_t>();
+      mb.offsets = moe_offsets.as<int32_t>();
+      mb.sorted_src = moe_sorted.as<int32_t>();
+      mb.slot_row = moe_slot_row.as<int32_t>();
+      mb.total = moe_total.as<int32_t>();
+      mb.xs = moe_xs.p;
+      mb.act = moe_act.p;
+      mb.y = moe_y.as<float>();
+      mb.out = moe_out.as<float>();
+      fwd->set_moe(mb);
+    }
   }
 
   ~Engine() {

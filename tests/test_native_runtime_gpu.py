@@ -34,9 +34,11 @@ def test_runtime_links_no_torch(exe):
     assert "torch" not in out and "python" not in out, out
 
 
-@pytest.mark.parametrize("mix", ["Q8_0", "Q4_K_M"])
-def test_runtime_matches_python_engine(exe, tmp_path, mix):
-    cfg = preset("tiny-llama")
+@pytest.mark.parametrize("model,mix", [("tiny-llama", "Q8_0"), ("tiny-llama", "Q4_K_M"), ("tiny-mixtral", "Q8_0")])
+def test_runtime_matches_python_engine(exe, tmp_path, model, mix):
+    # tiny-mixtral: the runtime serves Mixtral-architecture checkpoints with every expert on the GPU
+    # (router, routing, grouped expert GEMMs and combine of the native forward).
+    cfg = preset(model)
     if mix == "Q4_K_M":
         cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.n_layers = 1024, 8, 4, 128, 2816, 2
     path = str(tmp_path / "m.gguf")
