@@ -3,27 +3,14 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-namespace vmc {
+#include "sample_params.hpp"
 
-// Per-row sampling parameters (32 bytes, mirrored by a numpy structured dtype on the host).
-struct SampleParams {
-  float temperature;       // <= 0: greedy
-  int32_t top_k;           // <= 0: disabled
-  float top_p;             // >= 1: disabled
-  float min_p;             // <= 0: disabled
-  float repetition_penalty;
-  float frequency_penalty;
-  float presence_penalty;
-  int32_t step;            // per-request RNG step counter
-  uint64_t seed;
-};
-static_assert(sizeof(SampleParams) == 40, "SampleParams layout");
+namespace vmc {
 
 void sample(const float* logits, int S, int V, int64_t ld, const SampleParams* params, int32_t* out_tok, float* out_lp,
             cudaStream_t st);
 void apply_penalties(float* logits, int64_t ld, const int32_t* row_of, const int32_t* tok, const int32_t* out_count,
                      const SampleParams* params, int n, cudaStream_t st);
-
 
 // Vocabulary-parallel sampling state of one rank: the exchange buffers (peer addresses, one per
 // rank, each [nranks][max_rows] slots of tp_sample_row_bytes()) and arrival counters in the

@@ -10,13 +10,22 @@
 //   vmc_run MODEL.gguf --prompts FILE [--gen N] [--max-num-seqs S] [--max-num-batched-tokens T]
 //           [--max-model-len L] [--num-blocks B] [--no-graphs] [--dump-tokens FILE.json] [--runs K]
 //           [--warmup W]
+//   vmc_run MODEL.gguf --serve [--host H] [--port P] [--model-name NAME] [--port-file PATH]
+//           [--max-num-seqs S] [--max-num-batched-tokens T] [--max-model-len L] [--num-blocks B] [--no-graphs]
 //
 // --prompts: little-endian int32 count, int32 length, then count * length token ids. Greedy decoding
 // with ignore_eos (every request produces N tokens). One JSON line on stdout: device time of the timed
 // runs, output tokens/s, p50 time to first token and inter-token latency.
+//
+// --serve: the OpenAI-compatible HTTP server (csrc/server/) over the same engine. The serving loop runs
+// on the main thread (it owns the stream, the graphs and the scheduler); HTTP connections are served on
+// their own threads. Sampling parameters and penalties come from each request (the sampler kernels of
+// sampling.cu); SIGINT / SIGTERM stop it. Counterpart of the reference's server mode
+// (src/main.cpp:521-794 with src/server/http_server.cpp).
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstdint>
@@ -26,6 +35,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "attention.h"
@@ -33,9 +43,14 @@
 #include "forward.h"
 #include "gemm_tcgen05.h"
 #include "gguf.hpp"
+#include "http.hpp"
+#include "openai.hpp"
 #include "quants.hpp"
 #include "sampling.h"
 #include "scheduler.hpp"
+#include "serve_loop.hpp"
+#include "stop_signals.hpp"
+#include "text_tokenizer.hpp"
 #include "weights.h"
 
 namespace {
@@ -52,6 +67,10 @@ struct Args {
   std::string model, prompts, dump;
   int gen = 16, max_seqs = 64, max_batched = 2048, max_model_len = 0, runs = 1, warmup = 0, num_blocks = 0;
   bool graphs = true;
+  // --serve
+  bool serve = false;
+  std::string host = "127.0.0.1", model_name, port_file;
+  int port = 8000;
 };
 
 Args parse(int argc, char** argv) {
@@ -74,6 +93,11 @@ Args parse(int argc, char** argv) {
     else if (k == "--warmup") a.warmup = std::stoi(val());
     else if (k == "--num-blocks") a.num_blocks = std::stoi(val());
     else if (k == "--no-graphs") a.graphs = false;
+    else if (k == "--serve") a.serve = true;
+    else if (k == "--host") a.host = val();
+    else if (k == "--port") a.port = std::stoi(val());
+    else if (k == "--model-name") a.model_name = val();
+    else if (k == "--port-file") a.port_file = val();
     else throw std::runtime_error("unknown option " + k);
   }
   return a;
@@ -703,6 +727,150 @@ struct Engine {
   }
 };
 
+// The engine as the serving loop's step backend: metadata and per-row sampling parameters are
+// staged in pinned memory and copied in on the engine's stream; decode-only steps padded to a graph
+// bucket replay that bucket's graph; rows with penalties stop the forward after the lm_head logits,
+// apply the penalties and sample with the same kernels the Python engine uses.
+class GpuBackend : public vmc::StepBackend {
+ public:
+  explicit GpuBackend(Engine& e) : eng_(e) {
+    CK(cudaGetDevice(&dev_));
+    CK(cudaMallocHost(&lp_host_, static_cast<size_t>(eng_.max_tokens) * 4));
+    CK(cudaMallocHost(&err_host_, 4));
+  }
+  ~GpuBackend() override {
+    cudaFreeHost(lp_host_);
+    cudaFreeHost(err_host_);
+    if (pen_host_) cudaFreeHost(pen_host_);
+  }
+  vmc::BatchLayout layout() const override { return eng_.layout; }
+  int vocab() const override { return eng_.m.h.V; }
+  int graph_bucket(int n) const override { return eng_.a.graphs ? eng_.bucket(n) : 0; }
+
+  void step(const int32_t* meta, const vmc::SampleParams* params, int S, const vmc::Penalties& pen, int32_t* tokens,
+            float* logprobs) override {
+    CK(cudaSetDevice(dev_));
+    cudaStream_t st = eng_.st;
+    const size_t nmeta = static_cast<size_t>(eng_.layout.total());
+    memcpy(eng_.meta_host, meta, nmeta * 4);
+    const int32_t* cnt = eng_.meta_host + eng_.layout.off_counts();
+    const int T = cnt[0], R = cnt[1], nd = cnt[3], mq = cnt[4], Rp = cnt[7];
+    // the serving loop padded a decode-only, penalty-free step to graph_bucket(R): replay that graph
+    // (its padding rows sample too)
+    const bool use_graph = pen.empty() && eng_.a.graphs && nd == R && Rp == eng_.bucket(R) && eng_.graphs.count(Rp);
+    const int rows = use_graph ? std::max(S, Rp) : S;
+    if (rows > eng_.max_tokens) throw std::runtime_error("serve: more sample rows than the parameter buffer holds");
+    if (S > 0) memcpy(eng_.params_host, params, static_cast<size_t>(S) * sizeof(vmc::SampleParams));
+    if (rows > S) memset(eng_.params_host + S, 0, static_cast<size_t>(rows - S) * sizeof(vmc::SampleParams));
+    CK(cudaMemcpyAsync(eng_.meta_dev.p, eng_.meta_host, nmeta * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(eng_.params_dev.p, eng_.params_host, static_cast<size_t>(rows) * sizeof(vmc::SampleParams),
+                       cudaMemcpyHostToDevice, st));
+    if (use_graph) {
+      CK(cudaGraphLaunch(eng_.graphs[Rp], st));
+    } else if (pen.empty()) {
+      eng_.fwd->run(eng_.dims(T, R, S, nd, mq), st);
+    } else {
+      vmc::StepDims d = eng_.dims(T, R, S, nd, mq);
+      d.sample = false;
+      eng_.fwd->run(d, st);
+      const size_t n = pen.row.size();
+      stage_penalties(pen, st);
+      const int32_t* base = pen_dev_.as<int32_t>();
+      vmc::apply_penalties(eng_.logits.as<float>(), eng_.m.h.V, base, base + n, base + 2 * n,
+                           eng_.params_dev.as<vmc::SampleParams>(), static_cast<int>(n), st);
+      vmc::sample(eng_.logits.as<float>(), S, eng_.m.h.V, eng_.m.h.V, eng_.params_dev.as<vmc::SampleParams>(),
+                  eng_.tok_dev.as<int32_t>(), eng_.lp_dev.as<float>(), st);
+    }
+    CK(cudaGetLastError());
+    if (S > 0) {
+      CK(cudaMemcpyAsync(eng_.tok_host, eng_.tok_dev.p, static_cast<size_t>(S) * 4, cudaMemcpyDeviceToHost, st));
+      CK(cudaMemcpyAsync(lp_host_, eng_.lp_dev.p, static_cast<size_t>(S) * 4, cudaMemcpyDeviceToHost, st));
+    }
+    CK(cudaMemcpyAsync(err_host_, eng_.err.p, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (*err_host_ != 0) throw std::runtime_error("device error word " + std::to_string(*err_host_));
+    memcpy(tokens, eng_.tok_host, static_cast<size_t>(S) * 4);
+    memcpy(logprobs, lp_host_, static_cast<size_t>(S) * 4);
+  }
+
+ private:
+  // (row, token, count) arrays back to back in one pinned staging buffer and one device buffer
+  void stage_penalties(const vmc::Penalties& pen, cudaStream_t st) {
+    const size_t n = pen.row.size(), bytes = 3 * n * 4;
+    if (bytes > pen_cap_) {
+      CK(cudaStreamSynchronize(st));
+      if (pen_host_) cudaFreeHost(pen_host_);
+      pen_cap_ = std::max(bytes, 2 * pen_cap_);
+      CK(cudaMallocHost(&pen_host_, pen_cap_));
+      pen_dev_ = DevBuf(pen_cap_, false);
+    }
+    memcpy(pen_host_, pen.row.data(), n * 4);
+    memcpy(pen_host_ + n, pen.token.data(), n * 4);
+    memcpy(pen_host_ + 2 * n, pen.count.data(), n * 4);
+    CK(cudaMemcpyAsync(pen_dev_.p, pen_host_, bytes, cudaMemcpyHostToDevice, st));
+  }
+
+  Engine& eng_;
+  int dev_ = 0;
+  float* lp_host_ = nullptr;
+  uint32_t* err_host_ = nullptr;
+  int32_t* pen_host_ = nullptr;
+  size_t pen_cap_ = 0;
+  DevBuf pen_dev_;
+};
+
+
+int serve(const Args& a) {
+  vmc::StopSignals stop;  // before the CUDA runtime starts its threads, so that they inherit the mask
+  cudaStream_t st;
+  CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  auto gguf = vmc::GgufFile::open(a.model);
+  auto tok = vmc::TextTokenizer::from_gguf(*gguf);
+  Args args = a;
+  if (args.max_model_len <= 0) args.max_model_len = 4096;
+  if (args.num_blocks <= 0) args.num_blocks = args.max_seqs * ((args.max_model_len + 15) / 16) + 64;
+  Model model = load(a.model, args.max_model_len + 1, st);
+  Engine eng(model, args, st);
+  eng.capture_all();
+  GpuBackend be(eng);
+  vmc::ServeConfig sc;
+  sc.sched.max_num_seqs = args.max_seqs;
+  sc.sched.max_num_batched_tokens = args.max_batched;
+  sc.sched.max_model_len = args.max_model_len;
+  sc.num_blocks = args.num_blocks;
+  sc.eos_token_ids = tok->eos_ids();  // eos and end-of-turn, as the Python engine
+  vmc::ServeLoop loop(sc, be);
+  vmc::OpenAIConfig oc;
+  oc.model_name = a.model_name.empty() ? gguf->get_str("general.name", "vm_c") : a.model_name;
+  vmc::OpenAIServer api(loop, *tok, oc);
+  vmc::http::Server srv;
+  api.install(srv);
+  const int bound = srv.listen(a.host, a.port);
+  fprintf(stderr, "vmc_run: serving %s on %s:%d (chat format %s)\n", oc.model_name.c_str(), a.host.c_str(), bound,
+          vmc::chat_format_name(api.chat_format()));
+  if (!a.port_file.empty()) {
+    FILE* f = fopen(a.port_file.c_str(), "w");
+    if (!f) throw std::runtime_error("cannot write " + a.port_file);
+    fprintf(f, "%d\n", bound);
+    fclose(f);
+  }
+  srv.start();
+  std::atomic<bool> done{false};
+  std::thread watcher([&] {
+    while (!done.load())
+      if (stop.wait(100)) {
+        loop.request_stop();
+        return;
+      }
+  });
+  loop.run();  // the engine's thread: every CUDA call of the server happens here
+  done.store(true);
+  watcher.join();
+  srv.stop();
+  CK(cudaStreamSynchronize(st));
+  return loop.failed() ? 2 : 0;
+}
+
 std::vector<std::vector<int32_t>> read_prompts(const std::string& path) {
   FILE* f = fopen(path.c_str(), "rb");
   if (!f) throw std::runtime_error("cannot open " + path);
@@ -769,7 +937,8 @@ int run(const Args& a) {
 
 int main(int argc, char** argv) {
   try {
-    return run(parse(argc, argv));
+    const Args a = parse(argc, argv);
+    return a.serve ? serve(a) : run(a);
   } catch (const std::exception& e) {
     fprintf(stderr, "vmc_run: %s\n", e.what());
     return 1;

@@ -1,0 +1,476 @@
+"""Native OpenAI server (csrc/server/) on the CPU: vmc_serve_cpu serves GGUF vocabularies through the
+same HTTP routes, tokenizer, chat prompts, serving loop and scheduler as vmc_run --serve, with a
+deterministic rule in place of the model (token after t at position p = (31 t + 7 p + 11) mod V), so
+every completion can be predicted here. The text pipeline is compared with the Python server's
+(vm_c_b200/server/tokenizer.py, chat.py) and, for the pre-tokenisers, with the published regular
+expressions themselves."""
+import http.client
+import json
+import os
+import random
+import socket
+import subprocess
+import threading
+import time
+
+import pytest
+import regex
+
+from vm_c_b200 import _build
+from vm_c_b200.gguf.constants import VType
+from vm_c_b200.gguf.random_init import synthetic_vocab
+from vm_c_b200.server.chat import ChatTemplate, chatml, split_reasoning
+from vm_c_b200.server.tokenizer import _PRE, IncrementalDetokenizer, Tokenizer, _byte_unicode
+
+MAX_LEN = 512
+
+
+@pytest.fixture(scope="module")
+def exe():
+    return str(_build.build_serve_cpu())
+
+
+def write_vocab_gguf(path, toks, scores, types, merges, model, pre, bos, eos, template=None, add_bos=True):
+    from vm_c_b200 import _native
+    w = _native.host().GgufWriter(32)
+    md = [("general.architecture", VType.STRING, "llama", 0),
+          ("tokenizer.ggml.model", VType.STRING, model, 0),
+          ("tokenizer.ggml.pre", VType.STRING, pre, 0),
+          ("tokenizer.ggml.tokens", VType.ARRAY, toks, int(VType.STRING)),
+          ("tokenizer.ggml.token_type", VType.ARRAY, types, int(VType.INT32)),
+          ("tokenizer.ggml.bos_token_id", VType.UINT32, bos, 0),
+          ("tokenizer.ggml.eos_token_id", VType.UINT32, eos, 0),
+          ("tokenizer.ggml.add_bos_token", VType.BOOL, add_bos, 0)]
+    if scores:
+        md.append(("tokenizer.ggml.scores", VType.ARRAY, scores, int(VType.FLOAT32)))
+    if merges:
+        md.append(("tokenizer.ggml.merges", VType.ARRAY, merges, int(VType.STRING)))
+    if template:
+        md.append(("tokenizer.chat_template", VType.STRING, template, 0))
+    for key, vt, val, et in md:
+        w.set(key, int(vt), val, int(et))
+    w.write(path, lambda i: None)
+
+
+def spm_vocab():
+    toks, scores, types = synthetic_vocab(600)
+    scores = [float(len(t)) if ty == 1 else 0.0 for t, ty in zip(toks, types)]
+    return toks, scores, types
+
+
+CORPUS = ("the quick brown fox jumps over the lazy dog. It's 2024 and we'll see 12345 tokens!\n"
+          "naïve café déjà vu, 漢字 かな and emoji 😀 in text; don't stop believing\n\tindented  spaces") * 3
+
+
+def gpt2_vocab(n_merges=300):
+    """Byte-level vocabulary with merges learned on CORPUS (a few steps of BPE), plus specials."""
+    b2u, _ = _byte_unicode()
+    toks = [b2u[b] for b in range(256)]
+    words = [[b2u[b] for b in w.encode()] for w in regex.findall(_PRE["llama-bpe"], CORPUS)]
+    merges = []
+    for _ in range(n_merges):
+        counts = {}
+        for w in words:
+            for a, b in zip(w, w[1:]):
+                counts[(a, b)] = counts.get((a, b), 0) + 1
+        if not counts:
+            break
+        (a, b), _c = max(counts.items(), key=lambda kv: (kv[1], kv[0]))
+        merges.append(f"{a} {b}")
+        toks.append(a + b)
+        nw = []
+        for w in words:
+            out, i = [], 0
+            while i < len(w):
+                if i + 1 < len(w) and w[i] == a and w[i + 1] == b:
+                    out.append(a + b)
+                    i += 2
+                else:
+                    out.append(w[i])
+                    i += 1
+            nw.append(out)
+        words = nw
+    specials = ["<|endoftext|>", "<|im_start|>", "<|im_end|>"]
+    types = [1] * len(toks) + [3] * len(specials)
+    toks += specials
+    return toks, types, merges
+
+
+class Server:
+    def __init__(self, exe, gguf, tmp, *extra):
+        pf = os.path.join(tmp, f"port{random.randrange(1 << 30)}")
+        self.proc = subprocess.Popen([exe, gguf, "--port", "0", "--port-file", pf, "--max-model-len", str(MAX_LEN),
+                                      *extra], stdout=subprocess.DEVNULL, stderr=subprocess.PIPE)
+        t0 = time.time()
+        while not os.path.exists(pf) or not open(pf).read().strip():
+            if self.proc.poll() is not None:
+                raise RuntimeError("server exited: " + self.proc.stderr.read().decode())
+            if time.time() - t0 > 30:
+                raise RuntimeError("server did not start")
+            time.sleep(0.02)
+        self.port = int(open(pf).read())
+
+    def request(self, method, path, body=None, raw=None, headers=None):
+        c = http.client.HTTPConnection("127.0.0.1", self.port, timeout=30)
+        data = raw if raw is not None else (json.dumps(body).encode() if body is not None else None)
+        c.request(method, path, body=data, headers=headers or ({"Content-Type": "application/json"} if data else {}))
+        r = c.getresponse()
+        out = r.status, dict(r.getheaders()), r.read()
+        c.close()
+        return out
+
+    def post(self, path, body):
+        st, _, data = self.request("POST", path, body)
+        return st, json.loads(data)
+
+    def stream(self, path, body):
+        c = http.client.HTTPConnection("127.0.0.1", self.port, timeout=30)
+        c.request("POST", path, body=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+        r = c.getresponse()
+        assert r.status == 200 and r.getheader("Content-Type") == "text/event-stream"
+        events = [e for e in r.read().decode().split("\n\n") if e]
+        c.close()
+        assert events[-1] == "data: [DONE]"
+        return [json.loads(e[len("data: "):]) for e in events[:-1]]
+
+    def close(self):
+        self.proc.terminate()
+        try:
+            self.proc.wait(10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait()
+
+
+def predict(prompt, V, max_tokens, eos, ignore_eos=False, min_tokens=0, stop_ids=()):
+    """Tokens the rule backend produces for `prompt` and the finish reason (the scheduler's rules)."""
+    out, t, p = [], prompt[-1], len(prompt) - 1
+    while True:
+        t = (31 * t + 7 * p + 11) % V
+        p += 1
+        out.append(t)
+        n = len(out)
+        is_eos = t in eos and not ignore_eos and n > min_tokens
+        is_stop = t in stop_ids and n > min_tokens
+        if is_eos or is_stop:
+            return out, "stop"
+        if n >= max_tokens or len(prompt) + n >= MAX_LEN:
+            return out, "length"
+
+
+def detok(tok, ids, stop=None):
+    d = IncrementalDetokenizer(tok, stop)
+    text = "".join(d.push([i]) for i in ids)
+    return text + d.push([], final=True), d.stopped
+
+
+@pytest.fixture(scope="module")
+def spm(exe, tmp_path_factory):
+    tmp = str(tmp_path_factory.mktemp("spm"))
+    toks, scores, types = spm_vocab()
+    path = os.path.join(tmp, "spm.gguf")
+    write_vocab_gguf(path, toks, scores, types, [], "llama", "default", 1, 2)
+    tok = Tokenizer(toks, scores, types, [], "llama", "default", 1, [2], True)
+    srv = Server(exe, path, tmp, "--max-num-batched-tokens", "64", "--max-num-seqs", "8")
+    yield srv, tok
+    srv.close()
+
+
+@pytest.fixture(scope="module", params=["llama-bpe", "qwen2", "gpt2"])
+def bpe(exe, tmp_path_factory, request):
+    tmp = str(tmp_path_factory.mktemp("bpe"))
+    toks, types, merges = gpt2_vocab()
+    path = os.path.join(tmp, "bpe.gguf")
+    eos = toks.index("<|im_end|>")
+    write_vocab_gguf(path, toks, [], types, merges, "gpt2", request.param, toks.index("<|endoftext|>"), eos,
+                     add_bos=False)
+    tok = Tokenizer(toks, [], types, merges, "gpt2", request.param, toks.index("<|endoftext|>"), [eos], False)
+    srv = Server(exe, path, tmp)
+    yield srv, tok
+    srv.close()
+
+
+TEXTS = ["hello world", "I'm here, it's fine; they'll go", "  two  spaces\n\nand lines\r\n", "digits 1234567 x",
+         "naïve café 漢字 😀", "<|im_start|>user\nhi<|im_end|>", "", "tab\tsep", "UPPER 'S 'LL", CORPUS[:200]]
+
+
+def test_pre_tokenizers_match_regex(exe):
+    alphabet = list("abcXYZ'sStTrReEvVmMlLdD019 \t\n\r.,!?-_()\"") + \
+        ["é", "ü", "漢", "٣", "½", "Ⅻ", "😀", " ", "　", "​", "́", "ſ", "ǅ", "\x0b", "\x85", "ß"]
+    rng = random.Random(0)
+    texts = TEXTS + ["".join(rng.choice(alphabet) for _ in range(rng.randint(0, 24))) for _ in range(1500)]
+    for fam in ("gpt2", "llama-bpe", "qwen2"):
+        inp = "".join(json.dumps(t) + "\n" for t in texts).encode()
+        out = subprocess.run([exe, "--tool", "pre-split", fam], input=inp, capture_output=True, check=True).stdout
+        got = [json.loads(x) for x in out.decode().split("\n") if x]
+        rx = regex.compile(_PRE[fam])
+        bad = [(t, rx.findall(t), g) for t, g in zip(texts, got) if rx.findall(t) != g]
+        assert len(got) == len(texts) and not bad, (fam, bad[:3])
+
+
+def test_tokenize_matches_python_spm(spm):
+    srv, tok = spm
+    for text in TEXTS:
+        for add in (False, True):
+            st, r = srv.post("/tokenize", {"content": text, "add_special": add})
+            assert st == 200 and r["tokens"] == tok.encode(text, add_bos=add), text
+        st, r = srv.post("/detokenize", {"tokens": tok.encode(text, add_bos=True)})
+        assert r["content"] == tok.decode(tok.encode(text, add_bos=True), skip_special=False)
+
+
+def test_tokenize_matches_python_bpe(bpe):
+    srv, tok = bpe
+    rng = random.Random(1)
+    words = CORPUS.split(" ")
+    texts = TEXTS + [" ".join(rng.choice(words) for _ in range(rng.randint(1, 12))) for _ in range(60)]
+    for text in texts:
+        st, r = srv.post("/tokenize", {"content": text})
+        assert st == 200 and r["tokens"] == tok.encode(text, add_bos=False), text
+        ids = r["tokens"]
+        st, r = srv.post("/detokenize", {"tokens": ids})
+        assert r["content"] == tok.decode(ids, skip_special=False) == text
+
+
+def test_completion_matches_prediction(spm):
+    srv, tok = spm
+    V = len(tok.tokens)
+    for i, prompt in enumerate(["the rain in spain", "once upon a time there was a " * 5, "x"]):
+        body = {"prompt": prompt, "max_tokens": 20 + i, "temperature": 0}
+        st, r = srv.post("/v1/completions", body)
+        ids = tok.encode(prompt)
+        want, reason = predict(ids, V, 20 + i, [2])
+        text, _ = detok(tok, want)
+        assert st == 200 and r["object"] == "text_completion"
+        assert r["choices"][0]["text"] == text and r["choices"][0]["finish_reason"] == reason
+        assert r["usage"] == {"prompt_tokens": len(ids), "completion_tokens": len(want),
+                              "total_tokens": len(ids) + len(want)}
+        # the same request streamed: the deltas add up to the same text
+        ev = srv.stream("/v1/completions", {**body, "stream": True, "stream_options": {"include_usage": True}})
+        assert "".join(e["choices"][0]["text"] for e in ev if e["choices"]) == text
+        assert ev[-2]["choices"][0]["finish_reason"] == reason
+        assert ev[-1]["choices"] == [] and ev[-1]["usage"]["completion_tokens"] == len(want)
+
+
+def test_token_id_prompt_stop_ids_min_tokens_ignore_eos(spm):
+    srv, tok = spm
+    V = len(tok.tokens)
+    ids = tok.encode("ids given directly", add_bos=True)
+    want, _ = predict(ids, V, 40, [2], ignore_eos=True)
+    stop_id = want[5]
+    st, r = srv.post("/v1/completions", {"prompt": ids, "max_tokens": 40, "ignore_eos": True,
+                                         "stop_token_ids": [stop_id], "min_tokens": 3})
+    exp, reason = predict(ids, V, 40, [2], ignore_eos=True, min_tokens=3, stop_ids=[stop_id])
+    assert st == 200 and r["choices"][0]["finish_reason"] == reason == "stop"
+    assert r["usage"]["completion_tokens"] == len(exp) and r["choices"][0]["text"] == detok(tok, exp)[0]
+
+
+def test_stop_string_truncates(spm):
+    srv, tok = spm
+    V = len(tok.tokens)
+    ids = tok.encode("stop strings")
+    want, _ = predict(ids, V, 60, [2], ignore_eos=True)
+    full, _ = detok(tok, want)
+    stop = full[len(full) // 2: len(full) // 2 + 2]
+    expect, stopped = detok(tok, want, [stop])
+    assert stopped
+    for stream in (False, True):
+        body = {"prompt": "stop strings", "max_tokens": 60, "ignore_eos": True, "stop": stop}
+        if stream:
+            ev = srv.stream("/v1/completions", {**body, "stream": True})
+            text = "".join(e["choices"][0]["text"] for e in ev)
+            reason = ev[-1]["choices"][0]["finish_reason"]
+        else:
+            st, r = srv.post("/v1/completions", body)
+            text, reason = r["choices"][0]["text"], r["choices"][0]["finish_reason"]
+        assert text == expect and reason == "stop"
+
+
+def test_chat_chatml_prompt_and_reasoning(spm):
+    srv, tok = spm
+    V = len(tok.tokens)
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": [{"type": "text", "text": "hi"}]}]
+    for thinking in (True, False):
+        prompt = chatml([{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}], True, thinking)
+        ids = tok.encode(prompt, add_bos=not prompt.startswith(tok.tokens[tok.bos_id]))
+        want, reason = predict(ids, V, 30, [2])
+        text, _ = detok(tok, want)
+        reasoning, content = split_reasoning(text, thinking)
+        st, r = srv.post("/v1/chat/completions", {"messages": msgs, "max_tokens": 30,
+                                                  "chat_template_kwargs": {"enable_thinking": thinking}})
+        assert st == 200 and r["object"] == "chat.completion"
+        assert r["usage"]["prompt_tokens"] == len(ids)
+        m = r["choices"][0]["message"]
+        assert m["role"] == "assistant" and m["content"] == content and m.get("reasoning_content", "") == reasoning
+        ev = srv.stream("/v1/chat/completions", {"messages": msgs, "max_tokens": 30, "stream": True,
+                                                 "enable_thinking": thinking})
+        assert ev[0]["choices"][0]["delta"] == {"role": "assistant", "content": ""}
+        # streamed, everything before "</think>" is reasoning (all of it when the tag never comes)
+        s_reason, s_content = (text, "") if thinking and "</think>" not in text else (reasoning, content)
+        assert "".join(e["choices"][0]["delta"].get("reasoning_content", "") for e in ev) == s_reason
+        assert "".join(e["choices"][0]["delta"].get("content", "") for e in ev) == s_content
+        assert ev[-1]["choices"][0]["finish_reason"] == reason
+
+
+def test_concurrent_requests_continuous_batching(spm):
+    """Many clients at once: prompts of different lengths span several 64-token prefill chunks and the
+    decode batch changes every step; every answer must equal its own prediction."""
+    srv, tok = spm
+    V = len(tok.tokens)
+    rng = random.Random(3)
+    prompts = [" ".join(rng.choice(["alpha", "beta", "gamma", "delta"]) for _ in range(rng.randint(1, 40)))
+               for _ in range(24)]
+    results = [None] * len(prompts)
+
+    def run(i):
+        results[i] = srv.post("/v1/completions", {"prompt": prompts[i], "max_tokens": 5 + i, "temperature": 0,
+                                                  "ignore_eos": True})
+    th = [threading.Thread(target=run, args=(i,)) for i in range(len(prompts))]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(60)
+    for i, (st, r) in enumerate(results):
+        want, reason = predict(tok.encode(prompts[i]), V, 5 + i, [2], ignore_eos=True)
+        assert st == 200 and r["choices"][0]["text"] == detok(tok, want)[0] and r["usage"]["completion_tokens"] == len(want)
+    _, _, m = srv.request("GET", "/metrics")
+    m = dict(line.split(" ", 1) for line in m.decode().splitlines() if line and not line.startswith("#"))
+    assert float(m["vmc_num_running"]) == 0 and float(m["vmc_finished"]) >= len(prompts)
+
+
+def test_client_disconnect_aborts(exe, tmp_path):
+    toks, scores, types = spm_vocab()
+    path = str(tmp_path / "v.gguf")
+    write_vocab_gguf(path, toks, scores, types, [], "llama", "default", 1, 2)
+    srv = Server(exe, path, str(tmp_path), "--step-delay-ms", "20")
+    try:
+        s = socket.create_connection(("127.0.0.1", srv.port), timeout=10)
+        body = json.dumps({"prompt": "never ending", "max_tokens": 400, "ignore_eos": True, "stream": True}).encode()
+        s.sendall(b"POST /v1/completions HTTP/1.1\r\nHost: x\r\nContent-Type: application/json\r\n"
+                  b"Content-Length: " + str(len(body)).encode() + b"\r\n\r\n" + body)
+        got = b""
+        while got.count(b"data: ") < 3:
+            got += s.recv(4096)
+        s.close()
+        t0 = time.time()
+        while True:
+            _, _, m = srv.request("GET", "/metrics")
+            m = dict(line.split(" ", 1) for line in m.decode().splitlines() if line and not line.startswith("#"))
+            if float(m["vmc_aborted"]) == 1 and float(m["vmc_num_running"]) == 0:
+                break
+            assert time.time() - t0 < 10, m
+            time.sleep(0.05)
+        assert float(m["vmc_tokens_generated"]) < 400
+    finally:
+        srv.close()
+
+
+def test_routes_and_errors(spm):
+    srv, tok = spm
+    st, h, data = srv.request("GET", "/v1/models")
+    assert st == 200 and json.loads(data)["data"][0]["id"] == "vm_c" and h["Access-Control-Allow-Origin"] == "*"
+    assert json.loads(srv.request("GET", "/health")[2]) == {"status": "ok"}
+    assert "version" in json.loads(srv.request("GET", "/version")[2])
+    assert srv.request("OPTIONS", "/v1/completions")[0] == 204
+    assert srv.request("GET", "/nope")[0] == 404
+    assert srv.request("GET", "/v1/completions")[0] == 405
+    st, _, data = srv.request("POST", "/v1/completions", raw=b"{not json")
+    assert st == 400 and json.loads(data)["error"]["code"] == 400
+    assert srv.post("/v1/chat/completions", {"messages": []})[0] == 400
+    st, r = srv.post("/v1/completions", {"prompt": [len(tok.tokens) + 5]})
+    assert st == 400 and "vocabulary" in r["error"]["message"]
+    assert srv.post("/v1/completions", {"prompt": "x", "max_tokens": "many"})[0] == 400
+    # keep-alive: two requests over one connection
+    c = http.client.HTTPConnection("127.0.0.1", srv.port, timeout=10)
+    for _ in range(2):
+        c.request("GET", "/health")
+        assert c.getresponse().read() == b'{"status": "ok"}'
+    c.close()
+
+
+LLAMA3 = ("{% set loop_messages = messages %}{% for message in loop_messages %}{% set content = "
+          "'<|start_header_id|>' + message['role'] + '<|end_header_id|>\n\n'+ message['content'] | trim + "
+          "'<|eot_id|>' %}{% if loop.index0 == 0 %}{% set content = bos_token + content %}{% endif %}"
+          "{{ content }}{% endfor %}{% if add_generation_prompt %}"
+          "{{ '<|start_header_id|>assistant<|end_header_id|>\n\n' }}{% endif %}")
+MISTRAL = ("{{ bos_token }}{% for message in messages %}{% if (message['role'] == 'user') != "
+           "(loop.index0 % 2 == 0) %}{{ raise_exception('Conversation roles must alternate "
+           "user/assistant/user/assistant/...') }}{% endif %}{% if message['role'] == 'user' %}"
+           "{{ '[INST] ' + message['content'] + ' [/INST]' }}{% elif message['role'] == 'assistant' %}"
+           "{{ message['content'] + eos_token}}{% else %}{{ raise_exception('Only user and assistant roles "
+           "are supported!') }}{% endif %}{% endfor %}")
+
+
+@pytest.mark.parametrize("template", [LLAMA3, MISTRAL, ""])
+def test_chat_formats_match_jinja(exe, tmp_path, template):
+    tf = tmp_path / "t.jinja"
+    tf.write_text(template)
+    convs = [[{"role": "user", "content": " hello "}],
+             [{"role": "user", "content": "a"}, {"role": "assistant", "content": "b"}, {"role": "user", "content": "c"}]]
+    if template != MISTRAL:
+        convs.append([{"role": "system", "content": "sys"}, {"role": "user", "content": "q"}])
+    lines, want = [], []
+    for conv in convs:
+        for gen in (True, False):
+            lines.append(json.dumps({"messages": conv, "add_generation_prompt": gen, "bos": "<s>", "eos": "</s>"}))
+            want.append(ChatTemplate(template or None, "<s>", "</s>").render(conv, gen))
+    out = subprocess.run([exe, "--tool", "render-chat", str(tf)], input="\n".join(lines).encode() + b"\n",
+                         capture_output=True, check=True).stdout.decode()
+    got = [json.loads(x) for x in out.split("\n") if x]
+    assert got == want
+
+
+def test_qwen3_thinking_switch(exe, tmp_path):
+    tf = tmp_path / "q.jinja"
+    tf.write_text("<|im_start|>{{ role }} ... {% if enable_thinking is defined and enable_thinking is false %}")
+    conv = [{"role": "user", "content": "q1"}, {"role": "assistant", "content": "<think>\nr\n</think>\n\na1"},
+            {"role": "user", "content": "q2"}]
+    lines = [json.dumps({"messages": conv, "enable_thinking": t}) for t in (True, False)]
+    out = subprocess.run([exe, "--tool", "render-chat", str(tf)], input="\n".join(lines).encode() + b"\n",
+                         capture_output=True, check=True).stdout.decode()
+    got = [json.loads(x) for x in out.split("\n") if x]
+    base = "<|im_start|>user\nq1<|im_end|>\n<|im_start|>assistant\na1<|im_end|>\n<|im_start|>user\nq2<|im_end|>\n" \
+           "<|im_start|>assistant\n"
+    assert got == [base, base + "<think>\n\n</think>\n\n"]
+
+
+def test_server_threads_race_free_under_tsan(tmp_path):
+    """The server built with ThreadSanitizer: concurrent plain, streamed, stop-string and abandoned
+    requests plus metrics reads while the loop steps; no race may be reported and the process must exit
+    cleanly on SIGTERM."""
+    exe = str(_build.build_serve_cpu(tsan=True))
+    toks, scores, types = spm_vocab()
+    path = str(tmp_path / "v.gguf")
+    write_vocab_gguf(path, toks, scores, types, [], "llama", "default", 1, 2)
+    srv = Server(exe, path, str(tmp_path), "--step-delay-ms", "2", "--max-num-batched-tokens", "64",
+                 "--max-num-seqs", "6")
+    errors = []
+
+    def client(i):
+        try:
+            body = {"prompt": "tsan " * (1 + i % 7), "max_tokens": 10 + i, "ignore_eos": True}
+            if i % 4 == 0:
+                srv.stream("/v1/completions", {**body, "stream": True})
+            elif i % 4 == 1:
+                srv.post("/v1/chat/completions", {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 8})
+            elif i % 4 == 2:
+                s = socket.create_connection(("127.0.0.1", srv.port), timeout=10)
+                b = json.dumps({**body, "stream": True, "max_tokens": 200}).encode()
+                s.sendall(b"POST /v1/completions HTTP/1.1\r\nHost: x\r\nContent-Length: " + str(len(b)).encode() +
+                          b"\r\n\r\n" + b)
+                s.recv(100)
+                s.close()
+            else:
+                srv.request("GET", "/metrics")
+                srv.post("/v1/completions", {**body, "stop": "e"})
+        except Exception as e:  # noqa: BLE001
+            errors.append(repr(e))
+    th = [threading.Thread(target=client, args=(i,)) for i in range(16)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(120)
+    srv.proc.send_signal(2)
+    rc = srv.proc.wait(60)
+    err = srv.proc.stderr.read().decode()
+    assert not errors, errors
+    assert "ThreadSanitizer" not in err and rc == 0, err[-4000:]

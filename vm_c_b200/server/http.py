@@ -170,8 +170,9 @@ class OpenAIServer:
                 toks, finished, fr = await q.get()
                 n += len(toks)
                 delta = detok.push(toks, final=finished)
-                if detok.stopped and not finished:
-                    self.engine.finish_request(rid, FinishReason.STOP)
+                if detok.stopped:  # a stop string ends the request even when its last token hit a limit
+                    if not finished:
+                        self.engine.finish_request(rid, FinishReason.STOP)
                     finished, fr = True, FinishReason.STOP
                 if delta:
                     text.append(delta)
