@@ -846,8 +846,8 @@ int serve(const Args& a) {
   vmc::http::Server srv;
   api.install(srv);
   const int bound = srv.listen(a.host, a.port);
-  fprintf(stderr, "vmc_run: serving %s on %s:%d (chat format %s)\n", oc.model_name.c_str(), a.host.c_str(), bound,
-          vmc::chat_format_name(api.chat_format()));
+  fprintf(stderr, "vmc_run: serving %s on %s:%d (chat template: %s)\n", oc.model_name.c_str(), a.host.c_str(), bound,
+          api.chat_template().has_template() ? "jinja" : ("ChatML " + api.chat_template().parse_error()).c_str());
   if (!a.port_file.empty()) {
     FILE* f = fopen(a.port_file.c_str(), "w");
     if (!f) throw std::runtime_error("cannot write " + a.port_file);

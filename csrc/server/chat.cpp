@@ -1,6 +1,8 @@
 // Chat prompt formats and reasoning split (see chat.hpp).
 #include "chat.hpp"
 
+#include "jinja.hpp"
+
 namespace vmc {
 
 namespace {
@@ -13,92 +15,55 @@ std::string lstrip_newlines(const std::string& s) {
   return s.substr(i);
 }
 
-std::string trim(const std::string& s) {
-  const char* ws = " \t\r\n\v\f";
-  const size_t b = s.find_first_not_of(ws);
-  if (b == std::string::npos) return "";
-  const size_t e = s.find_last_not_of(ws);
-  return s.substr(b, e - b + 1);
-}
-
 bool chatml_role(const std::string& r) { return r == "system" || r == "user" || r == "assistant" || r == "tool"; }
 
 }  // namespace
 
-ChatFormat detect_chat_format(const std::string& t) {
-  if (t.find("<|start_header_id|>") != std::string::npos) return ChatFormat::Llama3;
-  if (t.find("<|im_start|>") != std::string::npos)
-    return t.find("enable_thinking") != std::string::npos ? ChatFormat::Qwen3 : ChatFormat::ChatML;
-  if (t.find("[INST]") != std::string::npos) return ChatFormat::Mistral;
-  return ChatFormat::ChatML;
-}
-
-const char* chat_format_name(ChatFormat f) {
-  switch (f) {
-    case ChatFormat::Qwen3: return "qwen3";
-    case ChatFormat::Llama3: return "llama3";
-    case ChatFormat::Mistral: return "mistral";
-    default: return "chatml";
-  }
-}
-
-std::string render_chat(ChatFormat f, const std::vector<ChatMessage>& msgs, bool add_generation_prompt,
-                        bool enable_thinking, const std::string& bos, const std::string& eos) {
+std::string chatml(const std::vector<ChatMessage>& msgs, bool add_generation_prompt, bool enable_thinking) {
   std::string out;
-  switch (f) {
-    case ChatFormat::ChatML:
-      for (const auto& m : msgs)
-        if (chatml_role(m.role)) out += "<|im_start|>" + m.role + "\n" + m.content + "<|im_end|>\n";
-      if (add_generation_prompt) {
-        out += "<|im_start|>assistant\n";
-        out += enable_thinking ? "<think>\n" : "<think>\n\n</think>\n\n";
-      }
-      break;
-    case ChatFormat::Qwen3: {
-      // earlier assistant turns (before the last user message) lose their reasoning block
-      size_t last_user = msgs.size();
-      for (size_t i = 0; i < msgs.size(); ++i)
-        if (msgs[i].role == "user") last_user = i;
-      for (size_t i = 0; i < msgs.size(); ++i) {
-        const auto& m = msgs[i];
-        if (!chatml_role(m.role)) continue;
-        std::string c = m.content;
-        if (m.role == "assistant" && (last_user == msgs.size() || i < last_user)) {
-          const size_t k = c.rfind(kThinkEnd);
-          if (k != std::string::npos) c = lstrip_newlines(c.substr(k + kThinkEnd.size()));
-        }
-        out += "<|im_start|>" + m.role + "\n" + c + "<|im_end|>\n";
-      }
-      if (add_generation_prompt) {
-        out += "<|im_start|>assistant\n";
-        if (!enable_thinking) out += "<think>\n\n</think>\n\n";
-      }
-      break;
-    }
-    case ChatFormat::Llama3:
-      for (size_t i = 0; i < msgs.size(); ++i) {
-        if (i == 0) out += bos;
-        out += "<|start_header_id|>" + msgs[i].role + "<|end_header_id|>\n\n" + trim(msgs[i].content) + "<|eot_id|>";
-      }
-      if (add_generation_prompt) out += "<|start_header_id|>assistant<|end_header_id|>\n\n";
-      break;
-    case ChatFormat::Mistral: {
-      out += bos;
-      std::string system;
-      for (const auto& m : msgs) {
-        if (m.role == "system") {
-          system += (system.empty() ? "" : "\n\n") + m.content;
-        } else if (m.role == "user") {
-          out += "[INST] " + (system.empty() ? "" : system + "\n\n") + m.content + " [/INST]";
-          system.clear();
-        } else if (m.role == "assistant") {
-          out += m.content + eos;
-        }
-      }
-      break;
-    }
+  for (const auto& m : msgs)
+    if (chatml_role(m.role)) out += "<|im_start|>" + m.role + "\n" + m.content + "<|im_end|>\n";
+  if (add_generation_prompt) {
+    out += "<|im_start|>assistant\n";
+    out += enable_thinking ? "<think>\n" : "<think>\n\n</think>\n\n";
   }
   return out;
+}
+
+ChatTemplate::ChatTemplate(const std::string& src, std::string bos, std::string eos)
+    : bos_(std::move(bos)), eos_(std::move(eos)) {
+  if (src.empty()) return;
+  try {
+    tmpl_ = std::make_unique<jinja::Template>(src);
+  } catch (const std::exception& e) {
+    error_ = e.what();
+  }
+}
+
+ChatTemplate::~ChatTemplate() = default;
+
+std::string ChatTemplate::render(const std::vector<ChatMessage>& msgs, bool add_generation_prompt,
+                                 bool enable_thinking, std::string* why) const {
+  if (why) *why = tmpl_ ? "" : error_;
+  if (tmpl_) {
+    try {
+      jinja::List ml;
+      for (const auto& m : msgs)
+        ml.push_back(jinja::Value::dict({{"role", jinja::Value::str(m.role)}, {"content", jinja::Value::str(m.content)}}));
+      jinja::Value g = jinja::Value::dict();
+      g.set("messages", jinja::Value::list(std::move(ml)));
+      g.set("add_generation_prompt", jinja::Value::boolean(add_generation_prompt));
+      g.set("enable_thinking", jinja::Value::boolean(enable_thinking));
+      g.set("bos_token", jinja::Value::str(bos_));
+      g.set("eos_token", jinja::Value::str(eos_));
+      std::string s = tmpl_->render(g);
+      if (!s.empty()) return s;
+      if (why) *why = "the template rendered nothing";
+    } catch (const std::exception& e) {  // raise_exception or an unsupported construct: ChatML
+      if (why) *why = e.what();
+    }
+  }
+  return chatml(msgs, add_generation_prompt, enable_thinking);
 }
 
 std::pair<std::string, std::string> split_reasoning(const std::string& text, bool enable_thinking) {

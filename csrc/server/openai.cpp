@@ -190,12 +190,15 @@ bool drive(ServeLoop& loop, const TextTokenizer& tok, const std::shared_ptr<GenS
 }  // namespace
 
 OpenAIServer::OpenAIServer(ServeLoop& loop, const TextTokenizer& tok, OpenAIConfig cfg)
-    : loop_(loop), tok_(tok), cfg_(std::move(cfg)) {
+    : loop_(loop),
+      tok_(tok),
+      cfg_(std::move(cfg)),
+      bos_text_(tok.bos_id() >= 0 && tok.bos_id() < tok.vocab_size() ? tok.token(tok.bos_id()) : ""),
+      eos_text_(!tok.eos_ids().empty() && tok.eos_ids()[0] >= 0 && tok.eos_ids()[0] < tok.vocab_size()
+                    ? tok.token(tok.eos_ids()[0])
+                    : ""),
+      chat_(tok.chat_template(), bos_text_, eos_text_) {
   if (cfg_.system_fingerprint.empty()) cfg_.system_fingerprint = "fp_" + hex_id(10);
-  fmt_ = detect_chat_format(tok_.chat_template());
-  if (tok_.bos_id() >= 0 && tok_.bos_id() < tok_.vocab_size()) bos_text_ = tok_.token(tok_.bos_id());
-  if (!tok_.eos_ids().empty() && tok_.eos_ids()[0] >= 0 && tok_.eos_ids()[0] < tok_.vocab_size())
-    eos_text_ = tok_.token(tok_.eos_ids()[0]);
 }
 
 void OpenAIServer::install(http::Server& srv) {
@@ -230,7 +233,7 @@ void OpenAIServer::chat(const http::Request& rq, http::Responder& res) {
     const Value* c = m.get("content");
     cm.push_back({m.get_string("role", "user"), c ? content_text(*c) : ""});
   }
-  const std::string prompt = render_chat(fmt_, cm, true, p.enable_thinking, bos_text_, eos_text_);
+  const std::string prompt = chat_.render(cm, true, p.enable_thinking);
   const bool add_bos = !bos_text_.empty() && prompt.compare(0, bos_text_.size(), bos_text_) != 0;
   p.gen.prompt = tok_.encode(prompt, add_bos ? 1 : 0);
   const std::string cid = "chatcmpl-" + hex_id(32);

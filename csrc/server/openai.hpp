@@ -29,7 +29,7 @@ class OpenAIServer {
  public:
   OpenAIServer(ServeLoop& loop, const TextTokenizer& tok, OpenAIConfig cfg);
   void install(http::Server& srv);
-  ChatFormat chat_format() const { return fmt_; }
+  const ChatTemplate& chat_template() const { return chat_; }
 
  private:
   void chat(const http::Request& rq, http::Responder& res);
@@ -44,8 +44,8 @@ class OpenAIServer {
   ServeLoop& loop_;
   const TextTokenizer& tok_;
   OpenAIConfig cfg_;
-  ChatFormat fmt_;
   std::string bos_text_, eos_text_;
+  ChatTemplate chat_;
 };
 
 }  // namespace vmc

@@ -16,7 +16,8 @@
 //   vmc_serve_cpu --tool pre-split FAMILY      a string -> the pieces of pre-tokeniser FAMILY
 //   vmc_serve_cpu --tool render-chat TEMPLATE_FILE
 //       {"messages": [...], "add_generation_prompt": b, "enable_thinking": b, "bos": s, "eos": s}
-//       -> the prompt in the format detected from the template text (an empty file: ChatML)
+//       -> the chat prompt the server builds with that Jinja template (an empty file: ChatML);
+//       TEMPLATE_FILE "-": each line carries its own "template"
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -70,13 +71,15 @@ class RuleBackend : public vmc::StepBackend {
 
 int run_tool(const std::string& tool, const std::string& arg) {
   using vmc::json::Value;
-  vmc::ChatFormat fmt = vmc::ChatFormat::ChatML;
+  std::string tmpl;
   if (tool == "render-chat") {
-    std::ifstream f(arg);
-    if (!f) throw std::runtime_error("cannot read " + arg);
-    std::stringstream ss;
-    ss << f.rdbuf();
-    fmt = vmc::detect_chat_format(ss.str());
+    if (arg != "-") {
+      std::ifstream f(arg);
+      if (!f) throw std::runtime_error("cannot read " + arg);
+      std::stringstream ss;
+      ss << f.rdbuf();
+      tmpl = ss.str();
+    }
   } else if (tool != "pre-split") {
     throw std::runtime_error("unknown tool " + tool);
   }
@@ -91,8 +94,11 @@ int run_tool(const std::string& tool, const std::string& arg) {
       std::vector<vmc::ChatMessage> msgs;
       for (const Value& m : in.get("messages")->as_array())
         msgs.push_back({m.get_string("role", "user"), m.get_string("content", "")});
-      out = vmc::render_chat(fmt, msgs, in.get_bool("add_generation_prompt", true), in.get_bool("enable_thinking", true),
-                             in.get_string("bos", ""), in.get_string("eos", ""));
+      const vmc::ChatTemplate ct(arg == "-" ? in.get_string("template", "") : tmpl, in.get_string("bos", ""),
+                                 in.get_string("eos", ""));
+      std::string why;
+      out = ct.render(msgs, in.get_bool("add_generation_prompt", true), in.get_bool("enable_thinking", true), &why);
+      if (!why.empty()) std::cerr << "chat template: " << why << "\n";
     }
     std::cout << vmc::json::dump(out) << "\n";
   }
@@ -147,8 +153,8 @@ int main(int argc, char** argv) {
     vmc::http::Server srv;
     api.install(srv);
     const int bound = srv.listen(host, port);
-    fprintf(stderr, "vmc_serve_cpu: listening on %s:%d (chat format %s)\n", host.c_str(), bound,
-            vmc::chat_format_name(api.chat_format()));
+    fprintf(stderr, "vmc_serve_cpu: listening on %s:%d (chat template: %s)\n", host.c_str(), bound,
+            api.chat_template().has_template() ? "jinja" : ("ChatML " + api.chat_template().parse_error()).c_str());
     if (!port_file.empty()) {
       FILE* f = fopen(port_file.c_str(), "w");
       if (!f) throw std::runtime_error("cannot write " + port_file);

@@ -398,39 +398,177 @@ MISTRAL = ("{{ bos_token }}{% for message in messages %}{% if (message['role'] =
            "{{ '[INST] ' + message['content'] + ' [/INST]' }}{% elif message['role'] == 'assistant' %}"
            "{{ message['content'] + eos_token}}{% else %}{{ raise_exception('Only user and assistant roles "
            "are supported!') }}{% endif %}{% endfor %}")
+GEMMA = ("{{ bos_token }}{% if messages[0]['role'] == 'system' %}{{ raise_exception('System role not supported') }}"
+         "{% endif %}{% for message in messages %}{% if (message['role'] == 'user') != (loop.index0 % 2 == 0) %}"
+         "{{ raise_exception('Conversation roles must alternate user/assistant/user/assistant/...') }}{% endif %}"
+         "{% if (message['role'] == 'assistant') %}{% set role = 'model' %}{% else %}{% set role = message['role'] %}"
+         "{% endif %}{{ '<start_of_turn>' + role + '\n' + message['content'] | trim + '<end_of_turn>\n' }}"
+         "{% endfor %}{% if add_generation_prompt %}{{'<start_of_turn>model\n'}}{% endif %}")
+PHI3 = ("{% for message in messages %}{% if message['role'] == 'system' %}{{'<|system|>\n' + message['content'] + "
+        "'<|end|>\n'}}{% elif message['role'] == 'user' %}{{'<|user|>\n' + message['content'] + '<|end|>\n'}}"
+        "{% elif message['role'] == 'assistant' %}{{'<|assistant|>\n' + message['content'] + '<|end|>\n'}}{% endif %}"
+        "{% endfor %}{% if add_generation_prompt %}{{ '<|assistant|>\n' }}{% else %}{{ eos_token }}{% endif %}")
+ZEPHYR = """{% for message in messages %}
+{% if message['role'] == 'user' %}
+{{ '<|user|>\n' + message['content'] + eos_token }}
+{% elif message['role'] == 'system' %}
+{{ '<|system|>\n' + message['content'] + eos_token }}
+{% elif message['role'] == 'assistant' %}
+{{ '<|assistant|>\n'  + message['content'] + eos_token }}
+{% endif %}
+{% if loop.last and add_generation_prompt %}
+{{ '<|assistant|>' }}
+{% endif %}
+{% endfor %}"""
+QWEN25 = """{%- if tools %}
+    {{- '<|im_start|>system\n' }}
+    {%- if messages[0]['role'] == 'system' %}
+        {{- messages[0]['content'] }}
+    {%- else %}
+        {{- 'You are Qwen, created by Alibaba Cloud. You are a helpful assistant.' }}
+    {%- endif %}
+    {{- "\n\n# Tools\n\n<tools>" }}
+    {%- for tool in tools %}
+        {{- "\n" }}
+        {{- tool | tojson }}
+    {%- endfor %}
+    {{- "\n</tools><|im_end|>\n" }}
+{%- else %}
+    {%- if messages[0]['role'] == 'system' %}
+        {{- '<|im_start|>system\n' + messages[0]['content'] + '<|im_end|>\n' }}
+    {%- else %}
+        {{- '<|im_start|>system\nYou are Qwen, created by Alibaba Cloud. You are a helpful assistant.<|im_end|>\n' }}
+    {%- endif %}
+{%- endif %}
+{%- for message in messages %}
+    {%- if (message.role == "user") or (message.role == "system" and not loop.first) or (message.role == "assistant" and not message.tool_calls) %}
+        {{- '<|im_start|>' + message.role + '\n' + message.content + '<|im_end|>' + '\n' }}
+    {%- elif message.role == "tool" %}
+        {%- if (loop.index0 == 0) or (messages[loop.index0 - 1].role != "tool") %}
+            {{- '<|im_start|>user' }}
+        {%- endif %}
+        {{- '\n<tool_response>\n' }}
+        {{- message.content }}
+        {{- '\n</tool_response>' }}
+        {%- if loop.last or (messages[loop.index0 + 1].role != "tool") %}
+            {{- '<|im_end|>\n' }}
+        {%- endif %}
+    {%- endif %}
+{%- endfor %}
+{%- if add_generation_prompt %}
+    {{- '<|im_start|>assistant\n' }}
+{%- endif %}
+"""
+QWEN3 = """{%- if messages[0].role == 'system' %}
+    {{- '<|im_start|>system\n' + messages[0].content + '<|im_end|>\n' }}
+{%- endif %}
+{%- set ns = namespace(multi_step_tool=true, last_query_index=messages|length - 1) %}
+{%- for message in messages[::-1] %}
+    {%- set index = (messages|length - 1) - loop.index0 %}
+    {%- if ns.multi_step_tool and message.role == "user" and message.content is string and not(message.content.startswith('<tool_response>') and message.content.endswith('</tool_response>')) %}
+        {%- set ns.multi_step_tool = false %}
+        {%- set ns.last_query_index = index %}
+    {%- endif %}
+{%- endfor %}
+{%- for message in messages %}
+    {%- if message.content is string %}
+        {%- set content = message.content %}
+    {%- else %}
+        {%- set content = '' %}
+    {%- endif %}
+    {%- if (message.role == "user") or (message.role == "system" and not loop.first) %}
+        {{- '<|im_start|>' + message.role + '\n' + content + '<|im_end|>' + '\n' }}
+    {%- elif message.role == "assistant" %}
+        {%- set reasoning_content = '' %}
+        {%- if message.reasoning_content is string %}
+            {%- set reasoning_content = message.reasoning_content %}
+        {%- else %}
+            {%- if '</think>' in content %}
+                {%- set reasoning_content = content.split('</think>')[0].rstrip('\n').split('<think>')[-1].lstrip('\n') %}
+                {%- set content = content.split('</think>')[-1].lstrip('\n') %}
+            {%- endif %}
+        {%- endif %}
+        {%- if loop.index0 > ns.last_query_index %}
+            {%- if loop.last or (not loop.last and reasoning_content) %}
+                {{- '<|im_start|>' + message.role + '\n<think>\n' + reasoning_content.strip('\n') + '\n</think>\n\n' + content.lstrip('\n') }}
+            {%- else %}
+                {{- '<|im_start|>' + message.role + '\n' + content }}
+            {%- endif %}
+        {%- else %}
+            {{- '<|im_start|>' + message.role + '\n' + content }}
+        {%- endif %}
+        {{- '<|im_end|>\n' }}
+    {%- endif %}
+{%- endfor %}
+{%- if add_generation_prompt %}
+    {{- '<|im_start|>assistant\n' }}
+    {%- if enable_thinking is defined and enable_thinking is false %}
+        {{- '<think>\n\n</think>\n\n' }}
+    {%- endif %}
+{%- endif %}"""
+# every construct the interpreter supports, in one template
+KITCHEN = """{%- macro fmt(m, prefix='> ') -%}{{ prefix }}{{ m.role | upper }}: {{ m.content | trim }}{%- endmacro -%}
+{%- set ns = namespace(n=0) -%}
+{%- for m in messages if m.role != 'tool' -%}
+  {%- set ns.n = ns.n + 1 -%}
+  {{ fmt(m) }}{{ loop.cycle('|', '/') }}{% if not loop.last %}
+{% endif %}
+{%- else -%}
+  no messages
+{%- endfor %}
+count={{ ns.n }} roles={{ messages | map(attribute='role') | join(',') }}
+users={{ messages | selectattr('role', 'equalto', 'user') | list | length }} others={{ messages | rejectattr('role', 'eq', 'user') | list | length }}
+{% set block %}{{ bos_token ~ 'x' }}{% endset %}{{ block | replace('x', 'y') }}
+{{ {'b': 1, 'a': [1, 2.5, none, true, "q<'&>"]} | tojson }} {{ [3, 'é'] | tojson(indent=2) }}
+{{ (messages | first).content[:3] }}|{{ messages[-1]['content'][::-1] }}|{{ messages[1:] | length }}
+{{ 'A' if enable_thinking else 'B' }} {{ 7 // 2 }} {{ -7 // 2 }} {{ 7 % 3 }} {{ -7 % 3 }} {{ 2 ** 10 }} {{ 1 / 4 }} {{ 'ab' * 2 }} {{ 3 - 5 }} {{ 1.5 + 1 }}
+{%- for i in range(6) %}{% if i == 4 %}{% break %}{% endif %}{% if i is odd %}{% continue %}{% endif %}{{ i }}{% endfor %}
+{{ undefined_var | default('dflt') }} {{ undefined_var is defined }} {{ none is none }} {{ '' | default('e', true) }} {{ 3 is divisibleby 3 }}
+{{ "  padded  " | trim }}|{{ "a-b-c".split("-") | join("+") }}|{{ "Hello World".lower().title() }}|{{ "x y  z".split() }}|{{ "a,b,c".rsplit(",", 1) }}
+{{ "line1\nline2\n\nline4" | indent(2) }}
+{% for k, v in {'x': 1, 'y': 2}.items() %}{{ k }}={{ v }};{% endfor %} {{ {'k': 'v'}.get('k') }} {{ {'k': 'v'}.get('z', 'dz') }}
+{{ [1, 2] + [3] }} {{ 'b' in ['a', 'b'] }} {{ 'z' not in 'abc' }} {{ [1, 2] == [1, 2] }} {{ 2 < 3 < 4 }} {{ 3 > 2 > 1 }} {{ 1 < 2 > 3 }} {{ not true or false and true }}
+{{ messages | length > 1 and messages[0].role }} {{ 1 if 0 else (2 if 1 else 3) }} {{ [3, 1, 2] | reverse | list }} {{ 'abc' | reverse }}
+{{ 42 | string ~ '!' }} {{ '12' | int + 1 }} {{ 'x' | int }} {{ 2.0 }} {{ 1e20 }} {{ 0.1 + 0.2 }} {{ [1, 'a', none, true] }} {{ {'a': [1]} }}
+{{ "It's" }} {{ 'say "hi"' | e }} {{ messages | map('upper') | list if false else 'mapped' }} {{ [1, 1, 2] | unique | list }}
+{{ fmt(messages[0]) + '<&>' }} {{ 'x' ~ ('<'|safe) }} {{ ['a'|safe, 'b'|e, 'c'] }} {{ ('q'|tojson) + '"' }}
+{#- a comment -#}
+{%+ if true %}kept{% endif %}
+  {% if true %}lstripped{% endif %}
+end"""
+TEMPLATES = [("llama3", LLAMA3), ("mistral", MISTRAL), ("gemma", GEMMA), ("phi3", PHI3), ("zephyr", ZEPHYR),
+             ("qwen25", QWEN25), ("qwen3", QWEN3), ("kitchen", KITCHEN), ("none", "")]
+CONVS = [
+    [{"role": "user", "content": " hello "}],
+    [{"role": "user", "content": "a"}, {"role": "assistant", "content": "b"}, {"role": "user", "content": "c"}],
+    [{"role": "system", "content": "sys"}, {"role": "user", "content": "q"}],
+    [{"role": "user", "content": "q1"}, {"role": "assistant", "content": "<think>\nr1\n</think>\n\na1"},
+     {"role": "user", "content": "q2"}, {"role": "assistant", "content": "<think>r2</think>a2"}],
+    [{"role": "system", "content": "s"}, {"role": "user", "content": "u"}, {"role": "tool", "content": "t1"},
+     {"role": "tool", "content": "t2"}, {"role": "assistant", "content": "x"}],
+    [{"role": "user", "content": "naïve ✓ 漢字\nline\ttab"}],
+]
 
 
-@pytest.mark.parametrize("template", [LLAMA3, MISTRAL, ""])
-def test_chat_formats_match_jinja(exe, tmp_path, template):
+@pytest.mark.parametrize("name,template", TEMPLATES)
+def test_chat_templates_match_jinja2(exe, tmp_path, name, template):
+    """The server's Jinja interpreter renders what the Python server's jinja2 renders (raise_exception
+    and unsupported templates fall back to ChatML in both)."""
     tf = tmp_path / "t.jinja"
     tf.write_text(template)
-    convs = [[{"role": "user", "content": " hello "}],
-             [{"role": "user", "content": "a"}, {"role": "assistant", "content": "b"}, {"role": "user", "content": "c"}]]
-    if template != MISTRAL:
-        convs.append([{"role": "system", "content": "sys"}, {"role": "user", "content": "q"}])
     lines, want = [], []
-    for conv in convs:
+    for conv in CONVS:
         for gen in (True, False):
-            lines.append(json.dumps({"messages": conv, "add_generation_prompt": gen, "bos": "<s>", "eos": "</s>"}))
-            want.append(ChatTemplate(template or None, "<s>", "</s>").render(conv, gen))
+            for think in (True, False):
+                lines.append(json.dumps({"messages": conv, "add_generation_prompt": gen, "enable_thinking": think,
+                                         "bos": "<s>", "eos": "</s>"}))
+                want.append(ChatTemplate(template or None, "<s>", "</s>").render(conv, gen, think))
     out = subprocess.run([exe, "--tool", "render-chat", str(tf)], input="\n".join(lines).encode() + b"\n",
                          capture_output=True, check=True).stdout.decode()
     got = [json.loads(x) for x in out.split("\n") if x]
-    assert got == want
-
-
-def test_qwen3_thinking_switch(exe, tmp_path):
-    tf = tmp_path / "q.jinja"
-    tf.write_text("<|im_start|>{{ role }} ... {% if enable_thinking is defined and enable_thinking is false %}")
-    conv = [{"role": "user", "content": "q1"}, {"role": "assistant", "content": "<think>\nr\n</think>\n\na1"},
-            {"role": "user", "content": "q2"}]
-    lines = [json.dumps({"messages": conv, "enable_thinking": t}) for t in (True, False)]
-    out = subprocess.run([exe, "--tool", "render-chat", str(tf)], input="\n".join(lines).encode() + b"\n",
-                         capture_output=True, check=True).stdout.decode()
-    got = [json.loads(x) for x in out.split("\n") if x]
-    base = "<|im_start|>user\nq1<|im_end|>\n<|im_start|>assistant\na1<|im_end|>\n<|im_start|>user\nq2<|im_end|>\n" \
-           "<|im_start|>assistant\n"
-    assert got == [base, base + "<think>\n\n</think>\n\n"]
+    assert len(got) == len(want)
+    for k, (g, w) in enumerate(zip(got, want)):
+        assert g == w, (name, k, lines[k], g, w)
 
 
 def test_server_threads_race_free_under_tsan(tmp_path):
@@ -474,3 +612,33 @@ def test_server_threads_race_free_under_tsan(tmp_path):
     err = srv.proc.stderr.read().decode()
     assert not errors, errors
     assert "ThreadSanitizer" not in err and rc == 0, err[-4000:]
+
+
+def test_chat_template_mutations_match_jinja2(exe):
+    """Random edits of the template bank (deleted spans, inserted delimiters, operators and keywords):
+    whatever jinja2 makes of each broken or altered template (a render, or an error and the ChatML
+    fallback), the native interpreter must produce the same prompt."""
+    rng = random.Random(2024)
+    base = [tm for _, tm in TEMPLATES if tm]
+    pieces = ["{%", "%}", "{{", "}}", "-", "+", "(", ")", "[", "]", "'", '"', "|", ".", ":", ",", "~", "*", "\n",
+              " ", " if ", " else ", " for ", " in ", " not ", " is ", "endfor", "endif", "loop.", "ns.", "none"]
+    lines, want = [], []
+    for _ in range(1500):
+        s = rng.choice(base)
+        for _ in range(rng.randint(1, 4)):
+            k = rng.randrange(len(s) + 1)
+            if rng.random() < 0.5 and len(s) > 2:
+                s = s[:k] + s[k + rng.randint(1, 5):]
+            else:
+                s = s[:k] + rng.choice(pieces) + s[k:]
+        conv = rng.choice(CONVS)
+        gen, think = rng.random() < 0.8, rng.random() < 0.5
+        lines.append(json.dumps({"template": s, "messages": conv, "add_generation_prompt": gen,
+                                 "enable_thinking": think, "bos": "<s>", "eos": "</s>"}))
+        want.append(ChatTemplate(s, "<s>", "</s>").render(conv, gen, think))
+    out = subprocess.run([exe, "--tool", "render-chat", "-"], input="\n".join(lines).encode() + b"\n",
+                         capture_output=True, check=True, timeout=300).stdout.decode()
+    got = [json.loads(x) for x in out.split("\n") if x]
+    assert len(got) == len(want)
+    bad = [k for k in range(len(want)) if got[k] != want[k]]
+    assert not bad, [(json.loads(lines[k])["template"][:300], got[k][:200], want[k][:200]) for k in bad[:3]]

@@ -42,6 +42,7 @@ class ChatTemplate:
                 import jinja2
                 from jinja2.sandbox import ImmutableSandboxedEnvironment
                 env = ImmutableSandboxedEnvironment(trim_blocks=True, lstrip_blocks=True,
+                                                    extensions=["jinja2.ext.loopcontrols"],
                                                     undefined=jinja2.Undefined)
 
                 def raise_exception(msg):
