@@ -642,3 +642,15 @@ def test_chat_template_mutations_match_jinja2(exe):
     assert len(got) == len(want)
     bad = [k for k in range(len(want)) if got[k] != want[k]]
     assert not bad, [(json.loads(lines[k])["template"][:300], got[k][:200], want[k][:200]) for k in bad[:3]]
+
+
+@pytest.mark.parametrize("impl", ["native", "python"])
+def test_host_bench_runs(impl):
+    """The host-path load test (vm_c_b200/server/host_bench.py) drives both servers to completion."""
+    import sys
+    r = subprocess.run([sys.executable, "-m", "vm_c_b200.server.host_bench", "--impl", impl, "--clients", "4",
+                        "--requests", "16", "--max-tokens", "8"], capture_output=True, text=True, timeout=300,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["errors"] == 0 and out["completion_tokens"] == 16 * 8
