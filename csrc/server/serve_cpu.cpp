@@ -14,6 +14,8 @@
 // Two tool modes read one JSON value per stdin line and print one JSON value per line, for checking
 // the text pipeline against the Python tokenizer and chat templates:
 //   vmc_serve_cpu --tool pre-split FAMILY      a string -> the pieces of pre-tokeniser FAMILY
+//   vmc_serve_cpu --tool utf8-stream -         byte chunks [[b, ...], ...] -> the text each chunk
+//                                              releases through the streaming UTF-8 decoder
 //   vmc_serve_cpu --tool render-chat TEMPLATE_FILE
 //       {"messages": [...], "add_generation_prompt": b, "enable_thinking": b, "bos": s, "eos": s}
 //       -> the chat prompt the server builds with that Jinja template (an empty file: ChatML);
@@ -36,6 +38,7 @@
 #include "serve_loop.hpp"
 #include "stop_signals.hpp"
 #include "text_tokenizer.hpp"
+#include "unicode.hpp"
 
 namespace {
 
@@ -80,7 +83,7 @@ int run_tool(const std::string& tool, const std::string& arg) {
       ss << f.rdbuf();
       tmpl = ss.str();
     }
-  } else if (tool != "pre-split") {
+  } else if (tool != "pre-split" && tool != "utf8-stream") {
     throw std::runtime_error("unknown tool " + tool);
   }
   std::string line;
@@ -90,6 +93,16 @@ int run_tool(const std::string& tool, const std::string& arg) {
     if (tool == "pre-split") {
       out = Value::array();
       for (const auto& p : vmc::TextTokenizer::pre_split(in.as_string(), arg)) out.push(p);
+    } else if (tool == "utf8-stream") {
+      out = Value::array();
+      std::string buf;
+      const auto& chunks = in.as_array();
+      for (size_t k = 0; k < chunks.size(); ++k) {
+        for (const Value& b : chunks[k].as_array()) buf += static_cast<char>(b.as_int());
+        std::string text;
+        buf.erase(0, vmc::uni::decode_stream(buf, k + 1 == chunks.size(), text));
+        out.push(text);
+      }
     } else {
       std::vector<vmc::ChatMessage> msgs;
       for (const Value& m : in.get("messages")->as_array())

@@ -349,13 +349,8 @@ std::string IncrementalDetokenizer::push(const std::vector<int32_t>& ids, bool f
   if (stopped_) return "";
   for (int32_t i : ids)
     if (!(skip_special_ && tok_.is_special(i))) buf_ += tok_.token_bytes(i);
-  size_t cut = uni::valid_prefix(buf_);
-  std::string s = buf_.substr(0, cut);
-  if (final && cut < buf_.size()) {
-    s = uni::sanitize(buf_);
-    cut = buf_.size();
-  }
-  buf_.erase(0, cut);
+  std::string s;
+  buf_.erase(0, uni::decode_stream(buf_, final, s));  // holds only an incomplete trailing sequence
   text_ += tok_.post(s);
   for (const auto& st : stop_) {
     const size_t k = text_.find(st);

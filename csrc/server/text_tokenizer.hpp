@@ -68,8 +68,9 @@ class TextTokenizer {
   std::unordered_map<uint32_t, uint8_t> cp_to_byte_;
 };
 
-// Streams text deltas for generated tokens; holds back bytes of incomplete UTF-8 sequences and text
-// that may be the start of a stop string.
+// Streams text deltas for generated tokens; holds back the bytes of an incomplete trailing UTF-8
+// sequence (ill-formed bytes are replaced by U+FFFD at once) and text that may be the start of a stop
+// string.
 class IncrementalDetokenizer {
  public:
   IncrementalDetokenizer(const TextTokenizer& tok, std::vector<std::string> stop, bool skip_special = true);

@@ -32,5 +32,10 @@ size_t valid_prefix(const std::string& s);
 // Decodes bytes replacing each maximal ill-formed subpart by U+FFFD (the Unicode-recommended
 // practice; the same output as Python's bytes.decode("utf-8", "replace")).
 std::string sanitize(const std::string& s);
+// Streaming form of sanitize(): appends the decoded text of `in` to `out` and returns how many bytes
+// were consumed. Unless `final`, an incomplete sequence at the end (one more byte could still
+// complete it) is left unconsumed; everything else, ill-formed bytes included, is decoded at once
+// (Python's incremental UTF-8 decoder with errors="replace").
+size_t decode_stream(const std::string& in, bool final, std::string& out);
 
 }  // namespace vmc::uni

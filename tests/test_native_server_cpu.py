@@ -654,3 +654,28 @@ def test_host_bench_runs(impl):
     assert r.returncode == 0, r.stderr[-2000:]
     out = json.loads(r.stdout.strip().splitlines()[-1])
     assert out["errors"] == 0 and out["completion_tokens"] == 16 * 8
+
+
+def test_streaming_utf8_decoder_matches_python(exe):
+    """The native detokenizer's streaming UTF-8 decoder releases, chunk by chunk, what Python's
+    incremental decoder (errors="replace") releases: incomplete trailing sequences wait for their next
+    byte, ill-formed bytes become U+FFFD at once."""
+    import codecs
+    rng = random.Random(7)
+    pool = [b for ch in "aé✓😀漢" for b in ch.encode()] + [0x80, 0xBF, 0xC0, 0xC2, 0xE0, 0xED, 0xF0, 0xF4, 0xF5, 0xFF]
+    cases = []
+    for _ in range(400):
+        data = [rng.choice(pool) for _ in range(rng.randint(0, 24))]
+        cuts = sorted(rng.sample(range(len(data) + 1), min(len(data) + 1, rng.randint(1, 6))))
+        chunks, prev = [], 0
+        for c in cuts + [len(data)]:
+            chunks.append(data[prev:c])
+            prev = c
+        cases.append(chunks)
+    inp = "".join(json.dumps(c) + "\n" for c in cases).encode()
+    out = subprocess.run([exe, "--tool", "utf8-stream", "-"], input=inp, capture_output=True, check=True).stdout
+    got = [json.loads(x) for x in out.decode().split("\n") if x]
+    for chunks, g in zip(cases, got):
+        dec = codecs.getincrementaldecoder("utf-8")(errors="replace")
+        want = [dec.decode(bytes(c), final=(k + 1 == len(chunks))) for k, c in enumerate(chunks)]
+        assert g == want, (chunks, g, want)

@@ -9,6 +9,7 @@ byte mapping are here.
 """
 from __future__ import annotations
 
+import codecs
 import functools
 from typing import Iterable, Optional
 
@@ -158,14 +159,15 @@ class Tokenizer:
 
 
 class IncrementalDetokenizer:
-    """Streams text deltas for generated tokens; holds back bytes of incomplete UTF-8 sequences and
+    """Streams text deltas for generated tokens; holds back the bytes of an incomplete trailing UTF-8
+    sequence (ill-formed bytes become U+FFFD at once, so one bad byte never stalls the stream) and
     text that may be the start of a stop string."""
 
     def __init__(self, tok: Tokenizer, stop: Optional[list[str]] = None, skip_special: bool = True):
         self.tok = tok
         self.stop = [s for s in (stop or []) if s]
         self.skip_special = skip_special
-        self.buf = b""
+        self.dec = codecs.getincrementaldecoder("utf-8")(errors="replace")
         self.text = ""        # decoded, not yet emitted
         self.emitted = ""
         self.stopped = False
@@ -174,25 +176,9 @@ class IncrementalDetokenizer:
     def push(self, ids: Iterable[int], final: bool = False) -> str:
         if self.stopped:
             return ""
-        for i in ids:
-            if self.skip_special and self.tok.is_special(i):
-                continue
-            self.buf += self.tok.token_bytes(i)
-        # decode the longest valid UTF-8 prefix
-        cut = len(self.buf)
-        while cut > 0:
-            try:
-                s = self.buf[:cut].decode("utf-8")
-                break
-            except UnicodeDecodeError:
-                cut -= 1
-        else:
-            s = ""
-        if final and cut < len(self.buf):
-            s = self.buf.decode("utf-8", "replace")
-            cut = len(self.buf)
-        self.buf = self.buf[cut:]
-        self.text += self.tok.post(s)
+        data = b"".join(self.tok.token_bytes(i) for i in ids
+                        if not (self.skip_special and self.tok.is_special(i)))
+        self.text += self.tok.post(self.dec.decode(data, final=final))
         for st in self.stop:
             k = self.text.find(st)
             if k >= 0:
