@@ -168,6 +168,9 @@ class OpenAIServer:
         try:
             while True:
                 toks, finished, fr = await q.get()
+                while not finished and not q.empty():  # the engine ran ahead: take everything queued
+                    more, finished, fr = q.get_nowait()
+                    toks = toks + more
                 n += len(toks)
                 delta = detok.push(toks, final=finished)
                 if detok.stopped:  # a stop string ends the request even when its last token hit a limit
@@ -272,10 +275,13 @@ class OpenAIServer:
                                       "usage": {"prompt_tokens": len(ids), "completion_tokens": n,
                                                 "total_tokens": len(ids) + n}})
         resp = await self._sse_start(request)
+        # every delta chunk is the same JSON around its text: serialise the rest once
+        head, tail = json.dumps({**base, "choices": [{"index": 0, "text": "\x00", "logprobs": None,
+                                                      "finish_reason": None}]}).split('"\\u0000"')
+        head, tail = ("data: " + head).encode(), (tail + "\n\n").encode()
 
         async def on_delta(d):
-            await self._sse(resp, {**base, "choices": [{"index": 0, "text": d, "logprobs": None,
-                                                        "finish_reason": None}]})
+            await resp.write(head + json.dumps(d).encode() + tail)
         text, n, reason = await self._generate(ids, sp, detok, on_delta)
         await self._sse(resp, {**base, "choices": [{"index": 0, "text": "", "logprobs": None,
                                                     "finish_reason": (reason or FinishReason.STOP).openai}]})
