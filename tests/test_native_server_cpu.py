@@ -679,3 +679,18 @@ def test_streaming_utf8_decoder_matches_python(exe):
         dec = codecs.getincrementaldecoder("utf-8")(errors="replace")
         want = [dec.decode(bytes(c), final=(k + 1 == len(chunks))) for k, c in enumerate(chunks)]
         assert g == want, (chunks, g, want)
+
+
+def test_cli_native_flag_builds_runtime_command():
+    """`vm_c_server --native` hands the options over to `vmc_run --serve` and refuses the ones that
+    runtime does not have."""
+    from vm_c_b200.cli import build_parser, native_argv
+    a = build_parser().parse_args(["m.gguf", "--native", "--port", "9001", "--served-model-name", "x",
+                                   "--max-num-seqs", "32", "--max-model-len", "4096"])
+    argv = native_argv(a)
+    assert argv[0].endswith("vmc_run") and argv[1:3] == ["m.gguf", "--serve"]
+    assert argv[argv.index("--port") + 1] == "9001" and argv[argv.index("--model-name") + 1] == "x"
+    assert argv[argv.index("--max-num-seqs") + 1] == "32" and argv[argv.index("--max-model-len") + 1] == "4096"
+    for extra in (["-tp", "2"], ["--kv-cache-dtype", "turboquant_4bit_nc"], ["--draft-model", "d.gguf"]):
+        with pytest.raises(ValueError):
+            native_argv(build_parser().parse_args(["m.gguf", "--native"] + extra))

@@ -9,6 +9,10 @@ never uses (the kv-offloading and expert-cache groups) are accepted and reported
 
 Tensor parallelism runs one process per GPU: with --tensor-parallel-size N the CLI spawns N worker
 processes (rank 0 serves HTTP and broadcasts each step's new requests to the others).
+
+--native replaces this process with the PyTorch-free runtime's server (`vmc_run MODEL --serve`,
+csrc/runtime/vmc_run.cpp + csrc/server/): one GPU, a Llama or Mixtral GGUF, bf16 paged KV. Options
+that runtime does not have are refused with a message rather than ignored.
 """
 from __future__ import annotations
 
@@ -63,6 +67,8 @@ def build_parser() -> argparse.ArgumentParser:
     g2.add_argument("--disable-chunked-prefill", dest="chunked_prefill", action="store_false")
     ap.add_argument("--long-prefill-token-threshold", type=int, default=0)
     ap.add_argument("--scheduling-policy", default="decode_first", choices=["decode_first", "fair"])
+    ap.add_argument("--native", action="store_true",
+                    help="serve with the native runtime (vmc_run --serve: no Python or PyTorch in the server process)")
     # accepted for compatibility; inactive in the reference as well
     ap.add_argument("--kv-offloading-size", type=float, default=0.0)
     ap.add_argument("--kv-offloading-backend", default="native")
@@ -191,8 +197,52 @@ def run_rank(rank: int, world: int, a, cfg: VmCConfig) -> None:
     serve(srv, cfg.server.host, cfg.server.port)
 
 
+def native_argv(a) -> list[str]:
+    """The `vmc_run --serve` command line for these options; ValueError for an option it lacks."""
+    from ._build import EXT_DIR
+    bad = []
+    if a.tensor_parallel_size > 1 or a.expert_parallel_size > 1:
+        bad.append("tensor / expert parallelism")
+    if a.spec_method not in ("", "none") or a.draft_model:
+        bad.append("speculative decoding")
+    if a.kv_cache_dtype not in ("auto", "bfloat16"):
+        bad.append(f"--kv-cache-dtype {a.kv_cache_dtype}")
+    if a.cpu_offload_gb or a.cpu_offload_params:
+        bad.append("CPU weight offload")
+    if a.tokenizer:
+        bad.append("--tokenizer")
+    if a.scheduling_policy != "decode_first" or not a.chunked_prefill or not a.prefix_caching:
+        bad.append("scheduler policy options")
+    if a.model.startswith("random:") or os.path.isdir(a.model):
+        bad.append("random: and HuggingFace checkpoints (the native runtime reads GGUF files)")
+    if bad:
+        raise ValueError("--native does not support: " + "; ".join(bad))
+    argv = [str(EXT_DIR / "runtime" / "vmc_run"), a.model, "--serve", "--host", a.host, "--port", str(a.port),
+            "--max-num-seqs", str(a.max_num_seqs)]
+    if a.served_model_name:
+        argv += ["--model-name", a.served_model_name]
+    if a.max_num_batched_tokens > 0:
+        argv += ["--max-num-batched-tokens", str(a.max_num_batched_tokens)]
+    if a.max_model_len > 0:
+        argv += ["--max-model-len", str(a.max_model_len)]
+    if a.num_gpu_blocks > 0:
+        argv += ["--num-blocks", str(a.num_gpu_blocks)]
+    return argv
+
+
 def main(argv=None) -> None:
     a = build_parser().parse_args(argv)
+    if a.native:
+        try:
+            args = native_argv(a)
+        except ValueError as e:
+            raise SystemExit(str(e))
+        if not os.path.exists(args[0]):
+            from ._build import build_runtime
+            build_runtime()
+        if a.gpu_devices:
+            os.environ["CUDA_VISIBLE_DEVICES"] = a.gpu_devices.split(",")[0]
+        os.execv(args[0], args)
     cfg = config_from_args(a)
     world = cfg.parallel.tensor_parallel_size
     if world <= 1:
