@@ -43,13 +43,15 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Flag protocol. 1 (default): GPU-scope fences around relaxed system-scope flag accesses — a peer
-// reads this GPU's partial through this GPU's L2 over NVLink, so the data only has to be visible at
-// GPU scope before the flag goes out. 0: system-scope fence + release store / acquire loads.
-// Measured on 2 B200s inside CUDA graphs (64 x 4096 fp32, 4 split-K partials): 14.5 us for 1,
-// 24.5 us for 0, 17.9 us for NCCL all-reduce + a separate residual/RMSNorm kernel.
+// Flag protocol. 0 (default): system-scope fence + release store / acquire loads, the PTX memory
+// model's guarantee that a peer which sees the flag sees the partial rows. 1: GPU-scope fences around
+// relaxed system-scope flag accesses, which relies on a peer reading this GPU's partial through this
+// GPU's L2 over NVLink rather than on the memory model; kept as a measurement option. Measured on 2
+// B200s inside CUDA graphs (64 x 4096 fp32, 4 split-K partials): 24.5 us for 0, 14.5 us for 1, 17.9 us
+// for NCCL all-reduce + a separate residual/RMSNorm kernel. The default serving path uses rs_norm_ag
+// (below), not this kernel.
 #ifndef VMC_AR_SYNC
-#define VMC_AR_SYNC 1
+#define VMC_AR_SYNC 0
 #endif
 // Peer data: bypass L1 so that a line cached by an earlier call is never reused.
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
