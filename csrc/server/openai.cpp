@@ -68,13 +68,18 @@ Value parse_body(const http::Request& rq) {
 struct BodyParams {
   GenRequest gen;
   std::vector<std::string> stop;
-  bool enable_thinking = true;
-  bool stream = false, include_usage = false;
+  bool enable_thinking = true, add_generation_prompt = true, echo = false;
+  bool stream = false, include_usage = false, running_usage = false;
 };
 
 BodyParams body_params(const Value& b, int default_max) {
   BodyParams p;
   GenRequest& g = p.gen;
+  // An HTTP request samples with temperature 1, top-p 1 and no top-k unless it says otherwise (the
+  // OpenAI defaults, as the reference's request parsers apply them: src/server/http_server.cpp:157-162).
+  g.temperature = 1.f;
+  g.top_p = 1.f;
+  g.top_k = 0;
   try {
     int64_t mt = b.get_int("max_completion_tokens", 0);
     if (mt == 0) mt = b.get_int("max_tokens", 0);
@@ -104,7 +109,12 @@ BodyParams body_params(const Value& b, int default_max) {
     if (!et || et->is_null()) et = b.get("enable_thinking");
     if (et && !et->is_null()) p.enable_thinking = et->as_bool();
     p.stream = b.get_bool("stream", false);
-    if (const Value* so = b.get("stream_options"); so && so->is_object()) p.include_usage = so->get_bool("include_usage", false);
+    p.echo = b.get_bool("echo", false);
+    p.add_generation_prompt = b.get_bool("add_generation_prompt", true);
+    if (const Value* so = b.get("stream_options"); so && so->is_object()) {
+      p.include_usage = so->get_bool("include_usage", false);
+      p.running_usage = so->get_bool("continuous_usage_stats", false);
+    }
   } catch (const HttpError&) {
     throw;
   } catch (const std::exception& e) {
@@ -153,7 +163,8 @@ std::shared_ptr<GenStream> submit(ServeLoop& loop, const GenRequest& g) {
 }
 
 bool drive(ServeLoop& loop, const TextTokenizer& tok, const std::shared_ptr<GenStream>& st, const BodyParams& p,
-           int poll_ms, http::Responder& res, GenResult& out, const std::function<bool(const std::string&)>& on_delta) {
+           int poll_ms, http::Responder& res, GenResult& out,
+           const std::function<bool(const std::string&, size_t)>& on_delta) {
   IncrementalDetokenizer detok(tok, p.stop);
   for (;;) {
     GenEvent ev;
@@ -175,7 +186,7 @@ bool drive(ServeLoop& loop, const TextTokenizer& tok, const std::shared_ptr<GenS
     }
     if (!delta.empty()) {
       out.text += delta;
-      if (on_delta && !on_delta(delta)) {
+      if (on_delta && !on_delta(delta, out.n)) {
         if (!finished) loop.abort(st->id());
         return false;
       }
@@ -233,7 +244,7 @@ void OpenAIServer::chat(const http::Request& rq, http::Responder& res) {
     const Value* c = m.get("content");
     cm.push_back({m.get_string("role", "user"), c ? content_text(*c) : ""});
   }
-  const std::string prompt = chat_.render(cm, true, p.enable_thinking);
+  const std::string prompt = chat_.render(cm, p.add_generation_prompt, p.enable_thinking);
   const bool add_bos = !bos_text_.empty() && prompt.compare(0, bos_text_.size(), bos_text_) != 0;
   p.gen.prompt = tok_.encode(prompt, add_bos ? 1 : 0);
   const std::string cid = "chatcmpl-" + hex_id(32);
@@ -248,7 +259,7 @@ void OpenAIServer::chat(const http::Request& rq, http::Responder& res) {
     if (!drive(loop_, tok_, st, p, cfg_.poll_ms, res, r, nullptr)) return;
     const auto [reasoning, content] = split_reasoning(r.text, p.enable_thinking);
     Value msg = Value::object();
-    msg.set("role", "assistant").set("content", content);
+    msg.set("role", "assistant").set("content", p.echo ? prompt + content : content);
     if (!reasoning.empty()) msg.set("reasoning_content", reasoning);
     Value choice = Value::object();
     choice.set("index", 0).set("message", msg).set("finish_reason", finish_str(r.reason));
@@ -260,29 +271,31 @@ void OpenAIServer::chat(const http::Request& rq, http::Responder& res) {
   res.begin_stream(200, "text/event-stream");
   Value chunk = base;
   chunk.set("object", "chat.completion.chunk");
-  auto send = [&](const Value& delta, const char* finish) {
+  auto send = [&](const Value& delta, const char* finish, size_t n_out = 0) {
     Value choice = Value::object();
     choice.set("index", 0).set("delta", delta).set("finish_reason", finish ? Value(finish) : Value());
     Value v = chunk;
     v.set("choices", Value::Array{choice});
+    if (n_out > 0) v.set("usage", usage(n_prompt, n_out));  // stream_options.continuous_usage_stats
     return sse(res, v);
   };
   Value first = Value::object();
   first.set("role", "assistant").set("content", "");
   send(first, nullptr);
   ReasoningStream rs(p.enable_thinking);
-  const bool ok = drive(loop_, tok_, st, p, cfg_.poll_ms, res, r, [&](const std::string& d) {
+  const bool ok = drive(loop_, tok_, st, p, cfg_.poll_ms, res, r, [&](const std::string& d, size_t n_out) {
     const auto [reasoning, content] = rs.feed(d);
+    const size_t u = p.running_usage ? n_out : 0;
     bool w = true;
     if (!reasoning.empty()) {
       Value dv = Value::object();
       dv.set("reasoning_content", reasoning);
-      w = send(dv, nullptr);
+      w = send(dv, nullptr, u);
     }
     if (w && !content.empty()) {
       Value dv = Value::object();
       dv.set("content", content);
-      w = send(dv, nullptr);
+      w = send(dv, nullptr, u);
     }
     return w;
   });
@@ -300,15 +313,19 @@ void OpenAIServer::completions(const http::Request& rq, http::Responder& res) {
   const Value body = parse_body(rq);
   BodyParams p = body_params(body, cfg_.default_completion_max_tokens);
   const Value* pr = body.get("prompt");
+  std::string prompt_text;
   try {
     if (pr && pr->is_array()) {
       if (pr->size() > 0 && pr->as_array()[0].is_number()) {
         for (const Value& x : pr->as_array()) p.gen.prompt.push_back(static_cast<int32_t>(x.as_int()));
-      } else {
-        p.gen.prompt = tok_.encode(pr->size() > 0 ? pr->as_array()[0].as_string() : "");
+        prompt_text = tok_.decode(p.gen.prompt, false);
+      } else {  // several prompt strings form one prompt, one per line (as the reference joins them)
+        for (const Value& x : pr->as_array()) prompt_text += (prompt_text.empty() ? "" : "\n") + x.as_string();
+        p.gen.prompt = tok_.encode(prompt_text);
       }
     } else {
-      p.gen.prompt = tok_.encode(pr && !pr->is_null() ? pr->as_string() : "");
+      prompt_text = pr && !pr->is_null() ? pr->as_string() : "";
+      p.gen.prompt = tok_.encode(prompt_text);
     }
   } catch (const std::runtime_error& e) {
     throw HttpError(400, std::string("bad prompt: ") + e.what());
@@ -329,14 +346,16 @@ void OpenAIServer::completions(const http::Request& rq, http::Responder& res) {
   if (!p.stream) {
     if (!drive(loop_, tok_, st, p, cfg_.poll_ms, res, r, nullptr)) return;
     Value v = base;
-    v.set("choices", Value::Array{choice(r.text, finish_str(r.reason))}).set("usage", usage(n_prompt, r.n));
+    v.set("choices", Value::Array{choice(p.echo ? prompt_text + r.text : r.text, finish_str(r.reason))})
+        .set("usage", usage(n_prompt, r.n));
     send_json(res, 200, v);
     return;
   }
   res.begin_stream(200, "text/event-stream");
-  const bool ok = drive(loop_, tok_, st, p, cfg_.poll_ms, res, r, [&](const std::string& d) {
+  const bool ok = drive(loop_, tok_, st, p, cfg_.poll_ms, res, r, [&](const std::string& d, size_t n_out) {
     Value v = base;
     v.set("choices", Value::Array{choice(d, nullptr)});
+    if (p.running_usage) v.set("usage", usage(n_prompt, n_out));
     return sse(res, v);
   });
   if (!ok) return;

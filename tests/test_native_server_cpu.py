@@ -694,3 +694,23 @@ def test_cli_native_flag_builds_runtime_command():
     for extra in (["-tp", "2"], ["--kv-cache-dtype", "turboquant_4bit_nc"], ["--draft-model", "d.gguf"]):
         with pytest.raises(ValueError):
             native_argv(build_parser().parse_args(["m.gguf", "--native"] + extra))
+
+
+def test_echo_joined_prompts_running_usage_and_no_generation_prompt(spm):
+    """Request options of the reference's API: `echo`, a list of prompt strings (one per line),
+    `stream_options.continuous_usage_stats` and `add_generation_prompt`."""
+    srv, tok = spm
+    V = len(tok.tokens)
+    st, r = srv.post("/v1/completions", {"prompt": "echo me", "max_tokens": 6, "echo": True, "temperature": 0})
+    want, _ = predict(tok.encode("echo me"), V, 6, [2])
+    assert st == 200 and r["choices"][0]["text"] == "echo me" + detok(tok, want)[0]
+    st, r = srv.post("/v1/completions", {"prompt": ["first", "second"], "max_tokens": 2})
+    assert st == 200 and r["usage"]["prompt_tokens"] == len(tok.encode("first\nsecond"))
+    ev = srv.stream("/v1/completions", {"prompt": "count", "max_tokens": 9, "ignore_eos": True, "stream": True,
+                                        "stream_options": {"continuous_usage_stats": True, "include_usage": True}})
+    counts = [e["usage"]["completion_tokens"] for e in ev[:-2] if e.get("usage")]
+    assert counts and counts == sorted(counts) and counts[-1] <= 9 and ev[-1]["usage"]["completion_tokens"] == 9
+    msgs = [{"role": "user", "content": "hi"}]
+    st, r = srv.post("/v1/chat/completions", {"messages": msgs, "max_tokens": 2, "add_generation_prompt": False})
+    prompt = chatml(msgs, False, True)
+    assert r["usage"]["prompt_tokens"] == len(tok.encode(prompt, add_bos=not prompt.startswith(tok.tokens[1])))

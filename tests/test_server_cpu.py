@@ -76,3 +76,18 @@ def test_bad_requests():
         assert (await c.post("/v1/chat/completions", data=b"{not json")).status == 400
         assert (await c.post("/v1/chat/completions", json={"messages": []})).status == 400
     run(with_client(body))
+
+
+def test_echo_joined_prompts_and_running_usage():
+    async def body(c, tok):
+        r = await c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 2, "temperature": 0, "echo": True})
+        j = await r.json()
+        assert j["choices"][0]["text"] == tok.decode([5, 6, 7], skip_special=False) + tok.decode([8, 9])
+        r = await c.post("/v1/completions", json={"prompt": ["he", "llo"], "max_tokens": 1, "temperature": 0})
+        assert (await r.json())["usage"]["prompt_tokens"] == len(tok.encode("he\nllo"))
+        r = await c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4, "temperature": 0, "stream": True,
+                                                  "stream_options": {"continuous_usage_stats": True}})
+        evs = [json.loads(x[6:]) for x in (await r.text()).split("\n\n") if x.startswith("data: {")]
+        counts = [e["usage"]["completion_tokens"] for e in evs if e.get("usage")]
+        assert counts and counts == sorted(counts) and counts[-1] <= 4
+    run(with_client(body))

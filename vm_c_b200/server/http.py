@@ -91,7 +91,10 @@ class EngineLoop(threading.Thread):
 
 
 def _sampling_from(body: dict, default_max: int) -> SamplingParams:
-    sp = SamplingParams()
+    # An HTTP request samples with temperature 1, top-p 1 and no top-k unless it says otherwise (the
+    # OpenAI defaults, as the reference's parse_chat_request / parse_completion_request apply them:
+    # src/server/http_server.cpp:157-162, 236-241), not with the offline SamplingParams defaults.
+    sp = SamplingParams(temperature=1.0, top_p=1.0, top_k=0)
     sp.max_tokens = int(body.get("max_completion_tokens") or body.get("max_tokens") or default_max)
     for k in ("temperature", "top_p", "min_p", "repetition_penalty", "frequency_penalty", "presence_penalty"):
         if body.get(k) is not None:
@@ -180,7 +183,7 @@ class OpenAIServer:
                 if delta:
                     text.append(delta)
                     if on_delta:
-                        await on_delta(delta)
+                        await on_delta(delta, n)
                 if finished:
                     reason = fr
                     break
@@ -199,7 +202,7 @@ class OpenAIServer:
         if not isinstance(msgs, list) or not msgs:
             return self._err(400, "messages must be a non-empty list")
         sp = _sampling_from(body, self.cfg.default_max_tokens)
-        prompt = self.template.render(msgs, True, sp.enable_thinking)
+        prompt = self.template.render(msgs, bool(body.get("add_generation_prompt", True)), sp.enable_thinking)
         ids = self.tok.encode(prompt, add_bos=not prompt.startswith(self.tok.tokens[self.tok.bos_id])
                               if 0 <= self.tok.bos_id < self.tok.vocab_size else False)
         try:
@@ -213,6 +216,8 @@ class OpenAIServer:
         if not body.get("stream"):
             text, n, reason = await self._generate(ids, sp, detok)
             reasoning, content = split_reasoning(text, sp.enable_thinking)
+            if body.get("echo"):
+                content = prompt + content
             msg: dict[str, Any] = {"role": "assistant", "content": content}
             if reasoning:
                 msg["reasoning_content"] = reasoning
@@ -224,22 +229,28 @@ class OpenAIServer:
         resp = await self._sse_start(request)
         rs = ReasoningStream(sp.enable_thinking)
         chunk = {**base, "object": "chat.completion.chunk"}
+        so = body.get("stream_options") or {}
+        running_usage = bool(so.get("continuous_usage_stats"))
 
-        async def send(delta_obj, finish=None):
-            await self._sse(resp, {**chunk, "choices": [{"index": 0, "delta": delta_obj, "finish_reason": finish}]})
+        async def send(delta_obj, finish=None, n_out=None):
+            c = {**chunk, "choices": [{"index": 0, "delta": delta_obj, "finish_reason": finish}]}
+            if n_out is not None:
+                c["usage"] = {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}
+            await self._sse(resp, c)
 
         await send({"role": "assistant", "content": ""})
 
-        async def on_delta(d):
+        async def on_delta(d, n_out):
             r, c = rs.feed(d)
+            u = n_out if running_usage else None
             if r:
-                await send({"reasoning_content": r})
+                await send({"reasoning_content": r}, n_out=u)
             if c:
-                await send({"content": c})
+                await send({"content": c}, n_out=u)
 
         text, n, reason = await self._generate(ids, sp, detok, on_delta)
         await send({}, (reason or FinishReason.STOP).openai)
-        if (body.get("stream_options") or {}).get("include_usage"):
+        if so.get("include_usage"):
             await self._sse(resp, {**chunk, "choices": [], "usage": {"prompt_tokens": len(ids), "completion_tokens": n,
                                                                      "total_tokens": len(ids) + n}})
         await resp.write(b"data: [DONE]\n\n")
@@ -255,8 +266,9 @@ class OpenAIServer:
         if isinstance(prompt, list):
             if prompt and isinstance(prompt[0], int):
                 ids = [int(x) for x in prompt]
-            else:
-                prompt = prompt[0] if prompt else ""
+                prompt = self.tok.decode(ids, skip_special=False)
+            else:  # several prompt strings form one prompt, one per line (as the reference joins them)
+                prompt = "\n".join(str(p) for p in prompt)
                 ids = self.tok.encode(prompt)
         else:
             ids = self.tok.encode(prompt)
@@ -270,6 +282,8 @@ class OpenAIServer:
         detok = IncrementalDetokenizer(self.tok, sp.stop)
         if not body.get("stream"):
             text, n, reason = await self._generate(ids, sp, detok)
+            if body.get("echo"):
+                text = prompt + text
             return web.json_response({**base, "choices": [{"index": 0, "text": text, "logprobs": None,
                                                            "finish_reason": (reason or FinishReason.STOP).openai}],
                                       "usage": {"prompt_tokens": len(ids), "completion_tokens": n,
@@ -279,13 +293,20 @@ class OpenAIServer:
         head, tail = json.dumps({**base, "choices": [{"index": 0, "text": "\x00", "logprobs": None,
                                                       "finish_reason": None}]}).split('"\\u0000"')
         head, tail = ("data: " + head).encode(), (tail + "\n\n").encode()
+        so = body.get("stream_options") or {}
+        running_usage = bool(so.get("continuous_usage_stats"))
 
-        async def on_delta(d):
-            await resp.write(head + json.dumps(d).encode() + tail)
+        async def on_delta(d, n_out):
+            if running_usage:
+                await self._sse(resp, {**base, "choices": [{"index": 0, "text": d, "logprobs": None, "finish_reason": None}],
+                                       "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out,
+                                                 "total_tokens": len(ids) + n_out}})
+            else:
+                await resp.write(head + json.dumps(d).encode() + tail)
         text, n, reason = await self._generate(ids, sp, detok, on_delta)
         await self._sse(resp, {**base, "choices": [{"index": 0, "text": "", "logprobs": None,
                                                     "finish_reason": (reason or FinishReason.STOP).openai}]})
-        if (body.get("stream_options") or {}).get("include_usage"):
+        if so.get("include_usage"):
             await self._sse(resp, {**base, "choices": [], "usage": {"prompt_tokens": len(ids), "completion_tokens": n,
                                                                     "total_tokens": len(ids) + n}})
         await resp.write(b"data: [DONE]\n\n")
