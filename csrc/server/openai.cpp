@@ -371,8 +371,15 @@ void OpenAIServer::completions(const http::Request& rq, http::Responder& res) {
 }
 
 void OpenAIServer::models(const http::Request&, http::Responder& res) {
+  const int64_t t = unix_now();
+  Value perm = Value::object();
+  perm.set("id", "modelperm-" + hex_id(24)).set("object", "model_permission").set("created", t)
+      .set("allow_create_engine", false).set("allow_sampling", true).set("allow_logprobs", true)
+      .set("allow_search_indices", false).set("allow_view", true).set("allow_fine_tuning", false)
+      .set("organization", "*").set("group", Value()).set("is_blocking", false);
   Value m = Value::object();
-  m.set("id", cfg_.model_name).set("object", "model").set("created", unix_now()).set("owned_by", "vm_c");
+  m.set("id", cfg_.model_name).set("object", "model").set("created", t).set("owned_by", "vm_c")
+      .set("root", cfg_.model_name).set("permission", Value::Array{perm});
   Value v = Value::object();
   v.set("object", "list").set("data", Value::Array{m});
   send_json(res, 200, v);
@@ -397,7 +404,8 @@ void OpenAIServer::version(const http::Request&, http::Responder& res) {
 
 void OpenAIServer::tokenize(const http::Request& rq, http::Responder& res) {
   const Value body = parse_body(rq);
-  std::string text = body.get_string("content", body.get_string("prompt", ""));
+  // "text" is the reference's field; "content" and "prompt" are accepted as well
+  std::string text = body.get_string("text", body.get_string("content", body.get_string("prompt", "")));
   const auto ids = tok_.encode(text, body.get_bool("add_special", false) ? 1 : 0);
   Value arr = Value::array();
   for (int32_t t : ids) arr.push(static_cast<int64_t>(t));
@@ -412,7 +420,8 @@ void OpenAIServer::detokenize(const http::Request& rq, http::Responder& res) {
   if (const Value* t = body.get("tokens"); t && t->is_array())
     for (const Value& x : t->as_array()) ids.push_back(static_cast<int32_t>(x.as_int()));
   Value v = Value::object();
-  v.set("content", tok_.decode(ids, false));
+  const std::string text = tok_.decode(ids, false);
+  v.set("text", text).set("content", text);  // "text" as the reference answers
   send_json(res, 200, v);
 }
 

@@ -215,7 +215,9 @@ def test_tokenize_matches_python_spm(spm):
             st, r = srv.post("/tokenize", {"content": text, "add_special": add})
             assert st == 200 and r["tokens"] == tok.encode(text, add_bos=add), text
         st, r = srv.post("/detokenize", {"tokens": tok.encode(text, add_bos=True)})
-        assert r["content"] == tok.decode(tok.encode(text, add_bos=True), skip_special=False)
+        assert r["content"] == r["text"] == tok.decode(tok.encode(text, add_bos=True), skip_special=False)
+        st, r = srv.post("/tokenize", {"text": text})  # the reference's field name
+        assert r["tokens"] == tok.encode(text, add_bos=False)
 
 
 def test_tokenize_matches_python_bpe(bpe):
@@ -368,6 +370,7 @@ def test_routes_and_errors(spm):
     srv, tok = spm
     st, h, data = srv.request("GET", "/v1/models")
     assert st == 200 and json.loads(data)["data"][0]["id"] == "vm_c" and h["Access-Control-Allow-Origin"] == "*"
+    assert json.loads(data)["data"][0]["permission"][0]["object"] == "model_permission"
     assert json.loads(srv.request("GET", "/health")[2]) == {"status": "ok"}
     assert "version" in json.loads(srv.request("GET", "/version")[2])
     assert srv.request("OPTIONS", "/v1/completions")[0] == 204

@@ -321,8 +321,14 @@ class OpenAIServer:
             raise ValueError("prompt contains token ids outside the model vocabulary")
 
     async def models(self, request):
-        return web.json_response({"object": "list", "data": [{"id": self.name, "object": "model",
-                                                              "created": int(time.time()), "owned_by": "vm_c"}]})
+        t = int(time.time())
+        perm = {"id": f"modelperm-{uuid.uuid4().hex[:24]}", "object": "model_permission", "created": t,
+                "allow_create_engine": False, "allow_sampling": True, "allow_logprobs": True,
+                "allow_search_indices": False, "allow_view": True, "allow_fine_tuning": False, "organization": "*",
+                "group": None, "is_blocking": False}
+        return web.json_response({"object": "list", "data": [{"id": self.name, "object": "model", "created": t,
+                                                              "owned_by": "vm_c", "root": self.name,
+                                                              "permission": [perm]}]})
 
     async def health(self, request):
         if self.loop_thread.error is not None:
@@ -334,13 +340,14 @@ class OpenAIServer:
 
     async def tokenize(self, request):
         body = await request.json()
-        text = body.get("content", body.get("prompt", ""))
+        text = body.get("text", body.get("content", body.get("prompt", "")))  # "text": the reference's field
         ids = self.tok.encode(text, add_bos=bool(body.get("add_special", False)))
         return web.json_response({"tokens": ids})
 
     async def detokenize(self, request):
         body = await request.json()
-        return web.json_response({"content": self.tok.decode(body.get("tokens", []), skip_special=False)})
+        text = self.tok.decode(body.get("tokens", []), skip_special=False)
+        return web.json_response({"text": text, "content": text})  # "text" as the reference answers
 
     async def metrics(self, request):
         m = self.engine.metrics.prometheus()
