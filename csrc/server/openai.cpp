@@ -3,6 +3,7 @@
 
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <ctime>
 #include <functional>
 #include <mutex>
@@ -143,6 +144,26 @@ Value usage(size_t prompt, size_t completion) {
 
 bool sse(http::Responder& res, const Value& v) { return res.write("data: " + json::dump(v) + "\n\n"); }
 
+// Request diagnostics (the reference's env switches, src/main.cpp:527-570, 673-700):
+// VMC_LOG_PROMPT_VERBOSE=1 logs each prompt with its token ids and whether detokenising them gives it
+// back; VMC_LOG_DETOK=1 logs every generated token's id and text when a request ends.
+bool env_on(const char* name) {
+  const char* v = getenv(name);
+  return v && v[0] == '1';
+}
+
+void log_prompt(const TextTokenizer& tok, const std::string& prompt, const std::vector<int32_t>& ids) {
+  static const bool on = env_on("VMC_LOG_PROMPT_VERBOSE");
+  if (!on) return;
+  std::string first, last;
+  for (size_t i = 0; i < ids.size() && i < 5; ++i) first += std::to_string(ids[i]) + " ";
+  for (size_t i = ids.size() > 5 ? ids.size() - 5 : 0; i < ids.size(); ++i) last += std::to_string(ids[i]) + " ";
+  auto strip = [](const std::string& x) { return x.substr(std::min(x.find_first_not_of(' '), x.size())); };
+  const bool rt = strip(tok.decode(ids, true)) == strip(prompt);  // special tokens (BOS) do not count
+  fprintf(stderr, "[PROMPT] %zu tokens first5=[%s] last5=[%s] round-trip=%s text=%s\n", ids.size(), first.c_str(),
+          last.c_str(), rt ? "Y" : "N", json::quote(prompt).c_str());
+}
+
 // Submits a request (validation errors become 400 responses before any stream starts), then drives
 // it to completion: detokenized deltas go through on_delta (which returns false when the client is
 // gone). drive() returns false if the request was aborted for a lost client.
@@ -165,6 +186,8 @@ std::shared_ptr<GenStream> submit(ServeLoop& loop, const GenRequest& g) {
 bool drive(ServeLoop& loop, const TextTokenizer& tok, const std::shared_ptr<GenStream>& st, const BodyParams& p,
            int poll_ms, http::Responder& res, GenResult& out,
            const std::function<bool(const std::string&, size_t)>& on_delta) {
+  static const bool log_detok = env_on("VMC_LOG_DETOK");
+  std::vector<int32_t> ids;
   IncrementalDetokenizer detok(tok, p.stop);
   for (;;) {
     GenEvent ev;
@@ -176,6 +199,7 @@ bool drive(ServeLoop& loop, const TextTokenizer& tok, const std::shared_ptr<GenS
       continue;
     }
     out.n += ev.tokens.size();
+    if (log_detok) ids.insert(ids.end(), ev.tokens.begin(), ev.tokens.end());
     bool finished = ev.finished;
     FinishReason reason = ev.reason;
     const std::string delta = detok.push(ev.tokens, finished);
@@ -193,6 +217,11 @@ bool drive(ServeLoop& loop, const TextTokenizer& tok, const std::shared_ptr<GenS
     }
     if (finished) {
       out.reason = reason == FinishReason::NONE ? FinishReason::STOP : reason;
+      if (log_detok) {
+        std::string line;
+        for (int32_t t : ids) line += "(" + std::to_string(t) + ", " + json::quote(tok.decode({t}, false)) + ") ";
+        fprintf(stderr, "[DETOK] request %lld: %s\n", static_cast<long long>(st->id()), line.c_str());
+      }
       return true;
     }
   }
@@ -247,6 +276,7 @@ void OpenAIServer::chat(const http::Request& rq, http::Responder& res) {
   const std::string prompt = chat_.render(cm, p.add_generation_prompt, p.enable_thinking);
   const bool add_bos = !bos_text_.empty() && prompt.compare(0, bos_text_.size(), bos_text_) != 0;
   p.gen.prompt = tok_.encode(prompt, add_bos ? 1 : 0);
+  log_prompt(tok_, prompt, p.gen.prompt);
   const std::string cid = "chatcmpl-" + hex_id(32);
   p.gen.name = cid;
   Value base = Value::object();
@@ -330,6 +360,7 @@ void OpenAIServer::completions(const http::Request& rq, http::Responder& res) {
   } catch (const std::runtime_error& e) {
     throw HttpError(400, std::string("bad prompt: ") + e.what());
   }
+  log_prompt(tok_, prompt_text, p.gen.prompt);
   const std::string id = "cmpl-" + hex_id(32);
   p.gen.name = id;
   Value base = Value::object();

@@ -717,3 +717,27 @@ def test_echo_joined_prompts_running_usage_and_no_generation_prompt(spm):
     st, r = srv.post("/v1/chat/completions", {"messages": msgs, "max_tokens": 2, "add_generation_prompt": False})
     prompt = chatml(msgs, False, True)
     assert r["usage"]["prompt_tokens"] == len(tok.encode(prompt, add_bos=not prompt.startswith(tok.tokens[1])))
+
+
+def test_prompt_and_detok_diagnostics(exe, tmp_path):
+    """VMC_LOG_PROMPT_VERBOSE / VMC_LOG_DETOK (the reference's request diagnostics) log the prompt with
+    its round-trip check and every generated token."""
+    toks, scores, types = spm_vocab()
+    path = str(tmp_path / "v.gguf")
+    write_vocab_gguf(path, toks, scores, types, [], "llama", "default", 1, 2)
+    pf = str(tmp_path / "port")
+    env = dict(os.environ, VMC_LOG_PROMPT_VERBOSE="1", VMC_LOG_DETOK="1")
+    proc = subprocess.Popen([exe, path, "--port", "0", "--port-file", pf], stderr=subprocess.PIPE, env=env)
+    try:
+        t0 = time.time()
+        while not os.path.exists(pf) or not open(pf).read().strip():
+            assert proc.poll() is None and time.time() - t0 < 30
+            time.sleep(0.02)
+        c = http.client.HTTPConnection("127.0.0.1", int(open(pf).read()), timeout=30)
+        c.request("POST", "/v1/completions", body=json.dumps({"prompt": "the rain", "max_tokens": 3}))
+        assert c.getresponse().status == 200
+        c.close()
+    finally:
+        proc.terminate()
+        err = proc.communicate(timeout=30)[1].decode()
+    assert "[PROMPT]" in err and "round-trip=Y" in err and "[DETOK]" in err, err

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import asyncio
 import json
+import os
 import threading
 import time
 import uuid
@@ -30,6 +31,11 @@ from .tokenizer import IncrementalDetokenizer, Tokenizer
 
 log = get_logger("server")
 VERSION = "vm_c_b200 0.1.0"
+# Request diagnostics (the reference's env switches, src/main.cpp:527-570, 673-700):
+# VMC_LOG_PROMPT_VERBOSE=1 logs each prompt in full with its token ids and whether detokenising them
+# gives the prompt back; VMC_LOG_DETOK=1 logs every generated token's id and text when a request ends.
+_LOG_PROMPT = os.environ.get("VMC_LOG_PROMPT_VERBOSE", "") == "1"
+_LOG_DETOK = os.environ.get("VMC_LOG_DETOK", "") == "1"
 
 
 class EngineLoop(threading.Thread):
@@ -162,10 +168,17 @@ class OpenAIServer:
         self.loop_thread.wake()
         return rid, q
 
+    def _log_prompt(self, prompt: str, ids: list[int]) -> None:
+        if _LOG_PROMPT:
+            back = self.tok.decode(ids)  # special tokens (BOS) do not count
+            log.info("[PROMPT] %d tokens first5=%s last5=%s round-trip=%s text=%r", len(ids), ids[:5], ids[-5:],
+                     "Y" if back.lstrip() == prompt.lstrip() else "N", prompt)
+
     async def _generate(self, ids, sp, detok, on_delta=None):
         """Drive one request; returns (text, n_tokens, finish_reason)."""
         rid, q = self._submit(ids, sp)
         n = 0
+        out_ids: list[int] = []
         text = []
         reason = None
         try:
@@ -175,6 +188,8 @@ class OpenAIServer:
                     more, finished, fr = q.get_nowait()
                     toks = toks + more
                 n += len(toks)
+                if _LOG_DETOK:
+                    out_ids += toks
                 delta = detok.push(toks, final=finished)
                 if detok.stopped:  # a stop string ends the request even when its last token hit a limit
                     if not finished:
@@ -186,6 +201,8 @@ class OpenAIServer:
                         await on_delta(delta, n)
                 if finished:
                     reason = fr
+                    if _LOG_DETOK:
+                        log.info("[DETOK] %s: %s", rid, [(t, self.tok.decode([t], skip_special=False)) for t in out_ids])
                     break
         except (asyncio.CancelledError, ConnectionResetError):
             self.engine.abort_request(rid)
@@ -205,6 +222,7 @@ class OpenAIServer:
         prompt = self.template.render(msgs, bool(body.get("add_generation_prompt", True)), sp.enable_thinking)
         ids = self.tok.encode(prompt, add_bos=not prompt.startswith(self.tok.tokens[self.tok.bos_id])
                               if 0 <= self.tok.bos_id < self.tok.vocab_size else False)
+        self._log_prompt(prompt, ids)
         try:
             self._validate(ids)
         except ValueError as e:
@@ -273,6 +291,7 @@ class OpenAIServer:
         else:
             ids = self.tok.encode(prompt)
         sp = _sampling_from(body, self.cfg.default_completion_max_tokens)
+        self._log_prompt(prompt, ids)
         try:
             self._validate(ids)
         except ValueError as e:
