@@ -81,19 +81,24 @@ size_t match_gpt2(const std::vector<uint32_t>& c, size_t i) {
   return trailing_space(c, i);
 }
 
-// 'llama-bpe' (digits = 3) and 'qwen2' (digits = 1):
+// 'llama-bpe' (digits = 3), 'qwen2' (digits = 1) and 'qwen35' (digits = 1, marks = true: combining
+// marks join letters):
 // (?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,D}| ?[^\s\p{L}\p{N}]+[\r\n]*|\s*[\r\n]+|\s+(?!\S)|\s+
-size_t match_llama3(const std::vector<uint32_t>& c, size_t i, int digits) {
+// with \p{L} read as [\p{L}\p{M}] in the word run and [^\s\p{L}\p{M}\p{N}] as "other" when marks.
+size_t match_llama3(const std::vector<uint32_t>& c, size_t i, int digits, bool marks) {
   if (size_t n = contraction(c, i, true)) return n;
   const size_t n = c.size();
+  const int word = marks ? (uni::kLetter | uni::kMark) : uni::kLetter;
+  const auto is_word = [&](uint32_t x) { return (uni::char_class(x) & word) != 0; };
+  const auto other = [&](uint32_t x) { return is_other(x) && !(marks && uni::is_mark(x)); };
   // [^\r\n\p{L}\p{N}]?\p{L}+
   {
     size_t b = n;
-    if (uni::is_letter(c[i])) b = i;
-    else if (!is_nl(c[i]) && !uni::is_number(c[i]) && i + 1 < n && uni::is_letter(c[i + 1])) b = i + 1;
+    if (is_word(c[i])) b = i;
+    else if (!is_nl(c[i]) && !uni::is_letter(c[i]) && !uni::is_number(c[i]) && i + 1 < n && is_word(c[i + 1])) b = i + 1;
     if (b < n) {
       size_t j = b;
-      while (j < n && uni::is_letter(c[j])) ++j;
+      while (j < n && is_word(c[j])) ++j;
       return j - i;
     }
   }
@@ -106,11 +111,11 @@ size_t match_llama3(const std::vector<uint32_t>& c, size_t i, int digits) {
   // ' ?[^\s\p{L}\p{N}]+[\r\n]*'
   {
     size_t b = n;
-    if (c[i] == ' ' && i + 1 < n && is_other(c[i + 1])) b = i + 1;
-    else if (is_other(c[i])) b = i;
+    if (c[i] == ' ' && i + 1 < n && other(c[i + 1])) b = i + 1;
+    else if (other(c[i])) b = i;
     if (b < n) {
       size_t j = b;
-      while (j < n && is_other(c[j])) ++j;
+      while (j < n && other(c[j])) ++j;
       while (j < n && is_nl(c[j])) ++j;
       return j - i;
     }
@@ -129,14 +134,27 @@ size_t match_llama3(const std::vector<uint32_t>& c, size_t i, int digits) {
 
 }  // namespace
 
+std::string TextTokenizer::pre_family(const std::string& pre) {
+  // tokenizer.ggml.pre names that use one of the four expressions (GGUF vocabulary convention)
+  static const std::pair<const char*, const char*> alias[] = {
+      {"llama3", "llama-bpe"}, {"llama-v3", "llama-bpe"}, {"falcon3", "llama-bpe"}, {"falcon-h1", "llama-bpe"},
+      {"pixtral", "llama-bpe"}, {"dbrx", "llama-bpe"}, {"smaug-bpe", "llama-bpe"}, {"deepseek-r1-qwen", "qwen2"},
+      {"gpt-2", "gpt2"}, {"phi-2", "gpt2"}};
+  for (const auto& a : alias)
+    if (pre == a.first) return a.second;
+  if (pre == "llama-bpe" || pre == "qwen2" || pre == "qwen35") return pre;
+  return "gpt2";
+}
+
 std::vector<std::string> TextTokenizer::pre_split(const std::string& text, const std::string& family) {
   const Cps c = decode_cps(text);
   std::vector<std::string> out;
   size_t i = 0;
   while (i < c.cp.size()) {
     size_t len;
-    if (family == "llama-bpe") len = match_llama3(c.cp, i, 3);
-    else if (family == "qwen2") len = match_llama3(c.cp, i, 1);
+    if (family == "llama-bpe") len = match_llama3(c.cp, i, 3, false);
+    else if (family == "qwen2") len = match_llama3(c.cp, i, 1, false);
+    else if (family == "qwen35") len = match_llama3(c.cp, i, 1, true);
     else len = match_gpt2(c.cp, i);
     len = std::max<size_t>(1, len);
     out.emplace_back(text, c.off[i], c.off[i + len] - c.off[i]);
@@ -222,7 +240,7 @@ std::unique_ptr<TextTokenizer> TextTokenizer::from_gguf(const GgufFile& f) {
 std::vector<int32_t> TextTokenizer::encode_text(const std::string& text, bool first) const {
   if (text.empty()) return {};
   if (gpt2_) {
-    const std::string fam = (pre_ == "llama-bpe" || pre_ == "qwen2") ? pre_ : "gpt2";
+    const std::string fam = pre_family(pre_);
     std::vector<int32_t> out;
     for (const std::string& piece : pre_split(text, fam)) {
       std::string mapped;

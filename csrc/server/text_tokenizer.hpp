@@ -5,8 +5,9 @@
 // llama_vocab tokenizer it is replaced by at run time (src/main.cpp:15-73, 496-513; SentencePiece-BPE
 // with byte fallback) and the incremental detokenizer
 // (include/vm_c/tokenizer/incremental_detokenizer.hpp:11-55). The merge loops are the shared native
-// core (csrc/host/tokenizer.cpp); the pre-tokenisers of the "gpt2", "llama-bpe" and "qwen2" vocabulary
-// families are written as scanners that split text exactly as the published regular expressions do.
+// core (csrc/host/tokenizer.cpp); the pre-tokenisers of the "gpt2", "llama-bpe", "qwen2" and "qwen35"
+// vocabulary families are written as scanners that split text exactly as the published regular
+// expressions do.
 #pragma once
 #include <cstdint>
 #include <memory>
@@ -49,6 +50,8 @@ class TextTokenizer {
 
   // The pre-tokeniser alone: the pieces one family's expression splits `text` into.
   static std::vector<std::string> pre_split(const std::string& text, const std::string& family);
+  // The expression family ("gpt2", "llama-bpe", "qwen2", "qwen35") of a tokenizer.ggml.pre name.
+  static std::string pre_family(const std::string& pre);
 
  private:
   std::vector<int32_t> encode_text(const std::string& text, bool first) const;

@@ -1,7 +1,7 @@
 // UTF-8 helpers and the Unicode character classes the pre-tokenisers need.
 //
-// Classes (letter = general category L*, number = N*, space = the `\s` class of Unicode regular
-// expressions) come from a range table that the build generates from the Python `regex` module the
+// Classes (letter = general category L*, number = N*, mark = M*, space = the `\s` class of Unicode
+// regular expressions) come from a range table that the build generates from the Python `regex` module the
 // Python tokenizer uses, so both tokenizers split text identically.
 #pragma once
 #include <cstddef>
@@ -10,13 +10,14 @@
 
 namespace vmc::uni {
 
-enum : int { kLetter = 1, kNumber = 2, kSpace = 4 };
+enum : int { kLetter = 1, kNumber = 2, kSpace = 4, kMark = 8 };
 
 // Class bits of code point `cp` (0 for "other").
 int char_class(uint32_t cp);
 inline bool is_letter(uint32_t cp) { return char_class(cp) & kLetter; }
 inline bool is_number(uint32_t cp) { return char_class(cp) & kNumber; }
 inline bool is_space(uint32_t cp) { return char_class(cp) & kSpace; }
+inline bool is_mark(uint32_t cp) { return char_class(cp) & kMark; }
 
 // Decodes the code point at s[i] and advances i. A byte that does not start a well-formed
 // sequence decodes as U+FFFD and advances by one.

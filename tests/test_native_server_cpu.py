@@ -176,7 +176,7 @@ def spm(exe, tmp_path_factory):
     srv.close()
 
 
-@pytest.fixture(scope="module", params=["llama-bpe", "qwen2", "gpt2"])
+@pytest.fixture(scope="module", params=["llama-bpe", "qwen2", "gpt2", "qwen35", "llama3"])
 def bpe(exe, tmp_path_factory, request):
     tmp = str(tmp_path_factory.mktemp("bpe"))
     toks, types, merges = gpt2_vocab()
@@ -191,15 +191,17 @@ def bpe(exe, tmp_path_factory, request):
 
 
 TEXTS = ["hello world", "I'm here, it's fine; they'll go", "  two  spaces\n\nand lines\r\n", "digits 1234567 x",
-         "naïve café 漢字 😀", "<|im_start|>user\nhi<|im_end|>", "", "tab\tsep", "UPPER 'S 'LL", CORPUS[:200]]
+         "naïve café 漢字 😀", "<|im_start|>user\nhi<|im_end|>", "", "tab\tsep", "UPPER 'S 'LL", CORPUS[:200],
+         "cafe\u0301 ke\u0300 नि क\u093fत \u20d7x"]
 
 
 def test_pre_tokenizers_match_regex(exe):
     alphabet = list("abcXYZ'sStTrReEvVmMlLdD019 \t\n\r.,!?-_()\"") + \
-        ["é", "ü", "漢", "٣", "½", "Ⅻ", "😀", " ", "　", "​", "́", "ſ", "ǅ", "\x0b", "\x85", "ß"]
+        ["é", "ü", "漢", "٣", "½", "Ⅻ", "😀", " ", "　", "​", "́", "ſ", "ǅ", "\x0b", "\x85", "ß",
+         "\u0300", "\u093f", "\u20d7", "क"]  # combining marks (Mn, Mc) and a letter they follow
     rng = random.Random(0)
     texts = TEXTS + ["".join(rng.choice(alphabet) for _ in range(rng.randint(0, 24))) for _ in range(1500)]
-    for fam in ("gpt2", "llama-bpe", "qwen2"):
+    for fam in ("gpt2", "llama-bpe", "qwen2", "qwen35"):
         inp = "".join(json.dumps(t) + "\n" for t in texts).encode()
         out = subprocess.run([exe, "--tool", "pre-split", fam], input=inp, capture_output=True, check=True).stdout
         got = [json.loads(x) for x in out.decode().split("\n") if x]

@@ -81,16 +81,17 @@ GEN_DIR = EXT_DIR / "gen"
 
 
 def gen_unicode_ranges() -> Path:
-    """Writes the letter / number / whitespace code point ranges of the server's pre-tokenisers
+    """Writes the letter / number / whitespace / mark code point ranges of the server's pre-tokenisers
     (csrc/server/unicode.cpp includes them), taken from the `regex` module that the Python tokenizer
     uses so that both split text identically."""
     out = GEN_DIR / "unicode_ranges.inc"
-    if out.exists():
+    version = "// unicode classes v2: letter 1, number 2, space 4, mark 8"
+    if out.exists() and out.read_text().startswith(version):
         return out
     import regex
     chars = "".join(chr(c) for c in range(0x110000) if not 0xD800 <= c <= 0xDFFF)
     cls = bytearray(0x110000)
-    for bit, pat in ((1, r"\p{L}+"), (2, r"\p{N}+"), (4, r"\s+")):
+    for bit, pat in ((1, r"\p{L}+"), (2, r"\p{N}+"), (4, r"\s+"), (8, r"\p{M}+")):
         for m in regex.compile(pat).finditer(chars):
             for ch in m.group(0):
                 cls[ord(ch)] |= bit
@@ -103,7 +104,7 @@ def gen_unicode_ranges() -> Path:
             rows.append((lo, c, cls[lo]))
         c += 1
     GEN_DIR.mkdir(parents=True, exist_ok=True)
-    lines = ["// Generated by vm_c_b200/_build.py gen_unicode_ranges(): {lo, hi, class bits}.",
+    lines = [version, "// Generated by vm_c_b200/_build.py gen_unicode_ranges(): {lo, hi, class bits}.",
              "const Range kRanges[] = {"]
     for k in range(0, len(rows), 4):
         lines.append("    " + " ".join("{0x%X, 0x%X, %d}," % r for r in rows[k:k + 4]))

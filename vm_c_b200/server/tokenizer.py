@@ -24,7 +24,20 @@ _PRE = {
                   r"""|\s*[\r\n]+|\s+(?!\S)|\s+"""),
     "qwen2": (r"""(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}| ?[^\s\p{L}\p{N}]+[\r\n]*"""
               r"""|\s*[\r\n]+|\s+(?!\S)|\s+"""),
+    # Qwen3.5 vocabularies: combining marks (\p{M}) belong to words
+    "qwen35": (r"""(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?[\p{L}\p{M}]+|\p{N}| ?[^\s\p{L}\p{M}\p{N}]+[\r\n]*"""
+               r"""|\s*[\r\n]+|\s+(?!\S)|\s+"""),
 }
+# tokenizer.ggml.pre names that use one of the expressions above (GGUF vocabulary convention)
+_PRE_ALIAS = {"llama3": "llama-bpe", "llama-v3": "llama-bpe", "falcon3": "llama-bpe", "falcon-h1": "llama-bpe",
+              "pixtral": "llama-bpe", "dbrx": "llama-bpe", "smaug-bpe": "llama-bpe", "deepseek-r1-qwen": "qwen2",
+              "gpt-2": "gpt2", "phi-2": "gpt2"}
+
+
+def pre_family(pre: str) -> str:
+    """The pre-tokeniser expression a vocabulary's tokenizer.ggml.pre names (unknown names: gpt2)."""
+    pre = _PRE_ALIAS.get(pre, pre)
+    return pre if pre in _PRE else "gpt2"
 
 TOKEN_NORMAL, TOKEN_UNKNOWN, TOKEN_CONTROL, TOKEN_USER, TOKEN_UNUSED, TOKEN_BYTE = 1, 2, 3, 4, 5, 6
 
@@ -60,7 +73,7 @@ class Tokenizer:
                                                 [m.encode("utf-8") for m in merges], self.model)
         if unk_id >= 0:
             self.core.set_unk(unk_id)
-        self.pre = regex.compile(_PRE.get(pre, _PRE["gpt2"]))
+        self.pre = regex.compile(_PRE[pre_family(pre)])
         self.special = {t: i for i, t in enumerate(tokens)
                         if self.types[i] in (TOKEN_CONTROL, TOKEN_USER) and t}
         self._special_re = regex.compile("(" + "|".join(regex.escape(t) for t in
