@@ -277,3 +277,15 @@ def test_f16_and_f32_weights(tmp_path):
     assert r.dtype == torch.uint8 and torch.equal(r.view(torch.float16), emb[3:7])
     assert torch.equal(h.rows("output.weight", 5, 9), out[5:9])
     assert torch.equal(h.rows("output_norm.weight").view(-1), torch.ones(H))
+
+
+def test_pre_tokenizer_family_from_tokenizer_json():
+    """HuggingFace tokenizer.json split expressions map onto the GGUF pre-tokeniser families."""
+    from vm_c_b200.hf.source import _pre_family
+    from vm_c_b200.server.tokenizer import _PRE
+    for fam in ("llama-bpe", "qwen2", "qwen35", "gpt2"):
+        pt = {"type": "Sequence", "pretokenizers": [
+            {"type": "Split", "pattern": {"Regex": _PRE[fam]}, "behavior": "Isolated", "invert": False},
+            {"type": "ByteLevel", "add_prefix_space": False}]}
+        assert _pre_family(pt) == fam
+    assert _pre_family({"type": "ByteLevel"}) == "gpt2"

@@ -243,6 +243,31 @@ def _spm_metadata(tj, model, vocab, tokens, types, merges, added, n, d, hf_confi
     return md
 
 
+
+def _pre_family(pre_tokenizer: dict) -> str:
+    """The GGUF pre-tokeniser family of a tokenizer.json pre_tokenizer, from its split expression:
+    "llama-bpe" (digits in groups of three), "qwen2" (single digits), "qwen35" (single digits, combining
+    marks join words), else "gpt2"."""
+    regs: list[str] = []
+
+    def walk(x):
+        if isinstance(x, dict):
+            pat = x.get("pattern")
+            if isinstance(pat, dict) and isinstance(pat.get("Regex"), str):
+                regs.append(pat["Regex"])
+            for v in x.values():
+                walk(v)
+        elif isinstance(x, list):
+            for v in x:
+                walk(v)
+    walk(pre_tokenizer)
+    for r in regs:
+        if "(?i:'s|'t|'re|'ve|'m|'ll|'d)" in r:
+            if "\\p{M}" in r:
+                return "qwen35"
+            return "llama-bpe" if "\\p{N}{1,3}" in r else "qwen2"
+    return "gpt2"
+
 def _tokenizer_metadata(d: str, hf_config: dict) -> dict:
     """GGUF tokenizer.* keys from tokenizer.json (byte-level BPE) and tokenizer_config.json."""
     p = os.path.join(d, "tokenizer.json")
@@ -273,9 +298,7 @@ def _tokenizer_metadata(d: str, hf_config: dict) -> dict:
     merges = [m if isinstance(m, str) else " ".join(m) for m in (model.get("merges") or [])]
     if spm:
         return _spm_metadata(tj, model, vocab, tokens, types, merges, added, n, d, hf_config)
-    pre = "gpt2"
-    if "(?i:'s|'t|'re|'ve|'m|'ll|'d)" in json.dumps(tj.get("pre_tokenizer") or {}):
-        pre = "llama-bpe"
+    pre = _pre_family(tj.get("pre_tokenizer") or {})
     tc_path = os.path.join(d, "tokenizer_config.json")
     tc = json.load(open(tc_path, encoding="utf-8")) if os.path.exists(tc_path) else {}
     bos = _token_id(tc.get("bos_token"), vocab)
