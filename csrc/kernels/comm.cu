@@ -122,12 +122,14 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rmsnorm_kernel(ArArgs a) {
       __threadfence();
       for (int q = 0; q < NR; ++q) st_relaxed_sys(a.flags[q] + b * kMaxRanks + a.rank, e);
     }
+    // Bounded by time (about 2 s of SM clock for all peers together), not by a poll count, so the
+    // bound does not depend on how long one system-scope load takes.
     int good = 1;
+    const long long t0 = clock64();
     for (int q = 0; q < NR && good; ++q) {
-      uint32_t i = 0;
       while ((VMC_AR_SYNC == 0 ? ld_acquire_sys(a.flags[a.rank] + b * kMaxRanks + q)
                                : ld_relaxed_sys(a.flags[a.rank] + b * kMaxRanks + q)) < e) {
-        if (++i > kSpinLimit) {
+        if (clock64() - t0 > (4ll << 30)) {
           atomicCAS(a.err, 0u, static_cast<uint32_t>(kErrCommWait));
           good = 0;
           break;
