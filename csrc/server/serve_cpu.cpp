@@ -16,6 +16,8 @@
 //   vmc_serve_cpu --tool pre-split FAMILY      a string -> the pieces of pre-tokeniser FAMILY
 //   vmc_serve_cpu --tool utf8-stream -         byte chunks [[b, ...], ...] -> the text each chunk
 //                                              releases through the streaming UTF-8 decoder
+//   vmc_serve_cpu --tool json -                a line -> the document re-serialised, or
+//                                              {"error": offset} if it is not valid JSON
 //   vmc_serve_cpu --tool render-chat TEMPLATE_FILE
 //       {"messages": [...], "add_generation_prompt": b, "enable_thinking": b, "bos": s, "eos": s}
 //       -> the chat prompt the server builds with that Jinja template (an empty file: ChatML);
@@ -83,11 +85,19 @@ int run_tool(const std::string& tool, const std::string& arg) {
       ss << f.rdbuf();
       tmpl = ss.str();
     }
-  } else if (tool != "pre-split" && tool != "utf8-stream") {
+  } else if (tool != "pre-split" && tool != "utf8-stream" && tool != "json") {
     throw std::runtime_error("unknown tool " + tool);
   }
   std::string line;
   while (std::getline(std::cin, line)) {
+    if (tool == "json") {  // the parser itself is under test: report a rejection instead of failing
+      try {
+        std::cout << vmc::json::dump(vmc::json::parse(line)) << "\n";
+      } catch (const vmc::json::ParseError& e) {
+        std::cout << "{\"error\": " << e.offset() << "}\n";
+      }
+      continue;
+    }
     const Value in = vmc::json::parse(line);
     Value out;
     if (tool == "pre-split") {

@@ -743,3 +743,72 @@ def test_prompt_and_detok_diagnostics(exe, tmp_path):
         proc.terminate()
         err = proc.communicate(timeout=30)[1].decode()
     assert "[PROMPT]" in err and "round-trip=Y" in err and "[DETOK]" in err, err
+
+
+def test_json_parser_matches_python(exe):
+    """The native JSON parser and writer against Python's json module: random documents survive the
+    round trip unchanged (integers stay exact), and random edits of them are accepted or rejected as
+    Python accepts or rejects them (Python's NaN / Infinity extension excluded)."""
+    rng = random.Random(11)
+
+    def value(depth):
+        k = rng.randrange(8 if depth < 4 else 5)
+        if k == 0:
+            return None
+        if k == 1:
+            return rng.random() < 0.5
+        if k == 2:
+            return rng.randrange(-2 ** 62, 2 ** 62)
+        if k == 3:
+            return rng.choice([0.5, -1e-300, 1.5e300, 3.141592653589793, -0.0, 2.5e-8])
+        if k == 4:
+            return "".join(rng.choice(["a", "é", "\\", '"', "\n", "\t", "\x01", "😀", "漢", "/", " "])
+                           for _ in range(rng.randrange(8)))
+        if k in (5, 6):
+            return [value(depth + 1) for _ in range(rng.randrange(4))]
+        return {f"k{rng.randrange(5)}{i}": value(depth + 1) for i in range(rng.randrange(4))}
+
+    docs = [json.dumps(value(0), ensure_ascii=rng.random() < 0.5) for _ in range(600)]
+    edits = []
+    for d in docs[:400]:
+        for _ in range(2):
+            k = rng.randrange(len(d) + 1)
+            e = d[:k] + rng.choice([",", "]", "}", '"', "\\", "{", "[", "1", "e", ".", "-", " ", ":", "tru"]) + d[k + rng.randrange(2):]
+            if "\n" not in e:
+                edits.append(e)
+    lines = docs + edits
+    out = subprocess.run([exe, "--tool", "json", "-"], input=("\n".join(lines) + "\n").encode(), capture_output=True,
+                         check=True, timeout=120).stdout.decode().split("\n")
+
+    def py(doc):
+        try:
+            return True, json.loads(doc, parse_constant=lambda c: (_ for _ in ()).throw(ValueError(c)))
+        except ValueError:
+            return False, None
+
+    def wide(v):  # integers beyond int64 are doubles, lone surrogates U+FFFD in the native model
+        if isinstance(v, int) and not isinstance(v, bool) and not -2 ** 63 <= v < 2 ** 63:
+            return float(v)
+        if isinstance(v, str):
+            return v.encode("utf-16-le", "surrogatepass").decode("utf-16-le", "replace")
+        if isinstance(v, list):
+            return [wide(x) for x in v]
+        if isinstance(v, dict):
+            return {wide(k): wide(x) for k, x in v.items()}
+        return v
+
+    def finite(v):
+        if isinstance(v, float):
+            return v == v and abs(v) != float("inf")
+        if isinstance(v, list):
+            return all(finite(x) for x in v)
+        if isinstance(v, dict):
+            return all(finite(x) for x in v.values())
+        return True
+
+    for doc, got in zip(lines, out):
+        ok, want = py(doc)
+        if not ok:
+            assert got.startswith('{"error": '), (doc, got)
+        elif finite(want):  # a literal beyond double range: Python keeps infinity, the writer emits null
+            assert json.loads(got) == wide(want), (doc, got)
