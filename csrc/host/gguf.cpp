@@ -125,20 +125,26 @@ void GgufFile::parse() {
     ti.name = c.read_str();
     uint32_t nd = c.read<uint32_t>();
     if (nd > 4) throw std::runtime_error("gguf: tensor rank > 4: " + ti.name);
-    for (uint32_t d = 0; d < nd; ++d) ti.ne.push_back(static_cast<int64_t>(c.read<uint64_t>()));
+    for (uint32_t d = 0; d < nd; ++d) {
+      const uint64_t n = c.read<uint64_t>();
+      if (n > (1ull << 40)) throw std::runtime_error("gguf: implausible dimension of tensor " + ti.name);
+      ti.ne.push_back(static_cast<int64_t>(n));
+    }
     uint32_t ty = c.read<uint32_t>();
     if (!gtype_known(ty)) throw std::runtime_error("gguf: unsupported tensor type " + std::to_string(ty) + " for " + ti.name);
     ti.type = static_cast<GType>(ty);
     ti.offset = c.read<uint64_t>();
     ti.nbytes = gtype_row_bytes(ti.type, ti.ne.empty() ? 1 : ti.ne[0]);
-    for (size_t d = 1; d < ti.ne.size(); ++d) ti.nbytes *= static_cast<uint64_t>(ti.ne[d]);
+    for (size_t d = 1; d < ti.ne.size(); ++d)  // a size that does not fit in 64 bits cannot be in the file
+      if (__builtin_mul_overflow(ti.nbytes, static_cast<uint64_t>(ti.ne[d]), &ti.nbytes))
+        throw std::runtime_error("gguf: size of tensor " + ti.name + " overflows");
     tensor_index_[ti.name] = tensors_.size();
     tensors_.push_back(std::move(ti));
   }
   uint64_t pos = static_cast<uint64_t>(c.p - base_);
   data_offset_ = (pos + alignment_ - 1) / alignment_ * alignment_;
-  for (auto& t : tensors_) {
-    if (data_offset_ + t.offset + t.nbytes > size_)
+  for (auto& t : tensors_) {  // compared without sums that could wrap around
+    if (data_offset_ > size_ || t.offset > size_ - data_offset_ || t.nbytes > size_ - data_offset_ - t.offset)
       throw std::runtime_error("gguf: tensor " + t.name + " extends past end of file");
   }
 }

@@ -78,3 +78,32 @@ def test_row_bytes():
     assert row_bytes(GType.Q8_0, 64) == 68
     with pytest.raises(ValueError):
         row_bytes(GType.Q4_K, 100)
+
+
+def _raw_gguf(path, ne, gtype=0, offset=0, data=b"\0" * 64):
+    """A GGUF v3 file with one tensor and no metadata, written byte by byte (dimensions and offset
+    as given, not as a writer would compute them)."""
+    import struct
+    name = b"t"
+    hdr = b"GGUF" + struct.pack("<IQQ", 3, 1, 0) + struct.pack("<Q", len(name)) + name
+    hdr += struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", n) for n in ne)
+    hdr += struct.pack("<IQ", gtype, offset)
+    hdr += b"\0" * ((32 - len(hdr) % 32) % 32)
+    open(path, "wb").write(hdr + data)
+
+
+def test_reader_rejects_corrupt_tensor_infos(host, tmp_path):
+    """Dimensions, sizes and offsets that would wrap 64-bit arithmetic are refused at open, so no
+    tensor view can point outside the mapped file."""
+    ok = str(tmp_path / "ok.gguf")
+    _raw_gguf(ok, [4, 4])
+    assert host.GgufFile.open(ok) is not None
+    for i, (ne, off) in enumerate([([4, 2 ** 63], 0),            # negative as int64
+                                   ([2 ** 33, 2 ** 33], 0),      # 64-bit size overflow
+                                   ([4, 4], 2 ** 64 - 16),       # offset wraps the end check
+                                   ([4, 5], 0),                  # past the end of the file
+                                   ([2 ** 41], 0)]):             # implausible dimension
+        p = str(tmp_path / f"bad{i}.gguf")
+        _raw_gguf(p, ne, offset=off)
+        with pytest.raises(RuntimeError):
+            host.GgufFile.open(p)
