@@ -272,13 +272,16 @@ void SafetensorsFile::parse() {
       const int es = st_dtype_size(t.dtype);
       if (!has_dtype || !has_shape || offs.size() != 2 || es == 0)
         throw std::runtime_error("safetensors: tensor " + name + " in " + path_ + " has a bad entry");
-      uint64_t numel = 1;
+      uint64_t numel = 1, nbytes = 0;
       for (int64_t d : t.shape) {
         if (d < 0) throw std::runtime_error("safetensors: negative dimension in " + name);
-        numel *= static_cast<uint64_t>(d);
+        if (__builtin_mul_overflow(numel, static_cast<uint64_t>(d), &numel))
+          throw std::runtime_error("safetensors: size of " + name + " overflows");
       }
-      if (offs[0] < 0 || offs[1] < offs[0] || static_cast<uint64_t>(offs[1] - offs[0]) != numel * es ||
-          data0 + static_cast<uint64_t>(offs[1]) > size_)
+      if (__builtin_mul_overflow(numel, static_cast<uint64_t>(es), &nbytes))
+        throw std::runtime_error("safetensors: size of " + name + " overflows");
+      if (offs[0] < 0 || offs[1] < offs[0] || static_cast<uint64_t>(offs[1] - offs[0]) != nbytes ||
+          static_cast<uint64_t>(offs[1]) > size_ - data0)
         throw std::runtime_error("safetensors: tensor " + name + " byte range does not match its shape in " + path_);
       t.begin = data0 + static_cast<uint64_t>(offs[0]);
       t.end = data0 + static_cast<uint64_t>(offs[1]);

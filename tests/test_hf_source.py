@@ -71,6 +71,25 @@ def test_native_header_parser_edge_cases(tmp_path):
         SafetensorsFile(str(p))
 
 
+
+@pytest.mark.parametrize("entry", [
+    {"dtype": "F32", "shape": [2 ** 62, 8], "data_offsets": [0, 0]},            # element count overflows
+    {"dtype": "F64", "shape": [2 ** 61], "data_offsets": [0, 0]},               # byte size overflows
+    {"dtype": "U8", "shape": [8], "data_offsets": [2 ** 63 - 9, 2 ** 63 - 1]},  # range far past the end
+    {"dtype": "U8", "shape": [8], "data_offsets": [8, 16]},                     # range just past the end
+    {"dtype": "U8", "shape": [-8], "data_offsets": [0, 8]},                     # negative dimension
+    {"dtype": "U8", "shape": [8], "data_offsets": [8, 0]},                      # reversed range
+])
+def test_crafted_header_is_rejected(tmp_path, entry):
+    """Sizes and offsets that would wrap 64-bit arithmetic, or reach past the file, are refused while
+    the header is read, so no tensor view can point outside the mapped file."""
+    import struct
+    h = json.dumps({"x": entry}).encode()
+    p = tmp_path / "crafted.safetensors"
+    p.write_bytes(struct.pack("<Q", len(h)) + h + b"\0" * 8)
+    with pytest.raises(ValueError):
+        SafetensorsFile(str(p))
+
 def test_name_map():
     assert gguf_name("model.layers.3.self_attn.o_proj.weight") == ("blk.3.attn_output.weight", None)
     assert gguf_name("model.layers.0.block_sparse_moe.experts.5.w2.weight") == ("blk.0.ffn_down_exps.weight", 5)
