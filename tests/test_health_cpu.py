@@ -12,6 +12,7 @@ import time
 import pytest
 import torch.distributed as dist
 
+from vm_c_b200.core.sampling_params import FinishReason
 from vm_c_b200.parallel.health import FaultPlan, Heartbeats, InjectedFault, RankFailure, StepWatchdog
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -72,13 +73,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run_pair(tmp_path, fault, ctrl_timeout=4):
+def _run_pair(tmp_path, fault, ctrl_timeout=4, workload=""):
     out = str(tmp_path / "res")
     port = _free_port()
     procs = []
     for r in range(2):
         env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(r), WORLD_SIZE="2",
-                   LOCAL_RANK=str(r), VMC_FAULT=fault, CTRL_TIMEOUT=str(ctrl_timeout))
+                   LOCAL_RANK=str(r), VMC_FAULT=fault, CTRL_TIMEOUT=str(ctrl_timeout), WORKLOAD=workload)
         procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "health_worker.py"), out], env=env,
                                       stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
     try:
@@ -103,6 +104,21 @@ def test_no_fault_runs_to_completion(tmp_path):
     res, codes = _run_pair(tmp_path, "")
     assert res[0]["error"] is None and res[1]["error"] is None
     assert res[0]["steps"] == res[1]["steps"] >= 40
+
+
+def test_ranks_stay_in_lock_step(tmp_path):
+    """Requests added over several steps, a client abort and a host-side finish reach the follower
+    through the control header + payload exchange; both engines emit the same tokens and finishes."""
+    res, codes = _run_pair(tmp_path, "", workload="mixed")
+    assert res[0]["error"] is None and res[1]["error"] is None
+    assert res[0]["steps"] == res[1]["steps"]
+    outs = res[0]["outs"]
+    assert set(outs) == {"a", "b", "c", "d", "e"}
+    assert outs == res[1]["outs"]
+    assert all(o[1] for o in outs.values())
+    assert outs["c"][2] == int(FinishReason.LENGTH) and len(outs["c"][0]) == 12
+    assert outs["a"][2] == int(FinishReason.STOP) and len(outs["a"][0]) < 30
+    assert outs["d"][2] == int(FinishReason.ABORTED)
 
 
 @pytest.mark.parametrize("kind", ["exit", "raise"])
