@@ -110,6 +110,7 @@ class LLMEngine:
         # Launch step n+1 before emitting step n's outputs (runners with launch / wait, no speculation;
         # VMC_PIPELINE=0 turns it off).
         self._inflight = None
+        self._snapshots = True  # step() returns snapshots of running requests (generate() turns this off)
         self.pipelined = (hasattr(runner, "launch") and getattr(runner, "spec_k", 0) == 0
                           and os.environ.get("VMC_PIPELINE", "1") != "0")
 
@@ -338,7 +339,7 @@ class LLMEngine:
                 self._finish(req, FinishReason(reason), new_toks)
             elif req.stream_callback:
                 req.stream_callback(req, new_toks, False)
-            outs.append(req.to_output() if (finished or req.stream_callback is None) else None)
+            outs.append(req.to_output() if (finished or (req.stream_callback is None and self._snapshots)) else None)
         dt = now - t0
         self.metrics.record_step(counts.T, counts.S, counts.num_decode, dt, plan.num_cached_tokens)
         self.step_id += 1
@@ -391,8 +392,14 @@ class LLMEngine:
         done: dict[str, RequestOutput] = {}
         reqs = [self.add_request(p, sp) for p, sp in zip(prompts, plist)]
         order = [r.request_id for r in reqs]
-        while self.has_unfinished():
-            for o in self.step():
-                if o.finished:
-                    done[o.request_id] = o
+        # only finished outputs are read here: skip the per-step snapshots of running requests (a copy
+        # of every token list each step, which grows with the output length)
+        self._snapshots = False
+        try:
+            while self.has_unfinished():
+                for o in self.step():
+                    if o.finished:
+                        done[o.request_id] = o
+        finally:
+            self._snapshots = True
         return [done[r] for r in order]
