@@ -110,6 +110,7 @@ class LLMEngine:
         # Launch step n+1 before emitting step n's outputs (runners with launch / wait, no speculation;
         # VMC_PIPELINE=0 turns it off).
         self._inflight = None
+        self._pen_ids: set[int] = set()  # running requests with repetition/frequency/presence penalties
         self._snapshots = True  # step() returns snapshots of running requests (generate() turns this off)
         self.pipelined = (hasattr(runner, "launch") and getattr(runner, "spec_k", 0) == 0
                           and os.environ.get("VMC_PIPELINE", "1") != "0")
@@ -154,6 +155,8 @@ class LLMEngine:
             sp.eos_token_ids = self.eos
             self.sched.add_request(iid, req.prompt_token_ids, sp)
             self.requests[iid] = req
+            if p.has_penalties:
+                self._pen_ids.add(iid)
             self.by_name[req.request_id] = iid
         for name in aborts:
             iid = self.by_name.get(name)
@@ -208,6 +211,8 @@ class LLMEngine:
 
     def _penalties(self, plan, S: int):
         """CSR triples (row, token, output count) for rows that use penalties (None if none)."""
+        if not self._pen_ids:
+            return None
         rows, toks, cnts = [], [], []
         for k, iid in enumerate(plan.sample_ids()):
             req = self.requests[int(iid)]
@@ -313,18 +318,25 @@ class LLMEngine:
         if self.logits_hook is not None:
             self.logits_hook([int(i) for i in sample_ids], self.runner.full_logits(counts.S))
         events = self.sched.update(plan, toks[:counts.S])
-        lp_by_id = {int(iid): float(lps[k]) for k, iid in enumerate(sample_ids)}
+        lp_by_id = dict(zip(sample_ids, lps[:len(sample_ids)].tolist()))
         return self._apply(events, lp_by_id, plan, counts, t0)
 
     def _apply(self, events, lp_by_id, plan, counts, t0):
         now = time.perf_counter()
+        reqs = self.requests
         for iid, new_toks, finished, reason in events:
-            req = self.requests.get(int(iid))
+            req = reqs.get(iid)
             if req is None:
                 continue
-            req.output_token_ids.extend(new_toks)
-            req.output_logprobs.extend([lp_by_id.get(int(iid), 0.0)] * len(new_toks))
-            req.token_times.extend([now] * len(new_toks))
+            lp = lp_by_id.get(iid, 0.0)
+            if len(new_toks) == 1:  # a decode step
+                req.output_token_ids.append(new_toks[0])
+                req.output_logprobs.append(lp)
+                req.token_times.append(now)
+            else:
+                req.output_token_ids.extend(new_toks)
+                req.output_logprobs.extend([lp] * len(new_toks))
+                req.token_times.extend([now] * len(new_toks))
         return events, plan, counts, t0, now
 
     def _emit(self, done) -> list[RequestOutput]:
@@ -357,6 +369,7 @@ class LLMEngine:
         if spec is not None:
             spec.forget(req.int_id)
         self.requests.pop(req.int_id, None)
+        self._pen_ids.discard(req.int_id)
         self.by_name.pop(req.request_id, None)
         self.metrics.record_finish(req)
         if req.stream_callback:
