@@ -205,8 +205,8 @@ class LLMEngine:
             self.slot_owner[slots[k]] = ids[k]
         out = np.zeros(max(S, R_pad_rows), dtype=SAMPLE_DTYPE)
         out[:S] = self.slot_params[slots]
-        for k in range(S):
-            out[k]["step"] = len(self.requests[int(ids[k])].output_token_ids)
+        reqs = self.requests
+        out["step"][:S] = [len(reqs[i].output_token_ids) for i in ids.tolist()]
         return out
 
     def _penalties(self, plan, S: int):
