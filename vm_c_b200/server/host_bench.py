@@ -8,6 +8,10 @@ token and the gap between streamed chunks, measured at the client.
     python -m vm_c_b200.server.host_bench --impl native --clients 64 --requests 512
     python -m vm_c_b200.server.host_bench --impl python --clients 64 --requests 512
 
+    # the engine alone (core/engine.py, no HTTP): host time per step and the gap between one step's
+    # wait and the next step's launch, where the GPU idles
+    python -m vm_c_b200.server.host_bench --engine --clients 64 --prompt-tokens 1024 --max-tokens 256
+
 With --impl, a tokenizer-only GGUF is written and the server is started with a deterministic rule in
 place of the model (token after t at position p = (31 t + 7 p + 11) mod V): `vmc_serve_cpu` for the
 native server (csrc/server/), and for the Python server (server/http.py) the same engine
@@ -92,6 +96,65 @@ def serve_python_rule(gguf: str, port: int, max_seqs: int, max_batched: int, max
     srv = OpenAIServer(eng, tok, "vm_c", ServerConfig())
     srv.app.middlewares.append(cors)
     web.run_app(srv.app, host="127.0.0.1", port=port, print=lambda *a: None)
+
+
+def engine_host_cost(seqs: int, prompt_tokens: int, max_tokens: int, vocab: int = 32000) -> dict:
+    """LLMEngine.generate over a runner that applies the rule in launch / wait form (the pipelined
+    path the GPU runner takes): wall time per step and the host gap between a step's wait and the next
+    launch, which on a GPU is device idle time."""
+    from ..config import VmCConfig
+    from ..core.engine import LLMEngine, ModelRunner
+    from ..core.sampling_params import SamplingParams
+    a, b, c = RULE
+    max_len = prompt_tokens + max_tokens + 16
+
+    class PipelinedRule(ModelRunner):
+        def __init__(self):
+            self.num_kv_blocks = seqs * (max_len // 16 + 1) + 1
+            self.max_model_len = max_len
+            self.gaps, self.t_wait = [], None
+
+        def bind_layout(self, layout):
+            self.layout = layout
+
+        def graph_bucket(self, n):
+            return n
+
+        def launch(self, meta, counts, params, penalties=None):
+            if self.t_wait is not None:
+                self.gaps.append(time.perf_counter() - self.t_wait)
+            L = self.layout
+            lidx = meta[L.off_logits_idx:L.off_logits_idx + counts.S]
+            ids = meta[L.off_input_ids + lidx].astype(np.int64)
+            pos = meta[L.off_positions + lidx].astype(np.int64)
+            return ((a * ids + b * pos + c) % vocab).astype(np.int32), np.zeros(counts.S, np.float32)
+
+        def wait(self, handle):
+            self.t_wait = time.perf_counter()
+            return handle
+
+        def execute(self, *args):
+            return self.wait(self.launch(*args))
+
+    cfg = VmCConfig()
+    cfg.model.vocab = vocab
+    cfg.model.max_model_len = max_len
+    cfg.model.eos_token_ids = [2]
+    cfg.scheduler.max_num_seqs = seqs
+    cfg.scheduler.max_num_batched_tokens = 2048
+    cfg.finalize()
+    runner = PipelinedRule()
+    eng = LLMEngine(cfg, runner)
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(3, vocab, prompt_tokens).tolist() for _ in range(seqs)]
+    t0 = time.perf_counter()
+    eng.generate(prompts, SamplingParams(temperature=0.8, top_k=40, max_tokens=max_tokens, ignore_eos=True))
+    wall = time.perf_counter() - t0
+    g = np.array(runner.gaps[len(runner.gaps) // 8:]) * 1e6  # decode steps (after the prefill chunks)
+    return {"engine": "core/engine.py (pipelined launch / wait)", "seqs": seqs, "prompt_tokens": prompt_tokens,
+            "max_tokens": max_tokens, "steps": eng.step_id, "host_us_per_step": round(wall / eng.step_id * 1e6, 1),
+            "gap_wait_to_launch_us_p50": round(float(np.median(g)), 1),
+            "gap_wait_to_launch_us_p90": round(float(np.percentile(g, 90)), 1)}
 
 
 def _free_port() -> int:
@@ -209,6 +272,7 @@ def main() -> None:
     g = ap.add_mutually_exclusive_group(required=True)
     g.add_argument("--url", help="load-test a running server")
     g.add_argument("--impl", choices=["native", "python"], help="start this server over the rule backend")
+    g.add_argument("--engine", action="store_true", help="time the engine's host path alone (no HTTP)")
     g.add_argument("--serve-python", metavar="GGUF", help=argparse.SUPPRESS)
     ap.add_argument("--port", type=int, default=0)
     ap.add_argument("--clients", type=int, default=64)
@@ -220,6 +284,9 @@ def main() -> None:
     ap.add_argument("--max-num-batched-tokens", type=int, default=2048)
     ap.add_argument("--max-model-len", type=int, default=1024)
     a = ap.parse_args()
+    if a.engine:
+        print(json.dumps(engine_host_cost(a.clients, a.prompt_tokens, a.max_tokens)), flush=True)
+        return
     if a.serve_python:
         serve_python_rule(a.serve_python, a.port, a.max_num_seqs, a.max_num_batched_tokens, a.max_model_len)
         return
