@@ -661,6 +661,14 @@ def test_host_bench_runs(impl):
     assert out["errors"] == 0 and out["completion_tokens"] == 16 * 8
 
 
+def test_host_bench_engine_mode():
+    """`host_bench --engine` runs the engine's pipelined path to completion and reports its host cost."""
+    from vm_c_b200.server.host_bench import engine_host_cost
+    out = engine_host_cost(8, 32, 16, vocab=1000)
+    assert out["steps"] >= 16 and out["host_us_per_step"] > 0
+    assert 0 < out["gap_wait_to_launch_us_p50"] <= out["gap_wait_to_launch_us_p90"]
+
+
 def test_streaming_utf8_decoder_matches_python(exe):
     """The native detokenizer's streaming UTF-8 decoder releases, chunk by chunk, what Python's
     incremental decoder (errors="replace") releases: incomplete trailing sequences wait for their next
