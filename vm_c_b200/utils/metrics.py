@@ -8,10 +8,16 @@ from __future__ import annotations
 
 import math
 import threading
+from collections import deque
 from dataclasses import dataclass, field
 
+# Latency samples kept for the percentiles: the most recent ones only, so a server that runs for
+# days holds a bounded history (the serving bench's whole run fits in these windows).
+TTFT_WINDOW = 1 << 16
+ITL_WINDOW = 1 << 20
 
-def percentile(xs: list[float], p: float) -> float:
+
+def percentile(xs, p: float) -> float:
     if not xs:
         return float("nan")
     s = sorted(xs)
@@ -30,8 +36,8 @@ class EngineMetrics:
     preemptions: int = 0
     finished: int = 0
     step_time_s: float = 0.0
-    ttft_s: list[float] = field(default_factory=list)
-    itl_s: list[float] = field(default_factory=list)
+    ttft_s: deque = field(default_factory=lambda: deque(maxlen=TTFT_WINDOW))
+    itl_s: deque = field(default_factory=lambda: deque(maxlen=ITL_WINDOW))
     _lock: threading.Lock = field(default_factory=threading.Lock, repr=False)
 
     def record_step(self, T: int, S: int, nd: int, dt: float, cached: int) -> None:
